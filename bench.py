@@ -1,0 +1,364 @@
+#!/usr/bin/env python3
+"""Benchmark of the paged-KV hot path on B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2] [--impl reference]
+
+Default workload: BASELINE config 2 -- one continuous-batching iteration of 64 sequences x
+2048 cached tokens (32 query / 8 kv heads, d 128, fp32 KV, 16-token blocks, 16384-block
+pool): upload the step's tables + slot mapping, append one new K/V row per sequence, decode
+every sequence.  A "step" is that iteration; tokens/s = sequences decoded per second.
+
+`value` times the step with inputs resident in HBM (CUDA events, max over ranks).  `e2e`
+times the same iteration through gkv_decode_step_host with pinned HOST buffers (q, new K/V,
+tables in; attention output out), copies included.  Multi-GPU runs are weak-scaled: every
+rank owns its own pool and its own 64 sequences (sequence partitioning, no collective).
+
+`--impl reference` times the CPU restatement of the reference's PagedAttentionKernel
+(oracle/, faithful threading: sequences serial, OpenMP over query heads) on the host cores;
+the reference itself is C# and cannot be built in this image.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "glacier.serve_b200"))
+
+METRIC = "decode KV GB/s per B200 vs HBM peak; decode tokens/s at 1/2/4/8 GPUs vs C# CPU"
+UNIT = "tokens/s"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def workload(name: str, rank: int):
+    from glacier_kv import workloads as W
+
+    seed = W.SEED + 1000003 * rank
+    if name == "cfg1":
+        return W.cfg1(seed)
+    if name == "cfg2":
+        return W.cfg2(seed)
+    if name == "cfg3":
+        return W.cfg3(seed, "f32")
+    if name == "cfg3-bf16":
+        return W.cfg3(seed, "bf16")
+    if name == "cfg5":
+        return W.cfg5_local(0, 8, seed)
+    raise SystemExit(f"unknown config {name}")
+
+
+def describe(w) -> str:
+    return (f"{w.name}: {'append+decode' if w.slot_mapping.size else 'decode'}, {w.batch} seqs, "
+            f"sum ctx {int(w.ctx_lens.sum())} (max {int(w.ctx_lens.max())}), {w.n_heads}q/{w.heads_kv}kv heads, "
+            f"d {w.head_dim}, {w.dtype} KV, block {w.block_size}, pool {w.total_blocks} blocks")
+
+
+class Clocks:
+    """nvidia-smi sampler running during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.rows = []
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) > 8 for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def traffic_from_profiles(cfg: str):
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        e = d.get(cfg)
+        if e:
+            return e.get("dram_bytes_per_launch")
+    return None
+
+
+def cpu_baseline_run(w, steps: int, budget_s: float, threads: int, seed: int):
+    """Times the CPU restatement (oracle/) of PagedAttentionKernel on a bounded sample of
+    the workload: `sample` sequences with their real context lengths, arena restricted to
+    their blocks, one sample per step."""
+    from oracle import pyoracle as O
+
+    rng = np.random.default_rng(seed)
+    sample = min(w.batch, 16)
+    rows = np.sort(rng.choice(w.batch, sample, replace=False))
+    ctx = w.ctx_lens[rows]
+    bs = w.block_size
+    nblk = [(int(c) + bs - 1) // bs for c in ctx]
+    tables = np.full((sample, max(nblk)), -1, np.int32)
+    at = 0
+    for i, n in enumerate(nblk):
+        tables[i, :n] = np.arange(at, at + n, dtype=np.int32)
+        at += n
+    g = O.geom(at, 1, w.heads_kv, w.head_dim, w.v_head_dim, bs, O.BF16 if w.dtype == "bf16" else O.F32)
+    K, V = O.new_arena(g)
+    for arr in (K, V):
+        x = rng.standard_normal(arr.shape, dtype=np.float32)
+        arr[...] = O.f32_to_bf16_bits(x) if w.dtype == "bf16" else x
+    q = rng.standard_normal((sample, w.n_heads, w.head_dim)).astype(np.float32)
+    O.decode_batch(K, V, g, 0, tables, ctx, q, w.n_heads, w.scale, n_threads=threads)  # warm-up
+    times = []
+    t_start = time.perf_counter()
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        O.decode_batch(K, V, g, 0, tables, ctx, q, w.n_heads, w.scale, n_threads=threads)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s:
+            break
+    med = statistics.median(times)
+    return {
+        "value": sample / med,
+        "unit": UNIT,
+        "cores": threads,
+        "kind": "port",
+        "sample": (f"{sample} of {w.batch} sequences of {w.name} (their real ctx lengths, "
+                   f"{int(ctx.sum())} tokens), median of {len(times)} runs; sequences serial, "
+                   f"OpenMP over query heads as PagedAttentionKernel.cs:48"),
+        "ms_per_sample": med * 1e3,
+    }
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import pyoracle as O
+
+    w = workload(args.config, 0)
+    threads = O.max_threads()
+    res = cpu_baseline_run(w, max(args.steps, 1), budget_s=120.0, threads=threads, seed=w.seed)
+    line = {
+        "metric": METRIC, "value": res["value"], "unit": UNIT, "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": res["ms_per_sample"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": describe(w), "l2": "n/a (CPU)",
+                   "implementation": "C restatement of PagedAttentionKernel.ComputeAttention "
+                                     "(the C# reference needs .NET 10 + un-vendored NuGet; not buildable here)"},
+        "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="cfg2")
+    ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import glacier_kv as G
+    from glacier_kv import workloads as W
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    w = workload(args.config, rank)
+    pool = W.make_pool(w, device=local)
+    W.fill_arena_randn(pool, seed=w.seed)
+    stream = torch.cuda.current_stream(dev)
+    rng = np.random.default_rng(w.seed + 17)
+    q = torch.from_numpy(rng.standard_normal((w.batch, w.n_heads, w.head_dim)).astype(np.float32)).to(dev)
+    n_tok = int(w.slot_mapping.size)
+    kn = torch.from_numpy(rng.standard_normal((max(n_tok, 1), w.heads_kv, w.head_dim)).astype(np.float32)).to(dev)
+    vn = torch.from_numpy(rng.standard_normal((max(n_tok, 1), w.heads_kv, w.v_head_dim)).astype(np.float32)).to(dev)
+    out = torch.zeros((w.batch, w.n_heads, w.v_head_dim), dtype=torch.float32, device=dev)
+    max_blocks = w.tables.shape[1]
+    pool.reserve_step(w.batch, max_blocks, max(n_tok, 1), w.n_heads)
+    kv_bytes = w.kv_bytes()
+    small = kv_bytes < 2 * 126e6  # working set within reach of L2: flush between steps
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if small else None
+
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+
+    def step(timed_decode=None):
+        pool.upload_step(w.tables, w.ctx_lens, w.slot_mapping, stream=stream)
+        launches = 0
+        if n_tok:
+            pool.kv_append(0, kn[:n_tok], vn[:n_tok], stream=stream)
+            launches += pool.last_launch_count
+        if timed_decode is not None:
+            timed_decode[0].record(stream)
+        pool.paged_decode(0, q, out, w.n_heads, w.scale, stream=stream)
+        if timed_decode is not None:
+            timed_decode[1].record(stream)
+        return launches + pool.last_launch_count
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+
+    # ---- device-resident timing ----
+    dec_events = [(ev(), ev()) for _ in range(args.steps)]
+    step_events = [(ev(), ev()) for _ in range(args.steps)]
+    launches = 0
+    barrier()
+    torch.cuda.synchronize(dev)
+    with Clocks(local) as clk:
+        t0 = ev()
+        t0.record(stream)
+        for i in range(args.steps):
+            if flush is not None:
+                flush.zero_()
+            step_events[i][0].record(stream)
+            launches += step(dec_events[i])
+            step_events[i][1].record(stream)
+        t1 = ev()
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    step_ms = sum(a.elapsed_time(b) for a, b in step_events) / args.steps
+    span_ms = t0.elapsed_time(t1) / args.steps
+    ms = max_over_ranks(step_ms if flush is not None else span_ms)
+    dec_ms = sum(a.elapsed_time(b) for a, b in dec_events) / args.steps
+    value = world * w.batch / (ms / 1e3)
+
+    # ---- end-to-end through the C ABI with host buffers ----
+    hq = q.cpu().pin_memory()
+    hk = kn[:max(n_tok, 1)].cpu().pin_memory()
+    hv = vn[:max(n_tok, 1)].cpu().pin_memory()
+    hout = torch.empty((w.batch, w.n_heads, w.v_head_dim), dtype=torch.float32).pin_memory()
+    meta_bytes = w.tables.nbytes + w.ctx_lens.nbytes + w.slot_mapping.nbytes
+    h2d = hq.numel() * 4 + (hk.numel() + hv.numel()) * 4 * (1 if n_tok else 0) + meta_bytes
+    d2h = hout.numel() * 4
+
+    def e2e_step():
+        pool.decode_step_host(0, w.tables, w.ctx_lens, w.slot_mapping, hk, hv, hq, hout, w.n_heads, w.scale,
+                              stream=stream)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0, e1 = ev(), ev()
+    e0.record(stream)
+    for _ in range(args.steps):
+        if flush is not None:
+            flush.zero_()
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    barrier()
+
+    if rank == 0:
+        peak, peak_kind = peaks()
+        alg_bytes = kv_bytes + w.qo_bytes()
+        achieved = alg_bytes / (dec_ms / 1e3) / 1e9
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) Q/K/V, seeded block tables)",
+            "config": {"workload": describe(w),
+                       "l2": "L2 flushed (256 MiB write) before every step" if small else
+                             f"inputs larger than L2 ({kv_bytes / 1e9:.2f} GB of KV read per step)",
+                       "parallelism": f"sequence-sharded: {world} GPU(s), one pool each, no collective",
+                       "step": "upload tables+slots (1 H2D) + kv_append + paged_decode (+ LSE merge)"},
+            "kv_gbs_per_gpu": kv_bytes / (ms / 1e3) / 1e9,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic_from_profiles(args.config),
+                         "kernel": "paged_decode (split-KV kernel + LSE merge kernel)",
+                         "bytes_per_launch": alg_bytes, "avg_launch_ms": dec_ms,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s"},
+            "e2e": {"value": world * w.batch / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms,
+                    "path": "gkv_decode_step_host (pinned host q/K/V/tables in, output out)"},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+        }
+        if not args.no_cpu_baseline and world == 1:
+            from oracle import pyoracle as O
+
+            line["cpu_baseline"] = {k: v for k, v in cpu_baseline_run(
+                w, steps=max(5, args.steps), budget_s=20.0, threads=O.max_threads(), seed=w.seed).items()
+                if k != "ms_per_sample"}
+        print(json.dumps(line), flush=True)
+    pool.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,173 @@
+// Internal C++ state behind the C ABI of include/glacier_kv.h.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/glacier_kv.h"
+#include "kernels.h"
+
+namespace gkv {
+
+// ---- error reporting -------------------------------------------------------------------
+int set_error(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int cuda_fail(cudaError_t e, const char* what);
+
+// Restores the calling thread's current device on scope exit.
+class DeviceGuard {
+   public:
+    explicit DeviceGuard(int device);
+    ~DeviceGuard();
+    bool ok() const { return ok_; }
+
+   private:
+    int prev_ = -1;
+    bool ok_ = false;
+};
+
+// ---- host mirror of the free list (PagedBlockPool.cs:39,112-120,178-189,251-279) --------
+// Treiber stack over block indices.  The head packs (ABA tag << 32 | (index + 1)); a tagged
+// compare-exchange makes pop safe against a concurrent pop/push of the same index.
+class FreeStack {
+   public:
+    void init(int32_t n);  // pushes n-1 .. 0 so that 0 pops first
+    void push(int32_t idx);
+    int32_t pop();         // -1 when empty
+    int32_t count() const { return count_.load(std::memory_order_acquire); }
+
+   private:
+    std::unique_ptr<std::atomic<int32_t>[]> next_;
+    std::atomic<uint64_t> head_{0};
+    std::atomic<int32_t> count_{0};
+};
+
+// ConcurrentDictionary<ulong,int> analogue for the prefix map (PagedBlockPool.cs:43):
+// sharded, each shard under its own mutex.
+class PrefixMap {
+   public:
+    bool find(uint64_t h, int32_t* out) const;
+    void set(uint64_t h, int32_t id);
+    void remove_if(uint64_t h, int32_t id);  // TryRemove(KeyValuePair(h, id))
+
+   private:
+    static constexpr int kShards = 64;
+    struct Shard {
+        mutable std::mutex mu;
+        std::unordered_map<uint64_t, int32_t> map;
+    };
+    Shard shards_[kShards];
+    static int shard_of(uint64_t h) { return static_cast<int>((h ^ (h >> 29) ^ (h >> 47)) & (kShards - 1)); }
+};
+
+// Device + pinned buffers of one step (block tables, ctx lens, slot mapping, work list).
+struct StepWorkspace {
+    int32_t max_batch = 0, max_blocks = 0, max_tokens = 0, n_heads = 0;
+    DecodeConfig cfg{};
+    int32_t n_ctas_max = 0;   // persistent grid size for this geometry
+    // packed metadata: one pinned staging buffer, one device buffer, one copy per step
+    char* h_meta = nullptr;
+    char* d_meta = nullptr;
+    size_t meta_cap = 0;
+    cudaEvent_t meta_copied = nullptr;  // staging buffer may be rewritten once this fires
+    bool meta_pending = false;
+    // partial results of split segments
+    float* d_part_acc = nullptr;
+    float* d_part_ml = nullptr;
+    size_t part_slots_cap = 0;  // slots (x head_groups x gp) the buffers hold
+    // device error word shared by every kernel of this pool
+    int* d_err = nullptr;
+    // e2e staging for gkv_decode_step_host
+    float* d_q = nullptr;
+    float* d_out = nullptr;
+    float* d_knew = nullptr;
+    float* d_vnew = nullptr;
+    size_t io_cap_q = 0, io_cap_out = 0, io_cap_k = 0, io_cap_v = 0;
+    // the uploaded step
+    int32_t batch = 0, n_tok = 0, up_max_blocks = 0;
+    DecodeWork work{};
+    const int64_t* d_slots = nullptr;
+    bool uploaded = false;
+};
+
+struct Pool {
+    gkv_pool_desc desc{};
+    ArenaGeom geom{};
+    size_t elem_bytes = 4;
+    int64_t k_bytes = 0, v_bytes = 0;
+    bool has_arena = false;
+
+    FreeStack free_stack;
+    std::unique_ptr<std::atomic<int32_t>[]> allocated;
+    std::unique_ptr<std::atomic<int32_t>[]> refcount;
+    std::unique_ptr<std::atomic<uint64_t>[]> prefix_hash;
+    PrefixMap prefix_map;
+
+    std::mutex pending_mu;
+    std::vector<int32_t> pending;  // queued CoW copies, (src, dst, valid) triples
+    int32_t* d_copy_ops = nullptr;
+    size_t copy_ops_cap = 0;
+    int32_t* h_copy_ops = nullptr;  // pinned staging for the op list
+    cudaEvent_t copy_ops_copied = nullptr;
+
+    StepWorkspace ws;
+    int last_launches = 0;
+
+    bool in_range(int32_t b) const {
+        return static_cast<uint32_t>(b) < static_cast<uint32_t>(desc.total_blocks);
+    }
+    // allocator primitives (reference semantics)
+    int32_t try_allocate();
+    int release(int32_t b);
+    int retain(int32_t b);
+    int refs(int32_t b) const;
+    bool try_find_prefix(uint64_t h, int32_t* out);
+    bool try_fork(int32_t src, int32_t valid, int32_t* out);
+    // device helpers (caller holds a DeviceGuard)
+    int flush_copies(cudaStream_t st);
+    int launch_copies(const int32_t* h_ops, int n, cudaStream_t st);
+};
+
+struct Table {
+    Pool* pool = nullptr;
+    std::vector<int32_t> ids;
+    int32_t token_count = 0;
+};
+
+// step.cpp
+int step_upload(Pool* p, const int32_t* tables, int32_t batch, int32_t max_blocks,
+                const int32_t* ctx_lens, const int64_t* slots, int32_t n_tok, cudaStream_t st);
+int step_decode(Pool* p, int32_t layer, const float* d_q, float* d_out, int32_t n_heads,
+                float scale, const float* d_sinks, cudaStream_t st);
+int step_append(Pool* p, int32_t layer, const float* d_k, const float* d_v, int32_t n_tok,
+                cudaStream_t st);
+int step_reserve(Pool* p, int32_t max_batch, int32_t max_blocks, int32_t max_tokens,
+                 int32_t n_heads);
+void step_free(Pool* p);
+
+// Work-list construction (host only; unit-tested through the C ABI helpers).
+struct WorkList {
+    std::vector<int32_t> piece_seg, piece_c0, piece_c1, piece_slot;
+    std::vector<int32_t> worker_begin;  // n_workers + 1
+    std::vector<int32_t> merge_seg, merge_slot0, merge_nslots;
+    int32_t n_slots = 0;
+    int64_t total_chunks = 0;
+};
+int32_t chunks_of(int32_t ctx, int32_t block_size);
+void build_work_list(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, int32_t block_size,
+                     int32_t n_workers, WorkList* out);
+
+}  // namespace gkv
+
+struct gkv_pool {
+    gkv::Pool impl;
+};
+struct gkv_table {
+    gkv::Table impl;
+};

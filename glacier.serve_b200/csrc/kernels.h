@@ -1,0 +1,88 @@
+// Host-side launch interface of the sm_100a kernels (C++ linkage, internal to the shim).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace gkv {
+
+// Geometry of one pool's arenas, in ELEMENTS of the storage type.
+struct ArenaGeom {
+    void* k;                 // K arena base
+    void* v;                 // V arena base
+    int64_t k_block_stride, k_layer_stride, k_head_stride;
+    int64_t v_block_stride, v_layer_stride, v_head_stride;
+    int32_t total_blocks, layers, heads_kv, head_dim, v_head_dim, block_size;
+    int32_t dtype;           // GKV_DTYPE_*
+};
+
+// ---- kv append ----
+// Writes token i's K/V rows into slot slots[i] (or `single_slot` when slots == nullptr and
+// n_tok == 1).  Source row stride in elements per token: k_tok_stride / v_tok_stride.
+cudaError_t launch_kv_append(const ArenaGeom& g, int layer, const float* k, const float* v,
+                             int64_t k_tok_stride, int64_t v_tok_stride, const int64_t* slots,
+                             int64_t single_slot, int n_tok, int* err, cudaStream_t stream);
+
+// ---- block copy ----
+// ops: [n][3] int32 (src, dst, valid_tokens) in device memory.
+cudaError_t launch_block_copy(const ArenaGeom& g, const int32_t* ops, int n, int* err,
+                              cudaStream_t stream);
+
+// ---- paged decode ----
+constexpr int kDecodeChunk = 8;  // tokens per decode work chunk
+
+// Work list of one step, built on the host (all pointers are device pointers).
+//  segment s = b * heads_kv + h; its chunks are k = 0 .. n_chunks(ctx_b) - 1, chunk k
+//  covering tokens [page*bs + sub*8, ...) with page = k / cpp, sub = k % cpp,
+//  cpp = ceil(block_size / 8).
+//  piece  = contiguous chunk range [c0, c1) of one segment handled by one warp worker.
+struct DecodeWork {
+    const int32_t* tables;             // [batch][max_blocks]
+    const int32_t* ctx_lens;           // [batch]
+    int32_t max_blocks;
+    const int32_t* piece_seg;          // [n_pieces]
+    const int32_t* piece_c0;           // [n_pieces]
+    const int32_t* piece_c1;           // [n_pieces]
+    const int32_t* piece_slot;         // partial slot, or -1 when the piece is a whole segment
+    const int32_t* worker_piece_begin; // [n_workers + 1]
+    int32_t n_ctas;                    // grid.x; n_workers = n_ctas * warps per CTA
+    int32_t n_slots;                   // partial slots in this step
+    const int32_t* merge_seg;          // [n_merge] segments split over several workers
+    const int32_t* merge_slot0;        // their first partial slot (slots are contiguous)
+    const int32_t* merge_nslots;
+    int32_t n_merge;
+};
+
+struct DecodeArgs {
+    int layer;
+    const float* q;      // [batch][n_heads][head_dim]
+    float* out;          // [batch][n_heads][v_head_dim]
+    int n_heads;
+    float scale;
+    const float* sinks;  // [n_heads] or nullptr
+    int has_sink_all;    // when sinks == nullptr: 1 = every head uses sink_all
+    float sink_all;
+    float* part_acc;     // [head_groups][n_slots][gp][v_head_dim]
+    float* part_ml;      // [head_groups][n_slots][gp][2]
+    int* err;
+};
+
+// Launch configuration the decode kernel uses for this geometry and query-head count.
+struct DecodeConfig {
+    bool supported;
+    int gp;            // query heads per pass (power of two <= 8)
+    int head_groups;   // ceil(group / gp)
+    int warps;         // warp workers per CTA
+    int threads;
+    size_t smem;
+    int ctas_per_sm;
+};
+DecodeConfig decode_config(const ArenaGeom& g, int n_heads);
+
+// Enqueues the split-KV decode and, when any segment spans several workers, the merge.
+// *launches receives the number of kernels enqueued.
+cudaError_t launch_paged_decode(const ArenaGeom& g, const DecodeWork& w, const DecodeArgs& a,
+                                int* launches, cudaStream_t stream);
+
+}  // namespace gkv

@@ -1,0 +1,586 @@
+// One decode/append step: packed metadata upload, split-KV work list, kernel dispatch.
+//
+// Replaces the per-sequence UploadBlockTable + ForwardPagedToken loop of
+// CudaPagedTransformerRunner.ForwardBatch (src/Glacier.Serve/Inference/PagedAttention/
+// CudaPagedTransformerRunner.cs:307-379) and the serial per-sequence Store +
+// ComputeAttention loop of PagedTransformerRunner.ForwardBatch (PagedTransformerRunner.cs:
+// 605-656): every table, context length and slot of the step travels in ONE host-to-device
+// copy, then one append launch and one decode launch (+ one merge launch) serve the batch.
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <thread>
+
+#include "gkv_internal.h"
+
+namespace gkv {
+
+namespace {
+
+constexpr int kMinChunksPerWorker = 16;  // below this a worker's pipeline never fills
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+int sm_count(int device) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n < 1) {
+        cudaGetLastError();
+        n = 148;
+    }
+    return n;
+}
+
+// Byte layout of the packed step metadata (identical on host and device).
+struct MetaLayout {
+    size_t slots, tables, ctx, pseg, pc0, pc1, pslot, wbeg, mseg, ms0, mns, total;
+};
+
+MetaLayout meta_layout(int64_t n_tok, int64_t batch, int64_t max_blocks, int64_t n_pieces,
+                       int64_t n_workers, int64_t n_merge) {
+    MetaLayout L{};
+    size_t o = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = o;
+        o = align_up(o + bytes, 16);
+        return at;
+    };
+    L.slots = take(static_cast<size_t>(n_tok) * 8);
+    L.tables = take(static_cast<size_t>(batch * max_blocks) * 4);
+    L.ctx = take(static_cast<size_t>(batch) * 4);
+    L.pseg = take(static_cast<size_t>(n_pieces) * 4);
+    L.pc0 = take(static_cast<size_t>(n_pieces) * 4);
+    L.pc1 = take(static_cast<size_t>(n_pieces) * 4);
+    L.pslot = take(static_cast<size_t>(n_pieces) * 4);
+    L.wbeg = take(static_cast<size_t>(n_workers + 1) * 4);
+    L.mseg = take(static_cast<size_t>(n_merge) * 4);
+    L.ms0 = take(static_cast<size_t>(n_merge) * 4);
+    L.mns = take(static_cast<size_t>(n_merge) * 4);
+    L.total = o;
+    return L;
+}
+
+int grow_device(void** p, size_t* cap, size_t need, const char* what) {
+    if (need <= *cap) return GKV_OK;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    const size_t sz = align_up(need + need / 4, 256);
+    cudaError_t e = cudaMalloc(p, sz);
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    *cap = sz;
+    return GKV_OK;
+}
+
+}  // namespace
+
+int32_t chunks_of(int32_t ctx, int32_t block_size) {
+    if (ctx <= 0) return 0;
+    const int32_t cpp = (block_size + kDecodeChunk - 1) / kDecodeChunk;
+    const int32_t full = ctx / block_size;
+    const int32_t rem = ctx - full * block_size;
+    return full * cpp + (rem + kDecodeChunk - 1) / kDecodeChunk;
+}
+
+void build_work_list(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, int32_t block_size,
+                     int32_t n_workers, WorkList* out) {
+    WorkList& W = *out;
+    W = WorkList{};
+    const int64_t n_seg = static_cast<int64_t>(batch) * heads_kv;
+    std::vector<int64_t> seg_start(static_cast<size_t>(n_seg) + 1, 0);
+    for (int32_t b = 0; b < batch; ++b) {
+        const int32_t c = chunks_of(ctx_lens[b], block_size);
+        for (int32_t h = 0; h < heads_kv; ++h) {
+            const int64_t s = static_cast<int64_t>(b) * heads_kv + h;
+            seg_start[static_cast<size_t>(s) + 1] = seg_start[static_cast<size_t>(s)] + c;
+        }
+    }
+    const int64_t total = seg_start[static_cast<size_t>(n_seg)];
+    W.total_chunks = total;
+    W.worker_begin.assign(static_cast<size_t>(n_workers) + 1, 0);
+    int64_t seg = 0;
+    for (int32_t w = 0; w < n_workers; ++w) {
+        W.worker_begin[static_cast<size_t>(w)] = static_cast<int32_t>(W.piece_seg.size());
+        int64_t lo = total * w / n_workers;
+        const int64_t hi = total * (w + 1) / n_workers;
+        while (lo < hi) {
+            while (seg_start[static_cast<size_t>(seg) + 1] <= lo) ++seg;
+            const int64_t s0 = seg_start[static_cast<size_t>(seg)];
+            const int64_t s1 = seg_start[static_cast<size_t>(seg) + 1];
+            const int64_t end = hi < s1 ? hi : s1;
+            W.piece_seg.push_back(static_cast<int32_t>(seg));
+            W.piece_c0.push_back(static_cast<int32_t>(lo - s0));
+            W.piece_c1.push_back(static_cast<int32_t>(end - s0));
+            lo = end;
+        }
+    }
+    W.worker_begin[static_cast<size_t>(n_workers)] = static_cast<int32_t>(W.piece_seg.size());
+    // Pieces of one segment are adjacent; a segment cut into several pieces gets
+    // contiguous partial slots and one merge entry.
+    const size_t np = W.piece_seg.size();
+    W.piece_slot.assign(np, -1);
+    size_t i = 0;
+    while (i < np) {
+        size_t j = i + 1;
+        while (j < np && W.piece_seg[j] == W.piece_seg[i]) ++j;
+        if (j - i > 1) {
+            W.merge_seg.push_back(W.piece_seg[i]);
+            W.merge_slot0.push_back(W.n_slots);
+            W.merge_nslots.push_back(static_cast<int32_t>(j - i));
+            for (size_t k = i; k < j; ++k) W.piece_slot[k] = W.n_slots++;
+        }
+        i = j;
+    }
+}
+
+int step_reserve(Pool* p, int32_t max_batch, int32_t max_blocks, int32_t max_tokens,
+                 int32_t n_heads) {
+    StepWorkspace& ws = p->ws;
+    if (max_batch < 0 || max_blocks < 0 || max_tokens < 0)
+        return set_error(GKV_EINVAL, "negative reservation");
+    if (n_heads <= 0) n_heads = ws.n_heads > 0 ? ws.n_heads : p->desc.heads_kv;
+    if (n_heads % p->desc.heads_kv != 0)
+        return set_error(GKV_EINVAL, "n_heads %d is not a multiple of heads_kv %d", n_heads, p->desc.heads_kv);
+    ws.n_heads = n_heads;
+    ws.cfg = decode_config(p->geom, n_heads);
+    const int ctas_per_sm = ws.cfg.supported ? ws.cfg.ctas_per_sm : 1;
+    ws.n_ctas_max = sm_count(p->desc.device) * ctas_per_sm;
+    if (max_batch > ws.max_batch) ws.max_batch = max_batch;
+    if (max_blocks > ws.max_blocks) ws.max_blocks = max_blocks;
+    if (max_tokens > ws.max_tokens) ws.max_tokens = max_tokens;
+    const int warps = ws.cfg.supported ? ws.cfg.warps : 4;
+    const int64_t workers = static_cast<int64_t>(ws.n_ctas_max) * warps;
+    const int64_t n_seg = static_cast<int64_t>(ws.max_batch) * p->desc.heads_kv;
+    const MetaLayout L = meta_layout(ws.max_tokens, ws.max_batch, ws.max_blocks, workers + n_seg,
+                                     workers, n_seg);
+    if (L.total > ws.meta_cap) {
+        if (ws.meta_pending && ws.meta_copied) cudaEventSynchronize(ws.meta_copied);
+        ws.meta_pending = false;
+        if (ws.h_meta) cudaFreeHost(ws.h_meta);
+        if (ws.d_meta) cudaFree(ws.d_meta);
+        ws.h_meta = nullptr;
+        ws.d_meta = nullptr;
+        ws.meta_cap = 0;
+        const size_t cap = align_up(L.total, 4096);
+        cudaError_t e = cudaMallocHost(&ws.h_meta, cap);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMallocHost(step metadata)");
+        e = cudaMalloc(&ws.d_meta, cap);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(step metadata)");
+        ws.meta_cap = cap;
+        ws.uploaded = false;
+    }
+    if (!ws.meta_copied) {
+        cudaError_t e = cudaEventCreateWithFlags(&ws.meta_copied, cudaEventDisableTiming);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
+    }
+    // partials: every piece of the largest work list could be a partial
+    if (ws.cfg.supported) {
+        const size_t slots = static_cast<size_t>(workers + n_seg) * ws.cfg.head_groups * ws.cfg.gp;
+        if (slots > ws.part_slots_cap) {
+            if (ws.d_part_acc) cudaFree(ws.d_part_acc);
+            if (ws.d_part_ml) cudaFree(ws.d_part_ml);
+            ws.d_part_acc = nullptr;
+            ws.d_part_ml = nullptr;
+            ws.part_slots_cap = 0;
+            cudaError_t e = cudaMalloc(&ws.d_part_acc, slots * p->desc.v_head_dim * sizeof(float));
+            if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(decode partials)");
+            e = cudaMalloc(&ws.d_part_ml, slots * 2 * sizeof(float));
+            if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(decode partials)");
+            ws.part_slots_cap = slots;
+        }
+    }
+    return GKV_OK;
+}
+
+void step_free(Pool* p) {
+    StepWorkspace& ws = p->ws;
+    if (ws.meta_copied) cudaEventDestroy(ws.meta_copied);
+    if (ws.h_meta) cudaFreeHost(ws.h_meta);
+    if (ws.d_meta) cudaFree(ws.d_meta);
+    if (ws.d_part_acc) cudaFree(ws.d_part_acc);
+    if (ws.d_part_ml) cudaFree(ws.d_part_ml);
+    if (ws.d_q) cudaFree(ws.d_q);
+    if (ws.d_out) cudaFree(ws.d_out);
+    if (ws.d_knew) cudaFree(ws.d_knew);
+    if (ws.d_vnew) cudaFree(ws.d_vnew);
+    ws.meta_copied = nullptr;
+    ws.h_meta = ws.d_meta = nullptr;
+    ws.d_part_acc = ws.d_part_ml = nullptr;
+    ws.d_q = ws.d_out = ws.d_knew = ws.d_vnew = nullptr;
+}
+
+int step_upload(Pool* p, const int32_t* tables, int32_t batch, int32_t max_blocks,
+                const int32_t* ctx_lens, const int64_t* slots, int32_t n_tok, cudaStream_t st) {
+    StepWorkspace& ws = p->ws;
+    const int32_t bs = p->desc.block_size;
+    if (batch < 0 || n_tok < 0 || max_blocks < 0)
+        return set_error(GKV_EINVAL, "negative batch/n_tok/max_blocks");
+    if (batch > 0 && (!ctx_lens || (max_blocks > 0 && !tables)))
+        return set_error(GKV_EINVAL, "tables/ctx_lens is NULL");
+    if (n_tok > 0 && !slots) return set_error(GKV_EINVAL, "slot_mapping is NULL");
+    // Host validation of everything a kernel will dereference.
+    for (int32_t b = 0; b < batch; ++b) {
+        const int32_t c = ctx_lens[b];
+        if (c < 0 || static_cast<int64_t>(c) > static_cast<int64_t>(max_blocks) * bs)
+            return set_error(GKV_EINVAL, "sequence %d: ctx_len %d outside [0, %lld]", b, c,
+                             static_cast<long long>(max_blocks) * bs);
+        const int32_t pages = (c + bs - 1) / bs;
+        for (int32_t pg = 0; pg < pages; ++pg) {
+            const int32_t id = tables[static_cast<int64_t>(b) * max_blocks + pg];
+            if (!p->in_range(id))
+                return set_error(GKV_EINVAL, "sequence %d: block table entry %d = %d outside [0, %d)",
+                                 b, pg, id, p->desc.total_blocks);
+        }
+    }
+    const int64_t n_slots_total = static_cast<int64_t>(p->desc.total_blocks) * bs;
+    for (int32_t i = 0; i < n_tok; ++i)
+        if (slots[i] < -1 || slots[i] >= n_slots_total)
+            return set_error(GKV_EINVAL, "slot_mapping[%d] = %lld outside [-1, %lld)", i,
+                             static_cast<long long>(slots[i]), static_cast<long long>(n_slots_total));
+
+    if (batch > ws.max_batch || max_blocks > ws.max_blocks || n_tok > ws.max_tokens ||
+        ws.meta_cap == 0) {
+        const int rc = step_reserve(p, batch, max_blocks, n_tok, ws.n_heads);
+        if (rc != GKV_OK) return rc;
+    }
+    // Work list over a persistent grid: enough workers for the chunks, at most one wave.
+    std::vector<int32_t> ctx_v(ctx_lens, ctx_lens + batch);
+    int64_t total = 0;
+    for (int32_t b = 0; b < batch; ++b) total += chunks_of(ctx_v[static_cast<size_t>(b)], bs);
+    total *= p->desc.heads_kv;
+    const int warps = ws.cfg.supported ? ws.cfg.warps : 4;
+    int64_t want_workers = (total + kMinChunksPerWorker - 1) / kMinChunksPerWorker;
+    int64_t ctas = (want_workers + warps - 1) / warps;
+    if (ctas > ws.n_ctas_max) ctas = ws.n_ctas_max;
+    if (ctas < 1 && total > 0) ctas = 1;
+    WorkList W;
+    build_work_list(ctx_v.data(), batch, p->desc.heads_kv, bs, static_cast<int32_t>(ctas * warps), &W);
+    const int64_t n_pieces = static_cast<int64_t>(W.piece_seg.size());
+    const int64_t n_workers = static_cast<int64_t>(ctas) * warps;
+    const int64_t n_merge = static_cast<int64_t>(W.merge_seg.size());
+    const MetaLayout L = meta_layout(n_tok, batch, max_blocks, n_pieces, n_workers, n_merge);
+    if (L.total > ws.meta_cap) return set_error(GKV_EINVAL, "step metadata exceeds the reserved workspace");
+
+    // The pinned staging buffer may still feed the previous step's copy.
+    if (ws.meta_pending) {
+        cudaError_t e = cudaEventSynchronize(ws.meta_copied);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaEventSynchronize(step metadata)");
+        ws.meta_pending = false;
+    }
+    char* h = ws.h_meta;
+    if (n_tok) memcpy(h + L.slots, slots, static_cast<size_t>(n_tok) * 8);
+    if (batch && max_blocks) memcpy(h + L.tables, tables, static_cast<size_t>(batch) * max_blocks * 4);
+    if (batch) memcpy(h + L.ctx, ctx_lens, static_cast<size_t>(batch) * 4);
+    auto put = [&](size_t off, const std::vector<int32_t>& v) {
+        if (!v.empty()) memcpy(h + off, v.data(), v.size() * 4);
+    };
+    put(L.pseg, W.piece_seg);
+    put(L.pc0, W.piece_c0);
+    put(L.pc1, W.piece_c1);
+    put(L.pslot, W.piece_slot);
+    put(L.wbeg, W.worker_begin);
+    put(L.mseg, W.merge_seg);
+    put(L.ms0, W.merge_slot0);
+    put(L.mns, W.merge_nslots);
+    cudaError_t e = cudaMemcpyAsync(ws.d_meta, ws.h_meta, L.total, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(step metadata)");
+    e = cudaEventRecord(ws.meta_copied, st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord(step metadata)");
+    ws.meta_pending = true;
+
+    char* d = ws.d_meta;
+    DecodeWork& w = ws.work;
+    w.tables = reinterpret_cast<const int32_t*>(d + L.tables);
+    w.ctx_lens = reinterpret_cast<const int32_t*>(d + L.ctx);
+    w.max_blocks = max_blocks;
+    w.piece_seg = reinterpret_cast<const int32_t*>(d + L.pseg);
+    w.piece_c0 = reinterpret_cast<const int32_t*>(d + L.pc0);
+    w.piece_c1 = reinterpret_cast<const int32_t*>(d + L.pc1);
+    w.piece_slot = reinterpret_cast<const int32_t*>(d + L.pslot);
+    w.worker_piece_begin = reinterpret_cast<const int32_t*>(d + L.wbeg);
+    w.n_ctas = total > 0 ? static_cast<int32_t>(ctas) : 0;
+    w.n_slots = W.n_slots;
+    w.merge_seg = reinterpret_cast<const int32_t*>(d + L.mseg);
+    w.merge_slot0 = reinterpret_cast<const int32_t*>(d + L.ms0);
+    w.merge_nslots = reinterpret_cast<const int32_t*>(d + L.mns);
+    w.n_merge = static_cast<int32_t>(n_merge);
+    ws.d_slots = reinterpret_cast<const int64_t*>(d + L.slots);
+    ws.batch = batch;
+    ws.n_tok = n_tok;
+    ws.up_max_blocks = max_blocks;
+    ws.uploaded = true;
+    return GKV_OK;
+}
+
+int step_append(Pool* p, int32_t layer, const float* d_k, const float* d_v, int32_t n_tok,
+                cudaStream_t st) {
+    StepWorkspace& ws = p->ws;
+    if (!ws.uploaded) return set_error(GKV_ESTATE, "no step uploaded (call gkv_upload_step first)");
+    if (layer < 0 || layer >= p->desc.layers)
+        return set_error(GKV_EINVAL, "layer %d outside [0, %d)", layer, p->desc.layers);
+    if (n_tok < 0 || n_tok > ws.n_tok)
+        return set_error(GKV_EINVAL, "n_tok %d exceeds the uploaded slot mapping (%d)", n_tok, ws.n_tok);
+    if (n_tok > 0 && (!d_k || !d_v)) return set_error(GKV_EINVAL, "k/v source is NULL");
+    int rc = p->flush_copies(st);
+    if (rc != GKV_OK) return rc;
+    if (n_tok == 0) return GKV_OK;
+    cudaError_t e = launch_kv_append(p->geom, layer, d_k, d_v,
+                                     static_cast<int64_t>(p->desc.heads_kv) * p->desc.head_dim,
+                                     static_cast<int64_t>(p->desc.heads_kv) * p->desc.v_head_dim,
+                                     ws.d_slots, 0, n_tok, ws.d_err, st);
+    if (e != cudaSuccess) return cuda_fail(e, "kv_append launch");
+    p->last_launches += 1;
+    return GKV_OK;
+}
+
+static int decode_common(Pool* p, int32_t layer, const float* d_q, float* d_out, int32_t n_heads,
+                         float scale, const float* d_sinks, bool has_sink_all, float sink_all,
+                         cudaStream_t st) {
+    StepWorkspace& ws = p->ws;
+    if (!ws.uploaded) return set_error(GKV_ESTATE, "no step uploaded (call gkv_upload_step first)");
+    if (layer < 0 || layer >= p->desc.layers)
+        return set_error(GKV_EINVAL, "layer %d outside [0, %d)", layer, p->desc.layers);
+    if (n_heads <= 0 || n_heads % p->desc.heads_kv != 0)
+        return set_error(GKV_EINVAL, "n_heads %d is not a positive multiple of heads_kv %d", n_heads,
+                         p->desc.heads_kv);
+    if (ws.batch > 0 && (!d_q || !d_out)) return set_error(GKV_EINVAL, "q/out is NULL");
+    if (n_heads != ws.n_heads || !ws.cfg.supported) {
+        const int rc = step_reserve(p, 0, 0, 0, n_heads);
+        if (rc != GKV_OK) return rc;
+    }
+    if (!ws.cfg.supported)
+        return set_error(GKV_EUNSUPPORTED, "decode not built for head_dim %d / v_head_dim %d",
+                         p->desc.head_dim, p->desc.v_head_dim);
+    int rc = p->flush_copies(st);
+    if (rc != GKV_OK) return rc;
+    const size_t need = static_cast<size_t>(ws.work.n_slots) * ws.cfg.head_groups * ws.cfg.gp;
+    if (need > ws.part_slots_cap) return set_error(GKV_ESTATE, "decode partial buffer too small");
+    DecodeArgs a{};
+    a.layer = layer;
+    a.q = d_q;
+    a.out = d_out;
+    a.n_heads = n_heads;
+    a.scale = scale;
+    a.sinks = d_sinks;
+    a.has_sink_all = has_sink_all ? 1 : 0;
+    a.sink_all = sink_all;
+    a.part_acc = ws.d_part_acc;
+    a.part_ml = ws.d_part_ml;
+    a.err = ws.d_err;
+    int launches = 0;
+    cudaError_t e = launch_paged_decode(p->geom, ws.work, a, &launches, st);
+    if (e != cudaSuccess) return cuda_fail(e, "paged_decode launch");
+    p->last_launches += launches;
+    return GKV_OK;
+}
+
+int step_decode(Pool* p, int32_t layer, const float* d_q, float* d_out, int32_t n_heads,
+                float scale, const float* d_sinks, cudaStream_t st) {
+    return decode_common(p, layer, d_q, d_out, n_heads, scale, d_sinks, false, 0.f, st);
+}
+
+}  // namespace gkv
+
+using gkv::Pool;
+using gkv::set_error;
+
+#define GKV_DEVICE_POOL(pool)                                                              \
+    do {                                                                                   \
+        if (!(pool)) return set_error(GKV_EINVAL, "pool handle is NULL");                  \
+        if (!(pool)->impl.has_arena)                                                       \
+            return set_error(GKV_ESTATE, "pool has no device arena (metadata-only pool)"); \
+    } while (0)
+
+extern "C" {
+
+int gkv_step_reserve(gkv_pool* pool, int32_t max_batch, int32_t max_blocks_per_seq,
+                     int32_t max_tokens, int32_t n_heads) {
+    GKV_DEVICE_POOL(pool);
+    gkv::DeviceGuard guard(pool->impl.desc.device);
+    return gkv::step_reserve(&pool->impl, max_batch, max_blocks_per_seq, max_tokens, n_heads);
+}
+
+int gkv_upload_step(gkv_pool* pool, const int32_t* h_block_tables, int32_t batch,
+                    int32_t max_blocks, const int32_t* h_ctx_lens, const int64_t* h_slot_mapping,
+                    int32_t n_tok, void* stream) {
+    GKV_DEVICE_POOL(pool);
+    gkv::DeviceGuard guard(pool->impl.desc.device);
+    return gkv::step_upload(&pool->impl, h_block_tables, batch, max_blocks, h_ctx_lens,
+                            h_slot_mapping, n_tok, static_cast<cudaStream_t>(stream));
+}
+
+int gkv_upload_step_tables(gkv_pool* pool, gkv_table* const* tables, int32_t batch,
+                           const int32_t* h_ctx_lens, const int64_t* h_slot_mapping, int32_t n_tok,
+                           void* stream) {
+    GKV_DEVICE_POOL(pool);
+    if (batch < 0 || (batch > 0 && !tables)) return set_error(GKV_EINVAL, "tables is NULL");
+    int32_t max_blocks = 1;
+    for (int32_t b = 0; b < batch; ++b) {
+        if (!tables[b] || tables[b]->impl.pool != &pool->impl)
+            return set_error(GKV_EINVAL, "table %d is NULL or belongs to another pool", b);
+        const int32_t n = static_cast<int32_t>(tables[b]->impl.ids.size());
+        if (n > max_blocks) max_blocks = n;
+    }
+    std::vector<int32_t> packed(static_cast<size_t>(batch) * max_blocks, -1);
+    std::vector<int32_t> ctx(static_cast<size_t>(batch));
+    for (int32_t b = 0; b < batch; ++b) {
+        const auto& ids = tables[b]->impl.ids;
+        std::copy(ids.begin(), ids.end(), packed.begin() + static_cast<int64_t>(b) * max_blocks);
+        ctx[static_cast<size_t>(b)] = h_ctx_lens ? h_ctx_lens[b] : tables[b]->impl.token_count;
+    }
+    gkv::DeviceGuard guard(pool->impl.desc.device);
+    return gkv::step_upload(&pool->impl, packed.data(), batch, max_blocks, ctx.data(),
+                            h_slot_mapping, n_tok, static_cast<cudaStream_t>(stream));
+}
+
+int gkv_kv_append(gkv_pool* pool, int32_t layer, const float* d_k, const float* d_v,
+                  int32_t n_tok, void* stream) {
+    GKV_DEVICE_POOL(pool);
+    gkv::DeviceGuard guard(pool->impl.desc.device);
+    pool->impl.last_launches = 0;
+    return gkv::step_append(&pool->impl, layer, d_k, d_v, n_tok, static_cast<cudaStream_t>(stream));
+}
+
+int gkv_paged_decode(gkv_pool* pool, int32_t layer, const float* d_q, float* d_out,
+                     int32_t n_heads, float scale, const float* d_sinks, void* stream) {
+    GKV_DEVICE_POOL(pool);
+    gkv::DeviceGuard guard(pool->impl.desc.device);
+    pool->impl.last_launches = 0;
+    return gkv::step_decode(&pool->impl, layer, d_q, d_out, n_heads, scale, d_sinks,
+                            static_cast<cudaStream_t>(stream));
+}
+
+int gkv_compute_attention(gkv_pool* pool, int32_t stage_layer, int32_t model_layer, int32_t pos,
+                          const float* d_q, float* d_out, const gkv_table* table, int32_t n_heads,
+                          int32_t n_heads_kv, int32_t head_dim, int32_t v_head_dim,
+                          float attn_scale, int32_t max_seq_len, int32_t has_sink,
+                          float sink_logit, void* stream) {
+    (void)model_layer;  // unused, as in PagedAttentionKernel.cs:19
+    GKV_DEVICE_POOL(pool);
+    if (!table) return set_error(GKV_EINVAL, "blockTable is NULL");
+    Pool& P = pool->impl;
+    // PagedAttentionKernel.cs:34-39
+    if (max_seq_len <= 0) return set_error(GKV_EINVAL, "maxSeqLen must be positive (got %d).", max_seq_len);
+    if (pos < 0 || pos >= max_seq_len)
+        return set_error(GKV_EINVAL, "Token position %d exceeds valid sequence range [0, %d].", pos, max_seq_len - 1);
+    const gkv::Table& T = table->impl;
+    if (T.token_count > max_seq_len)
+        return set_error(GKV_EINVAL, "BlockTable token count %d exceeds maxSeqLen %d.", T.token_count, max_seq_len);
+    if (T.pool != &P) return set_error(GKV_EINVAL, "blockTable belongs to another pool");
+    if (n_heads_kv != P.desc.heads_kv || head_dim != P.desc.head_dim || v_head_dim != P.desc.v_head_dim)
+        return set_error(GKV_EINVAL, "nHeadsKv/headDim/vHeadDim (%d/%d/%d) differ from the pool's (%d/%d/%d)",
+                         n_heads_kv, head_dim, v_head_dim, P.desc.heads_kv, P.desc.head_dim, P.desc.v_head_dim);
+    if (stage_layer < 0 || stage_layer >= P.desc.layers)
+        return set_error(GKV_EINVAL, "stageLayer %d outside [0, %d)", stage_layer, P.desc.layers);
+    // PagedAttentionKernel.cs:41-42
+    const int32_t n = T.token_count < pos + 1 ? T.token_count : pos + 1;
+    gkv::DeviceGuard guard(P.desc.device);
+    P.last_launches = 0;
+    if (n == 0) return GKV_OK;
+    const int32_t nb = static_cast<int32_t>(T.ids.size());
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int rc = gkv::step_upload(&P, T.ids.data(), 1, nb, &n, nullptr, 0, st);
+    if (rc != GKV_OK) return rc;
+    return gkv::decode_common(&P, stage_layer, d_q, d_out, n_heads, attn_scale, nullptr,
+                              has_sink != 0, sink_logit, st);
+}
+
+int gkv_decode_step_host(gkv_pool* pool, int32_t layer, const int32_t* h_block_tables,
+                         int32_t batch, int32_t max_blocks, const int32_t* h_ctx_lens,
+                         const int64_t* h_slot_mapping, int32_t n_tok, const float* h_k_new,
+                         const float* h_v_new, const float* h_q, float* h_out, int32_t n_heads,
+                         float scale, const float* d_sinks, void* stream) {
+    GKV_DEVICE_POOL(pool);
+    Pool& P = pool->impl;
+    if (batch > 0 && (!h_q || !h_out)) return set_error(GKV_EINVAL, "h_q/h_out is NULL");
+    if (n_tok > 0 && (!h_k_new || !h_v_new)) return set_error(GKV_EINVAL, "h_k_new/h_v_new is NULL");
+    if (n_heads <= 0 || n_heads % P.desc.heads_kv != 0)
+        return set_error(GKV_EINVAL, "n_heads %d is not a positive multiple of heads_kv %d", n_heads, P.desc.heads_kv);
+    gkv::DeviceGuard guard(P.desc.device);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    gkv::StepWorkspace& ws = P.ws;
+    P.last_launches = 0;
+    const size_t qb = static_cast<size_t>(batch) * n_heads * P.desc.head_dim * sizeof(float);
+    const size_t ob = static_cast<size_t>(batch) * n_heads * P.desc.v_head_dim * sizeof(float);
+    const size_t kb = static_cast<size_t>(n_tok) * P.desc.heads_kv * P.desc.head_dim * sizeof(float);
+    const size_t vb = static_cast<size_t>(n_tok) * P.desc.heads_kv * P.desc.v_head_dim * sizeof(float);
+    int rc = gkv::grow_device(reinterpret_cast<void**>(&ws.d_q), &ws.io_cap_q, qb, "cudaMalloc(q)");
+    if (rc == GKV_OK) rc = gkv::grow_device(reinterpret_cast<void**>(&ws.d_out), &ws.io_cap_out, ob, "cudaMalloc(out)");
+    if (rc == GKV_OK) rc = gkv::grow_device(reinterpret_cast<void**>(&ws.d_knew), &ws.io_cap_k, kb, "cudaMalloc(k_new)");
+    if (rc == GKV_OK) rc = gkv::grow_device(reinterpret_cast<void**>(&ws.d_vnew), &ws.io_cap_v, vb, "cudaMalloc(v_new)");
+    if (rc != GKV_OK) return rc;
+    cudaError_t e = cudaSuccess;
+    if (qb) e = cudaMemcpyAsync(ws.d_q, h_q, qb, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess && kb) e = cudaMemcpyAsync(ws.d_knew, h_k_new, kb, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess && vb) e = cudaMemcpyAsync(ws.d_vnew, h_v_new, vb, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return gkv::cuda_fail(e, "cudaMemcpyAsync(step inputs)");
+    rc = gkv::step_upload(&P, h_block_tables, batch, max_blocks, h_ctx_lens, h_slot_mapping, n_tok, st);
+    if (rc != GKV_OK) return rc;
+    rc = gkv::step_append(&P, layer, ws.d_knew, ws.d_vnew, n_tok, st);
+    if (rc != GKV_OK) return rc;
+    rc = gkv::step_decode(&P, layer, ws.d_q, ws.d_out, n_heads, scale, d_sinks, st);
+    if (rc != GKV_OK) return rc;
+    if (ob) e = cudaMemcpyAsync(h_out, ws.d_out, ob, cudaMemcpyDeviceToHost, st);
+    if (e != cudaSuccess) return gkv::cuda_fail(e, "cudaMemcpyAsync(step output)");
+    return GKV_OK;
+}
+
+int gkv_plan_decode(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, int32_t block_size,
+                    int32_t n_workers, gkv_plan_info* info, int32_t* piece_seg, int32_t* piece_c0,
+                    int32_t* piece_c1, int32_t* piece_slot, int32_t* worker_begin,
+                    int32_t cap_pieces) {
+    if (batch < 0 || heads_kv < 1 || block_size < 1 || n_workers < 1 || (batch > 0 && !ctx_lens))
+        return set_error(GKV_EINVAL, "batch=%d heads_kv=%d block_size=%d n_workers=%d", batch,
+                         heads_kv, block_size, n_workers);
+    gkv::WorkList W;
+    gkv::build_work_list(ctx_lens, batch, heads_kv, block_size, n_workers, &W);
+    const int32_t np = static_cast<int32_t>(W.piece_seg.size());
+    if (info) {
+        info->total_chunks = W.total_chunks;
+        info->n_pieces = np;
+        info->n_slots = W.n_slots;
+        info->n_merge = static_cast<int32_t>(W.merge_seg.size());
+        info->n_workers = n_workers;
+    }
+    if (piece_seg || piece_c0 || piece_c1 || piece_slot) {
+        if (cap_pieces < np) return set_error(GKV_EINVAL, "cap_pieces %d < %d pieces", cap_pieces, np);
+        for (int32_t i = 0; i < np; ++i) {
+            if (piece_seg) piece_seg[i] = W.piece_seg[static_cast<size_t>(i)];
+            if (piece_c0) piece_c0[i] = W.piece_c0[static_cast<size_t>(i)];
+            if (piece_c1) piece_c1[i] = W.piece_c1[static_cast<size_t>(i)];
+            if (piece_slot) piece_slot[i] = W.piece_slot[static_cast<size_t>(i)];
+        }
+    }
+    if (worker_begin)
+        for (int32_t w = 0; w <= n_workers; ++w) worker_begin[w] = W.worker_begin[static_cast<size_t>(w)];
+    return GKV_OK;
+}
+
+int gkv_sync(gkv_pool* pool, void* stream, int32_t timeout_ms) {
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    std::unique_ptr<gkv::DeviceGuard> guard;
+    if (pool && pool->impl.has_arena) guard.reset(new gkv::DeviceGuard(pool->impl.desc.device));
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        const cudaError_t e = cudaStreamQuery(st);
+        if (e == cudaSuccess) break;
+        if (e != cudaErrorNotReady) return gkv::cuda_fail(e, "cudaStreamQuery");
+        const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                            std::chrono::steady_clock::now() - t0).count();
+        if (timeout_ms >= 0 && ms >= timeout_ms)
+            return set_error(GKV_ETIMEDOUT, "stream still busy after %d ms", timeout_ms);
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+    if (pool && pool->impl.has_arena && pool->impl.ws.d_err) {
+        int flag = 0;
+        cudaError_t e = cudaMemcpy(&flag, pool->impl.ws.d_err, sizeof(int), cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) return gkv::cuda_fail(e, "cudaMemcpy(error word)");
+        if (flag != 0) {
+            cudaMemset(pool->impl.ws.d_err, 0, sizeof(int));
+            return set_error(GKV_EDEVICE, "a kernel reported error bits 0x%x (1 = bad block id, 2 = wait timeout, 4 = bad slot)", flag);
+        }
+    }
+    return GKV_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,283 @@
+/*
+ * glacier_kv.h -- C ABI of the B200 (sm_100a) paged-KV hot path for Glacier.Serve.
+ *
+ * The C# engine (ContinuousBatchEngine / CudaPagedTransformerRunner) P/Invokes these
+ * entry points in place of its host-side PagedBlockPool arena, its per-sequence
+ * BlockTable uploads and its CPU PagedAttentionKernel.  Every declaration below cites the
+ * reference member it replaces as `path:line` inside the Glacier.Serve repository
+ * (src/Glacier.Serve/Inference/PagedAttention/...).
+ *
+ * Conventions
+ *   - Every call returns an int status: GKV_OK (0) or a negative GKV_E* code.  Nothing
+ *     throws or aborts across the ABI; gkv_last_error() returns a thread-local message
+ *     for the last failing call on the calling thread.  The reference's
+ *     ArgumentOutOfRangeException maps to GKV_EINVAL, InvalidOperationException to
+ *     GKV_ESTATE.
+ *   - Calls named try_* return 1 (success) / 0 (pool exhausted or not found) like the
+ *     reference's bool TryXxx(out ...) methods, and a negative code on a bad argument.
+ *   - Pointers named d_* are device pointers on the pool's device, h_* are host pointers
+ *     (pinned memory recommended).  Streams are cudaStream_t passed as void*; NULL is the
+ *     legacy default stream.  All device work is enqueued asynchronously on the stream.
+ *   - Pool, table and step objects are not thread-safe for concurrent device calls, but the
+ *     allocator calls (allocate / retain / release / find / bind / fork) are lock-free or
+ *     internally locked and may be called from any thread, as in the reference
+ *     (PagedBlockPool.cs:16 "thread-safe O(1) lock-free block allocation").
+ */
+#ifndef GLACIER_KV_H
+#define GLACIER_KV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define GKV_API __attribute__((visibility("default")))
+#else
+#define GKV_API
+#endif
+
+/* ---- status codes -------------------------------------------------------------------- */
+enum {
+    GKV_OK = 0,
+    GKV_EINVAL = -1,        /* argument out of range (reference: ArgumentOutOfRangeException)  */
+    GKV_ENOMEM = -2,        /* device/pinned allocation failed                                */
+    GKV_ESTATE = -3,        /* invalid object state (reference: InvalidOperationException)    */
+    GKV_ECUDA = -4,         /* a CUDA runtime call failed                                     */
+    GKV_ETIMEDOUT = -5,     /* gkv_sync gave up waiting                                       */
+    GKV_ENCCL = -6,         /* an NCCL call failed or was aborted                              */
+    GKV_EDEVICE = -7,       /* a kernel reported a bad block id / bounded wait expiry          */
+    GKV_EUNSUPPORTED = -8   /* shape not compiled into this build (e.g. head_dim % 32 != 0)   */
+};
+
+/* KV storage types of the device arena.  Sources handed to append/store are always fp32
+ * (the reference stores fp32, PagedBlockPool.cs:151-161); bf16 storage rounds to nearest
+ * even on append. */
+enum { GKV_DTYPE_F32 = 0, GKV_DTYPE_BF16 = 1 };
+
+typedef struct gkv_pool gkv_pool;
+typedef struct gkv_table gkv_table;
+typedef struct gkv_comm gkv_comm;
+
+/* ---- 1. the device block arena (PagedBlockPool) ------------------------------------- */
+
+typedef struct gkv_pool_desc {
+    int32_t device;                /* CUDA device ordinal that holds the arena            */
+    int32_t total_blocks;          /* PagedBlockPool(totalBlocks ...)                     */
+    int32_t layers;
+    int32_t heads_kv;
+    int32_t head_dim;
+    int32_t v_head_dim;            /* <= 0 means head_dim (PagedBlockPool.cs:73)          */
+    int32_t block_size;            /* tokens per block; 0 means 16 (PagedBlockPool.cs:18) */
+    int32_t dtype;                 /* GKV_DTYPE_F32 or GKV_DTYPE_BF16                     */
+    int32_t allocate_device_arena; /* 0 = metadata-only pool: allocator, tables and CoW
+                                      bookkeeping without any CUDA call (the reference's
+                                      allocateHostBuffers:false, PagedBlockPool.cs:61,106) */
+} gkv_pool_desc;
+
+typedef struct gkv_pool_stats {
+    int32_t total_blocks;          /* TotalBlocks          PagedBlockPool.cs:46 */
+    int32_t free_blocks;           /* FreeBlocksCount      PagedBlockPool.cs:52 */
+    int32_t allocated_blocks;      /* AllocatedBlocksCount PagedBlockPool.cs:53 */
+    int32_t capacity_tokens;       /* CapacityTokens       PagedBlockPool.cs:54 */
+    int32_t active_tokens;         /* ActiveTokens         PagedBlockPool.cs:55 */
+    int32_t block_size;            /* BlockSize            PagedBlockPool.cs:47 */
+    int32_t pending_copies;        /* CoW forks queued for the next device call          */
+    int32_t has_device_arena;      /* HasHostBuffers analogue, PagedBlockPool.cs:56      */
+    int64_t total_memory_bytes;    /* TotalMemoryBytes     PagedBlockPool.cs:57 */
+} gkv_pool_stats;
+
+/* PagedBlockPool ctor, PagedBlockPool.cs:61-121: validates every size >= 1 (:63-67),
+ * allocates the zeroed K and V arenas in the layout [block][layer][head_kv][slot][dim]
+ * (strides :77-83) and fills the free list so that block 0 is popped first (:116-120). */
+GKV_API int gkv_pool_create(const gkv_pool_desc* desc, gkv_pool** out_pool);
+/* PagedBlockPool.Dispose, PagedBlockPool.cs:355-364. */
+GKV_API int gkv_pool_destroy(gkv_pool* pool);
+/* Counters of PagedBlockPool.cs:46-57. */
+GKV_API int gkv_pool_stats_get(const gkv_pool* pool, gkv_pool_stats* out_stats);
+/* KeyBufferAddress / ValueBufferAddress, PagedBlockPool.cs:58-59 (device pointers; NULL
+ * for a metadata-only pool). */
+GKV_API int gkv_pool_kv_ptrs(const gkv_pool* pool, void** d_k, void** d_v);
+/* Element offset of (block, layer, head_kv, slot) in the K or V arena:
+ * GetKeyPtr / GetValuePtr, PagedBlockPool.cs:124-145.  which: 0 = K, 1 = V. */
+GKV_API int gkv_pool_element_offset(const gkv_pool* pool, int32_t which, int32_t block,
+                                    int32_t layer, int32_t head_kv, int32_t slot,
+                                    int64_t* out_offset);
+
+/* TryAllocateBlock, PagedBlockPool.cs:178-189: returns 1 and the block id, or 0 and -1. */
+GKV_API int gkv_pool_try_allocate_block(gkv_pool* pool, int32_t* out_block);
+/* ReleaseBlock, PagedBlockPool.cs:251-279: returns the remaining reference count (>= 0);
+ * out-of-range ids and double releases return 0 and change nothing. */
+GKV_API int gkv_pool_release_block(gkv_pool* pool, int32_t block);
+/* FreeBlock / FreeBlocks, PagedBlockPool.cs:296-299,347-353 (idempotent). */
+GKV_API int gkv_pool_free_block(gkv_pool* pool, int32_t block);
+GKV_API int gkv_pool_free_blocks(gkv_pool* pool, const int32_t* blocks, int32_t n);
+/* RetainBlock, PagedBlockPool.cs:240-245: GKV_EINVAL for an out-of-range id, otherwise the
+ * new reference count. */
+GKV_API int gkv_pool_retain_block(gkv_pool* pool, int32_t block);
+/* GetRefCount, PagedBlockPool.cs:285-289 (0 for out-of-range ids). */
+GKV_API int gkv_pool_get_ref_count(const gkv_pool* pool, int32_t block);
+/* TryFindPrefixBlock, PagedBlockPool.cs:194-220 (hash computed by the caller, as in
+ * ContinuousBatchEngine.cs:232): 1 with the block id and one more reference, or 0 and -1. */
+GKV_API int gkv_pool_try_find_prefix_block(gkv_pool* pool, uint64_t prefix_hash,
+                                           int32_t* out_block);
+/* BindPrefixBlock, PagedBlockPool.cs:225-234: GKV_EINVAL for hash 0 or an out-of-range id. */
+GKV_API int gkv_pool_bind_prefix_block(gkv_pool* pool, uint64_t prefix_hash, int32_t block);
+/* TryForkBlock, PagedBlockPool.cs:332-342: allocates a block and queues a device copy of
+ * the first valid_tokens slots of every (layer, head) from src.  Queued copies are issued
+ * as ONE batched block-copy launch by the next device call on this pool (or by
+ * gkv_pool_flush_copies), always before that call's own kernels. */
+GKV_API int gkv_pool_try_fork_block(gkv_pool* pool, int32_t src_block, int32_t valid_tokens,
+                                    int32_t* out_block);
+/* Issues the queued CoW copies now (one launch). */
+GKV_API int gkv_pool_flush_copies(gkv_pool* pool, void* stream);
+/* CopyBlockData, PagedBlockPool.cs:304-327, batched: for i < n copies the first
+ * valid_tokens[i] slots (clamped to block_size; <= 0 skips) of every layer and head from
+ * src_blocks[i] to dst_blocks[i].  Host arrays; one kernel launch.  GKV_ESTATE on a
+ * metadata-only pool (PagedBlockPool.cs:306-307). */
+GKV_API int gkv_block_copy(gkv_pool* pool, const int32_t* h_src_blocks,
+                           const int32_t* h_dst_blocks, const int32_t* h_valid_tokens,
+                           int32_t n, void* stream);
+/* Store, PagedBlockPool.cs:151-161: writes one token's K [heads_kv][head_dim] and
+ * V [heads_kv][v_head_dim] (device fp32) into (block, layer, slot).  Bit-exact for fp32
+ * storage.  GKV_ESTATE on a metadata-only pool (PagedBlockPool.cs:126-127). */
+GKV_API int gkv_pool_store(gkv_pool* pool, int32_t block, int32_t layer, int32_t slot,
+                           const float* d_k, const float* d_v, void* stream);
+
+/* ---- 2. the per-sequence page table (BlockTable) ------------------------------------ */
+
+/* new BlockTable(pool), BlockTable.cs:23-26. */
+GKV_API int gkv_table_create(gkv_pool* pool, gkv_table** out_table);
+GKV_API int gkv_table_destroy(gkv_table* table);
+/* AttachPrefixBlocks, BlockTable.cs:31-39 (GKV_EINVAL for token_count < 0). */
+GKV_API int gkv_table_attach_prefix_blocks(gkv_table* table, const int32_t* blocks, int32_t n,
+                                           int32_t token_count);
+/* AppendToken, BlockTable.cs:46-80: allocates at block boundaries and CoW-forks a shared
+ * partial last block; returns 1 with (block, offset) or 0 with (-1, -1) when the pool is
+ * exhausted, leaving the table unchanged. */
+GKV_API int gkv_table_append_token(gkv_table* table, int32_t* out_block, int32_t* out_offset);
+/* GetTokenLocation, BlockTable.cs:86-91. */
+GKV_API int gkv_table_get_token_location(const gkv_table* table, int32_t token_index,
+                                         int32_t* out_block, int32_t* out_offset);
+/* GetBlockId, BlockTable.cs:94-97: the id, or GKV_EINVAL. */
+GKV_API int gkv_table_get_block_id(const gkv_table* table, int32_t block_index);
+/* TokenCount / BlockCount, BlockTable.cs:18-20. */
+GKV_API int gkv_table_token_count(const gkv_table* table);
+GKV_API int gkv_table_block_count(const gkv_table* table);
+/* AsSpan, BlockTable.cs:103: copies up to cap ids into out, returns BlockCount. */
+GKV_API int gkv_table_block_ids(const gkv_table* table, int32_t* out, int32_t cap);
+/* ReleaseAll, BlockTable.cs:108-116. */
+GKV_API int gkv_table_release_all(gkv_table* table);
+
+/* ---- 3. one decode / append step ------------------------------------------------------ */
+
+/* Sizes the pool's step workspace (device + pinned staging) once, outside the hot loop:
+ * up to max_batch sequences, max_blocks_per_seq table entries each, max_tokens appended
+ * tokens per step, and n_heads query heads for the decode launches.  Reference analogue:
+ * the device block-table buffer of CudaPagedTransformerRunner.cs:115-120,143. */
+GKV_API int gkv_step_reserve(gkv_pool* pool, int32_t max_batch, int32_t max_blocks_per_seq,
+                             int32_t max_tokens, int32_t n_heads);
+/* Uploads one step's packed metadata with ONE host-to-device copy on `stream`:
+ *   h_block_tables [batch][max_blocks] int32 (unused entries may hold -1),
+ *   h_ctx_lens     [batch] tokens each sequence attends (0 = skip, output untouched,
+ *                  PagedAttentionKernel.cs:42),
+ *   h_slot_mapping [n_tok] int64 slot = block * block_size + offset of each appended
+ *                  token (-1 = skip).
+ * Validates every referenced block id and every ctx_len <= max_blocks * block_size on the
+ * host (GKV_EINVAL), then builds the split-KV work list.  Replaces the per-sequence
+ * UploadBlockTable, CudaPagedTransformerRunner.cs:344,367-379. */
+GKV_API int gkv_upload_step(gkv_pool* pool, const int32_t* h_block_tables, int32_t batch,
+                            int32_t max_blocks, const int32_t* h_ctx_lens,
+                            const int64_t* h_slot_mapping, int32_t n_tok, void* stream);
+/* Packs `batch` host tables (BlockTable.AsSpan) plus ctx_lens / slot mapping and calls
+ * gkv_upload_step.  h_ctx_lens may be NULL (each table's TokenCount is used). */
+GKV_API int gkv_upload_step_tables(gkv_pool* pool, gkv_table* const* tables, int32_t batch,
+                                   const int32_t* h_ctx_lens, const int64_t* h_slot_mapping,
+                                   int32_t n_tok, void* stream);
+/* KV append (reshape-and-cache scatter) of the uploaded step's n_tok tokens:
+ * d_k [n_tok][heads_kv][head_dim], d_v [n_tok][heads_kv][v_head_dim] fp32, into `layer`.
+ * Replaces the per-sequence Store calls, PagedTransformerRunner.cs:634 /
+ * PagedBlockPool.cs:151-161.  Bit-exact for fp32 storage, RNE for bf16. */
+GKV_API int gkv_kv_append(gkv_pool* pool, int32_t layer, const float* d_k, const float* d_v,
+                          int32_t n_tok, void* stream);
+/* Split-KV GQA paged decode of the uploaded step for `layer`:
+ * d_q [batch][n_heads][head_dim] fp32 -> d_out [batch][n_heads][v_head_dim] fp32.
+ * out = softmax(scale * q.K^T [, sink]) . V over each sequence's ctx_len tokens, query
+ * head h reading kv head h / (n_heads / heads_kv).  d_sinks: NULL or [n_heads] sink
+ * logits (the reference's single sinkLogit is the all-equal case).  Replaces
+ * PagedAttentionKernel.ComputeAttention, PagedAttentionKernel.cs:17-372, for a batch. */
+GKV_API int gkv_paged_decode(gkv_pool* pool, int32_t layer, const float* d_q, float* d_out,
+                             int32_t n_heads, float scale, const float* d_sinks, void* stream);
+/* ComputeAttention for ONE sequence with the reference's argument checks
+ * (PagedAttentionKernel.cs:17-42): GKV_EINVAL when max_seq_len <= 0, pos outside
+ * [0, max_seq_len) or TokenCount > max_seq_len; a no-op when min(TokenCount, pos+1) == 0.
+ * head_dim / v_head_dim must equal the pool's.  has_sink / sink_logit mirror
+ * `float? sinkLogit`.  model_layer is accepted and unused, as in the reference. */
+GKV_API int gkv_compute_attention(gkv_pool* pool, int32_t stage_layer, int32_t model_layer,
+                                  int32_t pos, const float* d_q, float* d_out,
+                                  const gkv_table* table, int32_t n_heads, int32_t n_heads_kv,
+                                  int32_t head_dim, int32_t v_head_dim, float attn_scale,
+                                  int32_t max_seq_len, int32_t has_sink, float sink_logit,
+                                  void* stream);
+/* One whole continuous-batching attention iteration from HOST buffers, the shape of
+ * CudaPagedTransformerRunner.ForwardBatch (CudaPagedTransformerRunner.cs:307-364) for the
+ * attention part: copies h_q, h_k_new, h_v_new and the packed metadata to the device,
+ * appends the new tokens, decodes every sequence and copies the output back to h_out.
+ * Everything is enqueued on `stream`; call gkv_sync before reading h_out. */
+GKV_API int gkv_decode_step_host(gkv_pool* pool, int32_t layer, const int32_t* h_block_tables,
+                                 int32_t batch, int32_t max_blocks, const int32_t* h_ctx_lens,
+                                 const int64_t* h_slot_mapping, int32_t n_tok,
+                                 const float* h_k_new, const float* h_v_new, const float* h_q,
+                                 float* h_out, int32_t n_heads, float scale,
+                                 const float* d_sinks, void* stream);
+/* Number of kernel launches the last gkv_kv_append / gkv_paged_decode /
+ * gkv_decode_step_host / gkv_compute_attention call on this pool enqueued. */
+GKV_API int gkv_pool_last_launch_count(const gkv_pool* pool);
+/* Waits for `stream` with a bound: GKV_ETIMEDOUT after timeout_ms instead of hanging.  Also
+ * reports GKV_EDEVICE if a kernel of this pool flagged a bad block id or an expired wait
+ * since the last check (pool may be NULL to skip that check). */
+GKV_API int gkv_sync(gkv_pool* pool, void* stream, int32_t timeout_ms);
+
+/* Shape of the split-KV work list gkv_upload_step builds (diagnostics and tests). */
+typedef struct gkv_plan_info {
+    int64_t total_chunks;  /* chunks of <= 8 tokens over all (sequence, kv head) segments */
+    int32_t n_pieces;      /* contiguous chunk ranges, one segment each                 */
+    int32_t n_slots;       /* pieces that write a partial (segment split over workers)  */
+    int32_t n_merge;       /* segments merged by the log-sum-exp kernel                 */
+    int32_t n_workers;
+} gkv_plan_info;
+/* Builds the decode work list for n_workers warp workers without touching a GPU: the
+ * flattened chunk stream of all segments is split into n_workers equal contiguous ranges.
+ * The piece arrays (cap_pieces entries each) and worker_begin (n_workers + 1) are optional;
+ * pass NULL to query sizes only.  (No reference counterpart: the reference runs one
+ * sequence per call, PagedTransformerRunner.cs:605-656.) */
+GKV_API int gkv_plan_decode(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv,
+                            int32_t block_size, int32_t n_workers, gkv_plan_info* info,
+                            int32_t* piece_seg, int32_t* piece_c0, int32_t* piece_c1,
+                            int32_t* piece_slot, int32_t* worker_begin, int32_t cap_pieces);
+
+/* ---- 4. multi-GPU host logic ---------------------------------------------------------- */
+
+/* Sequence partitioning for the per-GPU pools: longest-processing-time-first bin packing
+ * of ctx_lens onto n_ranks (each rank owns its pool, no collective).  out_rank[i] = rank of
+ * sequence i.  Ties broken by lower index, then lower rank, so every rank computes the same
+ * answer.  (No reference counterpart: the reference is single-GPU,
+ * CudaPagedTransformerRunner.cs:108.) */
+GKV_API int gkv_partition_lpt(const int32_t* ctx_lens, int32_t n, int32_t n_ranks,
+                              int32_t* out_rank);
+/* Contiguous block range [begin, end) of rank r when n_blocks table entries are split over
+ * n_ranks for long-context split-KV (remainder to the lowest ranks). */
+GKV_API int gkv_split_block_range(int32_t n_blocks, int32_t n_ranks, int32_t rank,
+                                  int32_t* out_begin, int32_t* out_end);
+
+/* ---- misc ----------------------------------------------------------------------------- */
+GKV_API const char* gkv_last_error(void);
+/* Build identification, e.g. "glacier_kv 0.1 sm_100a". */
+GKV_API const char* gkv_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GLACIER_KV_H */

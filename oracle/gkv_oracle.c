@@ -1,0 +1,288 @@
+/*
+ * gkv_oracle.c -- CPU restatement of Glacier.Serve's paged-KV path (TEST INFRASTRUCTURE:
+ * the checker of the CUDA path and the timed CPU baseline; never part of the product).
+ *
+ * Follows src/Glacier.Serve/Inference/PagedAttention/PagedAttentionKernel.cs and
+ * PagedBlockPool.cs of the reference; see gkv_oracle.h for what is and is not pinned.
+ * Build: oracle/Makefile (gcc -O3 -march=native -fopenmp), output oracle/lib/.
+ */
+#include "gkv_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+uint16_t oracle_f32_to_bf16(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)0x7fff; /* canonical NaN */
+    u += 0x7fffu + ((u >> 16) & 1u);                                /* round half to even */
+    return (uint16_t)(u >> 16);
+}
+
+float oracle_bf16_to_f32(uint16_t h) {
+    uint32_t u = (uint32_t)h << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+static size_t elem_size(const oracle_geom* g) { return g->dtype == ORACLE_BF16 ? 2 : 4; }
+
+/* Element offsets of GetKeyPtr / GetValuePtr, PagedBlockPool.cs:124-145. */
+static int64_t k_off(const oracle_geom* g, int64_t blk, int64_t layer, int64_t h, int64_t slot) {
+    const int64_t hs = (int64_t)g->block_size * g->head_dim;
+    const int64_t ls = (int64_t)g->heads_kv * hs;
+    const int64_t bs = (int64_t)g->layers * ls;
+    return blk * bs + layer * ls + h * hs + slot * g->head_dim;
+}
+
+static int64_t v_off(const oracle_geom* g, int64_t blk, int64_t layer, int64_t h, int64_t slot) {
+    const int64_t hs = (int64_t)g->block_size * g->v_head_dim;
+    const int64_t ls = (int64_t)g->heads_kv * hs;
+    const int64_t bs = (int64_t)g->layers * ls;
+    return blk * bs + layer * ls + h * hs + slot * g->v_head_dim;
+}
+
+static inline float load_elem(const void* base, int dtype, int64_t i) {
+    if (dtype == ORACLE_BF16) return oracle_bf16_to_f32(((const uint16_t*)base)[i]);
+    return ((const float*)base)[i];
+}
+
+static inline void store_elem(void* base, int dtype, int64_t i, float v) {
+    if (dtype == ORACLE_BF16)
+        ((uint16_t*)base)[i] = oracle_f32_to_bf16(v);
+    else
+        ((float*)base)[i] = v;
+}
+
+int oracle_store(void* kpool, void* vpool, const oracle_geom* g, int32_t block, int32_t layer,
+                 int32_t slot, const float* k, const float* v) {
+    /* Store, PagedBlockPool.cs:151-161: per kv head, copy head_dim floats of K and
+     * v_head_dim floats of V from the contiguous [heads_kv][dim] sources. */
+    if (block < 0 || block >= g->total_blocks || layer < 0 || layer >= g->layers || slot < 0 ||
+        slot >= g->block_size)
+        return ORACLE_EINVAL;
+    for (int32_t h = 0; h < g->heads_kv; ++h) {
+        const int64_t ko = k_off(g, block, layer, h, slot);
+        const int64_t vo = v_off(g, block, layer, h, slot);
+        for (int32_t d = 0; d < g->head_dim; ++d)
+            store_elem(kpool, g->dtype, ko + d, k[(int64_t)h * g->head_dim + d]);
+        for (int32_t d = 0; d < g->v_head_dim; ++d)
+            store_elem(vpool, g->dtype, vo + d, v[(int64_t)h * g->v_head_dim + d]);
+    }
+    return ORACLE_OK;
+}
+
+int oracle_copy_block_data(void* kpool, void* vpool, const oracle_geom* g, int32_t src,
+                           int32_t dst, int32_t valid_tokens) {
+    /* CopyBlockData, PagedBlockPool.cs:304-327: the first min(valid, block_size) slots of
+     * every (layer, head), K and V. */
+    if (valid_tokens <= 0) return ORACLE_OK;
+    if (src < 0 || src >= g->total_blocks || dst < 0 || dst >= g->total_blocks) return ORACLE_EINVAL;
+    const int32_t count = valid_tokens < g->block_size ? valid_tokens : g->block_size;
+    const size_t es = elem_size(g);
+    for (int32_t l = 0; l < g->layers; ++l)
+        for (int32_t h = 0; h < g->heads_kv; ++h)
+            for (int32_t t = 0; t < count; ++t) {
+                memcpy((char*)kpool + k_off(g, dst, l, h, t) * es,
+                       (const char*)kpool + k_off(g, src, l, h, t) * es, (size_t)g->head_dim * es);
+                memcpy((char*)vpool + v_off(g, dst, l, h, t) * es,
+                       (const char*)vpool + v_off(g, src, l, h, t) * es, (size_t)g->v_head_dim * es);
+            }
+    return ORACLE_OK;
+}
+
+/* QuantKernels.VecDotF32 (NuGet Glacier.Inference 1.7.0, called at
+ * PagedAttentionKernel.cs:64): source absent.  Restated as an in-order fp32 fused
+ * multiply-add chain; the reference's lane order is unpinned. */
+static float vec_dot(const float* q, const void* kbase, int dtype, int64_t ko, int32_t n) {
+    float s = 0.f;
+    for (int32_t i = 0; i < n; ++i) s = fmaf(q[i], load_elem(kbase, dtype, ko + i), s);
+    return s;
+}
+
+/* QuantKernels.Softmax(scores, n, sinkLogit) (called at PagedAttentionKernel.cs:70): source
+ * absent.  Restated as the conventional max-subtracted softmax; an attention sink takes
+ * part in the max and adds exp(sink - max) to the denominator only.  Unpinned. */
+static void softmax(float* s, int32_t n, int32_t has_sink, float sink) {
+    float mx = -INFINITY;
+    for (int32_t i = 0; i < n; ++i) mx = s[i] > mx ? s[i] : mx;
+    if (has_sink && sink > mx) mx = sink;
+    float sum = 0.f;
+    for (int32_t i = 0; i < n; ++i) {
+        s[i] = expf(s[i] - mx);
+        sum += s[i];
+    }
+    if (has_sink) sum += expf(sink - mx);
+    const float inv = 1.f / sum;
+    for (int32_t i = 0; i < n; ++i) s[i] *= inv;
+}
+
+int oracle_compute_attention(const void* kpool, const void* vpool, const oracle_geom* g,
+                             int32_t stage_layer, int32_t pos, const float* q, float* out,
+                             const int32_t* block_ids, int32_t n_block_ids, int32_t token_count,
+                             int32_t n_heads, int32_t n_heads_kv, int32_t head_dim,
+                             int32_t v_head_dim, float attn_scale, float* head_scores,
+                             int32_t max_seq_len, int32_t has_sink, float sink_logit,
+                             int32_t n_threads) {
+    /* argument checks, PagedAttentionKernel.cs:34-39 */
+    if (max_seq_len <= 0) return ORACLE_EINVAL;
+    if (pos < 0 || pos >= max_seq_len) return ORACLE_EINVAL;
+    if (token_count > max_seq_len) return ORACLE_EINVAL;
+    /* causal length, :41-42 */
+    const int32_t total = token_count < pos + 1 ? token_count : pos + 1;
+    if (total == 0) return ORACLE_OK;
+    if (n_heads_kv <= 0 || n_heads % n_heads_kv != 0) return ORACLE_EINVAL;
+    const int32_t group = n_heads / n_heads_kv; /* :44 */
+    const int32_t bsz = g->block_size;          /* :45 */
+    const int32_t block_count = (total + bsz - 1) / bsz; /* :46 */
+    if (block_count > n_block_ids) return ORACLE_EINVAL; /* GetBlockId would throw */
+    for (int32_t b = 0; b < block_count; ++b)
+        if (block_ids[b] < 0 || block_ids[b] >= g->total_blocks) return ORACLE_EINVAL;
+
+#ifdef _OPENMP
+    const int nt = n_threads > 0 ? n_threads : omp_get_max_threads();
+#pragma omp parallel for num_threads(nt) schedule(static)
+#endif
+    for (int32_t h = 0; h < n_heads; ++h) { /* Parallel.For over heads, :48 */
+        const int32_t hkv = h / group;      /* :50 */
+        const float* qh = q + (int64_t)h * head_dim;
+        float* scores = head_scores + (int64_t)h * max_seq_len;
+        /* 1. Q.K^T per token through the block table, :55-67 */
+        for (int32_t b = 0; b < block_count; ++b) {
+            const int32_t pid = block_ids[b];
+            const int32_t base = b * bsz;
+            const int32_t tib = bsz < total - base ? bsz : total - base;
+            for (int32_t t = 0; t < tib; ++t) {
+                const float dot = vec_dot(qh, kpool, g->dtype, k_off(g, pid, stage_layer, hkv, t), head_dim);
+                scores[base + t] = dot * attn_scale;
+            }
+        }
+        /* 2. softmax over all valid tokens, :70 */
+        softmax(scores, total, has_sink, sink_logit);
+        /* 3. P.V: each output lane is an independent in-order FMA chain over tokens, exactly
+         * the reference's AVX-512 / AVX2 / generic accumulators, :75-117,:290-306,:326-370 */
+        float* oh = out + (int64_t)h * v_head_dim;
+        for (int32_t d = 0; d < v_head_dim; ++d) oh[d] = 0.f;
+        for (int32_t b = 0; b < block_count; ++b) {
+            const int32_t pid = block_ids[b];
+            const int32_t base = b * bsz;
+            const int32_t tib = bsz < total - base ? bsz : total - base;
+            for (int32_t t = 0; t < tib; ++t) {
+                const float w = scores[base + t];
+                const int64_t vo = v_off(g, pid, stage_layer, hkv, t);
+                for (int32_t d = 0; d < v_head_dim; ++d)
+                    oh[d] = fmaf(w, load_elem(vpool, g->dtype, vo + d), oh[d]);
+            }
+        }
+    }
+    return ORACLE_OK;
+}
+
+int oracle_decode_batch(const void* kpool, const void* vpool, const oracle_geom* g,
+                        int32_t layer, const int32_t* tables, int32_t batch, int32_t max_blocks,
+                        const int32_t* ctx_lens, const float* q, float* out, int32_t n_heads,
+                        float scale, int32_t has_sink, float sink_logit, int32_t n_threads) {
+    const int32_t max_seq = max_blocks * g->block_size;
+    if (max_seq <= 0) return batch > 0 ? ORACLE_EINVAL : ORACLE_OK;
+    float* scratch = (float*)malloc(sizeof(float) * (size_t)n_heads * (size_t)max_seq);
+    if (!scratch) return ORACLE_EINVAL;
+    int rc = ORACLE_OK;
+    for (int32_t b = 0; b < batch && rc == ORACLE_OK; ++b) { /* sequences serial */
+        const int32_t ctx = ctx_lens[b];
+        if (ctx <= 0) continue;
+        rc = oracle_compute_attention(kpool, vpool, g, layer, ctx - 1,
+                                      q + (int64_t)b * n_heads * g->head_dim,
+                                      out + (int64_t)b * n_heads * g->v_head_dim,
+                                      tables + (int64_t)b * max_blocks, max_blocks, ctx, n_heads,
+                                      g->heads_kv, g->head_dim, g->v_head_dim, scale, scratch,
+                                      max_seq, has_sink, sink_logit, n_threads);
+    }
+    free(scratch);
+    return rc;
+}
+
+int oracle_decode_batch_parallel(const void* kpool, const void* vpool, const oracle_geom* g,
+                                 int32_t layer, const int32_t* tables, int32_t batch,
+                                 int32_t max_blocks, const int32_t* ctx_lens, const float* q,
+                                 float* out, int32_t n_heads, float scale, int32_t n_threads) {
+    /* Same arithmetic as oracle_compute_attention, scheduled over (sequence, head) pairs. */
+    const int32_t max_seq = max_blocks * g->block_size;
+    const int32_t group = n_heads / g->heads_kv;
+    const int32_t bsz = g->block_size;
+    int bad = 0;
+#ifdef _OPENMP
+    const int nt = n_threads > 0 ? n_threads : omp_get_max_threads();
+#pragma omp parallel num_threads(nt) reduction(| : bad)
+#endif
+    {
+        float* scores = (float*)malloc(sizeof(float) * (size_t)(max_seq > 0 ? max_seq : 1));
+#ifdef _OPENMP
+#pragma omp for schedule(dynamic, 1)
+#endif
+        for (int64_t bh = 0; bh < (int64_t)batch * n_heads; ++bh) {
+            const int32_t b = (int32_t)(bh / n_heads);
+            const int32_t h = (int32_t)(bh % n_heads);
+            const int32_t total = ctx_lens[b];
+            if (total <= 0 || !scores) continue;
+            const int32_t* ids = tables + (int64_t)b * max_blocks;
+            const int32_t hkv = h / group;
+            const float* qh = q + ((int64_t)b * n_heads + h) * g->head_dim;
+            const int32_t block_count = (total + bsz - 1) / bsz;
+            if (block_count > max_blocks) { bad = 1; continue; }
+            for (int32_t bb = 0; bb < block_count; ++bb) {
+                const int32_t base = bb * bsz;
+                const int32_t tib = bsz < total - base ? bsz : total - base;
+                for (int32_t t = 0; t < tib; ++t)
+                    scores[base + t] = vec_dot(qh, kpool, g->dtype, k_off(g, ids[bb], layer, hkv, t), g->head_dim) * scale;
+            }
+            softmax(scores, total, 0, 0.f);
+            float* oh = out + ((int64_t)b * n_heads + h) * g->v_head_dim;
+            for (int32_t d = 0; d < g->v_head_dim; ++d) oh[d] = 0.f;
+            for (int32_t bb = 0; bb < block_count; ++bb) {
+                const int32_t base = bb * bsz;
+                const int32_t tib = bsz < total - base ? bsz : total - base;
+                for (int32_t t = 0; t < tib; ++t) {
+                    const float w = scores[base + t];
+                    const int64_t vo = v_off(g, ids[bb], layer, hkv, t);
+                    for (int32_t d = 0; d < g->v_head_dim; ++d)
+                        oh[d] = fmaf(w, load_elem(vpool, g->dtype, vo + d), oh[d]);
+                }
+            }
+        }
+        free(scores);
+    }
+    return bad ? ORACLE_EINVAL : ORACLE_OK;
+}
+
+int oracle_prefill_chunk(const void* kpool, const void* vpool, const oracle_geom* g,
+                         int32_t layer, const int32_t* block_ids, int32_t n_block_ids,
+                         int32_t token_count, int32_t start_pos, int32_t n_q, const float* q,
+                         float* out, int32_t n_heads, float scale, int32_t n_threads) {
+    /* ForwardPrefillSubBatch, PagedTransformerRunner.cs:454-471: one ComputeAttention per
+     * chunk token with pos = chunkStart + t; the causal mask is min(TokenCount, pos + 1). */
+    const int32_t max_seq = n_block_ids * g->block_size;
+    float* scratch = (float*)malloc(sizeof(float) * (size_t)n_heads * (size_t)(max_seq > 0 ? max_seq : 1));
+    if (!scratch) return ORACLE_EINVAL;
+    int rc = ORACLE_OK;
+    for (int32_t t = 0; t < n_q && rc == ORACLE_OK; ++t)
+        rc = oracle_compute_attention(kpool, vpool, g, layer, start_pos + t,
+                                      q + (int64_t)t * n_heads * g->head_dim,
+                                      out + (int64_t)t * n_heads * g->v_head_dim, block_ids,
+                                      n_block_ids, token_count, n_heads, g->heads_kv, g->head_dim,
+                                      g->v_head_dim, scale, scratch, max_seq, 0, 0.f, n_threads);
+    free(scratch);
+    return rc;
+}
+
+int oracle_max_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}

@@ -1,0 +1,142 @@
+"""ctypes wrapper of oracle/lib/libgkv_oracle.so (TEST INFRASTRUCTURE ONLY).
+
+numpy in, numpy out.  Arena arrays are host copies in the device layout
+[block][layer][head_kv][slot][dim], float32 or bf16 bit patterns (uint16).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+_DIR = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_DIR, "lib", "libgkv_oracle.so")
+
+
+def build() -> None:
+    subprocess.run(["make", "-s", "-C", _DIR], check=True)
+
+
+def _load() -> C.CDLL:
+    if not os.path.exists(LIB_PATH):
+        build()
+    lib = C.CDLL(LIB_PATH)
+    P, I, F = C.c_void_p, C.c_int32, C.c_float
+    lib.oracle_f32_to_bf16.restype = C.c_uint16
+    lib.oracle_f32_to_bf16.argtypes = [F]
+    lib.oracle_bf16_to_f32.restype = F
+    lib.oracle_bf16_to_f32.argtypes = [C.c_uint16]
+    lib.oracle_store.argtypes = [P, P, P, I, I, I, P, P]
+    lib.oracle_copy_block_data.argtypes = [P, P, P, I, I, I]
+    lib.oracle_compute_attention.argtypes = [P, P, P, I, I, P, P, P, I, I, I, I, I, I, F, P, I, I, F, I]
+    lib.oracle_decode_batch.argtypes = [P, P, P, I, P, I, I, P, P, P, I, F, I, F, I]
+    lib.oracle_decode_batch_parallel.argtypes = [P, P, P, I, P, I, I, P, P, P, I, F, I]
+    lib.oracle_prefill_chunk.argtypes = [P, P, P, I, P, I, I, I, I, P, P, I, F, I]
+    lib.oracle_max_threads.restype = C.c_int
+    for n in ("oracle_store", "oracle_copy_block_data", "oracle_compute_attention",
+              "oracle_decode_batch", "oracle_decode_batch_parallel", "oracle_prefill_chunk"):
+        getattr(lib, n).restype = C.c_int
+    return lib
+
+
+lib = _load()
+
+F32, BF16 = 0, 1
+
+
+class Geom(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in
+                ("total_blocks", "layers", "heads_kv", "head_dim", "v_head_dim", "block_size", "dtype")]
+
+
+def geom(total_blocks, layers, heads_kv, head_dim, v_head_dim=None, block_size=16, dtype=F32) -> Geom:
+    return Geom(total_blocks, layers, heads_kv, head_dim, v_head_dim or head_dim, block_size, dtype)
+
+
+def _p(a: np.ndarray) -> int:
+    assert a.flags["C_CONTIGUOUS"], "arrays must be C-contiguous"
+    return a.ctypes.data
+
+
+def new_arena(g: Geom):
+    kshape = (g.total_blocks, g.layers, g.heads_kv, g.block_size, g.head_dim)
+    vshape = (g.total_blocks, g.layers, g.heads_kv, g.block_size, g.v_head_dim)
+    dt = np.uint16 if g.dtype == BF16 else np.float32
+    return np.zeros(kshape, dt), np.zeros(vshape, dt)
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even fp32 -> bf16 bit patterns (vectorised restatement of
+    oracle_f32_to_bf16; tests check the two agree)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    r[nan] = 0x7FFF
+    return r
+
+
+def bf16_bits_to_f32(h: np.ndarray) -> np.ndarray:
+    return (np.asarray(h, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def store(K, V, g: Geom, block, layer, slot, k: np.ndarray, v: np.ndarray) -> int:
+    k = np.ascontiguousarray(k, np.float32)
+    v = np.ascontiguousarray(v, np.float32)
+    return lib.oracle_store(_p(K), _p(V), C.byref(g), block, layer, slot, _p(k), _p(v))
+
+
+def copy_block_data(K, V, g: Geom, src, dst, valid) -> int:
+    return lib.oracle_copy_block_data(_p(K), _p(V), C.byref(g), src, dst, valid)
+
+
+def compute_attention(K, V, g: Geom, stage_layer, pos, q, block_ids, token_count, n_heads, n_heads_kv,
+                      head_dim, v_head_dim, attn_scale, max_seq_len, sink_logit=None, n_threads=0):
+    """Returns (rc, out[n_heads, v_head_dim])."""
+    q = np.ascontiguousarray(q, np.float32)
+    ids = np.ascontiguousarray(np.asarray(block_ids, np.int32))
+    out = np.zeros((n_heads, v_head_dim), np.float32)
+    scratch = np.zeros(max(n_heads * max(max_seq_len, 1), 1), np.float32)
+    rc = lib.oracle_compute_attention(
+        _p(K), _p(V), C.byref(g), stage_layer, pos, _p(q), _p(out), _p(ids) if ids.size else None,
+        ids.size, token_count, n_heads, n_heads_kv, head_dim, v_head_dim, attn_scale, _p(scratch),
+        max_seq_len, 0 if sink_logit is None else 1, float(sink_logit or 0.0), n_threads)
+    return rc, out
+
+
+def decode_batch(K, V, g: Geom, layer, tables, ctx_lens, q, n_heads, scale, sink_logit=None,
+                 n_threads=0, out=None, parallel=False):
+    tables = np.ascontiguousarray(tables, np.int32)
+    ctx = np.ascontiguousarray(ctx_lens, np.int32)
+    q = np.ascontiguousarray(q, np.float32)
+    B = tables.shape[0]
+    if out is None:
+        out = np.zeros((B, n_heads, g.v_head_dim), np.float32)
+    if parallel:
+        assert sink_logit is None
+        rc = lib.oracle_decode_batch_parallel(_p(K), _p(V), C.byref(g), layer, _p(tables), B, tables.shape[1],
+                                              _p(ctx), _p(q), _p(out), n_heads, scale, n_threads)
+    else:
+        rc = lib.oracle_decode_batch(_p(K), _p(V), C.byref(g), layer, _p(tables), B, tables.shape[1], _p(ctx),
+                                     _p(q), _p(out), n_heads, scale, 0 if sink_logit is None else 1,
+                                     float(sink_logit or 0.0), n_threads)
+    if rc != 0:
+        raise ValueError(f"oracle_decode_batch failed ({rc})")
+    return out
+
+
+def prefill_chunk(K, V, g: Geom, layer, block_ids, token_count, start_pos, q, n_heads, scale, n_threads=0):
+    ids = np.ascontiguousarray(np.asarray(block_ids, np.int32))
+    q = np.ascontiguousarray(q, np.float32)
+    n_q = q.shape[0]
+    out = np.zeros((n_q, n_heads, g.v_head_dim), np.float32)
+    rc = lib.oracle_prefill_chunk(_p(K), _p(V), C.byref(g), layer, _p(ids), ids.size, token_count, start_pos,
+                                  n_q, _p(q), _p(out), n_heads, scale, n_threads)
+    if rc != 0:
+        raise ValueError(f"oracle_prefill_chunk failed ({rc})")
+    return out
+
+
+def max_threads() -> int:
+    return lib.oracle_max_threads()

@@ -1,0 +1,106 @@
+"""Shared helpers of the GPU parity tests (device arena <-> host oracle arrays)."""
+import math
+
+import numpy as np
+
+from oracle import pyoracle as O
+
+TOL = {"f32": 1e-4, "bf16": 2e-2}  # max-abs parity bars stated for this path
+
+
+def torch():
+    import torch as _t
+
+    return _t
+
+
+def geom_of(pool):
+    return O.geom(pool.total_blocks, pool.layers, pool.heads_kv, pool.head_dim, pool.value_head_dim,
+                  pool.block_size, O.BF16 if pool.dtype == "bf16" else O.F32)
+
+
+def arena_to_host(pool):
+    """Host copies of the K and V arenas in the oracle's representation."""
+    t = torch()
+    k, v = pool.key_view(), pool.value_view()
+    if pool.dtype == "bf16":
+        return (k.view(t.int16).cpu().numpy().view(np.uint16), v.view(t.int16).cpu().numpy().view(np.uint16))
+    return k.cpu().numpy(), v.cpu().numpy()
+
+
+def host_to_arena(pool, K, V):
+    t = torch()
+    for view, arr in ((pool.key_view(), K), (pool.value_view(), V)):
+        if pool.dtype == "bf16":
+            view.view(t.int16).copy_(t.from_numpy(np.ascontiguousarray(arr).view(np.int16)))
+        else:
+            view.copy_(t.from_numpy(np.ascontiguousarray(arr)))
+
+
+def random_arena(pool, rng):
+    g = geom_of(pool)
+    K, V = O.new_arena(g)
+    kf = rng.standard_normal(K.shape).astype(np.float32)
+    vf = rng.standard_normal(V.shape).astype(np.float32)
+    if pool.dtype == "bf16":
+        K[...] = O.f32_to_bf16_bits(kf)
+        V[...] = O.f32_to_bf16_bits(vf)
+    else:
+        K[...] = kf
+        V[...] = vf
+    host_to_arena(pool, K, V)
+    return K, V
+
+
+def random_tables(rng, ctx, bs, total_blocks):
+    mb = max(1, max((int(c) + bs - 1) // bs for c in ctx))
+    need = sum((int(c) + bs - 1) // bs for c in ctx)
+    assert need <= total_blocks
+    perm = rng.permutation(total_blocks).astype(np.int32)
+    tables = np.full((len(ctx), mb), -1, np.int32)
+    at = 0
+    for i, c in enumerate(ctx):
+        n = (int(c) + bs - 1) // bs
+        tables[i, :n] = perm[at: at + n]
+        at += n
+    return tables
+
+
+def gpu_decode(pool, layer, tables, ctx, q_np, n_heads, scale, sinks=None, out_init=0.0):
+    t = torch()
+    dev = f"cuda:{pool.device}"
+    q = t.from_numpy(np.ascontiguousarray(q_np, np.float32)).to(dev)
+    out = t.full((len(ctx), n_heads, pool.value_head_dim), out_init, dtype=t.float32, device=dev)
+    pool.upload_step(tables, np.asarray(ctx, np.int32))
+    pool.paged_decode(layer, q, out, n_heads, scale,
+                      None if sinks is None else t.from_numpy(np.asarray(sinks, np.float32)).to(dev))
+    pool.sync()
+    return out.cpu().numpy()
+
+
+def compact(pool, tables, ctx, rows):
+    """Device-side gather of the blocks `rows` use into a small host arena + renumbered tables,
+    so the oracle can check sampled sequences of a multi-GB pool."""
+    t = torch()
+    sub = tables[rows]
+    ids = sorted({int(b) for r, c in zip(sub, np.asarray(ctx)[rows]) for b in r[: (int(c) + pool.block_size - 1) // pool.block_size]})
+    remap = {b: i for i, b in enumerate(ids)}
+    idx = t.tensor(ids, dtype=t.long, device=f"cuda:{pool.device}")
+    k = pool.key_view().index_select(0, idx)
+    v = pool.value_view().index_select(0, idx)
+    if pool.dtype == "bf16":
+        K = k.view(t.int16).cpu().numpy().view(np.uint16)
+        V = v.view(t.int16).cpu().numpy().view(np.uint16)
+    else:
+        K, V = k.cpu().numpy(), v.cpu().numpy()
+    new = np.full_like(sub, -1)
+    for i, (r, c) in enumerate(zip(sub, np.asarray(ctx)[rows])):
+        n = (int(c) + pool.block_size - 1) // pool.block_size
+        new[i, :n] = [remap[int(b)] for b in r[:n]]
+    g = O.geom(len(ids), pool.layers, pool.heads_kv, pool.head_dim, pool.value_head_dim, pool.block_size,
+               O.BF16 if pool.dtype == "bf16" else O.F32)
+    return g, np.ascontiguousarray(K), np.ascontiguousarray(V), new
+
+
+def scale_of(d):
+    return 1.0 / math.sqrt(d)

@@ -1,0 +1,184 @@
+"""Pins the CPU oracle against the reference's own fixtures before it is trusted as checker.
+
+The reference (C#) cannot run here; these are the values its tests fix (see
+tests/golden/make_golden.py for provenance) plus the argument checks it throws on.
+"""
+import glob
+import json
+import math
+import os
+
+import numpy as np
+import pytest
+
+from conftest import ROOT
+from oracle import pyoracle as O
+
+GOLD = os.path.join(ROOT, "tests", "golden")
+
+
+def kat_inputs(dtype=O.F32):
+    kat = json.load(open(os.path.join(GOLD, "kat_compute_attention.json")))
+    d, T, nH, nKv, bs = kat["head_dim"], kat["tokens"], kat["n_heads"], kat["n_heads_kv"], kat["block_size"]
+    g = O.geom(8, 1, nKv, d, d, bs, dtype)
+    K, V = O.new_arena(g)
+    ids = []
+    for t in range(T):  # BlockTable.AppendToken on a fresh pool -> blocks 0, 1
+        blk, off = t // bs, t % bs
+        if off == 0:
+            ids.append(blk)
+        k = np.zeros((nKv, d), np.float32)
+        v = np.zeros((nKv, d), np.float32)
+        for h in range(nKv):
+            k[h] = kat["k_value_per_token"][t]
+            v[h] = kat["v_scale_per_kv_head"][h] * (t + 1)
+        assert O.store(K, V, g, blk, 0, off, k.ravel(), v.ravel()) == 0
+    q = np.full((nH, d), kat["q_value"], np.float32)
+    return kat, g, K, V, ids, q
+
+
+def test_oracle_matches_closed_form_kat():
+    kat, g, K, V, ids, q = kat_inputs()
+    rc, out = O.compute_attention(K, V, g, 0, kat["tokens"] - 1, q, ids, kat["tokens"], kat["n_heads"],
+                                  kat["n_heads_kv"], kat["head_dim"], kat["head_dim"], kat["attn_scale"],
+                                  kat["tokens"])
+    assert rc == 0
+    for h, e in enumerate(kat["expected_per_head"]):
+        assert out[h].min() > 0  # the reference test's assertion
+        np.testing.assert_allclose(out[h], e, rtol=2e-6)  # fp32 arithmetic vs float64 closed form
+        assert np.all(out[h] == out[h][0])  # per-head uniformity (:171-177)
+
+
+def test_oracle_store_retrieve_exact():
+    s = json.load(open(os.path.join(GOLD, "store_retrieve.json")))
+    g = O.geom(s["total_blocks"], s["layers"], s["heads_kv"], s["head_dim"], s["head_dim"], s["block_size"])
+    K, V = O.new_arena(g)
+    assert O.store(K, V, g, 0, s["layer"], s["slot"], np.array(s["k"], np.float32), np.array(s["v"], np.float32)) == 0
+    for h in range(2):
+        assert list(K[0, s["layer"], h, s["slot"]]) == s["k"][4 * h: 4 * h + 4]
+        assert list(V[0, s["layer"], h, s["slot"]]) == s["v"][4 * h: 4 * h + 4]
+    assert K.sum() == sum(s["k"]) and V.sum() == sum(s["v"])
+
+
+def test_oracle_copy_block_data_sentinels():
+    """PrefixHashKvCacheTests.cs:134-181: the fork holds 42.0; mutating it leaves the source."""
+    g = O.geom(16, 2, 2, 32, 32, 16)
+    K, V = O.new_arena(g)
+    K[0, 0, 0, 0, 0] = 42.0
+    assert O.copy_block_data(K, V, g, 0, 1, 10) == 0
+    assert K[1, 0, 0, 0, 0] == 42.0
+    K[1, 0, 0, 0, 0] = 999.0
+    assert K[0, 0, 0, 0, 0] == 42.0
+    # only the first `valid` slots are copied (PagedBlockPool.cs:309-315)
+    K[0, 1, 1, 12, :] = 7.0
+    assert O.copy_block_data(K, V, g, 0, 2, 10) == 0
+    assert np.all(K[2, 1, 1, 12] == 0)
+    assert O.copy_block_data(K, V, g, 0, 3, 0) == 0 and np.all(K[3] == 0)
+
+
+@pytest.mark.parametrize("pos", [16, -1])
+def test_oracle_rejects_out_of_bounds_position(pos):
+    """PhaseCServeRemediationTests.cs:117-174: pos outside [0, maxSeqLen) throws."""
+    g = O.geom(4, 1, 1, 32, 32, 16)
+    K, V = O.new_arena(g)
+    rc, _ = O.compute_attention(K, V, g, 0, pos, np.zeros((1, 32), np.float32), [0], 1, 1, 1, 32, 32,
+                                1 / math.sqrt(32), 16)
+    assert rc == -1
+
+
+def test_oracle_other_argument_checks_and_noop():
+    g = O.geom(4, 1, 1, 32, 32, 16)
+    K, V = O.new_arena(g)
+    q = np.ones((1, 32), np.float32)
+    assert O.compute_attention(K, V, g, 0, 0, q, [0], 1, 1, 1, 32, 32, 1.0, 0)[0] == -1   # maxSeqLen <= 0
+    assert O.compute_attention(K, V, g, 0, 0, q, [0], 17, 1, 1, 32, 32, 1.0, 16)[0] == -1  # TokenCount > max
+    rc, out = O.compute_attention(K, V, g, 0, 3, q, [], 0, 1, 1, 32, 32, 1.0, 16)          # n == 0: no-op
+    assert rc == 0 and np.all(out == 0)
+
+
+def test_oracle_causal_length_is_min_of_count_and_pos():
+    """n = min(TokenCount, pos + 1) (PagedAttentionKernel.cs:41): pos < count attends a prefix."""
+    rng = np.random.default_rng(3)
+    g = O.geom(4, 1, 1, 32, 32, 16)
+    K, V = O.new_arena(g)
+    K[...] = rng.standard_normal(K.shape)
+    V[...] = rng.standard_normal(V.shape)
+    q = rng.standard_normal((2, 32)).astype(np.float32)
+    _, a = O.compute_attention(K, V, g, 0, 9, q, [2, 0], 20, 2, 1, 32, 32, 0.2, 32)
+    _, b = O.compute_attention(K, V, g, 0, 31, q, [2, 0], 10, 2, 1, 32, 32, 0.2, 32)
+    np.testing.assert_array_equal(a, b)
+
+
+def test_oracle_sink_only_enters_the_denominator():
+    rng = np.random.default_rng(4)
+    g = O.geom(2, 1, 1, 32, 32, 16)
+    K, V = O.new_arena(g)
+    K[...] = rng.standard_normal(K.shape)
+    V[...] = rng.standard_normal(V.shape)
+    q = rng.standard_normal((1, 32)).astype(np.float32)
+    _, plain = O.compute_attention(K, V, g, 0, 11, q, [1], 12, 1, 1, 32, 32, 0.3, 16)
+    _, sunk = O.compute_attention(K, V, g, 0, 11, q, [1], 12, 1, 1, 32, 32, 0.3, 16, sink_logit=0.5)
+    # double-precision restatement of softmax with a sink
+    s = np.array([float(np.dot(q[0].astype(np.float64), K[1, 0, 0, t])) * 0.3 for t in range(12)])
+    m = max(s.max(), 0.5)
+    w = np.exp(s - m)
+    den = w.sum() + math.exp(0.5 - m)
+    ref = (w[:, None] * V[1, 0, 0, :12].astype(np.float64)).sum(0) / den
+    np.testing.assert_allclose(sunk[0], ref, atol=1e-5)
+    np.testing.assert_allclose(plain[0] * (w.sum() / den), sunk[0], atol=1e-5)
+
+
+def test_bf16_rounding_restatements_agree():
+    rng = np.random.default_rng(5)
+    x = np.concatenate([rng.standard_normal(4096).astype(np.float32) * 10 ** rng.uniform(-30, 30, 4096).astype(np.float32),
+                        np.array([0.0, -0.0, 1.0, np.inf, -np.inf, 1.00390625, 1.01171875, 3.4e38], np.float32)])
+    bits = O.f32_to_bf16_bits(x)
+    for v, b in zip(x[::37], bits[::37]):
+        assert O.lib.oracle_f32_to_bf16(float(v)) == b
+    # ties go to even: 1 + 2^-8 is halfway between 1 and 1 + 2^-7
+    assert O.lib.oracle_f32_to_bf16(1.00390625) == 0x3F80
+    assert O.lib.oracle_f32_to_bf16(1.01171875) == 0x3F82
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLD, "decode_small_*.npz"))))
+def test_oracle_reproduces_committed_decode_fixtures(path):
+    z = np.load(path)
+    g = O.geom(*[int(x) for x in z["geom"]])
+    out = O.decode_batch(z["K"], z["V"], g, 0, z["tables"], z["ctx"], z["q"], int(z["n_heads"]), float(z["scale"]))
+    np.testing.assert_array_equal(out, z["out"])
+    # the scheduling variant computes the same numbers
+    par = O.decode_batch(z["K"], z["V"], g, 0, z["tables"], z["ctx"], z["q"], int(z["n_heads"]), float(z["scale"]),
+                         parallel=True)
+    np.testing.assert_array_equal(par, z["out"])
+
+
+def test_oracle_decode_against_float64_numpy():
+    """Independent float64 restatement of the math on one fixture (checks the C oracle)."""
+    z = np.load(os.path.join(GOLD, "decode_small_gqa4_d32_bs16_f32.npz"))
+    K, V, tables, ctx, q = z["K"], z["V"], z["tables"], z["ctx"], z["q"]
+    nH, scale = int(z["n_heads"]), float(z["scale"])
+    nKv = K.shape[2]
+    for b, c in enumerate(ctx):
+        rows = [(tables[b, t // 16], t % 16) for t in range(c)]
+        for h in range(nH):
+            kv = h // (nH // nKv)
+            kk = np.stack([K[blk, 0, kv, o] for blk, o in rows]).astype(np.float64)
+            vv = np.stack([V[blk, 0, kv, o] for blk, o in rows]).astype(np.float64)
+            s = kk @ q[b, h].astype(np.float64) * scale
+            p = np.exp(s - s.max())
+            p /= p.sum()
+            np.testing.assert_allclose(z["out"][b, h], p @ vv, atol=2e-6)
+
+
+def test_oracle_prefill_equals_per_token_compute():
+    rng = np.random.default_rng(9)
+    g = O.geom(6, 1, 2, 32, 32, 16)
+    K, V = O.new_arena(g)
+    K[...] = rng.standard_normal(K.shape)
+    V[...] = rng.standard_normal(V.shape)
+    ids = [4, 1, 3]
+    q = rng.standard_normal((10, 4, 32)).astype(np.float32)
+    out = O.prefill_chunk(K, V, g, 0, ids, 40, 30, q, 4, 0.25)
+    for t in range(10):
+        _, o = O.compute_attention(K, V, g, 0, 30 + t, q[t], ids, 40, 4, 2, 32, 32, 0.25, 48)
+        np.testing.assert_array_equal(out[t], o)
