@@ -24,7 +24,6 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -71,48 +70,75 @@ def describe(w) -> str:
 
 
 class Clocks:
-    """nvidia-smi sampler running during the timed region."""
+    """Read-only NVML poller (SM clock, max clock, power, clock-event reasons) on a thread.
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.rows = []
+    Started before warm-up and stopped after the timed region; `mark()` opens and closes the
+    timed window so the summary reports the samples taken inside it (plus one sample taken
+    synchronously at each edge, so even a short window has data)."""
+
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
+
+    def __init__(self, device):
+        self.rows = []          # (t, sm_mhz, max_mhz, power_w, reasons_mask)
+        self.window = [None, None]
+        self.h = None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            p = torch.cuda.get_device_properties(device)
+            bus = f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            self.h = None
+
+    def sample(self):
+        nv = self.nv
+        try:
+            sm = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+            mx = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
+            pw = nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
+            rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            self.rows.append((time.perf_counter(), sm, mx, pw, rs))
+        except Exception:
+            pass
+
+    def _run(self):
+        while not self._stop.is_set():
+            self.sample()
+            time.sleep(0.005)
 
     def __enter__(self):
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-        try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+        if self.h is not None:
+            self.thread = threading.Thread(target=self._run, daemon=True)
             self.thread.start()
-        except (OSError, ValueError):
-            self.proc = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append([x.strip() for x in line.split(",")])
+    def mark(self, edge: int):
+        if self.h is not None:
+            self.sample()
+            self.window[edge] = time.perf_counter()
 
     def __exit__(self, *exc):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        if self.h is not None:
+            self._stop.set()
+            self.thread.join(timeout=2)
 
     def summary(self):
         if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows if len(r) > 8 for i in range(4) if r[5 + i] == "Active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled: NVML unavailable"]}
+        lo, hi = self.window
+        inside = [r for r in self.rows if lo is not None and hi is not None and lo <= r[0] <= hi]
+        rows = inside or self.rows
+        reasons = sorted({n for r in rows for n, m in self.REASONS.items() if r[4] & m})
+        return {"sm_mhz": statistics.median(r[1] for r in rows), "sm_max_mhz": max(r[2] for r in rows),
+                "reasons": reasons, "samples": len(rows),
+                "window": "timed region" if inside else "warm-up + timed region",
+                "power_w_max": max(r[3] for r in rows)}
 
 
 def traffic_from_profiles(cfg: str):
@@ -196,7 +222,7 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="cfg2")
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
@@ -265,6 +291,8 @@ def main():
             timed_decode[1].record(stream)
         return launches + pool.last_launch_count
 
+    clk = Clocks(dev)
+    clk.__enter__()
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize(dev)
@@ -275,18 +303,20 @@ def main():
     launches = 0
     barrier()
     torch.cuda.synchronize(dev)
-    with Clocks(local) as clk:
-        t0 = ev()
-        t0.record(stream)
-        for i in range(args.steps):
-            if flush is not None:
-                flush.zero_()
-            step_events[i][0].record(stream)
-            launches += step(dec_events[i])
-            step_events[i][1].record(stream)
-        t1 = ev()
-        t1.record(stream)
-        torch.cuda.synchronize(dev)
+    clk.mark(0)
+    t0 = ev()
+    t0.record(stream)
+    for i in range(args.steps):
+        if flush is not None:
+            flush.zero_()
+        step_events[i][0].record(stream)
+        launches += step(dec_events[i])
+        step_events[i][1].record(stream)
+    t1 = ev()
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    clk.mark(1)
+    clk.__exit__()
     barrier()
     torch.cuda.synchronize(dev)
     step_ms = sum(a.elapsed_time(b) for a, b in step_events) / args.steps
