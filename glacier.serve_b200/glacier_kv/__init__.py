@@ -436,6 +436,31 @@ def partition_lpt(ctx_lens: Sequence[int], n_ranks: int) -> np.ndarray:
     return out[: cl.size]
 
 
+def arena_desc(pool: PagedBlockPool) -> _lib.gkv_arena_desc:
+    """The raw-pointer description of a pool's arena (for gkv_paged_decode_noalloc)."""
+    k, v = pool._kv_ptrs()
+    return _lib.gkv_arena_desc(k, v, pool.total_blocks, pool.layers, pool.heads_kv, pool.head_dim,
+                               pool.value_head_dim, pool.block_size,
+                               GKV_DTYPE_BF16 if pool.dtype == "bf16" else GKV_DTYPE_F32)
+
+
+def paged_decode_noalloc(pool: PagedBlockPool, layer: int, block_tables, ctx_lens, q, out, n_heads: int,
+                         scale: float, sinks=None, stream=None) -> None:
+    """gkv_paged_decode_noalloc on the pool's arena: the same decode as upload_step +
+    paged_decode, with every scratch buffer in the library's fixed per-device array (nothing
+    is allocated).  Runs on the pool's device."""
+    import torch
+
+    desc = arena_desc(pool)
+    bt = np.ascontiguousarray(block_tables, dtype=np.int32)
+    cl = np.ascontiguousarray(ctx_lens, dtype=np.int32)
+    with torch.cuda.device(pool.device):
+        _check(lib.gkv_paged_decode_noalloc(
+            C.byref(desc), layer, _ptr(bt), bt.shape[0], bt.shape[1], _ptr(cl), _f32_dev(q, "q"),
+            _f32_dev(out, "out"), n_heads, float(scale), None if sinks is None else _f32_dev(sinks, "sinks"),
+            _stream(stream, pool.device)))
+
+
 def plan_decode(ctx_lens: Sequence[int], heads_kv: int, block_size: int, n_workers: int) -> dict:
     """The split-KV work list gkv_upload_step would build (host only, no GPU)."""
     cl = np.ascontiguousarray(np.asarray(ctx_lens, dtype=np.int32))

@@ -50,6 +50,20 @@ class gkv_plan_info(C.Structure):
     ]
 
 
+class gkv_arena_desc(C.Structure):
+    _fields_ = [
+        ("d_k", C.c_void_p),
+        ("d_v", C.c_void_p),
+        ("total_blocks", C.c_int32),
+        ("layers", C.c_int32),
+        ("heads_kv", C.c_int32),
+        ("head_dim", C.c_int32),
+        ("v_head_dim", C.c_int32),
+        ("block_size", C.c_int32),
+        ("dtype", C.c_int32),
+    ]
+
+
 class gkv_pool_stats(C.Structure):
     _fields_ = [
         ("total_blocks", C.c_int32),
@@ -113,6 +127,10 @@ SIGNATURES = {
     "gkv_decode_step_host": (
         C.c_int,
         [P, I32, P, I32, I32, P, P, I32, P, P, P, P, I32, F32, P, P],
+    ),
+    "gkv_paged_decode_noalloc": (
+        C.c_int,
+        [C.POINTER(gkv_arena_desc), I32, P, I32, I32, P, P, P, I32, F32, P, P],
     ),
     "gkv_pool_last_launch_count": (C.c_int, [P]),
     "gkv_sync": (C.c_int, [P, P, I32]),

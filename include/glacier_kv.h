@@ -232,6 +232,30 @@ GKV_API int gkv_decode_step_host(gkv_pool* pool, int32_t layer, const int32_t* h
                                  const float* h_k_new, const float* h_v_new, const float* h_q,
                                  float* h_out, int32_t n_heads, float scale,
                                  const float* d_sinks, void* stream);
+/* A KV arena described by raw device pointers, in the same layout and meaning as a pool's
+ * (gkv_pool_kv_ptrs returns a pool's pointers). */
+typedef struct gkv_arena_desc {
+    void* d_k;
+    void* d_v;
+    int32_t total_blocks, layers, heads_kv, head_dim, v_head_dim, block_size, dtype;
+} gkv_arena_desc;
+/* Decode that allocates nothing.  No counterpart in the reference: it exists for callers
+ * that cannot call cudaMalloc on the decode path -- hosts whose device memory belongs to
+ * another allocator or to a region reserved at start-up under a hard budget, and serving
+ * loops that cannot afford a call that may synchronize the device.  The caller passes the
+ * arena, host block tables and context lengths (as gkv_upload_step), q and out (as
+ * gkv_paged_decode); the packed tables, the work list and the split-KV partials live in one
+ * fixed 16 MiB device array per GPU inside the library, held until the process exits.
+ * Calls that would need more (about 4 MiB of tables and work list, 12 MiB of partials)
+ * return GKV_EINVAL.  Runs on the calling thread's current device and on `stream`.  The
+ * first call on each device looks up that array's device address; make it before any stream
+ * capture.  All calls on a device share the array and leave their contents in it; calls
+ * whose kernels overlap on the GPU race on it, so order them on one stream. */
+GKV_API int gkv_paged_decode_noalloc(const gkv_arena_desc* arena, int32_t layer,
+                                     const int32_t* h_block_tables, int32_t batch,
+                                     int32_t max_blocks, const int32_t* h_ctx_lens,
+                                     const float* d_q, float* d_out, int32_t n_heads, float scale,
+                                     const float* d_sinks, void* stream);
 /* Number of kernel launches the last gkv_kv_append / gkv_paged_decode /
  * gkv_decode_step_host / gkv_compute_attention call on this pool enqueued. */
 GKV_API int gkv_pool_last_launch_count(const gkv_pool* pool);
