@@ -81,6 +81,9 @@ struct StepWorkspace {
     float* d_part_acc = nullptr;
     float* d_part_ml = nullptr;
     size_t part_slots_cap = 0;  // slots (x head_groups x gp) the buffers hold
+    // arrival counters of the fused merge; zero between launches (kernels reset them)
+    int32_t* d_merge_count = nullptr;
+    size_t merge_count_cap = 0;
     // device error word shared by every kernel of this pool
     int* d_err = nullptr;
     // e2e staging for gkv_decode_step_host
@@ -153,7 +156,7 @@ void step_free(Pool* p);
 
 // Work-list construction (host only; unit-tested through the C ABI helpers).
 struct WorkList {
-    std::vector<int32_t> piece_seg, piece_c0, piece_c1, piece_slot;
+    std::vector<int32_t> piece_seg, piece_c0, piece_c1, piece_slot, piece_merge;
     std::vector<int32_t> worker_begin;  // n_workers + 1
     std::vector<int32_t> merge_seg, merge_slot0, merge_nslots;
     int32_t n_slots = 0;

@@ -51,7 +51,12 @@ struct DecodeWork {
     const int32_t* merge_seg;          // [n_merge] segments split over several workers
     const int32_t* merge_slot0;        // their first partial slot (slots are contiguous)
     const int32_t* merge_nslots;
+    const int32_t* piece_merge;        // [n_pieces] merge entry of a split piece, else -1
     int32_t n_merge;
+    // Arrival counters of the fused merge, [head_groups][n_merge] ints.  They must be zero
+    // when a launch starts; the worker that completes a segment resets its counter, so they
+    // are zero again after every launch that ran to completion.
+    int32_t* merge_count;
 };
 
 struct DecodeArgs {
@@ -80,8 +85,8 @@ struct DecodeConfig {
 };
 DecodeConfig decode_config(const ArenaGeom& g, int n_heads);
 
-// Enqueues the split-KV decode and, when any segment spans several workers, the merge.
-// *launches receives the number of kernels enqueued.
+// Enqueues the split-KV decode (the cross-worker merge is fused into it).  *launches
+// receives the number of kernels enqueued.
 cudaError_t launch_paged_decode(const ArenaGeom& g, const DecodeWork& w, const DecodeArgs& a,
                                 int* launches, cudaStream_t stream);
 

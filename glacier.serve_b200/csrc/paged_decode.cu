@@ -14,14 +14,17 @@
 //    range intersects a few segments ("pieces").  Each warp prefetches S chunks ahead with
 //    its own ring, across piece boundaries, and never waits for another warp.
 //  * One pass serves all GP query heads that share the kv head, so each K/V byte is read
-//    from HBM once.  Lane l owns dims [l*D/32, (l+1)*D/32) of q and of the accumulators;
-//    the GP x 8 partial dot products of a chunk are reduced across the warp with a
-//    transpose-reduce (each shuffle step halves the values a lane holds), ~GP*8 shuffles per
-//    chunk instead of 5*GP*8.
+//    from HBM once.  Lane l owns dims [l*D/32, (l+1)*D/32) of q and of the accumulators.
+//    The GP x 8 partial dot products of a chunk are reduced across the warp with a
+//    transpose-reduce in which each shuffle level halves the values a lane holds.  Each
+//    lane stores its partials at register positions XOR-permuted by its lane id, so at
+//    every level the half a lane keeps is the lower half of its registers and the half it
+//    sends is the upper half: one shuffle and one add per value, no selects.
+//  * Products use the packed two-wide fp32 FMA of sm_100 (fma.rn.f32x2).
 //  * Softmax is online (running max and sum per head, base-2 exponent).  A piece that is a
-//    whole segment writes the normalised output; otherwise it writes an unnormalised
-//    partial (acc, max, sum) and a second small kernel merges a segment's partials by
-//    log-sum-exp.
+//    whole segment writes the normalised output.  Otherwise it writes an unnormalised
+//    partial (acc, max, sum) and bumps an arrival counter; the worker that completes a
+//    segment merges its partials by log-sum-exp and resets the counter (no second launch).
 //
 // Roofline: HBM.  Algorithmic bytes per step = sum_b ctx_b * heads_kv * (D + DV) * elem
 // (+ q and out).  FLOPs = 2 * sum_b ctx_b * n_heads * (D + DV) on the FP32 pipe.
@@ -39,27 +42,73 @@ namespace {
 constexpr int kChunk = kDecodeChunk;
 constexpr float kLog2e = 1.4426950408889634f;
 
-// Warp transpose-reduce of CUR values per lane.  After the call lane L holds
-// R = max(CUR/32, 1) fully reduced values x[0..R-1] whose value index is L*R + r
-// (CUR >= 32), or L >> log2(32/CUR) (CUR < 32; 32/CUR lanes hold the same value).
+constexpr int ilog2(int x) { return x <= 1 ? 0 : 1 + ilog2(x / 2); }
+
+// Selectless warp transpose-reduce of CUR values per lane (see file comment).  Positions
+// must hold value j at position j ^ X(lane); afterwards lane L holds its R values at
+// positions 0..R-1.
 template <int CUR, int MASK>
-__device__ __forceinline__ void transpose_reduce(float* x, int lane) {
+__device__ __forceinline__ void transpose_reduce(float* x) {
     if constexpr (MASK >= 1) {
         if constexpr (CUR >= 2) {
             constexpr int H = CUR / 2;
-            const bool upper = (lane & MASK) != 0;
 #pragma unroll
-            for (int i = 0; i < H; ++i) {
-                const float send = upper ? x[i] : x[i + H];
-                const float keep = upper ? x[i + H] : x[i];
-                x[i] = keep + __shfl_xor_sync(0xffffffffu, send, MASK);
-            }
-            transpose_reduce<H, MASK / 2>(x, lane);
+            for (int i = 0; i < H; ++i) x[i] += __shfl_xor_sync(0xffffffffu, x[i + H], MASK);
+            transpose_reduce<H, MASK / 2>(x);
         } else {
             x[0] += __shfl_xor_sync(0xffffffffu, x[0], MASK);
-            transpose_reduce<1, MASK / 2>(x, lane);
+            transpose_reduce<1, MASK / 2>(x);
         }
     }
+}
+
+// Loads EPL consecutive KV elements from shared memory as EP2 = ceil(EPL/2) fp32 pairs
+// (the odd tail, EPL == 1, gets a zero partner).
+template <typename KV, int EPL>
+__device__ __forceinline__ void load_pairs(const KV* p, float2 (&o)[(EPL + 1) / 2]) {
+    if constexpr (std::is_same<KV, float>::value) {
+        if constexpr (EPL == 1) {
+            o[0] = make_float2(p[0], 0.f);
+        } else if constexpr (EPL == 2) {
+            o[0] = *reinterpret_cast<const float2*>(p);
+        } else {
+#pragma unroll
+            for (int i = 0; i < EPL; i += 4) {
+                const float4 v = *reinterpret_cast<const float4*>(p + i);
+                o[i / 2] = make_float2(v.x, v.y);
+                o[i / 2 + 1] = make_float2(v.z, v.w);
+            }
+        }
+    } else {
+        const uint16_t* u = reinterpret_cast<const uint16_t*>(p);
+        if constexpr (EPL == 1) {
+            o[0] = make_float2(__uint_as_float(static_cast<uint32_t>(u[0]) << 16), 0.f);
+        } else if constexpr (EPL == 2) {
+            const uint32_t w = *reinterpret_cast<const uint32_t*>(u);
+            o[0] = make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+        } else if constexpr (EPL == 4) {
+            const uint2 w = *reinterpret_cast<const uint2*>(u);
+            o[0] = make_float2(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u));
+            o[1] = make_float2(__uint_as_float(w.y << 16), __uint_as_float(w.y & 0xffff0000u));
+        } else {
+#pragma unroll
+            for (int i = 0; i < EPL; i += 8) {
+                const uint4 w = *reinterpret_cast<const uint4*>(u + i);
+                o[i / 2 + 0] = make_float2(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u));
+                o[i / 2 + 1] = make_float2(__uint_as_float(w.y << 16), __uint_as_float(w.y & 0xffff0000u));
+                o[i / 2 + 2] = make_float2(__uint_as_float(w.z << 16), __uint_as_float(w.z & 0xffff0000u));
+                o[i / 2 + 3] = make_float2(__uint_as_float(w.w << 16), __uint_as_float(w.w & 0xffff0000u));
+            }
+        }
+    }
+}
+
+template <int EP2>
+__device__ __forceinline__ float dot_pairs(const float2 (&q)[EP2], const float2 (&k)[EP2]) {
+    float2 p = __fmul2_rn(q[0], k[0]);
+#pragma unroll
+    for (int i = 1; i < EP2; ++i) p = __ffma2_rn(q[i], k[i], p);
+    return p.x + p.y;
 }
 
 template <typename KV, int D, int DV, int GP, int NW, int S>
@@ -67,14 +116,18 @@ struct DecodeKernelTraits {
     static constexpr int EB = sizeof(KV);
     static constexpr int EPL = D / 32;
     static constexpr int EPLV = DV / 32;
+    static constexpr int EP2 = (EPL + 1) / 2;
+    static constexpr int EV2 = (EPLV + 1) / 2;
     static constexpr int KSTAGE = kChunk * D * EB;
     static constexpr int VSTAGE = kChunk * DV * EB;
     static constexpr int STAGE = ((KSTAGE + VSTAGE) + 127) / 128 * 128;
     static constexpr int NV = GP * kChunk;              // values per transpose-reduce
+    static constexpr int NB = ilog2(NV);
     static constexpr int R = NV >= 32 ? NV / 32 : 1;    // reduced values per lane
     static constexpr int DUP = NV >= 32 ? 1 : 32 / NV;  // lanes holding the same value
     static constexpr int LG = 32 / GP;                  // lanes per query head after reduce
-    static constexpr int PBUF = (GP * kChunk + GP + 3) / 4 * 4;  // per-warp p / max scratch
+    // per-warp scratch: p duplicated into pairs [GP*8] float2, then the GP running maxima
+    static constexpr int PBUF = (GP * kChunk * 2 + GP + 3) / 4 * 4;
     static constexpr size_t OFF_BAR = static_cast<size_t>(NW) * S * STAGE;
     static constexpr size_t OFF_PBUF = (OFF_BAR + static_cast<size_t>(NW) * S * 8 + 15) / 16 * 16;
     static constexpr size_t SMEM = OFF_PBUF + static_cast<size_t>(NW) * PBUF * 4;
@@ -82,35 +135,12 @@ struct DecodeKernelTraits {
     static_assert(GP == 1 || GP == 2 || GP == 4 || GP == 8, "GP");
 };
 
-struct ChunkLoc {
-    int b, h, ntok, tok0;
-    int64_t blk;
-};
-
-__device__ __forceinline__ ChunkLoc locate(const ArenaGeom& g, const DecodeWork& w, int piece,
-                                           int j, int cpp) {
-    ChunkLoc L;
-    const int seg = __ldg(w.piece_seg + piece);
-    L.b = seg / g.heads_kv;
-    L.h = seg - L.b * g.heads_kv;
-    const int k = __ldg(w.piece_c0 + piece) + j;
-    const int page = k / cpp;
-    const int sub = k - page * cpp;
-    L.tok0 = sub * kChunk;
-    const int ctx = __ldg(w.ctx_lens + L.b);
-    int nt = g.block_size - L.tok0;
-    nt = nt < kChunk ? nt : kChunk;
-    const int rem = ctx - page * g.block_size - L.tok0;
-    L.ntok = nt < rem ? nt : rem;
-    L.blk = __ldg(w.tables + static_cast<int64_t>(L.b) * w.max_blocks + page);
-    return L;
-}
-
 template <typename KV, int D, int DV, int GP, int NW, int S>
 __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, DecodeWork w,
                                                                DecodeArgs a, int group, int cpp) {
     using Tr = DecodeKernelTraits<KV, D, DV, GP, NW, S>;
-    constexpr int EPL = Tr::EPL, EPLV = Tr::EPLV, R = Tr::R, DUP = Tr::DUP, LG = Tr::LG;
+    constexpr int EPL = Tr::EPL, EPLV = Tr::EPLV, EP2 = Tr::EP2, EV2 = Tr::EV2;
+    constexpr int NV = Tr::NV, NB = Tr::NB, R = Tr::R, DUP = Tr::DUP, LG = Tr::LG;
     extern __shared__ __align__(128) unsigned char smem[];
 
     const int warp = threadIdx.x >> 5;
@@ -120,6 +150,8 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
 
     uint64_t* my_bars = reinterpret_cast<uint64_t*>(smem + Tr::OFF_BAR) + warp * S;
     float* pbuf = reinterpret_cast<float*>(smem + Tr::OFF_PBUF) + warp * Tr::PBUF;
+    float2* pdup = reinterpret_cast<float2*>(pbuf);
+    float* mbuf = pbuf + GP * kChunk * 2;
     unsigned char* my_stages = smem + static_cast<size_t>(warp) * S * Tr::STAGE;
 
     if (lane < S) mbar_init(&my_bars[lane], 1);
@@ -134,19 +166,46 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
     const char* Vb = static_cast<const char*>(g.v);
     const int64_t k_l = static_cast<int64_t>(a.layer) * g.k_layer_stride;
     const int64_t v_l = static_cast<int64_t>(a.layer) * g.v_layer_stride;
+    const int bs = g.block_size;
+    const bool cpp2 = (cpp == 2);  // the 16-token block fast path: page = k >> 1
 
-    // Producer: lane 0 issues the bulk copies of chunk (piece, j) into stage st.
-    auto issue = [&](int piece, int j, int st) {
-        const ChunkLoc L = locate(g, w, piece, j, cpp);
+    // ---- producer: lane 0 issues the two bulk copies of chunk j of piece `piece` ----
+    auto chunk_geom = [&](int c, int ctx, int& page, int& tok0, int& ntok) {
+        if (cpp2) {
+            page = c >> 1;
+            tok0 = (c & 1) * kChunk;
+        } else {
+            page = c / cpp;
+            tok0 = (c - page * cpp) * kChunk;
+        }
+        int nt = bs - tok0;
+        nt = nt < kChunk ? nt : kChunk;
+        const int rem = ctx - page * bs - tok0;
+        ntok = nt < rem ? nt : rem;
+    };
+    int p_piece = pb, p_j = 0, p_c0 = 0, p_cnt = 0, p_b = 0, p_h = 0, p_ctx = 0;
+    auto p_load = [&]() {
+        const int seg = __ldg(w.piece_seg + p_piece);
+        p_b = seg / g.heads_kv;
+        p_h = seg - p_b * g.heads_kv;
+        p_c0 = __ldg(w.piece_c0 + p_piece);
+        p_cnt = __ldg(w.piece_c1 + p_piece) - p_c0;
+        p_ctx = __ldg(w.ctx_lens + p_b);
+    };
+    p_load();
+    auto issue = [&](int st) {
+        int page, tok0, ntok;
+        chunk_geom(p_c0 + p_j, p_ctx, page, tok0, ntok);
         if (lane == 0) {
+            const int64_t blk = __ldg(w.tables + static_cast<int64_t>(p_b) * w.max_blocks + page);
             uint64_t* bar = &my_bars[st];
-            if (L.blk >= 0 && L.blk < g.total_blocks && L.ntok > 0) {
-                const uint32_t kb = static_cast<uint32_t>(L.ntok * D * Tr::EB);
-                const uint32_t vb = static_cast<uint32_t>(L.ntok * DV * Tr::EB);
-                const char* ks = Kb + (L.blk * g.k_block_stride + k_l + L.h * g.k_head_stride +
-                                       static_cast<int64_t>(L.tok0) * D) * Tr::EB;
-                const char* vs = Vb + (L.blk * g.v_block_stride + v_l + L.h * g.v_head_stride +
-                                       static_cast<int64_t>(L.tok0) * DV) * Tr::EB;
+            if (blk >= 0 && blk < g.total_blocks && ntok > 0) {
+                const uint32_t kb = static_cast<uint32_t>(ntok * D * Tr::EB);
+                const uint32_t vb = static_cast<uint32_t>(ntok * DV * Tr::EB);
+                const char* ks = Kb + (blk * g.k_block_stride + k_l + p_h * g.k_head_stride +
+                                       static_cast<int64_t>(tok0) * D) * Tr::EB;
+                const char* vs = Vb + (blk * g.v_block_stride + v_l + p_h * g.v_head_stride +
+                                       static_cast<int64_t>(tok0) * DV) * Tr::EB;
                 unsigned char* dst = my_stages + static_cast<size_t>(st) * Tr::STAGE;
                 fence_proxy_async_smem();
                 mbar_arrive_expect_tx(bar, kb + vb);
@@ -154,58 +213,60 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
                 bulk_g2s(dst + Tr::KSTAGE, vs, vb, bar);
             } else {
                 if (a.err) atomicOr(a.err, kErrBadBlock);
-                mbar_arrive(bar);  // completes the phase without data; consumer skips it
+                mbar_arrive(bar);  // completes the phase without data; the consumer skips it
             }
         }
-    };
-
-    // Producer cursor, S chunks ahead of the consumer.
-    int p_piece = pb, p_j = 0;
-    int p_cnt = __ldg(w.piece_c1 + pb) - __ldg(w.piece_c0 + pb);
-    auto p_advance = [&]() {
         if (++p_j >= p_cnt) {
             p_j = 0;
-            if (++p_piece < pe) p_cnt = __ldg(w.piece_c1 + p_piece) - __ldg(w.piece_c0 + p_piece);
+            if (++p_piece < pe) p_load();
         }
     };
 #pragma unroll 1
-    for (int s = 0; s < S && p_piece < pe; ++s) {
-        issue(p_piece, p_j, s);
-        p_advance();
-    }
+    for (int s = 0; s < S && p_piece < pe; ++s) issue(s);
 
     bool dead = false;  // a bounded wait expired: stop consuming, skip remaining work
     int ck = 0;         // chunks consumed by this warp
     const float scale_log2 = a.scale * kLog2e;
-    // value index of this lane's first reduced score, its head and token
-    const int idx0 = (Tr::NV >= 32) ? lane * R : (lane / DUP);
+    // this lane's register-position permutation and its first reduced value
+    const int X = (NB >= 5) ? (lane << (NB - 5)) : (lane >> (5 - NB));
+    const int Xg = X >> 3;
+    const int Xt = X & 7;
+    const int idx0 = (NV >= 32) ? lane * R : (lane / DUP);
     const int g_own = idx0 / kChunk;
     const int t_own = idx0 - g_own * kChunk;
 
 #pragma unroll 1
     for (int i = pb; i < pe; ++i) {
         const int seg = __ldg(w.piece_seg + i);
-        const int cnt = __ldg(w.piece_c1 + i) - __ldg(w.piece_c0 + i);
+        const int c0 = __ldg(w.piece_c0 + i);
+        const int cnt = __ldg(w.piece_c1 + i) - c0;
         const int b = seg / g.heads_kv;
         const int h = seg - b * g.heads_kv;
+        const int ctx = __ldg(w.ctx_lens + b);
         const int q_head0 = h * group + hg * GP;
         const int gcount = min(GP, group - hg * GP);
 
-        float q[GP][EPL];
+        // q in permuted slots: slot gs holds head gs ^ Xg
+        float2 q[GP][EP2];
 #pragma unroll
-        for (int gg = 0; gg < GP; ++gg) {
+        for (int gs = 0; gs < GP; ++gs) {
+            const int gh = gs ^ Xg;
             const float* qp =
-                a.q + (static_cast<int64_t>(b) * a.n_heads + q_head0 + gg) * D + lane * EPL;
+                a.q + (static_cast<int64_t>(b) * a.n_heads + q_head0 + gh) * D + lane * EPL;
 #pragma unroll
-            for (int e = 0; e < EPL; ++e) q[gg][e] = (gg < gcount) ? __ldg(qp + e) : 0.f;
+            for (int e = 0; e < EP2; ++e) {
+                const bool live = gh < gcount;
+                q[gs][e].x = live ? __ldg(qp + 2 * e) : 0.f;
+                q[gs][e].y = (live && 2 * e + 1 < EPL) ? __ldg(qp + 2 * e + 1) : 0.f;
+            }
         }
         float m[GP];
-        float acc[GP][EPLV];
+        float2 acc[GP][EV2];
 #pragma unroll
         for (int gg = 0; gg < GP; ++gg) {
             m[gg] = -INFINITY;
 #pragma unroll
-            for (int e = 0; e < EPLV; ++e) acc[gg][e] = 0.f;
+            for (int e = 0; e < EV2; ++e) acc[gg][e] = make_float2(0.f, 0.f);
         }
         float m_own = -INFINITY, l_own = 0.f;
 
@@ -213,36 +274,27 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
         for (int j = 0; j < cnt; ++j) {
             const int st = ck % S;
             const uint32_t ph = static_cast<uint32_t>(ck / S) & 1u;
-            const ChunkLoc L = locate(g, w, i, j, cpp);
+            int page, tok0, ntok;
+            chunk_geom(c0 + j, ctx, page, tok0, ntok);
+            const int64_t blk = __ldg(w.tables + static_cast<int64_t>(b) * w.max_blocks + page);
             if (!dead && !mbar_wait(&my_bars[st], ph)) {
                 dead = true;
                 if (lane == 0 && a.err) atomicOr(a.err, kErrWaitTimeout);
             }
-            if (!dead && L.blk >= 0 && L.blk < g.total_blocks && L.ntok > 0) {
+            if (!dead && blk >= 0 && blk < g.total_blocks && ntok > 0) {
                 const unsigned char* stage = my_stages + static_cast<size_t>(st) * Tr::STAGE;
                 const KV* Ks = reinterpret_cast<const KV*>(stage);
                 const KV* Vs = reinterpret_cast<const KV*>(stage + Tr::KSTAGE);
-                const int ntok = L.ntok;
-                // ---- partial dots over this lane's dims, then transpose-reduce ----
-                float sc[Tr::NV];
+                // ---- scores at permuted positions, then the selectless transpose-reduce ----
+                float sc[NV];
 #pragma unroll
-                for (int t = 0; t < kChunk; ++t) {
-                    if (t < ntok) {
-                        float kv[EPL];
-                        SmemVec<KV, EPL>::load(Ks + t * D + lane * EPL, kv);
+                for (int ts = 0; ts < kChunk; ++ts) {
+                    float2 kv[EP2];
+                    load_pairs<KV, EPL>(Ks + (ts ^ Xt) * D + lane * EPL, kv);
 #pragma unroll
-                        for (int gg = 0; gg < GP; ++gg) {
-                            float s = q[gg][0] * kv[0];
-#pragma unroll
-                            for (int e = 1; e < EPL; ++e) s = fmaf(q[gg][e], kv[e], s);
-                            sc[gg * kChunk + t] = s;
-                        }
-                    } else {
-#pragma unroll
-                        for (int gg = 0; gg < GP; ++gg) sc[gg * kChunk + t] = 0.f;
-                    }
+                    for (int gs = 0; gs < GP; ++gs) sc[gs * kChunk + ts] = dot_pairs<EP2>(q[gs], kv);
                 }
-                transpose_reduce<Tr::NV, 16>(sc, lane);
+                transpose_reduce<NV, 16>(sc);
                 // ---- online softmax of this lane's head ----
                 float s2[R];
                 float cmax = -INFINITY;
@@ -265,55 +317,69 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
 #pragma unroll
                 for (int mask = LG / 2; mask >= DUP; mask >>= 1)
                     psum += __shfl_xor_sync(0xffffffffu, psum, mask);
+                const bool changed = m_new > m_own;
                 l_own = l_own * exp2f(m_own - m_new) + psum;
                 m_own = m_new;
                 if ((lane % DUP) == 0) {
 #pragma unroll
-                    for (int r = 0; r < R; ++r) pbuf[idx0 + r] = p[r];
+                    for (int r = 0; r < R; ++r) pdup[idx0 + r] = make_float2(p[r], p[r]);
                 }
-                if ((lane % LG) == 0) pbuf[GP * kChunk + g_own] = m_new;
+                if ((lane % LG) == 0) mbuf[g_own] = m_new;
                 __syncwarp();
-                // ---- rescale the accumulators to the new maxima, then P.V ----
+                // ---- rescale the accumulators if any head's maximum moved ----
+                if (__any_sync(0xffffffffu, changed)) {
 #pragma unroll
-                for (int gg = 0; gg < GP; ++gg) {
-                    const float mn = pbuf[GP * kChunk + gg];
-                    const float alpha = exp2f(m[gg] - mn);
-                    m[gg] = mn;
+                    for (int gg = 0; gg < GP; ++gg) {
+                        const float mn = mbuf[gg];
+                        const float alpha = exp2f(m[gg] - mn);
+                        m[gg] = mn;
+                        const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll
-                    for (int e = 0; e < EPLV; ++e) acc[gg][e] *= alpha;
+                        for (int e = 0; e < EV2; ++e) acc[gg][e] = __fmul2_rn(acc[gg][e], a2);
+                    }
                 }
-                float pw[GP][kChunk];
+                // ---- P.V ----
+                if (ntok == kChunk) {
 #pragma unroll
-                for (int gg = 0; gg < GP; ++gg) {
-                    const float4 p0 = *reinterpret_cast<const float4*>(pbuf + gg * kChunk);
-                    const float4 p1 = *reinterpret_cast<const float4*>(pbuf + gg * kChunk + 4);
-                    pw[gg][0] = p0.x; pw[gg][1] = p0.y; pw[gg][2] = p0.z; pw[gg][3] = p0.w;
-                    pw[gg][4] = p1.x; pw[gg][5] = p1.y; pw[gg][6] = p1.z; pw[gg][7] = p1.w;
-                }
-#pragma unroll
-                for (int t = 0; t < kChunk; ++t) {
-                    if (t < ntok) {
-                        float vv[EPLV];
-                        SmemVec<KV, EPLV>::load(Vs + t * DV + lane * EPLV, vv);
+                    for (int t = 0; t < kChunk; t += 2) {
+                        float2 v0[EV2], v1[EV2];
+                        load_pairs<KV, EPLV>(Vs + t * DV + lane * EPLV, v0);
+                        load_pairs<KV, EPLV>(Vs + (t + 1) * DV + lane * EPLV, v1);
 #pragma unroll
                         for (int gg = 0; gg < GP; ++gg) {
+                            const float4 pp = *reinterpret_cast<const float4*>(pdup + gg * kChunk + t);
+                            const float2 pa = make_float2(pp.x, pp.y), pb2 = make_float2(pp.z, pp.w);
 #pragma unroll
-                            for (int e = 0; e < EPLV; ++e)
-                                acc[gg][e] = fmaf(pw[gg][t], vv[e], acc[gg][e]);
+                            for (int e = 0; e < EV2; ++e) {
+                                acc[gg][e] = __ffma2_rn(pa, v0[e], acc[gg][e]);
+                                acc[gg][e] = __ffma2_rn(pb2, v1[e], acc[gg][e]);
+                            }
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int t = 0; t < kChunk; ++t) {
+                        if (t < ntok) {
+                            float2 v0[EV2];
+                            load_pairs<KV, EPLV>(Vs + t * DV + lane * EPLV, v0);
+#pragma unroll
+                            for (int gg = 0; gg < GP; ++gg) {
+                                const float2 pa = pdup[gg * kChunk + t];
+#pragma unroll
+                                for (int e = 0; e < EV2; ++e) acc[gg][e] = __ffma2_rn(pa, v0[e], acc[gg][e]);
+                            }
                         }
                     }
                 }
             }
             __syncwarp();
             // ---- refill the stage just consumed with the chunk S positions ahead ----
-            if (p_piece < pe && !dead) {
-                issue(p_piece, p_j, st);
-                p_advance();
-            }
+            if (p_piece < pe && !dead) issue(st);
             ++ck;
         }
+        if (dead) continue;
 
-        // ---- end of piece: final output or partial ----
+        // ---- end of piece: final output, or partial + fused merge ----
         float lg[GP];
 #pragma unroll
         for (int gg = 0; gg < GP; ++gg) lg[gg] = __shfl_sync(0xffffffffu, l_own, gg * LG);
@@ -333,7 +399,10 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
                 const float inv = Ls > 0.f ? f / Ls : 0.f;
                 float* op = a.out + (static_cast<int64_t>(b) * a.n_heads + qh) * DV + lane * EPLV;
 #pragma unroll
-                for (int e = 0; e < EPLV; ++e) op[e] = acc[gg][e] * inv;
+                for (int e = 0; e < EV2; ++e) {
+                    op[2 * e] = acc[gg][e].x * inv;
+                    if (2 * e + 1 < EPLV) op[2 * e + 1] = acc[gg][e].y * inv;
+                }
             }
         } else {
             const int64_t base = (static_cast<int64_t>(hg) * w.n_slots + slot) * GP;
@@ -341,71 +410,88 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
             for (int gg = 0; gg < GP; ++gg) {
                 float* ap = a.part_acc + (base + gg) * DV + lane * EPLV;
 #pragma unroll
-                for (int e = 0; e < EPLV; ++e) ap[e] = acc[gg][e];
+                for (int e = 0; e < EV2; ++e) {
+                    ap[2 * e] = acc[gg][e].x;
+                    if (2 * e + 1 < EPLV) ap[2 * e + 1] = acc[gg][e].y;
+                }
             }
             if (lane < GP) {
                 float mm = m[0], ll = lg[0];
 #pragma unroll
                 for (int gg = 1; gg < GP; ++gg)
-                    if (lane == gg) { mm = m[gg]; ll = lg[gg]; }
+                    if (lane == gg) {
+                        mm = m[gg];
+                        ll = lg[gg];
+                    }
                 a.part_ml[(base + lane) * 2 + 0] = mm;
                 a.part_ml[(base + lane) * 2 + 1] = ll;
             }
-        }
-    }
-}
-
-// Log-sum-exp merge of the partials of segments split over several workers.
-template <int GP, int DV>
-__global__ void __launch_bounds__(128) paged_decode_merge_kernel(ArenaGeom g, DecodeWork w,
-                                                                 DecodeArgs a, int group) {
-    const int i = blockIdx.x;
-    const int hg = blockIdx.y;
-    const int seg = w.merge_seg[i];
-    const int s0 = w.merge_slot0[i];
-    const int ns = w.merge_nslots[i];
-    const int b = seg / g.heads_kv;
-    const int h = seg - b * g.heads_kv;
-    const int q_head0 = h * group + hg * GP;
-    const int gcount = min(GP, group - hg * GP);
-    for (int e = threadIdx.x; e < GP * DV; e += blockDim.x) {
-        const int gg = e / DV;
-        const int d = e - gg * DV;
-        if (gg >= gcount) continue;
-        float M = -INFINITY;
-        for (int s = 0; s < ns; ++s) {
-            const int64_t ps = (static_cast<int64_t>(hg) * w.n_slots + s0 + s) * GP + gg;
-            M = fmaxf(M, a.part_ml[ps * 2]);
-        }
-        float Ls = 0.f, A = 0.f;
-        if (M != -INFINITY) {
-            for (int s = 0; s < ns; ++s) {
-                const int64_t ps = (static_cast<int64_t>(hg) * w.n_slots + s0 + s) * GP + gg;
-                const float f = exp2f(a.part_ml[ps * 2] - M);
-                Ls += a.part_ml[ps * 2 + 1] * f;
-                A += a.part_acc[ps * DV + d] * f;
+            // arrival: the worker completing the segment merges every partial of it
+            const int mi = __ldg(w.piece_merge + i);
+            const int ns = __ldg(w.merge_nslots + mi);
+            __threadfence();
+            __syncwarp();
+            int prev = 0;
+            int* counter = w.merge_count + static_cast<int64_t>(hg) * w.n_merge + mi;
+            if (lane == 0) prev = atomicAdd(counter, 1);
+            prev = __shfl_sync(0xffffffffu, prev, 0);
+            if (prev == ns - 1) {
+                __threadfence();
+                const int s0 = __ldg(w.merge_slot0 + mi);
+                const int64_t b0 = (static_cast<int64_t>(hg) * w.n_slots + s0) * GP;
+#pragma unroll 1
+                for (int gg = 0; gg < gcount; ++gg) {
+                    float M = -INFINITY;
+                    for (int s = 0; s < ns; ++s) M = fmaxf(M, __ldcg(a.part_ml + (b0 + s * GP + gg) * 2));
+                    float Ls = 0.f;
+                    float2 A[EV2];
+#pragma unroll
+                    for (int e = 0; e < EV2; ++e) A[e] = make_float2(0.f, 0.f);
+                    if (M != -INFINITY) {
+                        for (int s = 0; s < ns; ++s) {
+                            const int64_t ps = b0 + s * GP + gg;
+                            const float f = exp2f(__ldcg(a.part_ml + ps * 2) - M);
+                            Ls += __ldcg(a.part_ml + ps * 2 + 1) * f;
+                            const float* ap = a.part_acc + ps * DV + lane * EPLV;
+                            const float2 f2 = make_float2(f, f);
+#pragma unroll
+                            for (int e = 0; e < EV2; ++e) {
+                                const float2 v = make_float2(__ldcg(ap + 2 * e),
+                                                             2 * e + 1 < EPLV ? __ldcg(ap + 2 * e + 1) : 0.f);
+                                A[e] = __ffma2_rn(f2, v, A[e]);
+                            }
+                        }
+                    }
+                    const int qh = q_head0 + gg;
+                    float f = 1.f;
+                    if (a.sinks || a.has_sink_all) {
+                        const float sk = (a.sinks ? __ldg(a.sinks + qh) : a.sink_all) * kLog2e;
+                        const float M2 = fmaxf(M, sk);
+                        f = (M == -INFINITY) ? 0.f : exp2f(M - M2);
+                        Ls = Ls * f + exp2f(sk - M2);
+                    }
+                    const float inv = Ls > 0.f ? f / Ls : 0.f;
+                    float* op = a.out + (static_cast<int64_t>(b) * a.n_heads + qh) * DV + lane * EPLV;
+#pragma unroll
+                    for (int e = 0; e < EV2; ++e) {
+                        op[2 * e] = A[e].x * inv;
+                        if (2 * e + 1 < EPLV) op[2 * e + 1] = A[e].y * inv;
+                    }
+                }
+                if (lane == 0) atomicExch(counter, 0);
             }
         }
-        const int qh = q_head0 + gg;
-        if (a.sinks || a.has_sink_all) {
-            const float sk = (a.sinks ? a.sinks[qh] : a.sink_all) * kLog2e;
-            const float M2 = fmaxf(M, sk);
-            const float f = (M == -INFINITY) ? 0.f : exp2f(M - M2);
-            Ls = Ls * f + exp2f(sk - M2);
-            A *= f;
-        }
-        a.out[(static_cast<int64_t>(b) * a.n_heads + qh) * DV + d] = Ls > 0.f ? A / Ls : 0.f;
     }
 }
 
 // Warp workers per CTA and ring stages per warp.  Sized so that two CTAs fit on an SM
-// (<= ~113 KB of shared memory each) with 2-3 chunks of 8 tokens in flight per warp.
+// (<= ~110 KB of shared memory each) with 2-6 chunks of 8 tokens in flight per warp.
 template <typename KV, int D, int DV>
 struct RingShape {
     static constexpr int NW = 4;
     static constexpr int STAGE = kChunk * (D + DV) * static_cast<int>(sizeof(KV));
     static constexpr int S_MAX = sizeof(KV) == 4 ? 3 : 6;
-    static constexpr int S_FIT = (110 * 1024) / (NW * STAGE);
+    static constexpr int S_FIT = (108 * 1024) / (NW * STAGE);
     static constexpr int S = S_FIT < 2 ? 2 : (S_FIT < S_MAX ? S_FIT : S_MAX);
 };
 
@@ -455,14 +541,7 @@ struct Inst {
         dim3 grid(static_cast<unsigned>(w.n_ctas), static_cast<unsigned>(head_groups));
         paged_decode_kernel<KV, D, DV, GP, NW, S><<<grid, NW * 32, Tr::SMEM, st>>>(g, w, a, group, cpp);
         e = cudaGetLastError();
-        if (e != cudaSuccess) return e;
-        *launches = 1;
-        if (w.n_merge > 0) {
-            dim3 mg(static_cast<unsigned>(w.n_merge), static_cast<unsigned>(head_groups));
-            paged_decode_merge_kernel<GP, DV><<<mg, 128, 0, st>>>(g, w, a, group);
-            e = cudaGetLastError();
-            *launches = 2;
-        }
+        if (e == cudaSuccess) *launches = 1;
         return e;
     }
 };

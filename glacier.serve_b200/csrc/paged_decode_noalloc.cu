@@ -53,11 +53,11 @@ alignas(64) unsigned char g_stage[kMetaBytes];
 size_t up16(size_t x) { return (x + 15) & ~static_cast<size_t>(15); }
 
 struct Layout {
-    size_t tables, ctx, pseg, pc0, pc1, pslot, wbeg, mseg, ms0, mns, total;
+    size_t tables, ctx, pseg, pc0, pc1, pslot, pmerge, wbeg, mseg, ms0, mns, counters, total;
 };
 
 Layout layout_for(int64_t batch, int64_t max_blocks, int64_t max_pieces, int64_t n_workers,
-                  int64_t max_merge) {
+                  int64_t max_merge, int64_t head_groups) {
     Layout L{};
     size_t o = 0;
     auto take = [&](int64_t bytes) {
@@ -71,10 +71,12 @@ Layout layout_for(int64_t batch, int64_t max_blocks, int64_t max_pieces, int64_t
     L.pc0 = take(max_pieces * 4);
     L.pc1 = take(max_pieces * 4);
     L.pslot = take(max_pieces * 4);
+    L.pmerge = take(max_pieces * 4);
     L.wbeg = take((n_workers + 1) * 4);
     L.mseg = take(max_merge * 4);
     L.ms0 = take(max_merge * 4);
     L.mns = take(max_merge * 4);
+    L.counters = take(max_merge * head_groups * 4);  // merge arrival counters, staged as zeros
     L.total = o;
     return L;
 }
@@ -82,7 +84,7 @@ Layout layout_for(int64_t batch, int64_t max_blocks, int64_t max_pieces, int64_t
 // The work list of step.cpp's build_work_list, written into fixed arrays (no heap).
 void plan_fixed(const int32_t* ctx, int32_t batch, int32_t heads_kv, int32_t bs, int32_t n_workers,
                 int64_t total, int32_t* pseg, int32_t* pc0, int32_t* pc1, int32_t* pslot,
-                int32_t* wbeg, int32_t* mseg, int32_t* ms0, int32_t* mns, int32_t* n_pieces,
+                int32_t* pmerge, int32_t* wbeg, int32_t* mseg, int32_t* ms0, int32_t* mns, int32_t* n_pieces,
                 int32_t* n_slots, int32_t* n_merge) {
     const int64_t n_seg = static_cast<int64_t>(batch) * heads_kv;
     int64_t s = 0, s0 = 0, s1 = n_seg > 0 ? chunks_of(ctx[0], bs) : 0;
@@ -114,10 +116,14 @@ void plan_fixed(const int32_t* ctx, int32_t batch, int32_t heads_kv, int32_t bs,
             mseg[merges] = pseg[i];
             ms0[merges] = slots;
             mns[merges] = j - i;
+            for (int32_t k = i; k < j; ++k) {
+                pslot[k] = slots++;
+                pmerge[k] = merges;
+            }
             ++merges;
-            for (int32_t k = i; k < j; ++k) pslot[k] = slots++;
         } else {
             pslot[i] = -1;
+            pmerge[i] = -1;
         }
         i = j;
     }
@@ -213,7 +219,7 @@ extern "C" int gkv_paged_decode_noalloc(const gkv_arena_desc* arena, int32_t lay
     const int32_t n_workers = static_cast<int32_t>(ctas * cfg.warps);
     const int64_t n_seg = static_cast<int64_t>(batch) * A.heads_kv;
     const int64_t max_pieces = n_workers + n_seg;
-    const Layout L = layout_for(batch, max_blocks, max_pieces, n_workers, n_seg);
+    const Layout L = layout_for(batch, max_blocks, max_pieces, n_workers, n_seg, cfg.head_groups);
     if (L.total > kMetaBytes)
         return set_error(GKV_EINVAL, "step metadata needs %zu bytes, more than the %zu-byte static scratch allows",
                          L.total, kMetaBytes);
@@ -223,7 +229,10 @@ extern "C" int gkv_paged_decode_noalloc(const gkv_arena_desc* arena, int32_t lay
     int32_t np = 0, nslots = 0, nmerge = 0;
     auto at = [&](size_t off) { return reinterpret_cast<int32_t*>(h + off); };
     plan_fixed(h_ctx_lens, batch, A.heads_kv, bs, n_workers, total, at(L.pseg), at(L.pc0), at(L.pc1),
-               at(L.pslot), at(L.wbeg), at(L.mseg), at(L.ms0), at(L.mns), &np, &nslots, &nmerge);
+               at(L.pslot), at(L.pmerge), at(L.wbeg), at(L.mseg), at(L.ms0), at(L.mns), &np, &nslots,
+               &nmerge);
+    // the fused merge's arrival counters must start at zero on every call
+    memset(h + L.counters, 0, static_cast<size_t>(n_seg) * cfg.head_groups * 4);
     const size_t part_floats =
         static_cast<size_t>(nslots) * cfg.head_groups * cfg.gp * (static_cast<size_t>(dv) + 2);
     if (part_floats * sizeof(float) > kPartBytes)
@@ -251,7 +260,9 @@ extern "C" int gkv_paged_decode_noalloc(const gkv_arena_desc* arena, int32_t lay
     w.merge_seg = dp(L.mseg);
     w.merge_slot0 = dp(L.ms0);
     w.merge_nslots = dp(L.mns);
+    w.piece_merge = dp(L.pmerge);
     w.n_merge = nmerge;
+    w.merge_count = reinterpret_cast<int32_t*>(dbase + L.counters);
 
     DecodeArgs a{};
     a.layer = layer;

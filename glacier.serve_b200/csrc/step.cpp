@@ -33,7 +33,7 @@ int sm_count(int device) {
 
 // Byte layout of the packed step metadata (identical on host and device).
 struct MetaLayout {
-    size_t slots, tables, ctx, pseg, pc0, pc1, pslot, wbeg, mseg, ms0, mns, total;
+    size_t slots, tables, ctx, pseg, pc0, pc1, pslot, pmerge, wbeg, mseg, ms0, mns, total;
 };
 
 MetaLayout meta_layout(int64_t n_tok, int64_t batch, int64_t max_blocks, int64_t n_pieces,
@@ -52,6 +52,7 @@ MetaLayout meta_layout(int64_t n_tok, int64_t batch, int64_t max_blocks, int64_t
     L.pc0 = take(static_cast<size_t>(n_pieces) * 4);
     L.pc1 = take(static_cast<size_t>(n_pieces) * 4);
     L.pslot = take(static_cast<size_t>(n_pieces) * 4);
+    L.pmerge = take(static_cast<size_t>(n_pieces) * 4);
     L.wbeg = take(static_cast<size_t>(n_workers + 1) * 4);
     L.mseg = take(static_cast<size_t>(n_merge) * 4);
     L.ms0 = take(static_cast<size_t>(n_merge) * 4);
@@ -119,15 +120,20 @@ void build_work_list(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, i
     // contiguous partial slots and one merge entry.
     const size_t np = W.piece_seg.size();
     W.piece_slot.assign(np, -1);
+    W.piece_merge.assign(np, -1);
     size_t i = 0;
     while (i < np) {
         size_t j = i + 1;
         while (j < np && W.piece_seg[j] == W.piece_seg[i]) ++j;
         if (j - i > 1) {
+            const int32_t mi = static_cast<int32_t>(W.merge_seg.size());
             W.merge_seg.push_back(W.piece_seg[i]);
             W.merge_slot0.push_back(W.n_slots);
             W.merge_nslots.push_back(static_cast<int32_t>(j - i));
-            for (size_t k = i; k < j; ++k) W.piece_slot[k] = W.n_slots++;
+            for (size_t k = i; k < j; ++k) {
+                W.piece_slot[k] = W.n_slots++;
+                W.piece_merge[k] = mi;
+            }
         }
         i = j;
     }
@@ -188,6 +194,21 @@ int step_reserve(Pool* p, int32_t max_batch, int32_t max_blocks, int32_t max_tok
             if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(decode partials)");
             ws.part_slots_cap = slots;
         }
+        // one arrival counter per (head group, split segment), zeroed once here
+        const size_t counters = static_cast<size_t>(n_seg > 0 ? n_seg : 1) * ws.cfg.head_groups;
+        if (counters > ws.merge_count_cap) {
+            if (ws.d_merge_count) {
+                cudaDeviceSynchronize();
+                cudaFree(ws.d_merge_count);
+            }
+            ws.d_merge_count = nullptr;
+            ws.merge_count_cap = 0;
+            cudaError_t e = cudaMalloc(&ws.d_merge_count, counters * sizeof(int32_t));
+            if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(merge counters)");
+            e = cudaMemset(ws.d_merge_count, 0, counters * sizeof(int32_t));
+            if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(merge counters)");
+            ws.merge_count_cap = counters;
+        }
     }
     return GKV_OK;
 }
@@ -199,6 +220,8 @@ void step_free(Pool* p) {
     if (ws.d_meta) cudaFree(ws.d_meta);
     if (ws.d_part_acc) cudaFree(ws.d_part_acc);
     if (ws.d_part_ml) cudaFree(ws.d_part_ml);
+    if (ws.d_merge_count) cudaFree(ws.d_merge_count);
+    ws.d_merge_count = nullptr;
     if (ws.d_q) cudaFree(ws.d_q);
     if (ws.d_out) cudaFree(ws.d_out);
     if (ws.d_knew) cudaFree(ws.d_knew);
@@ -278,6 +301,7 @@ int step_upload(Pool* p, const int32_t* tables, int32_t batch, int32_t max_block
     put(L.pc0, W.piece_c0);
     put(L.pc1, W.piece_c1);
     put(L.pslot, W.piece_slot);
+    put(L.pmerge, W.piece_merge);
     put(L.wbeg, W.worker_begin);
     put(L.mseg, W.merge_seg);
     put(L.ms0, W.merge_slot0);
@@ -303,7 +327,9 @@ int step_upload(Pool* p, const int32_t* tables, int32_t batch, int32_t max_block
     w.merge_seg = reinterpret_cast<const int32_t*>(d + L.mseg);
     w.merge_slot0 = reinterpret_cast<const int32_t*>(d + L.ms0);
     w.merge_nslots = reinterpret_cast<const int32_t*>(d + L.mns);
+    w.piece_merge = reinterpret_cast<const int32_t*>(d + L.pmerge);
     w.n_merge = static_cast<int32_t>(n_merge);
+    w.merge_count = ws.d_merge_count;
     ws.d_slots = reinterpret_cast<const int64_t*>(d + L.slots);
     ws.batch = batch;
     ws.n_tok = n_tok;
@@ -355,6 +381,9 @@ static int decode_common(Pool* p, int32_t layer, const float* d_q, float* d_out,
     if (rc != GKV_OK) return rc;
     const size_t need = static_cast<size_t>(ws.work.n_slots) * ws.cfg.head_groups * ws.cfg.gp;
     if (need > ws.part_slots_cap) return set_error(GKV_ESTATE, "decode partial buffer too small");
+    if (static_cast<size_t>(ws.work.n_merge) * ws.cfg.head_groups > ws.merge_count_cap)
+        return set_error(GKV_ESTATE, "decode merge counters too small");
+    ws.work.merge_count = ws.d_merge_count;  // may have been reallocated by a re-reserve
     DecodeArgs a{};
     a.layer = layer;
     a.q = d_q;
@@ -577,6 +606,9 @@ int gkv_sync(gkv_pool* pool, void* stream, int32_t timeout_ms) {
         if (e != cudaSuccess) return gkv::cuda_fail(e, "cudaMemcpy(error word)");
         if (flag != 0) {
             cudaMemset(pool->impl.ws.d_err, 0, sizeof(int));
+            // a decode that stopped early may leave merge counters raised: start clean
+            if (pool->impl.ws.d_merge_count)
+                cudaMemset(pool->impl.ws.d_merge_count, 0, pool->impl.ws.merge_count_cap * sizeof(int32_t));
             return set_error(GKV_EDEVICE, "a kernel reported error bits 0x%x (1 = bad block id, 2 = wait timeout, 4 = bad slot)", flag);
         }
     }
