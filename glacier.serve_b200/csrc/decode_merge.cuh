@@ -1,0 +1,179 @@
+// Log-sum-exp merge of one split segment's partials, run by the warp that completes the
+// segment (fused into the decode kernels).
+//
+// Partials of a segment are contiguous slots s0 .. s0+ns-1; slot s holds, for each of the GP
+// heads of the head group, an unnormalised accumulator acc[dv] and (max, sum) in the base-2
+// domain.  The merge is three passes: per-head maxima and sums with the lanes striding over
+// the slots (then warp reductions), and the accumulators with lane l owning dims
+// [l*DV/32, (l+1)*DV/32) for every head at once, so each slot costs one round of independent
+// loads instead of GP dependent ones.
+#pragma once
+
+#include "gkv_device.cuh"
+#include "kernels.h"
+
+namespace gkv {
+
+template <int GP, int DV>
+__device__ __forceinline__ void merge_segment(const DecodeArgs& a, const DecodeWork& w, int hg,
+                                              int s0, int ns, int b, int q_head0, int gcount,
+                                              int lane) {
+    constexpr int EPLV = DV / 32;
+    constexpr float kL2e = 1.4426950408889634f;
+    const int64_t b0 = (static_cast<int64_t>(hg) * w.n_slots + s0) * GP;
+    const float* ml = a.part_ml;
+    float M[GP], Ls[GP];
+#pragma unroll
+    for (int g = 0; g < GP; ++g) {
+        M[g] = -INFINITY;
+        Ls[g] = 0.f;
+    }
+    for (int s = lane; s < ns; s += 32) {
+#pragma unroll
+        for (int g = 0; g < GP; ++g) M[g] = fmaxf(M[g], __ldcg(ml + (b0 + s * GP + g) * 2));
+    }
+#pragma unroll
+    for (int g = 0; g < GP; ++g) {
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) M[g] = fmaxf(M[g], __shfl_xor_sync(0xffffffffu, M[g], o));
+    }
+    for (int s = lane; s < ns; s += 32) {
+#pragma unroll
+        for (int g = 0; g < GP; ++g) {
+            const int64_t ps = b0 + s * GP + g;
+            const float mm = __ldcg(ml + ps * 2);
+            if (M[g] != -INFINITY) Ls[g] += __ldcg(ml + ps * 2 + 1) * exp2f(mm - M[g]);
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < GP; ++g) {
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) Ls[g] += __shfl_xor_sync(0xffffffffu, Ls[g], o);
+    }
+    float A[GP][EPLV];
+#pragma unroll
+    for (int g = 0; g < GP; ++g) {
+#pragma unroll
+        for (int e = 0; e < EPLV; ++e) A[g][e] = 0.f;
+    }
+#pragma unroll 2
+    for (int s = 0; s < ns; ++s) {
+#pragma unroll
+        for (int g = 0; g < GP; ++g) {
+            const int64_t ps = b0 + s * GP + g;
+            const float mm = __ldcg(ml + ps * 2);
+            const float f = (M[g] == -INFINITY) ? 0.f : exp2f(mm - M[g]);
+            const float* ap = a.part_acc + ps * DV + lane * EPLV;
+            if constexpr (EPLV % 4 == 0) {
+#pragma unroll
+                for (int e = 0; e < EPLV; e += 4) {
+                    const float4 v = __ldcg(reinterpret_cast<const float4*>(ap + e));
+                    A[g][e] = fmaf(f, v.x, A[g][e]);
+                    A[g][e + 1] = fmaf(f, v.y, A[g][e + 1]);
+                    A[g][e + 2] = fmaf(f, v.z, A[g][e + 2]);
+                    A[g][e + 3] = fmaf(f, v.w, A[g][e + 3]);
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < EPLV; ++e) A[g][e] = fmaf(f, __ldcg(ap + e), A[g][e]);
+            }
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < GP; ++g) {
+        if (g >= gcount) continue;
+        const int qh = q_head0 + g;
+        float L = Ls[g], f = 1.f;
+        if (a.sinks || a.has_sink_all) {
+            const float sk = (a.sinks ? __ldg(a.sinks + qh) : a.sink_all) * kL2e;
+            const float M2 = fmaxf(M[g], sk);
+            f = (M[g] == -INFINITY) ? 0.f : exp2f(M[g] - M2);
+            L = L * f + exp2f(sk - M2);
+        }
+        const float inv = L > 0.f ? f / L : 0.f;
+        float* op = a.out + (static_cast<int64_t>(b) * a.n_heads + qh) * DV + lane * EPLV;
+#pragma unroll
+        for (int e = 0; e < EPLV; ++e) op[e] = A[g][e] * inv;
+    }
+}
+
+// Merge of the segments split into more than kFusedMergeMaxSlots pieces, run as a second
+// launch so that the merge of a long segment is spread over a whole CTA instead of one warp
+// at the tail of the decode.  One CTA per (deferred segment, head group x head); its 256
+// threads are SL slot lanes x DV dims (SL = 256 / DV).
+template <int GP, int DV>
+__global__ void __launch_bounds__(256) deferred_merge_kernel(ArenaGeom g, DecodeWork w,
+                                                             DecodeArgs a, int group) {
+    constexpr int T = 256;
+    constexpr int SL = T / DV;
+    static_assert(SL >= 1 && DV * SL == T, "DV must divide 256");
+    constexpr float kL2e = 1.4426950408889634f;
+    __shared__ float red[T];
+    __shared__ float wred[T / 32];
+    const int t = threadIdx.x;
+    const int hg = blockIdx.y / GP;
+    const int gg = blockIdx.y - hg * GP;
+    const int mi = __ldg(w.merge_deferred + blockIdx.x);
+    const int seg = __ldg(w.merge_seg + mi);
+    const int s0 = __ldg(w.merge_slot0 + mi);
+    const int ns = __ldg(w.merge_nslots + mi);
+    const int b = seg / g.heads_kv;
+    const int h = seg - b * g.heads_kv;
+    const int q_head0 = h * group + hg * GP;
+    const int gcount = min(GP, group - hg * GP);
+    if (gg >= gcount) return;
+    const int64_t base = (static_cast<int64_t>(hg) * w.n_slots + s0) * GP + gg;  // + s * GP
+    auto block_reduce = [&](float v, bool is_max) {
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+            const float u = __shfl_xor_sync(0xffffffffu, v, o);
+            v = is_max ? fmaxf(v, u) : v + u;
+        }
+        if ((t & 31) == 0) wred[t >> 5] = v;
+        __syncthreads();
+        float r = wred[0];
+#pragma unroll
+        for (int i = 1; i < T / 32; ++i) r = is_max ? fmaxf(r, wred[i]) : r + wred[i];
+        __syncthreads();
+        return r;
+    };
+    float M = -INFINITY;
+    for (int s = t; s < ns; s += T) M = fmaxf(M, __ldcg(a.part_ml + (base + s * GP) * 2));
+    M = block_reduce(M, true);
+    float L = 0.f;
+    if (M != -INFINITY) {
+        for (int s = t; s < ns; s += T) {
+            const int64_t ps = base + s * GP;
+            L += __ldcg(a.part_ml + ps * 2 + 1) * exp2f(__ldcg(a.part_ml + ps * 2) - M);
+        }
+    }
+    L = block_reduce(L, false);
+    const int d = t % DV;
+    const int sl = t / DV;
+    float A = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll 4
+        for (int s = sl; s < ns; s += SL) {
+            const int64_t ps = base + s * GP;
+            A = fmaf(exp2f(__ldcg(a.part_ml + ps * 2) - M), __ldcg(a.part_acc + ps * DV + d), A);
+        }
+    }
+    if constexpr (SL > 1) {
+        red[t] = A;
+        __syncthreads();
+        if (sl != 0) return;
+#pragma unroll
+        for (int k = 1; k < SL; ++k) A += red[d + k * DV];
+    }
+    const int qh = q_head0 + gg;
+    float f = 1.f;
+    if (a.sinks || a.has_sink_all) {
+        const float sk = (a.sinks ? __ldg(a.sinks + qh) : a.sink_all) * kL2e;
+        const float M2 = fmaxf(M, sk);
+        f = (M == -INFINITY) ? 0.f : exp2f(M - M2);
+        L = L * f + exp2f(sk - M2);
+    }
+    a.out[(static_cast<int64_t>(b) * a.n_heads + qh) * DV + d] = L > 0.f ? A * (f / L) : 0.f;
+}
+
+}  // namespace gkv

@@ -121,6 +121,9 @@ struct Pool {
 
     StepWorkspace ws;
     int last_launches = 0;
+    // TMA maps of the arena for the tensor-core decode, encoded once at creation
+    alignas(64) unsigned char tmap_k[128];
+    alignas(64) unsigned char tmap_v[128];
 
     bool in_range(int32_t b) const {
         return static_cast<uint32_t>(b) < static_cast<uint32_t>(desc.total_blocks);
@@ -156,7 +159,7 @@ void step_free(Pool* p);
 
 // Work-list construction (host only; unit-tested through the C ABI helpers).
 struct WorkList {
-    std::vector<int32_t> piece_seg, piece_c0, piece_c1, piece_slot, piece_merge;
+    std::vector<int32_t> piece_seg, piece_c0, piece_c1, piece_slot, piece_merge, merge_deferred;
     std::vector<int32_t> worker_begin;  // n_workers + 1
     std::vector<int32_t> merge_seg, merge_slot0, merge_nslots;
     int32_t n_slots = 0;

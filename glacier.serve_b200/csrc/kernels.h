@@ -15,6 +15,10 @@ struct ArenaGeom {
     int64_t v_block_stride, v_layer_stride, v_head_stride;
     int32_t total_blocks, layers, heads_kv, head_dim, v_head_dim, block_size;
     int32_t dtype;           // GKV_DTYPE_*
+    // Host-side cache of the TMA tensor maps of K and V (CUtensorMap, 64-byte aligned) for
+    // the tensor-core decode; nullptr means "encode at launch".  Never read on the device.
+    const void* tmap_k = nullptr;
+    const void* tmap_v = nullptr;
 };
 
 // ---- kv append ----
@@ -31,6 +35,7 @@ cudaError_t launch_block_copy(const ArenaGeom& g, const int32_t* ops, int n, int
 
 // ---- paged decode ----
 constexpr int kDecodeChunk = 8;  // tokens per decode work chunk
+constexpr int kFusedMergeMaxSlots = 8;  // segments split into more pieces use the merge kernel
 
 // Work list of one step, built on the host (all pointers are device pointers).
 //  segment s = b * heads_kv + h; its chunks are k = 0 .. n_chunks(ctx_b) - 1, chunk k
@@ -51,8 +56,13 @@ struct DecodeWork {
     const int32_t* merge_seg;          // [n_merge] segments split over several workers
     const int32_t* merge_slot0;        // their first partial slot (slots are contiguous)
     const int32_t* merge_nslots;
-    const int32_t* piece_merge;        // [n_pieces] merge entry of a split piece, else -1
+    // [n_pieces] merge entry of a split piece whose segment is merged inside the decode
+    // kernel (few pieces); -1 for an unsplit piece; -2 when the segment is merged afterwards
+    // by the deferred-merge kernel (many pieces: one warp would serialise the merge).
+    const int32_t* piece_merge;
     int32_t n_merge;
+    const int32_t* merge_deferred;     // [n_deferred] merge entries left to the merge kernel
+    int32_t n_deferred;
     // Arrival counters of the fused merge, [head_groups][n_merge] ints.  They must be zero
     // when a launch starts; the worker that completes a segment resets its counter, so they
     // are zero again after every launch that ran to completion.
@@ -84,6 +94,19 @@ struct DecodeConfig {
     int ctas_per_sm;
 };
 DecodeConfig decode_config(const ArenaGeom& g, int n_heads);
+
+// Second launch of a decode whose work list defers merges (w.n_deferred > 0).
+cudaError_t launch_deferred_merge(const ArenaGeom& g, const DecodeWork& w, const DecodeArgs& a,
+                                  int group, int gp, int head_groups, cudaStream_t st);
+
+// Tensor-core variant (paged_decode_tc.cu): bf16 KV, d = dv = 128, block size a multiple of
+// 8, query group 5..8 per head group.  Same work list and partial layout; 4 warps per CTA.
+bool decode_tc_eligible(const ArenaGeom& g, int n_heads);
+// Encodes the K and V TMA maps of the arena into two 128-byte, 64-byte aligned buffers.
+bool encode_decode_tmaps(const ArenaGeom& g, void* tmap_k, void* tmap_v);
+void decode_tc_config(DecodeConfig& c);
+cudaError_t launch_paged_decode_tc(const ArenaGeom& g, const DecodeWork& w, const DecodeArgs& a,
+                                   int group, int head_groups, int* launches, cudaStream_t st);
 
 // Enqueues the split-KV decode (the cross-worker merge is fused into it).  *launches
 // receives the number of kernels enqueued.

@@ -31,6 +31,7 @@
 #include <atomic>
 #include <type_traits>
 
+#include "decode_merge.cuh"
 #include "gkv_device.cuh"
 #include "kernels.h"
 #include "../../include/glacier_kv.h"
@@ -428,57 +429,19 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
             }
             // arrival: the worker completing the segment merges every partial of it
             const int mi = __ldg(w.piece_merge + i);
-            const int ns = __ldg(w.merge_nslots + mi);
-            __threadfence();
-            __syncwarp();
-            int prev = 0;
-            int* counter = w.merge_count + static_cast<int64_t>(hg) * w.n_merge + mi;
-            if (lane == 0) prev = atomicAdd(counter, 1);
-            prev = __shfl_sync(0xffffffffu, prev, 0);
-            if (prev == ns - 1) {
+            if (mi >= 0) {  // merged here; otherwise the deferred-merge kernel does it
+                const int ns = __ldg(w.merge_nslots + mi);
                 __threadfence();
-                const int s0 = __ldg(w.merge_slot0 + mi);
-                const int64_t b0 = (static_cast<int64_t>(hg) * w.n_slots + s0) * GP;
-#pragma unroll 1
-                for (int gg = 0; gg < gcount; ++gg) {
-                    float M = -INFINITY;
-                    for (int s = 0; s < ns; ++s) M = fmaxf(M, __ldcg(a.part_ml + (b0 + s * GP + gg) * 2));
-                    float Ls = 0.f;
-                    float2 A[EV2];
-#pragma unroll
-                    for (int e = 0; e < EV2; ++e) A[e] = make_float2(0.f, 0.f);
-                    if (M != -INFINITY) {
-                        for (int s = 0; s < ns; ++s) {
-                            const int64_t ps = b0 + s * GP + gg;
-                            const float f = exp2f(__ldcg(a.part_ml + ps * 2) - M);
-                            Ls += __ldcg(a.part_ml + ps * 2 + 1) * f;
-                            const float* ap = a.part_acc + ps * DV + lane * EPLV;
-                            const float2 f2 = make_float2(f, f);
-#pragma unroll
-                            for (int e = 0; e < EV2; ++e) {
-                                const float2 v = make_float2(__ldcg(ap + 2 * e),
-                                                             2 * e + 1 < EPLV ? __ldcg(ap + 2 * e + 1) : 0.f);
-                                A[e] = __ffma2_rn(f2, v, A[e]);
-                            }
-                        }
-                    }
-                    const int qh = q_head0 + gg;
-                    float f = 1.f;
-                    if (a.sinks || a.has_sink_all) {
-                        const float sk = (a.sinks ? __ldg(a.sinks + qh) : a.sink_all) * kLog2e;
-                        const float M2 = fmaxf(M, sk);
-                        f = (M == -INFINITY) ? 0.f : exp2f(M - M2);
-                        Ls = Ls * f + exp2f(sk - M2);
-                    }
-                    const float inv = Ls > 0.f ? f / Ls : 0.f;
-                    float* op = a.out + (static_cast<int64_t>(b) * a.n_heads + qh) * DV + lane * EPLV;
-#pragma unroll
-                    for (int e = 0; e < EV2; ++e) {
-                        op[2 * e] = A[e].x * inv;
-                        if (2 * e + 1 < EPLV) op[2 * e + 1] = A[e].y * inv;
-                    }
+                __syncwarp();
+                int prev = 0;
+                int* counter = w.merge_count + static_cast<int64_t>(hg) * w.n_merge + mi;
+                if (lane == 0) prev = atomicAdd(counter, 1);
+                prev = __shfl_sync(0xffffffffu, prev, 0);
+                if (prev == ns - 1) {
+                    __threadfence();
+                    merge_segment<GP, DV>(a, w, hg, __ldg(w.merge_slot0 + mi), ns, b, q_head0, gcount, lane);
+                    if (lane == 0) atomicExch(counter, 0);
                 }
-                if (lane == 0) atomicExch(counter, 0);
             }
         }
     }
@@ -541,7 +504,12 @@ struct Inst {
         dim3 grid(static_cast<unsigned>(w.n_ctas), static_cast<unsigned>(head_groups));
         paged_decode_kernel<KV, D, DV, GP, NW, S><<<grid, NW * 32, Tr::SMEM, st>>>(g, w, a, group, cpp);
         e = cudaGetLastError();
-        if (e == cudaSuccess) *launches = 1;
+        if (e != cudaSuccess) return e;
+        *launches = 1;
+        if (w.n_deferred > 0) {
+            e = launch_deferred_merge(g, w, a, group, GP, head_groups, st);
+            if (e == cudaSuccess) *launches = 2;
+        }
         return e;
     }
 };
@@ -594,8 +562,38 @@ DecodeConfig decode_config(const ArenaGeom& g, int n_heads) {
     const int group = n_heads / g.heads_kv;
     c.gp = pick_gp(group);
     c.head_groups = (group + c.gp - 1) / c.gp;
+    if (decode_tc_eligible(g, n_heads)) {
+        decode_tc_config(c);
+        return c;
+    }
     dispatch(g, c.gp, [&](auto inst) { decltype(inst)::config(c); });
     return c;
+}
+
+cudaError_t launch_deferred_merge(const ArenaGeom& g, const DecodeWork& w, const DecodeArgs& a,
+                                  int group, int gp, int head_groups, cudaStream_t st) {
+    if (w.n_deferred <= 0) return cudaSuccess;
+    const dim3 grid(static_cast<unsigned>(w.n_deferred), static_cast<unsigned>(head_groups * gp));
+    auto go = [&](auto kern) {
+        kern<<<grid, 256, 0, st>>>(g, w, a, group);
+        return cudaGetLastError();
+    };
+#define GKV_MERGE_DV(GPV)                                                                  \
+    switch (g.v_head_dim) {                                                               \
+        case 32: return go(deferred_merge_kernel<GPV, 32>);                               \
+        case 64: return go(deferred_merge_kernel<GPV, 64>);                               \
+        case 128: return go(deferred_merge_kernel<GPV, 128>);                             \
+        case 256: return go(deferred_merge_kernel<GPV, 256>);                             \
+        default: return cudaErrorInvalidValue;                                            \
+    }
+    switch (gp) {
+        case 1: GKV_MERGE_DV(1)
+        case 2: GKV_MERGE_DV(2)
+        case 4: GKV_MERGE_DV(4)
+        case 8: GKV_MERGE_DV(8)
+    }
+#undef GKV_MERGE_DV
+    return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_paged_decode(const ArenaGeom& g, const DecodeWork& w, const DecodeArgs& a,
@@ -605,6 +603,10 @@ cudaError_t launch_paged_decode(const ArenaGeom& g, const DecodeWork& w, const D
     const int group = a.n_heads / g.heads_kv;
     const int gp = pick_gp(group);
     const int head_groups = (group + gp - 1) / gp;
+    const bool aligned = ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.out) |
+                           reinterpret_cast<uintptr_t>(a.part_acc)) & 15) == 0;
+    if (aligned && decode_tc_eligible(g, a.n_heads))
+        return launch_paged_decode_tc(g, w, a, group, head_groups, launches, stream);
     cudaError_t err = cudaErrorInvalidValue;
     dispatch(g, gp, [&](auto inst) {
         err = decltype(inst)::launch(g, w, a, group, head_groups, launches, stream);

@@ -53,7 +53,7 @@ alignas(64) unsigned char g_stage[kMetaBytes];
 size_t up16(size_t x) { return (x + 15) & ~static_cast<size_t>(15); }
 
 struct Layout {
-    size_t tables, ctx, pseg, pc0, pc1, pslot, pmerge, wbeg, mseg, ms0, mns, counters, total;
+    size_t tables, ctx, pseg, pc0, pc1, pslot, pmerge, wbeg, mseg, ms0, mns, mdef, counters, total;
 };
 
 Layout layout_for(int64_t batch, int64_t max_blocks, int64_t max_pieces, int64_t n_workers,
@@ -76,6 +76,7 @@ Layout layout_for(int64_t batch, int64_t max_blocks, int64_t max_pieces, int64_t
     L.mseg = take(max_merge * 4);
     L.ms0 = take(max_merge * 4);
     L.mns = take(max_merge * 4);
+    L.mdef = take(max_merge * 4);
     L.counters = take(max_merge * head_groups * 4);  // merge arrival counters, staged as zeros
     L.total = o;
     return L;
@@ -84,8 +85,8 @@ Layout layout_for(int64_t batch, int64_t max_blocks, int64_t max_pieces, int64_t
 // The work list of step.cpp's build_work_list, written into fixed arrays (no heap).
 void plan_fixed(const int32_t* ctx, int32_t batch, int32_t heads_kv, int32_t bs, int32_t n_workers,
                 int64_t total, int32_t* pseg, int32_t* pc0, int32_t* pc1, int32_t* pslot,
-                int32_t* pmerge, int32_t* wbeg, int32_t* mseg, int32_t* ms0, int32_t* mns, int32_t* n_pieces,
-                int32_t* n_slots, int32_t* n_merge) {
+                int32_t* pmerge, int32_t* wbeg, int32_t* mseg, int32_t* ms0, int32_t* mns, int32_t* mdef,
+                int32_t* n_pieces, int32_t* n_slots, int32_t* n_merge, int32_t* n_deferred) {
     const int64_t n_seg = static_cast<int64_t>(batch) * heads_kv;
     int64_t s = 0, s0 = 0, s1 = n_seg > 0 ? chunks_of(ctx[0], bs) : 0;
     int32_t np = 0;
@@ -108,17 +109,19 @@ void plan_fixed(const int32_t* ctx, int32_t batch, int32_t heads_kv, int32_t bs,
         }
     }
     wbeg[n_workers] = np;
-    int32_t slots = 0, merges = 0, i = 0;
+    int32_t slots = 0, merges = 0, deferred = 0, i = 0;
     while (i < np) {
         int32_t j = i + 1;
         while (j < np && pseg[j] == pseg[i]) ++j;
         if (j - i > 1) {
+            const bool defer = (j - i) > kFusedMergeMaxSlots;
             mseg[merges] = pseg[i];
             ms0[merges] = slots;
             mns[merges] = j - i;
+            if (defer) mdef[deferred++] = merges;
             for (int32_t k = i; k < j; ++k) {
                 pslot[k] = slots++;
-                pmerge[k] = merges;
+                pmerge[k] = defer ? -2 : merges;
             }
             ++merges;
         } else {
@@ -130,6 +133,7 @@ void plan_fixed(const int32_t* ctx, int32_t batch, int32_t heads_kv, int32_t bs,
     *n_pieces = np;
     *n_slots = slots;
     *n_merge = merges;
+    *n_deferred = deferred;
 }
 
 }  // namespace
@@ -226,11 +230,11 @@ extern "C" int gkv_paged_decode_noalloc(const gkv_arena_desc* arena, int32_t lay
     unsigned char* h = g_stage;
     if (batch && max_blocks) memcpy(h + L.tables, h_block_tables, static_cast<size_t>(batch) * max_blocks * 4);
     memcpy(h + L.ctx, h_ctx_lens, static_cast<size_t>(batch) * 4);
-    int32_t np = 0, nslots = 0, nmerge = 0;
+    int32_t np = 0, nslots = 0, nmerge = 0, ndef = 0;
     auto at = [&](size_t off) { return reinterpret_cast<int32_t*>(h + off); };
     plan_fixed(h_ctx_lens, batch, A.heads_kv, bs, n_workers, total, at(L.pseg), at(L.pc0), at(L.pc1),
-               at(L.pslot), at(L.pmerge), at(L.wbeg), at(L.mseg), at(L.ms0), at(L.mns), &np, &nslots,
-               &nmerge);
+               at(L.pslot), at(L.pmerge), at(L.wbeg), at(L.mseg), at(L.ms0), at(L.mns), at(L.mdef), &np,
+               &nslots, &nmerge, &ndef);
     // the fused merge's arrival counters must start at zero on every call
     memset(h + L.counters, 0, static_cast<size_t>(n_seg) * cfg.head_groups * 4);
     const size_t part_floats =
@@ -263,6 +267,8 @@ extern "C" int gkv_paged_decode_noalloc(const gkv_arena_desc* arena, int32_t lay
     w.piece_merge = dp(L.pmerge);
     w.n_merge = nmerge;
     w.merge_count = reinterpret_cast<int32_t*>(dbase + L.counters);
+    w.merge_deferred = dp(L.mdef);
+    w.n_deferred = ndef;
 
     DecodeArgs a{};
     a.layer = layer;

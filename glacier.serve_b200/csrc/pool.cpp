@@ -338,6 +338,12 @@ int gkv_pool_create(const gkv_pool_desc* desc, gkv_pool** out_pool) {
         g.k = k;
         g.v = v;
         P.has_arena = true;
+        // TMA maps for the tensor-core decode (bf16, d = dv = 128, 8-token-aligned blocks)
+        if (d.dtype == GKV_DTYPE_BF16 && d.head_dim == 128 && d.v_head_dim == 128 && d.block_size % 8 == 0 &&
+            gkv::encode_decode_tmaps(g, P.tmap_k, P.tmap_v)) {
+            g.tmap_k = P.tmap_k;
+            g.tmap_v = P.tmap_v;
+        }
     }
     *out_pool = p;
     return GKV_OK;

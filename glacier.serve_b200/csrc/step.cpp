@@ -33,7 +33,7 @@ int sm_count(int device) {
 
 // Byte layout of the packed step metadata (identical on host and device).
 struct MetaLayout {
-    size_t slots, tables, ctx, pseg, pc0, pc1, pslot, pmerge, wbeg, mseg, ms0, mns, total;
+    size_t slots, tables, ctx, pseg, pc0, pc1, pslot, pmerge, wbeg, mseg, ms0, mns, mdef, total;
 };
 
 MetaLayout meta_layout(int64_t n_tok, int64_t batch, int64_t max_blocks, int64_t n_pieces,
@@ -57,6 +57,7 @@ MetaLayout meta_layout(int64_t n_tok, int64_t batch, int64_t max_blocks, int64_t
     L.mseg = take(static_cast<size_t>(n_merge) * 4);
     L.ms0 = take(static_cast<size_t>(n_merge) * 4);
     L.mns = take(static_cast<size_t>(n_merge) * 4);
+    L.mdef = take(static_cast<size_t>(n_merge) * 4);
     L.total = o;
     return L;
 }
@@ -127,16 +128,88 @@ void build_work_list(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, i
         while (j < np && W.piece_seg[j] == W.piece_seg[i]) ++j;
         if (j - i > 1) {
             const int32_t mi = static_cast<int32_t>(W.merge_seg.size());
+            const bool deferred = (j - i) > static_cast<size_t>(kFusedMergeMaxSlots);
             W.merge_seg.push_back(W.piece_seg[i]);
             W.merge_slot0.push_back(W.n_slots);
             W.merge_nslots.push_back(static_cast<int32_t>(j - i));
+            if (deferred) W.merge_deferred.push_back(mi);
             for (size_t k = i; k < j; ++k) {
                 W.piece_slot[k] = W.n_slots++;
-                W.piece_merge[k] = mi;
+                W.piece_merge[k] = deferred ? -2 : mi;
             }
         }
         i = j;
     }
+}
+
+// Sizes the pinned + device metadata buffers for `bytes`.  Only called while no step of
+// this pool is in use by a kernel that has not been ordered before the next upload
+// (cudaFree synchronises the device).
+static int ensure_meta(Pool* p, size_t bytes) {
+    StepWorkspace& ws = p->ws;
+    if (!ws.meta_copied) {
+        cudaError_t e = cudaEventCreateWithFlags(&ws.meta_copied, cudaEventDisableTiming);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
+    }
+    if (bytes <= ws.meta_cap) return GKV_OK;
+    if (ws.meta_pending) cudaEventSynchronize(ws.meta_copied);
+    ws.meta_pending = false;
+    if (ws.h_meta) cudaFreeHost(ws.h_meta);
+    if (ws.d_meta) cudaFree(ws.d_meta);
+    ws.h_meta = nullptr;
+    ws.d_meta = nullptr;
+    ws.meta_cap = 0;
+    ws.uploaded = false;  // the previous step's metadata is gone
+    const size_t cap = align_up(bytes, 4096);
+    cudaError_t e = cudaMallocHost(&ws.h_meta, cap);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMallocHost(step metadata)");
+    e = cudaMalloc(&ws.d_meta, cap);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(step metadata)");
+    ws.meta_cap = cap;
+    return GKV_OK;
+}
+
+// Decode configuration for n_heads plus partial / counter buffers for `slots` partial slots
+// and `merges` split segments.  Never touches the uploaded step metadata, so it is safe
+// between gkv_upload_step and gkv_paged_decode.
+static int decode_buffers(Pool* p, int32_t n_heads, int64_t slots, int64_t merges) {
+    StepWorkspace& ws = p->ws;
+    if (n_heads % p->desc.heads_kv != 0)
+        return set_error(GKV_EINVAL, "n_heads %d is not a multiple of heads_kv %d", n_heads, p->desc.heads_kv);
+    if (n_heads != ws.n_heads || !ws.cfg.supported) {
+        ws.n_heads = n_heads;
+        ws.cfg = decode_config(p->geom, n_heads);
+        const int ctas_per_sm = ws.cfg.supported ? ws.cfg.ctas_per_sm : 1;
+        ws.n_ctas_max = sm_count(p->desc.device) * ctas_per_sm;  // grid of the next upload
+    }
+    if (!ws.cfg.supported) return GKV_OK;
+    const size_t need = static_cast<size_t>(slots > 0 ? slots : 1) * ws.cfg.head_groups * ws.cfg.gp;
+    if (need > ws.part_slots_cap) {
+        if (ws.d_part_acc) cudaFree(ws.d_part_acc);
+        if (ws.d_part_ml) cudaFree(ws.d_part_ml);
+        ws.d_part_acc = nullptr;
+        ws.d_part_ml = nullptr;
+        ws.part_slots_cap = 0;
+        cudaError_t e = cudaMalloc(&ws.d_part_acc, need * p->desc.v_head_dim * sizeof(float));
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(decode partials)");
+        e = cudaMalloc(&ws.d_part_ml, need * 2 * sizeof(float));
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(decode partials)");
+        ws.part_slots_cap = need;
+    }
+    // one arrival counter per (head group, split segment), zeroed when allocated; kernels
+    // leave them at zero
+    const size_t counters = static_cast<size_t>(merges > 0 ? merges : 1) * ws.cfg.head_groups;
+    if (counters > ws.merge_count_cap) {
+        if (ws.d_merge_count) cudaFree(ws.d_merge_count);
+        ws.d_merge_count = nullptr;
+        ws.merge_count_cap = 0;
+        cudaError_t e = cudaMalloc(&ws.d_merge_count, counters * sizeof(int32_t));
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(merge counters)");
+        e = cudaMemset(ws.d_merge_count, 0, counters * sizeof(int32_t));
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(merge counters)");
+        ws.merge_count_cap = counters;
+    }
+    return GKV_OK;
 }
 
 int step_reserve(Pool* p, int32_t max_batch, int32_t max_blocks, int32_t max_tokens,
@@ -145,72 +218,21 @@ int step_reserve(Pool* p, int32_t max_batch, int32_t max_blocks, int32_t max_tok
     if (max_batch < 0 || max_blocks < 0 || max_tokens < 0)
         return set_error(GKV_EINVAL, "negative reservation");
     if (n_heads <= 0) n_heads = ws.n_heads > 0 ? ws.n_heads : p->desc.heads_kv;
-    if (n_heads % p->desc.heads_kv != 0)
-        return set_error(GKV_EINVAL, "n_heads %d is not a multiple of heads_kv %d", n_heads, p->desc.heads_kv);
-    ws.n_heads = n_heads;
-    ws.cfg = decode_config(p->geom, n_heads);
-    const int ctas_per_sm = ws.cfg.supported ? ws.cfg.ctas_per_sm : 1;
-    ws.n_ctas_max = sm_count(p->desc.device) * ctas_per_sm;
     if (max_batch > ws.max_batch) ws.max_batch = max_batch;
     if (max_blocks > ws.max_blocks) ws.max_blocks = max_blocks;
     if (max_tokens > ws.max_tokens) ws.max_tokens = max_tokens;
+    // the worker count depends on the decode configuration: settle it first
+    int rc = decode_buffers(p, n_heads, 0, 0);
+    if (rc != GKV_OK) return rc;
     const int warps = ws.cfg.supported ? ws.cfg.warps : 4;
     const int64_t workers = static_cast<int64_t>(ws.n_ctas_max) * warps;
     const int64_t n_seg = static_cast<int64_t>(ws.max_batch) * p->desc.heads_kv;
     const MetaLayout L = meta_layout(ws.max_tokens, ws.max_batch, ws.max_blocks, workers + n_seg,
                                      workers, n_seg);
-    if (L.total > ws.meta_cap) {
-        if (ws.meta_pending && ws.meta_copied) cudaEventSynchronize(ws.meta_copied);
-        ws.meta_pending = false;
-        if (ws.h_meta) cudaFreeHost(ws.h_meta);
-        if (ws.d_meta) cudaFree(ws.d_meta);
-        ws.h_meta = nullptr;
-        ws.d_meta = nullptr;
-        ws.meta_cap = 0;
-        const size_t cap = align_up(L.total, 4096);
-        cudaError_t e = cudaMallocHost(&ws.h_meta, cap);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaMallocHost(step metadata)");
-        e = cudaMalloc(&ws.d_meta, cap);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(step metadata)");
-        ws.meta_cap = cap;
-        ws.uploaded = false;
-    }
-    if (!ws.meta_copied) {
-        cudaError_t e = cudaEventCreateWithFlags(&ws.meta_copied, cudaEventDisableTiming);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
-    }
-    // partials: every piece of the largest work list could be a partial
-    if (ws.cfg.supported) {
-        const size_t slots = static_cast<size_t>(workers + n_seg) * ws.cfg.head_groups * ws.cfg.gp;
-        if (slots > ws.part_slots_cap) {
-            if (ws.d_part_acc) cudaFree(ws.d_part_acc);
-            if (ws.d_part_ml) cudaFree(ws.d_part_ml);
-            ws.d_part_acc = nullptr;
-            ws.d_part_ml = nullptr;
-            ws.part_slots_cap = 0;
-            cudaError_t e = cudaMalloc(&ws.d_part_acc, slots * p->desc.v_head_dim * sizeof(float));
-            if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(decode partials)");
-            e = cudaMalloc(&ws.d_part_ml, slots * 2 * sizeof(float));
-            if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(decode partials)");
-            ws.part_slots_cap = slots;
-        }
-        // one arrival counter per (head group, split segment), zeroed once here
-        const size_t counters = static_cast<size_t>(n_seg > 0 ? n_seg : 1) * ws.cfg.head_groups;
-        if (counters > ws.merge_count_cap) {
-            if (ws.d_merge_count) {
-                cudaDeviceSynchronize();
-                cudaFree(ws.d_merge_count);
-            }
-            ws.d_merge_count = nullptr;
-            ws.merge_count_cap = 0;
-            cudaError_t e = cudaMalloc(&ws.d_merge_count, counters * sizeof(int32_t));
-            if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(merge counters)");
-            e = cudaMemset(ws.d_merge_count, 0, counters * sizeof(int32_t));
-            if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(merge counters)");
-            ws.merge_count_cap = counters;
-        }
-    }
-    return GKV_OK;
+    rc = ensure_meta(p, L.total);
+    if (rc != GKV_OK) return rc;
+    // every piece of the largest work list could be a partial, every segment a merge
+    return decode_buffers(p, n_heads, workers + n_seg, n_seg);
 }
 
 void step_free(Pool* p) {
@@ -282,7 +304,8 @@ int step_upload(Pool* p, const int32_t* tables, int32_t batch, int32_t max_block
     const int64_t n_workers = static_cast<int64_t>(ctas) * warps;
     const int64_t n_merge = static_cast<int64_t>(W.merge_seg.size());
     const MetaLayout L = meta_layout(n_tok, batch, max_blocks, n_pieces, n_workers, n_merge);
-    if (L.total > ws.meta_cap) return set_error(GKV_EINVAL, "step metadata exceeds the reserved workspace");
+    int mrc = ensure_meta(p, L.total);
+    if (mrc != GKV_OK) return mrc;
 
     // The pinned staging buffer may still feed the previous step's copy.
     if (ws.meta_pending) {
@@ -306,6 +329,7 @@ int step_upload(Pool* p, const int32_t* tables, int32_t batch, int32_t max_block
     put(L.mseg, W.merge_seg);
     put(L.ms0, W.merge_slot0);
     put(L.mns, W.merge_nslots);
+    put(L.mdef, W.merge_deferred);
     cudaError_t e = cudaMemcpyAsync(ws.d_meta, ws.h_meta, L.total, cudaMemcpyHostToDevice, st);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(step metadata)");
     e = cudaEventRecord(ws.meta_copied, st);
@@ -329,6 +353,8 @@ int step_upload(Pool* p, const int32_t* tables, int32_t batch, int32_t max_block
     w.merge_nslots = reinterpret_cast<const int32_t*>(d + L.mns);
     w.piece_merge = reinterpret_cast<const int32_t*>(d + L.pmerge);
     w.n_merge = static_cast<int32_t>(n_merge);
+    w.merge_deferred = reinterpret_cast<const int32_t*>(d + L.mdef);
+    w.n_deferred = static_cast<int32_t>(W.merge_deferred.size());
     w.merge_count = ws.d_merge_count;
     ws.d_slots = reinterpret_cast<const int64_t*>(d + L.slots);
     ws.batch = batch;
@@ -370,8 +396,11 @@ static int decode_common(Pool* p, int32_t layer, const float* d_q, float* d_out,
         return set_error(GKV_EINVAL, "n_heads %d is not a positive multiple of heads_kv %d", n_heads,
                          p->desc.heads_kv);
     if (ws.batch > 0 && (!d_q || !d_out)) return set_error(GKV_EINVAL, "q/out is NULL");
-    if (n_heads != ws.n_heads || !ws.cfg.supported) {
-        const int rc = step_reserve(p, 0, 0, 0, n_heads);
+    {
+        // decode config + partial/counter capacity for the uploaded work list; the uploaded
+        // metadata itself is left alone (the work list works with any kernel variant: every
+        // variant runs the same number of warps per CTA)
+        const int rc = decode_buffers(p, n_heads, ws.work.n_slots, ws.work.n_merge);
         if (rc != GKV_OK) return rc;
     }
     if (!ws.cfg.supported)

@@ -74,6 +74,9 @@ CASES = [
     (3, 3, 32, 32, 4, "f32", [13, 4, 1]),           # MHA, block size 4
     (8, 2, 128, 64, 12, "f32", [50, 12, 13]),       # block size 12: chunks of 8 + 4
     (4, 4, 64, 64, 16, "f32", [20000]),             # one long sequence split over many workers
+    (16, 2, 128, 128, 8, "bf16", [37, 8, 1, 100]),  # tensor-core kernel, block size 8
+    (8, 1, 128, 128, 24, "bf16", [50, 24, 25, 3]),  # tensor-core kernel, block size 24
+    (56, 8, 128, 128, 16, "bf16", [9000, 17]),      # group 7, long sequence: fused merge
 ]
 
 
@@ -89,6 +92,27 @@ def test_decode_parity(cuda, case):
     out = gpu_decode(pool, 0, tables, ctx, q, nH, scale_of(d))
     ref = O.decode_batch(K, V, geom_of(pool), 0, tables, np.array(ctx, np.int32), q, nH, scale_of(d))
     np.testing.assert_allclose(out, ref, atol=TOL[dtype], rtol=0)
+
+
+def test_one_upload_serves_decodes_with_other_head_counts(cuda):
+    """A decode whose head count selects another kernel variant (and grid occupancy) than
+    the one the upload planned for must reuse the uploaded step as is."""
+    import torch
+
+    rng = np.random.default_rng(15)
+    pool = G.PagedBlockPool(700, 1, 8, 128, 16, dtype="bf16")
+    K, V = random_arena(pool, rng)
+    ctx = [3000, 40, 1500, 7]
+    tables = random_tables(rng, ctx, 16, 700)
+    pool.upload_step(tables, np.array(ctx, np.int32))  # planned without a head count
+    for n_heads in (64, 8, 32, 56):  # tensor-core, group 1, group 4, tensor-core group 7
+        q = rng.standard_normal((4, n_heads, 128)).astype(np.float32)
+        out = torch.zeros((4, n_heads, 128), device=cuda)
+        pool.paged_decode(0, torch.from_numpy(q).to(cuda), out, n_heads, 0.09)
+        pool.sync()
+        ref = O.decode_batch(K, V, geom_of(pool), 0, tables, np.array(ctx, np.int32), q, n_heads, 0.09)
+        np.testing.assert_allclose(out.cpu().numpy(), ref, atol=TOL["bf16"], rtol=0)
+    pool.close()
 
 
 def test_layer_addressing_multi_layer_pool(cuda):
