@@ -14,6 +14,11 @@
 
 namespace gkv {
 
+// Natural-log softmax denominator from a base-2 running max and sum.
+__device__ __forceinline__ float lse_ln(float m2, float l) {
+    return (l > 0.f && m2 != -INFINITY) ? (m2 + log2f(l)) * 0.6931471805599453f : -INFINITY;
+}
+
 template <int GP, int DV>
 __device__ __forceinline__ void merge_segment(const DecodeArgs& a, const DecodeWork& w, int hg,
                                               int s0, int ns, int b, int q_head0, int gcount,
@@ -83,14 +88,16 @@ __device__ __forceinline__ void merge_segment(const DecodeArgs& a, const DecodeW
     for (int g = 0; g < GP; ++g) {
         if (g >= gcount) continue;
         const int qh = q_head0 + g;
-        float L = Ls[g], f = 1.f;
+        float L = Ls[g], f = 1.f, Mref = M[g];
         if (a.sinks || a.has_sink_all) {
             const float sk = (a.sinks ? __ldg(a.sinks + qh) : a.sink_all) * kL2e;
             const float M2 = fmaxf(M[g], sk);
             f = (M[g] == -INFINITY) ? 0.f : exp2f(M[g] - M2);
             L = L * f + exp2f(sk - M2);
+            Mref = M2;
         }
         const float inv = L > 0.f ? f / L : 0.f;
+        if (a.lse && lane == 0) a.lse[static_cast<int64_t>(b) * a.n_heads + qh] = lse_ln(Mref, L);
         float* op = a.out + (static_cast<int64_t>(b) * a.n_heads + qh) * DV + lane * EPLV;
 #pragma unroll
         for (int e = 0; e < EPLV; ++e) op[e] = A[g][e] * inv;
@@ -166,14 +173,50 @@ __global__ void __launch_bounds__(256) deferred_merge_kernel(ArenaGeom g, Decode
         for (int k = 1; k < SL; ++k) A += red[d + k * DV];
     }
     const int qh = q_head0 + gg;
-    float f = 1.f;
+    float f = 1.f, Mref = M;
     if (a.sinks || a.has_sink_all) {
         const float sk = (a.sinks ? __ldg(a.sinks + qh) : a.sink_all) * kL2e;
         const float M2 = fmaxf(M, sk);
         f = (M == -INFINITY) ? 0.f : exp2f(M - M2);
         L = L * f + exp2f(sk - M2);
+        Mref = M2;
     }
     a.out[(static_cast<int64_t>(b) * a.n_heads + qh) * DV + d] = L > 0.f ? A * (f / L) : 0.f;
+    if (a.lse && d == 0) a.lse[static_cast<int64_t>(b) * a.n_heads + qh] = lse_ln(Mref, L);
+}
+
+// Cross-part merge of normalised outputs with their log-sum-exps (multi-GPU split-KV: the
+// parts are the ranks' block ranges).  One warp per row (= sequence x query head), lanes
+// over dims.
+static __global__ void __launch_bounds__(256) lse_merge_kernel(const float* __restrict__ parts, int n_parts,
+                                                        int rows, int dv, const float* __restrict__ sinks,
+                                                        int n_heads, float* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    if (row >= rows) return;
+    const int64_t part_stride = static_cast<int64_t>(rows) * (dv + 1);
+    const float* lses = parts + static_cast<int64_t>(rows) * dv;  // lse block of part 0
+    float M = -INFINITY;
+    for (int p = 0; p < n_parts; ++p) M = fmaxf(M, __ldg(lses + p * part_stride + row));
+    float sk = -INFINITY;
+    if (sinks) {
+        sk = __ldg(sinks + row % n_heads);
+        M = fmaxf(M, sk);
+    }
+    float den = (M == -INFINITY) ? 0.f : ((sk == -INFINITY) ? 0.f : expf(sk - M));
+    for (int p = 0; p < n_parts; ++p) {
+        const float l = __ldg(lses + p * part_stride + row);
+        if (l != -INFINITY) den += expf(l - M);
+    }
+    for (int d = lane; d < dv; d += 32) {
+        float acc = 0.f;
+        for (int p = 0; p < n_parts; ++p) {
+            const float l = __ldg(lses + p * part_stride + row);
+            if (l == -INFINITY) continue;
+            acc = fmaf(expf(l - M), __ldg(parts + p * part_stride + row * dv + d), acc);
+        }
+        out[row * dv + d] = den > 0.f ? acc / den : 0.f;
+    }
 }
 
 }  // namespace gkv

@@ -153,6 +153,8 @@ int step_decode(Pool* p, int32_t layer, const float* d_q, float* d_out, int32_t 
                 float scale, const float* d_sinks, cudaStream_t st);
 int step_append(Pool* p, int32_t layer, const float* d_k, const float* d_v, int32_t n_tok,
                 cudaStream_t st);
+int step_decode_lse(Pool* p, int32_t layer, const float* d_q, float* d_out, float* d_lse,
+                    int32_t n_heads, float scale, const float* d_sinks, cudaStream_t st);
 int step_reserve(Pool* p, int32_t max_batch, int32_t max_blocks, int32_t max_tokens,
                  int32_t n_heads);
 void step_free(Pool* p);

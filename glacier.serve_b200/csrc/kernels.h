@@ -81,7 +81,17 @@ struct DecodeArgs {
     float* part_acc;     // [head_groups][n_slots][gp][v_head_dim]
     float* part_ml;      // [head_groups][n_slots][gp][2]
     int* err;
+    // Optional [batch][n_heads]: natural-log softmax denominator of every written output row,
+    // ln(sum_t exp(s_t) [+ exp(sink)]), for merging outputs computed over disjoint token ranges.
+    float* lse = nullptr;
 };
+
+// out[r][d] = sum_p exp(lse_p[r] - LSE[r]) * part_p[r][d] with LSE[r] = ln(sum_p exp(lse_p[r])
+// [+ exp(sink[r % n_heads])]).  parts: n_parts blocks of (rows * dv outputs, then rows lses).
+cudaError_t launch_lse_merge(const float* parts, int n_parts, int rows, int dv, const float* sinks,
+                             int n_heads, float* out, cudaStream_t st);
+// x[0..n) = value
+cudaError_t launch_fill(float* x, int64_t n, float value, cudaStream_t st);
 
 // Launch configuration the decode kernel uses for this geometry and query-head count.
 struct DecodeConfig {

@@ -390,14 +390,16 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
             for (int gg = 0; gg < GP; ++gg) {
                 if (gg >= gcount) continue;
                 const int qh = q_head0 + gg;
-                float Ls = lg[gg], f = 1.f;
+                float Ls = lg[gg], f = 1.f, Mref = m[gg];
                 if (a.sinks || a.has_sink_all) {
                     const float sk = (a.sinks ? __ldg(a.sinks + qh) : a.sink_all) * kLog2e;
                     const float M2 = fmaxf(m[gg], sk);
                     f = (m[gg] == -INFINITY) ? 0.f : exp2f(m[gg] - M2);
                     Ls = Ls * f + exp2f(sk - M2);
+                    Mref = M2;
                 }
                 const float inv = Ls > 0.f ? f / Ls : 0.f;
+                if (a.lse && lane == 0) a.lse[static_cast<int64_t>(b) * a.n_heads + qh] = lse_ln(Mref, Ls);
                 float* op = a.out + (static_cast<int64_t>(b) * a.n_heads + qh) * DV + lane * EPLV;
 #pragma unroll
                 for (int e = 0; e < EV2; ++e) {
@@ -568,6 +570,31 @@ DecodeConfig decode_config(const ArenaGeom& g, int n_heads) {
     }
     dispatch(g, c.gp, [&](auto inst) { decltype(inst)::config(c); });
     return c;
+}
+
+namespace {
+__global__ void fill_kernel(float* x, int64_t n, float value) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        x[i] = value;
+}
+}  // namespace
+
+cudaError_t launch_fill(float* x, int64_t n, float value, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 1184) blocks = 1184;
+    fill_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(x, n, value);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_lse_merge(const float* parts, int n_parts, int rows, int dv, const float* sinks,
+                             int n_heads, float* out, cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    const int64_t threads = static_cast<int64_t>(rows) * 32;
+    lse_merge_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, st>>>(parts, n_parts, rows, dv,
+                                                                                   sinks, n_heads, out);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_deferred_merge(const ArenaGeom& g, const DecodeWork& w, const DecodeArgs& a,

@@ -273,15 +273,17 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_tc_kernel(
                 const int hh = cc ? hB : hA;
                 if (hh >= gcount) continue;
                 const float mm = cc ? mB : mA;
-                float Ls = cc ? lB : lA, f = 1.f;
+                float Ls = cc ? lB : lA, f = 1.f, Mref = mm;
                 const int qh2 = q_head0 + hh;
                 if (a.sinks || a.has_sink_all) {
                     const float sk = (a.sinks ? __ldg(a.sinks + qh2) : a.sink_all) * kLog2e;
                     const float M2 = fmaxf(mm, sk);
                     f = (mm == -INFINITY) ? 0.f : exp2f(mm - M2);
                     Ls = Ls * f + exp2f(sk - M2);
+                    Mref = M2;
                 }
                 const float inv = Ls > 0.f ? f / Ls : 0.f;
+                if (a.lse && gq == 0) a.lse[static_cast<int64_t>(b) * a.n_heads + qh2] = lse_ln(Mref, Ls);
                 float* op = a.out + (static_cast<int64_t>(b) * a.n_heads + qh2) * kDV;
 #pragma unroll
                 for (int t = 0; t < 8; ++t) {

@@ -387,7 +387,7 @@ int step_append(Pool* p, int32_t layer, const float* d_k, const float* d_v, int3
 
 static int decode_common(Pool* p, int32_t layer, const float* d_q, float* d_out, int32_t n_heads,
                          float scale, const float* d_sinks, bool has_sink_all, float sink_all,
-                         cudaStream_t st) {
+                         cudaStream_t st, float* d_lse = nullptr) {
     StepWorkspace& ws = p->ws;
     if (!ws.uploaded) return set_error(GKV_ESTATE, "no step uploaded (call gkv_upload_step first)");
     if (layer < 0 || layer >= p->desc.layers)
@@ -425,6 +425,7 @@ static int decode_common(Pool* p, int32_t layer, const float* d_q, float* d_out,
     a.part_acc = ws.d_part_acc;
     a.part_ml = ws.d_part_ml;
     a.err = ws.d_err;
+    a.lse = d_lse;
     int launches = 0;
     cudaError_t e = launch_paged_decode(p->geom, ws.work, a, &launches, st);
     if (e != cudaSuccess) return cuda_fail(e, "paged_decode launch");
@@ -435,6 +436,11 @@ static int decode_common(Pool* p, int32_t layer, const float* d_q, float* d_out,
 int step_decode(Pool* p, int32_t layer, const float* d_q, float* d_out, int32_t n_heads,
                 float scale, const float* d_sinks, cudaStream_t st) {
     return decode_common(p, layer, d_q, d_out, n_heads, scale, d_sinks, false, 0.f, st);
+}
+
+int step_decode_lse(Pool* p, int32_t layer, const float* d_q, float* d_out, float* d_lse,
+                    int32_t n_heads, float scale, const float* d_sinks, cudaStream_t st) {
+    return decode_common(p, layer, d_q, d_out, n_heads, scale, d_sinks, false, 0.f, st, d_lse);
 }
 
 }  // namespace gkv

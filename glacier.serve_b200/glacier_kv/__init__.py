@@ -339,6 +339,21 @@ class PagedBlockPool:
             _ptr(k_new), _ptr(v_new), _ptr(q), _ptr(out), n_heads, float(scale),
             None if sinks is None else _f32_dev(sinks, "sinks"), _stream(stream, self.device)))
 
+    def paged_decode_lse(self, layer: int, q, out, lse, n_heads: int, scale: float, sinks=None, stream=None) -> None:
+        """paged_decode plus lse [batch, n_heads] = ln(softmax denominator) of every row."""
+        _check(lib.gkv_paged_decode_lse(self._h, layer, _f32_dev(q, "q"), _f32_dev(out, "out"),
+                                        _f32_dev(lse, "lse"), n_heads, float(scale),
+                                        None if sinks is None else _f32_dev(sinks, "sinks"),
+                                        _stream(stream, self.device)))
+
+    def paged_decode_splitkv_dist(self, comm: "Comm", layer: int, q, out, n_heads: int, scale: float,
+                                  sinks=None, stream=None) -> None:
+        """This rank's block ranges -> NCCL all-gather of (out, lse) -> LSE merge into out."""
+        _check(lib.gkv_paged_decode_splitkv_dist(self._h, comm.handle, layer, _f32_dev(q, "q"),
+                                                 _f32_dev(out, "out"), n_heads, float(scale),
+                                                 None if sinks is None else _f32_dev(sinks, "sinks"),
+                                                 _stream(stream, self.device)))
+
     @property
     def last_launch_count(self) -> int:
         return _check(lib.gkv_pool_last_launch_count(self._h))
@@ -434,6 +449,53 @@ def partition_lpt(ctx_lens: Sequence[int], n_ranks: int) -> np.ndarray:
     out = np.zeros(max(cl.size, 1), dtype=np.int32)
     _check(lib.gkv_partition_lpt(_ptr(cl), cl.size, n_ranks, _ptr(out)))
     return out[: cl.size]
+
+
+class Comm:
+    """NCCL communicator of the ranks that split long sequences (gkv_comm_*)."""
+
+    def __init__(self, unique_id: bytes, n_ranks: int, rank: int, device: int, timeout_ms: int = 60_000):
+        if len(unique_id) != 128:
+            raise ValueError("unique id must be 128 bytes")
+        buf = (C.c_uint8 * 128).from_buffer_copy(unique_id)
+        h = C.c_void_p()
+        _check(lib.gkv_comm_init(buf, n_ranks, rank, device, timeout_ms, C.byref(h)))
+        self._h = h
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = (C.c_uint8 * 128)()
+        _check(lib.gkv_comm_unique_id(buf))
+        return bytes(buf)
+
+    @property
+    def handle(self):
+        return self._h
+
+    def abort(self) -> None:
+        if self._h:
+            lib.gkv_comm_abort(self._h)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib.gkv_comm_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def lse_merge(parts, n_parts: int, rows: int, dv: int, out, sinks=None, n_heads: int = 1, stream=None) -> None:
+    """gkv_lse_merge: parts = n_parts blocks of ([rows, dv] outputs, [rows] lse), float32 CUDA."""
+    import torch
+
+    dev = parts.device.index or 0
+    _check(lib.gkv_lse_merge(_f32_dev(parts, "parts"), n_parts, rows, dv,
+                             None if sinks is None else _f32_dev(sinks, "sinks"), n_heads,
+                             _f32_dev(out, "out"), _stream(stream, dev)))
 
 
 def arena_desc(pool: PagedBlockPool) -> _lib.gkv_arena_desc:

@@ -135,6 +135,13 @@ SIGNATURES = {
     "gkv_pool_last_launch_count": (C.c_int, [P]),
     "gkv_sync": (C.c_int, [P, P, I32]),
     "gkv_plan_decode": (C.c_int, [P, I32, I32, I32, I32, C.POINTER(gkv_plan_info), P, P, P, P, P, I32]),
+    "gkv_paged_decode_lse": (C.c_int, [P, I32, P, P, P, I32, F32, P, P]),
+    "gkv_lse_merge": (C.c_int, [P, I32, I32, I32, P, I32, P, P]),
+    "gkv_comm_unique_id": (C.c_int, [P]),
+    "gkv_comm_init": (C.c_int, [P, I32, I32, I32, I32, C.POINTER(P)]),
+    "gkv_comm_abort": (C.c_int, [P]),
+    "gkv_comm_destroy": (C.c_int, [P]),
+    "gkv_paged_decode_splitkv_dist": (C.c_int, [P, P, I32, P, P, I32, F32, P, P]),
     "gkv_partition_lpt": (C.c_int, [P, I32, I32, P]),
     "gkv_split_block_range": (C.c_int, [I32, I32, I32, PI32, PI32]),
     "gkv_last_error": (C.c_char_p, []),

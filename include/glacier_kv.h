@@ -296,6 +296,40 @@ GKV_API int gkv_partition_lpt(const int32_t* ctx_lens, int32_t n, int32_t n_rank
 GKV_API int gkv_split_block_range(int32_t n_blocks, int32_t n_ranks, int32_t rank,
                                   int32_t* out_begin, int32_t* out_end);
 
+/* Long-context split-KV across GPUs (no reference counterpart: the reference runs one
+ * sequence on one GPU, CudaPagedTransformerRunner.cs:108).  A sequence's block table is
+ * split into contiguous ranges (gkv_split_block_range); each rank uploads its range as the
+ * step (ctx_len = tokens in its range) and calls gkv_paged_decode_splitkv_dist. */
+
+/* gkv_paged_decode plus, per (sequence, query head), the natural-log softmax denominator
+ * lse = ln(sum_t exp(s_t) [+ exp(sink)]) into d_lse [batch][n_heads].  Rows of sequences
+ * with ctx_len 0 are left untouched in both outputs. */
+GKV_API int gkv_paged_decode_lse(gkv_pool* pool, int32_t layer, const float* d_q, float* d_out,
+                                 float* d_lse, int32_t n_heads, float scale, const float* d_sinks,
+                                 void* stream);
+/* Merges n_parts partial decodes of the same rows over disjoint token ranges:
+ * d_parts = n_parts blocks of [rows][dv] outputs followed by [rows] lse (a row of lse
+ * -inf contributes nothing); out[r] = sum_p exp(lse_p - LSE) out_p with
+ * LSE = ln(sum_p exp(lse_p) [+ exp(sink[r % n_heads])]). */
+GKV_API int gkv_lse_merge(const float* d_parts, int32_t n_parts, int32_t rows, int32_t dv,
+                          const float* d_sinks, int32_t n_heads, float* d_out, void* stream);
+/* NCCL communicator of the ranks that split sequences.  The 128-byte id comes from
+ * gkv_comm_unique_id on one rank and reaches the others through the host's own channel.
+ * Initialisation and every later NCCL wait give up after timeout_ms (< 0: never), abort the
+ * communicator and return GKV_ETIMEDOUT instead of hanging. */
+GKV_API int gkv_comm_unique_id(uint8_t* out_id_128);
+GKV_API int gkv_comm_init(const uint8_t* unique_id_128, int32_t n_ranks, int32_t rank,
+                          int32_t device, int32_t timeout_ms, gkv_comm** out_comm);
+GKV_API int gkv_comm_abort(gkv_comm* comm);
+GKV_API int gkv_comm_destroy(gkv_comm* comm);
+/* This rank's share of a split-KV decode: decode of the uploaded step (this rank's block
+ * ranges) with lse, NCCL all-gather of (out, lse) over the ranks, log-sum-exp merge (plus the
+ * optional sinks, applied once) into d_out [batch][n_heads][v_head_dim] on every rank.
+ * All ranks must call it with the same batch and n_heads. */
+GKV_API int gkv_paged_decode_splitkv_dist(gkv_pool* pool, gkv_comm* comm, int32_t layer,
+                                          const float* d_q, float* d_out, int32_t n_heads,
+                                          float scale, const float* d_sinks, void* stream);
+
 /* ---- misc ----------------------------------------------------------------------------- */
 GKV_API const char* gkv_last_error(void);
 /* Build identification, e.g. "glacier_kv 0.1 sm_100a". */
