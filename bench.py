@@ -46,7 +46,7 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def workload(name: str, rank: int):
+def workload(name: str, rank: int, world: int = 1):
     from glacier_kv import workloads as W
 
     seed = W.SEED + 1000003 * rank
@@ -58,8 +58,8 @@ def workload(name: str, rank: int):
         return W.cfg3(seed, "f32")
     if name == "cfg3-bf16":
         return W.cfg3(seed, "bf16")
-    if name == "cfg5":
-        return W.cfg5_local(0, 8, seed)
+    if name == "cfg5":  # this rank's block range of the 4 x 131072 sequences
+        return W.cfg5_local(rank, world, W.SEED)
     raise SystemExit(f"unknown config {name}")
 
 
@@ -260,7 +260,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    w = workload(args.config, rank)
+    w = workload(args.config, rank, world)
     pool = W.make_pool(w, device=local)
     W.fill_arena_randn(pool, seed=w.seed)
     stream = torch.cuda.current_stream(dev)
@@ -278,6 +278,21 @@ def main():
 
     ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
 
+    # long-context split-KV (cfg5) over several GPUs: each rank holds its block range and the
+    # step ends with the NCCL exchange + LSE merge; total work is fixed (strong scaling)
+    split_kv = args.config == "cfg5" and world > 1
+    comm = None
+    if split_kv:
+        uid = [G.Comm.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = G.Comm(uid[0], world, rank, local, timeout_ms=120_000)
+
+    def decode():
+        if split_kv:
+            pool.paged_decode_splitkv_dist(comm, 0, q, out, w.n_heads, w.scale, stream=stream)
+        else:
+            pool.paged_decode(0, q, out, w.n_heads, w.scale, stream=stream)
+
     def step(timed_decode=None):
         pool.upload_step(w.tables, w.ctx_lens, w.slot_mapping, stream=stream)
         launches = 0
@@ -286,7 +301,7 @@ def main():
             launches += pool.last_launch_count
         if timed_decode is not None:
             timed_decode[0].record(stream)
-        pool.paged_decode(0, q, out, w.n_heads, w.scale, stream=stream)
+        decode()
         if timed_decode is not None:
             timed_decode[1].record(stream)
         return launches + pool.last_launch_count
@@ -323,7 +338,8 @@ def main():
     span_ms = t0.elapsed_time(t1) / args.steps
     ms = max_over_ranks(step_ms if flush is not None else span_ms)
     dec_ms = sum(a.elapsed_time(b) for a, b in dec_events) / args.steps
-    value = world * w.batch / (ms / 1e3)
+    seqs_per_step = w.batch if split_kv else world * w.batch  # split-KV: ranks share sequences
+    value = seqs_per_step / (ms / 1e3)
 
     # ---- end-to-end through the C ABI with host buffers ----
     hq = q.cpu().pin_memory()
@@ -335,8 +351,14 @@ def main():
     d2h = hout.numel() * 4
 
     def e2e_step():
-        pool.decode_step_host(0, w.tables, w.ctx_lens, w.slot_mapping, hk, hv, hq, hout, w.n_heads, w.scale,
-                              stream=stream)
+        if split_kv:  # host q in, host output out, around the distributed C-ABI call
+            q.copy_(hq, non_blocking=True)
+            pool.upload_step(w.tables, w.ctx_lens, w.slot_mapping, stream=stream)
+            decode()
+            hout.copy_(out, non_blocking=True)
+        else:
+            pool.decode_step_host(0, w.tables, w.ctx_lens, w.slot_mapping, hk, hv, hq, hout, w.n_heads, w.scale,
+                                  stream=stream)
 
     for _ in range(args.warmup):
         e2e_step()
@@ -359,20 +381,23 @@ def main():
         achieved = alg_bytes / (dec_ms / 1e3) / 1e9
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong" if args.config == "cfg5" else "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) Q/K/V, seeded block tables)",
             "config": {"workload": describe(w),
                        "l2": "L2 flushed (256 MiB write) before every step" if small else
                              f"inputs larger than L2 ({kv_bytes / 1e9:.2f} GB of KV read per step)",
-                       "parallelism": f"sequence-sharded: {world} GPU(s), one pool each, no collective",
+                       "parallelism": (f"split-KV: each sequence's blocks split over {world} GPU(s), NCCL all-gather "
+                                       "of (out, lse) + LSE merge") if split_kv else
+                                      f"sequence-sharded: {world} GPU(s), one pool each, no collective",
                        "step": "upload tables+slots (1 H2D) + kv_append + paged_decode (+ LSE merge)"},
             "kv_gbs_per_gpu": kv_bytes / (ms / 1e3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic_from_profiles(args.config),
-                         "kernel": "paged_decode (split-KV kernel + LSE merge kernel)",
+                         "kernel": "paged_decode (split-KV decode kernel; merge fused or a second launch for long splits)",
                          "bytes_per_launch": alg_bytes, "avg_launch_ms": dec_ms,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s"},
-            "e2e": {"value": world * w.batch / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+            "e2e": {"value": seqs_per_step / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms,
                     "path": "gkv_decode_step_host (pinned host q/K/V/tables in, output out)"},
             "gpu_launches": launches,
@@ -385,6 +410,8 @@ def main():
                 w, steps=max(5, args.steps), budget_s=20.0, threads=O.max_threads(), seed=w.seed).items()
                 if k != "ms_per_sample"}
         print(json.dumps(line), flush=True)
+    if comm is not None:
+        comm.close()
     pool.close()
     if world > 1:
         dist.destroy_process_group()
