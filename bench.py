@@ -196,11 +196,73 @@ def cpu_baseline_run(w, steps: int, budget_s: float, threads: int, seed: int):
     }
 
 
+PREFILL_METRIC = "chunked causal prefill TFLOP/s (causal FLOP count) per B200 vs bf16 tensor peak"
+
+
+def prefill_cpu_baseline(w, steps: int, budget_s: float, threads: int, seed: int, n_q: int = 24):
+    """Times the CPU restatement (oracle/) of the reference's prefill (one ComputeAttention per
+    chunk token, PagedTransformerRunner.cs:454-471) on a bounded sample: the last n_q queries of
+    one sequence's chunk (the heaviest rows), arena restricted to that sequence's blocks."""
+    from oracle import pyoracle as O
+
+    rng = np.random.default_rng(seed)
+    b = int(np.argmax(w.prefix))
+    tok = int(w.token_counts[b])
+    bs = w.block_size
+    nblk = (tok + bs - 1) // bs
+    g = O.geom(nblk, 1, w.heads_kv, w.head_dim, w.v_head_dim, bs, O.BF16)
+    K, V = O.new_arena(g)
+    for arr in (K, V):
+        arr[...] = O.f32_to_bf16_bits(rng.standard_normal(arr.shape, dtype=np.float32))
+    ids = np.arange(nblk, dtype=np.int32)
+    q = rng.standard_normal((n_q, w.n_heads, w.head_dim)).astype(np.float32)
+    start = tok - n_q
+    O.prefill_chunk(K, V, g, 0, ids, tok, start, q, w.n_heads, w.scale, n_threads=threads)  # warm-up
+    times = []
+    t_start = time.perf_counter()
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        O.prefill_chunk(K, V, g, 0, ids, tok, start, q, w.n_heads, w.scale, n_threads=threads)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s:
+            break
+    med = statistics.median(times)
+    flops = 2 * (w.head_dim + w.v_head_dim) * w.n_heads * sum(start + t + 1 for t in range(n_q))
+    return {
+        "value": flops / med / 1e12,
+        "unit": "TFLOP/s",
+        "cores": threads,
+        "kind": "port",
+        "sample": (f"last {n_q} chunk queries of {w.name} sequence {b} (positions {start}..{tok - 1}), "
+                   f"median of {len(times)} runs; one ComputeAttention per query, OpenMP over query heads"),
+        "ms_per_sample": med * 1e3,
+    }
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     from oracle import pyoracle as O
+
+    if args.config == "cfg4":
+        from glacier_kv import workloads as W
+
+        w = W.cfg4(W.SEED)
+        res = prefill_cpu_baseline(w, max(args.steps, 1), budget_s=120.0, threads=O.max_threads(), seed=w.seed)
+        line = {
+            "metric": PREFILL_METRIC, "value": res["value"], "unit": "TFLOP/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": res["ms_per_sample"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
+            "config": {"workload": describe_prefill(w), "l2": "n/a (CPU)",
+                       "implementation": "C restatement of PagedTransformerRunner.ForwardPrefillSubBatch + "
+                                         "PagedAttentionKernel.ComputeAttention"},
+            "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": res["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
+        return
 
     w = workload(args.config, 0)
     threads = O.max_threads()
@@ -217,6 +279,141 @@ def run_reference(args):
         "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def describe_prefill(w) -> str:
+    return (f"{w.name}: append {w.chunk} tokens per sequence + chunked causal prefill, {w.batch} seqs, "
+            f"prefixes {w.prefix.tolist()}, {w.n_heads}q/{w.heads_kv}kv heads, d {w.head_dim}, {w.dtype} Q/K/V, "
+            f"fp32 softmax and output, block {w.block_size}, pool {w.total_blocks} blocks")
+
+
+def tensor_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return float(json.load(open(p))["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+    return 1590.0, "fallback 1.59 PFLOP/s"
+
+
+def run_prefill(args, world, rank, local, dev, barrier, max_over_ranks):
+    """cfg4: one step = upload tables + slots, append the 8 x 2048 chunk tokens, prefill them.
+    Weak scaling: every rank owns a pool and its own 8 sequences."""
+    import torch
+
+    import glacier_kv as G
+    from glacier_kv import workloads as W
+
+    w = W.cfg4(W.SEED + 1000003 * rank)
+    pool = G.PagedBlockPool(w.total_blocks, 1, w.heads_kv, w.head_dim, w.block_size, w.v_head_dim,
+                            device=local, dtype=w.dtype)
+    W.fill_arena_randn(pool, seed=w.seed)
+    stream = torch.cuda.current_stream(dev)
+    rng = np.random.default_rng(w.seed + 17)
+    nq = w.n_queries
+    q = torch.from_numpy(rng.standard_normal((nq, w.n_heads, w.head_dim), dtype=np.float32)).to(dev).to(torch.bfloat16)
+    kn = torch.from_numpy(rng.standard_normal((nq, w.heads_kv, w.head_dim), dtype=np.float32)).to(dev)
+    vn = torch.from_numpy(rng.standard_normal((nq, w.heads_kv, w.v_head_dim), dtype=np.float32)).to(dev)
+    out = torch.empty((nq, w.n_heads, w.v_head_dim), dtype=torch.float32, device=dev)
+    toks, qs, ql = w.token_counts, w.prefix.astype(np.int32), w.q_lens
+    pool.reserve_step(w.batch, w.tables.shape[1], nq, w.n_heads)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+
+    def step(pre_ev=None):
+        pool.upload_step(w.tables, toks, w.slot_mapping, stream=stream)
+        pool.kv_append(0, kn, vn, stream=stream)
+        n = pool.last_launch_count
+        if pre_ev is not None:
+            pre_ev[0].record(stream)
+        pool.paged_prefill(0, q, out, qs, ql, w.n_heads, w.scale, stream=stream)
+        if pre_ev is not None:
+            pre_ev[1].record(stream)
+        return n + pool.last_launch_count
+
+    clk = Clocks(dev)
+    clk.__enter__()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    pre_events = [(ev(), ev()) for _ in range(args.steps)]
+    step_events = [(ev(), ev()) for _ in range(args.steps)]
+    launches = 0
+    barrier()
+    torch.cuda.synchronize(dev)
+    clk.mark(0)
+    for i in range(args.steps):
+        flush.zero_()
+        step_events[i][0].record(stream)
+        launches += step(pre_events[i])
+        step_events[i][1].record(stream)
+    torch.cuda.synchronize(dev)
+    clk.mark(1)
+    clk.__exit__()
+    pool.sync()
+    barrier()
+    step_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in step_events) / args.steps)
+    pre_ms = sum(a.elapsed_time(b) for a, b in pre_events) / args.steps
+    flops = w.flops()
+    value = world * flops / (step_ms / 1e3) / 1e12
+
+    # end to end: pinned host q / new K,V / tables in, attention output out, around the C ABI
+    hq = q.cpu().pin_memory()
+    hk = kn.cpu().pin_memory()
+    hv = vn.cpu().pin_memory()
+    hout = torch.empty(out.shape, dtype=torch.float32).pin_memory()
+    h2d = hq.numel() * 2 + (hk.numel() + hv.numel()) * 4 + w.tables.nbytes + toks.nbytes + w.slot_mapping.nbytes
+    d2h = hout.numel() * 4
+
+    def e2e_step():
+        q.copy_(hq, non_blocking=True)
+        kn.copy_(hk, non_blocking=True)
+        vn.copy_(hv, non_blocking=True)
+        step()
+        hout.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0, e1 = ev(), ev()
+    e0.record(stream)
+    for _ in range(args.steps):
+        flush.zero_()
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    pool.sync()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    barrier()
+    if rank == 0:
+        peak, peak_src = tensor_peak()
+        achieved = flops / (pre_ms / 1e3) / 1e12
+        line = {
+            "metric": PREFILL_METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) Q/K/V, seeded block tables)",
+            "config": {"workload": describe_prefill(w), "l2": "L2 flushed (256 MiB write) before every step",
+                       "parallelism": f"sequence-sharded: {world} GPU(s), one pool each, no collective",
+                       "step": "upload tables+slots (1 H2D) + kv_append (16384 tokens) + paged_prefill",
+                       "flops_per_step_per_gpu": flops, "queries_per_step_per_gpu": nq},
+            "prefill_tokens_per_s": world * nq / (step_ms / 1e3),
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": traffic_from_profiles("cfg4"),
+                         "kernel": "paged_prefill_tc (tcgen05 QK^T and PV, TMEM accumulators)",
+                         "flops_per_launch": flops, "avg_launch_ms": pre_ms, "peak_source": peak_src},
+            "e2e": {"value": world * flops / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms,
+                    "path": "pinned host q/K/V/tables in, C-ABI upload + append + prefill, output out"},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+        }
+        if not args.no_cpu_baseline and world == 1:
+            from oracle import pyoracle as O
+
+            line["cpu_baseline"] = {k: v for k, v in prefill_cpu_baseline(
+                w, steps=max(5, args.steps), budget_s=20.0, threads=O.max_threads(), seed=w.seed).items()
+                if k != "ms_per_sample"}
+        print(json.dumps(line), flush=True)
+    pool.close()
 
 
 def main():
@@ -259,6 +456,12 @@ def main():
         t = torch.tensor([x], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    if args.config == "cfg4":
+        run_prefill(args, world, rank, local, dev, barrier, max_over_ranks)
+        if world > 1:
+            dist.destroy_process_group()
+        return
 
     w = workload(args.config, rank, world)
     pool = W.make_pool(w, device=local)

@@ -14,6 +14,11 @@
 
 namespace gkv {
 
+// Block-table row of sequence b of a work list.
+__device__ __forceinline__ int64_t table_row(const DecodeWork& w, int b) {
+    return w.table_row ? static_cast<int64_t>(__ldg(w.table_row + b)) : static_cast<int64_t>(b);
+}
+
 // Natural-log softmax denominator from a base-2 running max and sum.
 __device__ __forceinline__ float lse_ln(float m2, float l) {
     return (l > 0.f && m2 != -INFINITY) ? (m2 + log2f(l)) * 0.6931471805599453f : -INFINITY;

@@ -97,6 +97,16 @@ struct StepWorkspace {
     DecodeWork work{};
     const int64_t* d_slots = nullptr;
     bool uploaded = false;
+    std::vector<int32_t> h_ctx;  // ctx_lens of the uploaded step
+    // chunked prefill: pinned + device buffer of its work items / work list, and q in the
+    // dtype its kernel reads
+    char* h_pre = nullptr;
+    char* d_pre = nullptr;
+    size_t pre_cap = 0;
+    cudaEvent_t pre_copied = nullptr;
+    bool pre_pending = false;
+    void* d_qconv = nullptr;
+    size_t qconv_cap = 0;
 };
 
 struct Pool {
@@ -157,6 +167,9 @@ int step_decode_lse(Pool* p, int32_t layer, const float* d_q, float* d_out, floa
                     int32_t n_heads, float scale, const float* d_sinks, cudaStream_t st);
 int step_reserve(Pool* p, int32_t max_batch, int32_t max_blocks, int32_t max_tokens,
                  int32_t n_heads);
+int step_prefill(Pool* p, int32_t layer, const void* d_q, int32_t q_dtype, float* d_out,
+                 const int32_t* q_start, const int32_t* q_len, int32_t n_heads, float scale,
+                 cudaStream_t st);
 void step_free(Pool* p);
 
 // Work-list construction (host only; unit-tested through the C ABI helpers).

@@ -67,6 +67,9 @@ struct DecodeWork {
     // when a launch starts; the worker that completes a segment resets its counter, so they
     // are zero again after every launch that ran to completion.
     int32_t* merge_count;
+    // [batch] table row of each sequence, or nullptr for row = sequence.  The prefill over
+    // the decode kernel makes every query of a sequence a sequence of its own on one row.
+    const int32_t* table_row;
 };
 
 struct DecodeArgs {
@@ -114,9 +117,41 @@ cudaError_t launch_deferred_merge(const ArenaGeom& g, const DecodeWork& w, const
 bool decode_tc_eligible(const ArenaGeom& g, int n_heads);
 // Encodes the K and V TMA maps of the arena into two 128-byte, 64-byte aligned buffers.
 bool encode_decode_tmaps(const ArenaGeom& g, void* tmap_k, void* tmap_v);
+// Tiled TMA maps (bf16, 128-byte swizzle, no interleave; `map` is a 64-byte aligned
+// 128-byte CUtensorMap).  encode_arena_map: the 3-D view [block*layer*head][slot][dim] of
+// one arena with boxes of 8 slots x 64 dims.
+bool tmap_encoder_available();
+bool encode_bf16_map3(void* map, const void* base, const uint64_t dims[3], const uint64_t strides[2],
+                      const uint32_t box[3]);
+bool encode_arena_map(void* map, void* base, const ArenaGeom& g, int dim);
 void decode_tc_config(DecodeConfig& c);
 cudaError_t launch_paged_decode_tc(const ArenaGeom& g, const DecodeWork& w, const DecodeArgs& a,
                                    int group, int head_groups, int* launches, cudaStream_t st);
+
+// ---- chunked causal prefill (paged_prefill_tc.cu) ----
+// One work item = up to 128 consecutive queries of one sequence; the kernel runs one CTA per
+// (item, query head).  Item ints: sequence (table row), position of the first query, its
+// row in the packed q / out, query count, keys attended by the item (min(token_count,
+// last position + 1)), token_count, 2 unused.
+constexpr int kPrefillItemInts = 8;
+struct PrefillArgs {
+    const int32_t* items;    // device [n_items][kPrefillItemInts], heaviest first
+    int32_t n_items;
+    const int32_t* tables;   // uploaded block tables [batch][max_blocks]
+    int32_t max_blocks;
+    int32_t layer;
+    int32_t n_heads;
+    float scale;
+    float* out;              // [total_q][n_heads][v_head_dim] fp32
+    int* err;
+};
+// bf16 KV, d = dv = 128, block size a multiple of 8.
+bool prefill_tc_eligible(const ArenaGeom& g, int n_heads);
+// q_bf16: [total_q][n_heads][128] bf16, 16-byte aligned.
+cudaError_t launch_paged_prefill_tc(const ArenaGeom& g, const PrefillArgs& a, const void* q_bf16,
+                                    int64_t total_q, cudaStream_t st);
+cudaError_t launch_f32_to_bf16(const float* src, void* dst, int64_t n, cudaStream_t st);
+cudaError_t launch_bf16_to_f32(const void* src, float* dst, int64_t n, cudaStream_t st);
 
 // Enqueues the split-KV decode (the cross-worker merge is fused into it).  *launches
 // receives the number of kernels enqueued.

@@ -198,7 +198,7 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
         int page, tok0, ntok;
         chunk_geom(p_c0 + p_j, p_ctx, page, tok0, ntok);
         if (lane == 0) {
-            const int64_t blk = __ldg(w.tables + static_cast<int64_t>(p_b) * w.max_blocks + page);
+            const int64_t blk = __ldg(w.tables + table_row(w, p_b) * w.max_blocks + page);
             uint64_t* bar = &my_bars[st];
             if (blk >= 0 && blk < g.total_blocks && ntok > 0) {
                 const uint32_t kb = static_cast<uint32_t>(ntok * D * Tr::EB);
@@ -277,7 +277,7 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
             const uint32_t ph = static_cast<uint32_t>(ck / S) & 1u;
             int page, tok0, ntok;
             chunk_geom(c0 + j, ctx, page, tok0, ntok);
-            const int64_t blk = __ldg(w.tables + static_cast<int64_t>(b) * w.max_blocks + page);
+            const int64_t blk = __ldg(w.tables + table_row(w, b) * w.max_blocks + page);
             if (!dead && !mbar_wait(&my_bars[st], ph)) {
                 dead = true;
                 if (lane == 0 && a.err) atomicOr(a.err, kErrWaitTimeout);

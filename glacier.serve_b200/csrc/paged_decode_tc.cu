@@ -103,7 +103,7 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_tc_kernel(
         int page, tok0, ntok;
         chunk_geom(p_c0 + p_j, p_ctx, page, tok0, ntok);
         if (lane == 0) {
-            const int64_t blk = __ldg(w.tables + static_cast<int64_t>(p_b) * w.max_blocks + page);
+            const int64_t blk = __ldg(w.tables + table_row(w, p_b) * w.max_blocks + page);
             uint64_t* bar = &my_bars[st];
             if (blk >= 0 && blk < g.total_blocks && ntok > 0) {
                 const int z = static_cast<int>((blk * g.layers + a.layer) * g.heads_kv + p_h);
@@ -176,7 +176,7 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_tc_kernel(
             const uint32_t ph = static_cast<uint32_t>(ck / S) & 1u;
             int page, tok0, ntok;
             chunk_geom(c0 + j, ctx, page, tok0, ntok);
-            const int64_t blk = __ldg(w.tables + static_cast<int64_t>(b) * w.max_blocks + page);
+            const int64_t blk = __ldg(w.tables + table_row(w, b) * w.max_blocks + page);
             if (!dead && !mbar_wait(&my_bars[st], ph)) {
                 dead = true;
                 if (lane == 0 && a.err) atomicOr(a.err, kErrWaitTimeout);
@@ -331,36 +331,6 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_tc_kernel(
 
 constexpr size_t kTcSmem = static_cast<size_t>(kNW) * kS * kStage + kNW * kS * 8 + 1024;
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-        else
-            cudaGetLastError();
-    });
-    return fn;
-}
-
-// 3-D view [block * layer * head][slot][dim] of one bf16 arena, boxes of 8 slots x 64 dims.
-bool encode_arena_map(CUtensorMap* m, void* base, const ArenaGeom& g, int dim) {
-    auto fn = encode_fn();
-    if (!fn) return false;
-    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(dim), static_cast<cuuint64_t>(g.block_size),
-                                static_cast<cuuint64_t>(g.total_blocks) * g.layers * g.heads_kv};
-    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(dim) * 2,
-                                   static_cast<cuuint64_t>(g.block_size) * dim * 2};
-    const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(kChunk), 1};
-    const cuuint32_t estr[3] = {1, 1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 cudaError_t tc_prepare() {
     static std::atomic<uint64_t> done_mask{0};
     int dev = 0;
@@ -376,6 +346,45 @@ cudaError_t tc_prepare() {
 
 }  // namespace
 
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
+bool tmap_encoder_available() { return encode_fn() != nullptr; }
+
+bool encode_bf16_map3(void* map, const void* base, const uint64_t dims[3], const uint64_t strides[2],
+                      const uint32_t box[3]) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+    const cuuint64_t s[2] = {strides[0], strides[1]};
+    const cuuint32_t b[3] = {box[0], box[1], box[2]};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return fn(static_cast<CUtensorMap*>(map), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), d, s,
+              b, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 3-D view [block * layer * head][slot][dim] of one bf16 arena, boxes of 8 slots x 64 dims.
+bool encode_arena_map(void* map, void* base, const ArenaGeom& g, int dim) {
+    const uint64_t dims[3] = {static_cast<uint64_t>(dim), static_cast<uint64_t>(g.block_size),
+                              static_cast<uint64_t>(g.total_blocks) * g.layers * g.heads_kv};
+    const uint64_t strides[2] = {static_cast<uint64_t>(dim) * 2, static_cast<uint64_t>(g.block_size) * dim * 2};
+    const uint32_t box[3] = {64, static_cast<uint32_t>(kDecodeChunk), 1};
+    return encode_bf16_map3(map, base, dims, strides, box);
+}
+
 bool encode_decode_tmaps(const ArenaGeom& g, void* tmap_k, void* tmap_v) {
     return encode_arena_map(static_cast<CUtensorMap*>(tmap_k), g.k, g, kD) &&
            encode_arena_map(static_cast<CUtensorMap*>(tmap_v), g.v, g, kDV);
@@ -388,7 +397,7 @@ bool decode_tc_eligible(const ArenaGeom& g, int n_heads) {
     if (group < 5) return false;  // gp 8 only; smaller groups are HBM-bound on the FP32 pipe
     if ((reinterpret_cast<uintptr_t>(g.k) | reinterpret_cast<uintptr_t>(g.v)) & 15) return false;
     const int64_t rows = static_cast<int64_t>(g.total_blocks) * g.layers * g.heads_kv;
-    return rows < (int64_t{1} << 31) && encode_fn() != nullptr;
+    return rows < (int64_t{1} << 31) && tmap_encoder_available();
 }
 
 void decode_tc_config(DecodeConfig& c) {

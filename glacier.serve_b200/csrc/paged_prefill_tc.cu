@@ -1,0 +1,446 @@
+// Chunked causal prefill over the paged arena on the 5th-generation tensor cores (tcgen05,
+// accumulators in tensor memory).
+//
+// The reference's CPU runner attends a prefill chunk one query at a time
+// (PagedTransformerRunner.ForwardPrefillSubBatch, PagedTransformerRunner.cs:424-471): the
+// chunk's K/V are stored first, then query t runs ComputeAttention with pos = start + t,
+// whose causal length is min(TokenCount, pos + 1) (PagedAttentionKernel.cs:41).  Here one
+// CTA takes 128 consecutive queries of one (sequence, query head) and streams the
+// sequence's pages in tiles of 64 keys:
+//
+//  * warp 4 (TMA producer): the Q tile once (two boxes of 128 rows x 64 dims), then per key
+//    tile 8 chunks of 8 keys x 2 dim halves of K, and the same of V, gathered from the arena
+//    through the block table with tiled cp.async.bulk.tensor (128-byte swizzle, no
+//    multicast) into 2-stage K and V rings.
+//  * warp 5 (one thread issues): S = Q K^T (M=128, N=64, K=128: 8 tcgen05.mma kind::f16,
+//    both operands K-major in shared memory) into one of two TMEM S buffers, then
+//    O += P V (M=128, N=128, K=64: 4 MMAs, P read from TMEM, V MN-major in shared memory).
+//    S of tile j+1 is issued before P V of tile j, so the tensor pipe works while the
+//    softmax runs.
+//  * warps 0-3 (query row r = thread r = TMEM lane r): load S, causal mask, base-2 online
+//    softmax with lazy rescaling (O in TMEM is rescaled only when the running max grows by
+//    more than 8, so P stays <= 2^8), P as bf16 written back over its own S columns.
+//    Epilogue: O / l through shared memory as coalesced fp32 rows.
+//
+// Two CTAs share an SM (96 KB shared memory and 256 TMEM columns each), so one CTA's softmax
+// overlaps the other's MMAs.  Every mbarrier wait is bounded: on expiry the CTA raises
+// kErrWaitTimeout, lets its copies and MMAs finish and frees its TMEM.
+#include <cuda.h>
+
+#include <atomic>
+#include <cmath>
+
+#include "gkv_device.cuh"
+#include "kernels.h"
+#include "../../include/glacier_kv.h"
+
+namespace gkv {
+
+namespace {
+
+constexpr int kBM = 128;                           // query rows per CTA
+constexpr int kBN = 64;                            // keys per tile
+constexpr int kD = 128;                            // head_dim = v_head_dim
+constexpr int kThreads = 192;                      // 4 softmax warps, producer, MMA
+constexpr uint32_t kQBytes = kBM * kD * 2;         // 32 KB
+constexpr uint32_t kQHalf = kQBytes / 2;           // 128 rows x 128 B (64 dims)
+constexpr uint32_t kTile = kBN * kD * 2;           // 16 KB: one K or V tile
+constexpr uint32_t kHalf = kTile / 2;              // 64 rows x 128 B
+constexpr uint32_t kTmemCols = 256;                // S0 [0,64) S1 [64,128) O [128,256)
+constexpr uint32_t kColO = 128;
+constexpr size_t kSmemData = kQBytes + 4 * kTile;  // Q + 2 K stages + 2 V stages = 96 KB
+constexpr size_t kSmem = kSmemData + 256 + 1024;   // + barriers + 1024-byte alignment slack
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleLog2 = 8.f;
+
+// Instruction descriptor of tcgen05.mma kind::f16 with bf16 A and B, fp32 D, A K-major.
+constexpr uint32_t idesc_bf16(int m, int n, bool b_mn_major) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+           (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// One key tile (64 keys from key0, fewer at the end) of K or V: chunk c of 8 keys lands at
+// dst + c*1 KB (dims 0-63) and dst + 8 KB + c*1 KB (dims 64-127); 1 KB = one swizzle atom.
+__device__ __forceinline__ void load_kv_tile(uint8_t* dst, const CUtensorMap* tm, uint64_t* full, int key0,
+                                             int n_keys, const int32_t* trow, const ArenaGeom& g, int layer,
+                                             int hkv, int* err) {
+    int nch = (n_keys - key0 + 7) >> 3;
+    if (nch > kBN / 8) nch = kBN / 8;
+    mbar_arrive_expect_tx(full, static_cast<uint32_t>(nch) * 2048u);
+    for (int c = 0; c < nch; ++c) {
+        const int key = key0 + c * 8;
+        const int page = key / g.block_size;
+        const int slot = key - page * g.block_size;
+        int blk = __ldg(trow + page);
+        if (blk < 0 || blk >= g.total_blocks) {  // validated on the host; never dereference it
+            atomicOr(err, kErrBadBlock);
+            blk = 0;
+        }
+        const int z = static_cast<int>((static_cast<int64_t>(blk) * g.layers + layer) * g.heads_kv + hkv);
+        tma_load_3d(dst + c * 1024, tm, 0, slot, z, full);
+        tma_load_3d(dst + kHalf + c * 1024, tm, 64, slot, z, full);
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 2)
+    paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                            const __grid_constant__ CUtensorMap tmv, const ArenaGeom g, const PrefillArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t{1023});
+    uint8_t* sQ = smem;
+    uint8_t* sK = smem + kQBytes;
+    uint8_t* sV = sK + 2 * kTile;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sV + 2 * kTile);
+    uint64_t* q_full = bar;
+    uint64_t* k_full = bar + 1;   // [2] per stage
+    uint64_t* k_empty = bar + 3;  // [2]
+    uint64_t* v_full = bar + 5;   // [2]
+    uint64_t* v_empty = bar + 7;  // [2]
+    uint64_t* s_full = bar + 9;   // [2] per S buffer
+    uint64_t* p_full = bar + 11;  // [2]
+    uint64_t* pv_done = bar + 13; // [2]
+    uint64_t* drained = bar + 15;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 16);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 17);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int item = blockIdx.x / a.n_heads;
+    const int h = blockIdx.x - item * a.n_heads;
+    const int32_t* it = a.items + static_cast<int64_t>(item) * kPrefillItemInts;
+    const int seq = __ldg(it + 0), qpos0 = __ldg(it + 1), qrow0 = __ldg(it + 2);
+    const int n_q = __ldg(it + 3), n_keys = __ldg(it + 4), tok = __ldg(it + 5);
+    const int n_tiles = (n_keys + kBN - 1) / kBN;
+    const int hkv = h / (a.n_heads / g.heads_kv);
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(k_full + s, 1);
+            mbar_init(k_empty + s, 1);
+            mbar_init(v_full + s, 1);
+            mbar_init(v_empty + s, 1);
+            mbar_init(s_full + s, 1);
+            mbar_init(p_full + s, kBM);
+            mbar_init(pv_done + s, 1);
+        }
+        mbar_init(drained, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 5) tmem_alloc(tmem_slot, kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tmem_slot;
+
+    if (warp == 4) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            uint32_t armed_k[2] = {0, 0}, armed_v[2] = {0, 0};
+            const int32_t* trow = a.tables + static_cast<int64_t>(seq) * a.max_blocks;
+            mbar_arrive_expect_tx(q_full, kQBytes);
+            tma_load_3d(sQ, &tmq, 0, h, qrow0, q_full);
+            tma_load_3d(sQ + kQHalf, &tmq, 64, h, qrow0, q_full);
+            for (int j = 0; j < n_tiles; ++j) {
+                const int s = j & 1;
+                const uint32_t par = ((j >> 1) & 1) ^ 1;
+                if (j >= 2 && !mbar_wait(k_empty + s, par)) {
+                    atomicOr(a.err, kErrWaitTimeout);
+                    *abort_flag = 1;
+                }
+                if (*abort_flag) break;
+                load_kv_tile(sK + s * kTile, &tmk, k_full + s, j * kBN, n_keys, trow, g, a.layer, hkv, a.err);
+                ++armed_k[s];
+                if (j >= 2 && !mbar_wait(v_empty + s, par)) {
+                    atomicOr(a.err, kErrWaitTimeout);
+                    *abort_flag = 1;
+                }
+                if (*abort_flag) break;
+                load_kv_tile(sV + s * kTile, &tmv, v_full + s, j * kBN, n_keys, trow, g, a.layer, hkv, a.err);
+                ++armed_v[s];
+            }
+            if (*abort_flag) {
+                // every armed copy must land before the CTA's shared memory goes away
+                mbar_wait(q_full, 0);
+                for (int s = 0; s < 2; ++s) {
+                    if (armed_k[s]) mbar_wait(k_full + s, (armed_k[s] - 1) & 1);
+                    if (armed_v[s]) mbar_wait(v_full + s, (armed_v[s] - 1) & 1);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 5) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t kIdS = idesc_bf16(kBM, kBN, false);
+            constexpr uint32_t kIdO = idesc_bf16(kBM, kD, true);
+            const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+            bool ok = mbar_wait(q_full, 0);
+            tc_fence_after();
+            for (int j = 0; ok && j <= n_tiles; ++j) {
+                if (*abort_flag) break;
+                if (j < n_tiles) {
+                    const int b = j & 1;
+                    // S buffer b last held P of tile j-2: its P V must be complete
+                    if (j >= 2 && !(ok = mbar_wait(pv_done + b, ((j - 2) >> 1) & 1))) break;
+                    if (!(ok = mbar_wait(k_full + b, (j >> 1) & 1))) break;
+                    tc_fence_after();
+                    const uint32_t kb = k_addr + b * kTile;
+#pragma unroll
+                    for (int kk = 0; kk < kD / 16; ++kk) {
+                        const uint64_t da = umma_desc_sw128(q_addr + (kk >> 2) * kQHalf + (kk & 3) * 32, 16, 1024);
+                        const uint64_t db = umma_desc_sw128(kb + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+                        umma_f16(tbase + b * kBN, da, db, kIdS, kk > 0 ? 1u : 0u);
+                    }
+                    umma_commit(s_full + b);
+                    umma_commit(k_empty + b);
+                }
+                if (j >= 1) {
+                    const int jj = j - 1, b = jj & 1;
+                    if (!(ok = mbar_wait(p_full + b, (jj >> 1) & 1))) break;
+                    if (!(ok = mbar_wait(v_full + b, (jj >> 1) & 1))) break;
+                    tc_fence_after();
+                    const uint32_t vb = v_addr + b * kTile;
+#pragma unroll
+                    for (int kk = 0; kk < kBN / 16; ++kk) {
+                        // V tile [key][dv]: MN-major, 8-key groups 1 KB apart (SBO), dv 64-127
+                        // in the second half (LBO)
+                        const uint64_t dv = umma_desc_sw128(vb + kk * 2048, kHalf, 1024);
+                        umma_f16_ts(tbase + kColO, tbase + b * kBN + kk * 8, dv, kIdO,
+                                    (jj > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    umma_commit(pv_done + b);
+                    umma_commit(v_empty + b);
+                }
+            }
+            if (!ok) {
+                atomicOr(a.err, kErrWaitTimeout);
+                *abort_flag = 1;
+            }
+            umma_commit(drained);  // all MMAs of this CTA complete before TMEM is freed
+            if (!mbar_wait(drained, 0)) atomicOr(a.err, kErrWaitTimeout);
+        }
+        __syncwarp();
+    } else {
+        // ---------------- softmax + epilogue (row r) ----------------
+        const int r = threadIdx.x;
+        const uint32_t t_lane = tbase + (static_cast<uint32_t>(warp * 32) << 16);
+        const int qpos = qpos0 + r;
+        const int limit = min(tok, qpos + 1);  // keys [0, limit) are visible to this row
+        const float sl = a.scale * kLog2e;
+        const int tail = n_keys - (n_tiles - 1) * kBN;  // valid keys of the last tile
+        float m_run = -INFINITY, l_run = 0.f;
+        bool ok = true;
+        for (int j = 0; j < n_tiles; ++j) {
+            if (__any_sync(~0u, *abort_flag != 0)) {
+                ok = false;
+                break;
+            }
+            const int b = j & 1;
+            if (!__all_sync(~0u, mbar_wait(s_full + b, (j >> 1) & 1))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            uint32_t s0[32], s1[32];
+            tmem_ld32(t_lane + b * kBN, s0);
+            tmem_ld32(t_lane + b * kBN + 32, s1);
+            tmem_wait_ld();
+            float x[kBN];
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+                x[c] = __uint_as_float(s0[c]) * sl;
+                x[c + 32] = __uint_as_float(s1[c]) * sl;
+            }
+            const int kb = j * kBN;
+            if (kb + kBN > limit) {
+#pragma unroll
+                for (int c = 0; c < kBN; ++c) x[c] = (kb + c < limit) ? x[c] : -INFINITY;
+            }
+            float mt = x[0];
+#pragma unroll
+            for (int c = 1; c < kBN; ++c) mt = fmaxf(mt, x[c]);
+            const bool need = mt > m_run + kRescaleLog2;
+            float alpha = 1.f;
+            if (need) {
+                alpha = fast_exp2(m_run - mt);  // 0 on the first tile (m_run = -inf)
+                m_run = mt;
+                l_run *= alpha;
+            }
+            uint32_t pk[32];
+            float sum = 0.f;
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+                const float p0 = fast_exp2(x[2 * c] - m_run);
+                const float p1 = fast_exp2(x[2 * c + 1] - m_run);
+                sum += p0 + p1;
+                pk[c] = pack_bf16x2(p0, p1);
+            }
+            l_run += sum;
+            if (j == n_tiles - 1 && tail < kBN) {
+                // keys past n_keys were never loaded (or are unwritten slots): zero their V
+                // rows so that P = 0 never meets a non-finite value in the MMA
+                if (!__all_sync(~0u, mbar_wait(v_full + b, (j >> 1) & 1))) {
+                    ok = false;
+                    break;
+                }
+                const int row = r & (kBN - 1);
+                if (row >= tail) {
+                    uint4* dst = reinterpret_cast<uint4*>(sV + b * kTile + (r >> 6) * kHalf + (row >> 3) * 1024 +
+                                                          (row & 7) * 128);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) dst[i] = make_uint4(0, 0, 0, 0);
+                }
+                fence_proxy_async_smem();
+            }
+            tmem_st32(t_lane + b * kBN, pk);  // P over the first 32 columns of its S buffer
+            if (j > 0 && __any_sync(~0u, need)) {
+                // O holds P V up to tile j-1: wait for it, then rescale the rows that need it
+                if (!__all_sync(~0u, mbar_wait(pv_done + ((j - 1) & 1), ((j - 1) >> 1) & 1))) {
+                    tmem_wait_st();
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll 1
+                for (int c4 = 0; c4 < kD / 32; ++c4) {
+                    uint32_t o[32];
+                    tmem_ld32(t_lane + kColO + c4 * 32, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                    tmem_st32(t_lane + kColO + c4 * 32, o);
+                }
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(p_full + b);
+        }
+        if (!ok) {
+            atomicOr(a.err, kErrWaitTimeout);
+            *abort_flag = 1;
+        } else if (!__all_sync(~0u, mbar_wait(pv_done + ((n_tiles - 1) & 1), ((n_tiles - 1) >> 1) & 1))) {
+            atomicOr(a.err, kErrWaitTimeout);
+            *abort_flag = 1;
+        } else {
+            tc_fence_after();
+            // all MMAs and copies are complete: the K/V rings (64 KB) become the staging area,
+            // 16 KB = 32 rows x 512 B per warp, 16-byte chunks XOR-swizzled by row
+            const float inv = 1.f / l_run;
+            uint8_t* stage = sK + warp * (32 * 512);
+#pragma unroll 1
+            for (int c4 = 0; c4 < kD / 32; ++c4) {
+                uint32_t o[32];
+                tmem_ld32(t_lane + kColO + c4 * 32, o);
+                tmem_wait_ld();
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const int ch = c4 * 8 + q;
+                    const float4 v = make_float4(__uint_as_float(o[4 * q]) * inv, __uint_as_float(o[4 * q + 1]) * inv,
+                                                 __uint_as_float(o[4 * q + 2]) * inv,
+                                                 __uint_as_float(o[4 * q + 3]) * inv);
+                    *reinterpret_cast<float4*>(stage + lane * 512 + ((ch ^ (lane & 7)) << 4)) = v;
+                }
+            }
+            __syncwarp();
+#pragma unroll 4
+            for (int rr = 0; rr < 32; ++rr) {
+                const int t = warp * 32 + rr;
+                if (t < n_q) {
+                    const float4 v = *reinterpret_cast<const float4*>(stage + rr * 512 + ((lane ^ (rr & 7)) << 4));
+                    float* dst = a.out + (static_cast<int64_t>(qrow0 + t) * a.n_heads + h) * kD + lane * 4;
+                    __stcs(reinterpret_cast<float4*>(dst), v);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc(tbase, kTmemCols);
+    }
+}
+
+__global__ void f32_to_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, int64_t n) {
+    const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+    if (i + 3 < n) {
+        const float4 v = *reinterpret_cast<const float4*>(src + i);
+        __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+        *reinterpret_cast<__nv_bfloat162*>(dst + i) = lo;
+        *reinterpret_cast<__nv_bfloat162*>(dst + i + 2) = hi;
+    } else {
+        for (int64_t k = i; k < n; ++k) dst[k] = __float2bfloat16_rn(src[k]);
+    }
+}
+
+__global__ void bf16_to_f32_kernel(const __nv_bfloat16* __restrict__ src, float* __restrict__ dst, int64_t n) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) dst[i] = __bfloat162float(src[i]);
+}
+
+cudaError_t prefill_prepare() {
+    static std::atomic<uint64_t> done_mask{0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = 1ull << (dev & 63);
+    if (done_mask.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    e = cudaFuncSetAttribute(paged_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmem));
+    if (e == cudaSuccess) done_mask.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
+}
+
+}  // namespace
+
+bool prefill_tc_eligible(const ArenaGeom& g, int n_heads) {
+    if (g.dtype != GKV_DTYPE_BF16 || g.head_dim != kD || g.v_head_dim != kD) return false;
+    if (g.block_size % 8 != 0 || g.heads_kv <= 0 || n_heads <= 0 || n_heads % g.heads_kv != 0) return false;
+    if ((reinterpret_cast<uintptr_t>(g.k) | reinterpret_cast<uintptr_t>(g.v)) & 15) return false;
+    const int64_t rows = static_cast<int64_t>(g.total_blocks) * g.layers * g.heads_kv;
+    return rows < (int64_t{1} << 31) && tmap_encoder_available();
+}
+
+cudaError_t launch_f32_to_bf16(const float* src, void* dst, int64_t n, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    const int64_t quads = (n + 3) / 4;
+    const unsigned grid = static_cast<unsigned>((quads + 255) / 256);
+    f32_to_bf16_kernel<<<grid, 256, 0, st>>>(src, static_cast<__nv_bfloat16*>(dst), n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_bf16_to_f32(const void* src, float* dst, int64_t n, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    bf16_to_f32_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(src), dst, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_paged_prefill_tc(const ArenaGeom& g, const PrefillArgs& a, const void* q_bf16,
+                                    int64_t total_q, cudaStream_t st) {
+    if (a.n_items <= 0) return cudaSuccess;
+    alignas(64) CUtensorMap mq;
+    alignas(64) CUtensorMap ek;
+    alignas(64) CUtensorMap ev;
+    const uint64_t dims[3] = {static_cast<uint64_t>(kD), static_cast<uint64_t>(a.n_heads),
+                              static_cast<uint64_t>(total_q)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(kD) * 2, static_cast<uint64_t>(a.n_heads) * kD * 2};
+    const uint32_t box[3] = {64, 1, static_cast<uint32_t>(kBM)};
+    if (!encode_bf16_map3(&mq, q_bf16, dims, strides, box)) return cudaErrorInvalidValue;
+    const CUtensorMap* tk = static_cast<const CUtensorMap*>(g.tmap_k);
+    const CUtensorMap* tv = static_cast<const CUtensorMap*>(g.tmap_v);
+    if (!tk || !tv) {
+        if (!encode_arena_map(&ek, g.k, g, kD) || !encode_arena_map(&ev, g.v, g, kD)) return cudaErrorInvalidValue;
+        tk = &ek;
+        tv = &ev;
+    }
+    cudaError_t e = prefill_prepare();
+    if (e != cudaSuccess) return e;
+    const int64_t grid = static_cast<int64_t>(a.n_items) * a.n_heads;
+    if (grid > 0x7fffffff) return cudaErrorInvalidValue;
+    paged_prefill_tc_kernel<<<static_cast<unsigned>(grid), kThreads, kSmem, st>>>(mq, *tk, *tv, g, a);
+    return cudaGetLastError();
+}
+
+}  // namespace gkv

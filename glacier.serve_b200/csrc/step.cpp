@@ -248,6 +248,13 @@ void step_free(Pool* p) {
     if (ws.d_out) cudaFree(ws.d_out);
     if (ws.d_knew) cudaFree(ws.d_knew);
     if (ws.d_vnew) cudaFree(ws.d_vnew);
+    if (ws.pre_copied) cudaEventDestroy(ws.pre_copied);
+    if (ws.h_pre) cudaFreeHost(ws.h_pre);
+    if (ws.d_pre) cudaFree(ws.d_pre);
+    if (ws.d_qconv) cudaFree(ws.d_qconv);
+    ws.pre_copied = nullptr;
+    ws.h_pre = ws.d_pre = nullptr;
+    ws.d_qconv = nullptr;
     ws.meta_copied = nullptr;
     ws.h_meta = ws.d_meta = nullptr;
     ws.d_part_acc = ws.d_part_ml = nullptr;
@@ -356,7 +363,9 @@ int step_upload(Pool* p, const int32_t* tables, int32_t batch, int32_t max_block
     w.merge_deferred = reinterpret_cast<const int32_t*>(d + L.mdef);
     w.n_deferred = static_cast<int32_t>(W.merge_deferred.size());
     w.merge_count = ws.d_merge_count;
+    w.table_row = nullptr;
     ws.d_slots = reinterpret_cast<const int64_t*>(d + L.slots);
+    ws.h_ctx.assign(ctx_lens, ctx_lens + batch);
     ws.batch = batch;
     ws.n_tok = n_tok;
     ws.up_max_blocks = max_blocks;
@@ -443,6 +452,254 @@ int step_decode_lse(Pool* p, int32_t layer, const float* d_q, float* d_out, floa
     return decode_common(p, layer, d_q, d_out, n_heads, scale, d_sinks, false, 0.f, st, d_lse);
 }
 
+// ---- chunked causal prefill ------------------------------------------------------------
+
+namespace {
+
+constexpr int kPrefillRows = 128;  // queries per tensor-core work item
+
+// Copies `bytes` of host data into the prefill device buffer (one pinned staging copy).
+int stage_prefill(Pool* p, const std::vector<char>& host, cudaStream_t st) {
+    StepWorkspace& ws = p->ws;
+    if (!ws.pre_copied) {
+        cudaError_t e = cudaEventCreateWithFlags(&ws.pre_copied, cudaEventDisableTiming);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
+    }
+    if (ws.pre_pending) {
+        cudaError_t e = cudaEventSynchronize(ws.pre_copied);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaEventSynchronize(prefill metadata)");
+        ws.pre_pending = false;
+    }
+    if (host.size() > ws.pre_cap) {
+        if (ws.h_pre) cudaFreeHost(ws.h_pre);
+        if (ws.d_pre) cudaFree(ws.d_pre);
+        ws.h_pre = ws.d_pre = nullptr;
+        ws.pre_cap = 0;
+        const size_t cap = align_up(host.size(), 4096);
+        cudaError_t e = cudaMallocHost(&ws.h_pre, cap);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMallocHost(prefill metadata)");
+        e = cudaMalloc(&ws.d_pre, cap);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(prefill metadata)");
+        ws.pre_cap = cap;
+    }
+    if (host.empty()) return GKV_OK;
+    memcpy(ws.h_pre, host.data(), host.size());
+    cudaError_t e = cudaMemcpyAsync(ws.d_pre, ws.h_pre, host.size(), cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(prefill metadata)");
+    e = cudaEventRecord(ws.pre_copied, st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord(prefill metadata)");
+    ws.pre_pending = true;
+    return GKV_OK;
+}
+
+int ensure_qconv(Pool* p, size_t bytes) {
+    StepWorkspace& ws = p->ws;
+    if (bytes <= ws.qconv_cap) return GKV_OK;
+    if (ws.d_qconv) cudaFree(ws.d_qconv);
+    ws.d_qconv = nullptr;
+    ws.qconv_cap = 0;
+    cudaError_t e = cudaMalloc(&ws.d_qconv, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(prefill q conversion)");
+    ws.qconv_cap = bytes;
+    return GKV_OK;
+}
+
+template <class T>
+void put_vec(std::vector<char>& buf, size_t off, const std::vector<T>& v) {
+    if (!v.empty()) memcpy(buf.data() + off, v.data(), v.size() * sizeof(T));
+}
+
+}  // namespace
+
+int step_prefill(Pool* p, int32_t layer, const void* d_q, int32_t q_dtype, float* d_out,
+                 const int32_t* q_start, const int32_t* q_len, int32_t n_heads, float scale,
+                 cudaStream_t st) {
+    StepWorkspace& ws = p->ws;
+    if (!ws.uploaded) return set_error(GKV_ESTATE, "no step uploaded (call gkv_upload_step first)");
+    if (layer < 0 || layer >= p->desc.layers)
+        return set_error(GKV_EINVAL, "layer %d outside [0, %d)", layer, p->desc.layers);
+    if (n_heads <= 0 || n_heads % p->desc.heads_kv != 0)
+        return set_error(GKV_EINVAL, "n_heads %d is not a positive multiple of heads_kv %d", n_heads,
+                         p->desc.heads_kv);
+    if (q_dtype != GKV_DTYPE_F32 && q_dtype != GKV_DTYPE_BF16)
+        return set_error(GKV_EINVAL, "q_dtype %d is neither GKV_DTYPE_F32 nor GKV_DTYPE_BF16", q_dtype);
+    const int32_t batch = ws.batch;
+    if (batch > 0 && (!q_start || !q_len)) return set_error(GKV_EINVAL, "q_start/q_len is NULL");
+    const int64_t max_seq = static_cast<int64_t>(ws.up_max_blocks) * p->desc.block_size;
+    int64_t total_q = 0;
+    for (int32_t b = 0; b < batch; ++b) {
+        if (q_len[b] < 0 || q_start[b] < 0)
+            return set_error(GKV_EINVAL, "sequence %d: negative q_start %d / q_len %d", b, q_start[b], q_len[b]);
+        // ComputeAttention throws for pos >= maxSeqLen (PagedAttentionKernel.cs:34-39)
+        if (q_len[b] > 0 && static_cast<int64_t>(q_start[b]) + q_len[b] > max_seq)
+            return set_error(GKV_EINVAL, "sequence %d: positions up to %lld reach the table capacity %lld", b,
+                             static_cast<long long>(q_start[b]) + q_len[b] - 1, static_cast<long long>(max_seq));
+        total_q += q_len[b];
+    }
+    if (total_q > 0 && (!d_q || !d_out)) return set_error(GKV_EINVAL, "q/out is NULL");
+    if (total_q * n_heads >= (int64_t{1} << 31))
+        return set_error(GKV_EINVAL, "%lld query rows exceed the supported size", static_cast<long long>(total_q));
+    int rc = p->flush_copies(st);
+    if (rc != GKV_OK) return rc;
+    if (total_q == 0) return GKV_OK;
+    const int64_t q_elems = total_q * n_heads * p->desc.head_dim;
+
+    if (prefill_tc_eligible(p->geom, n_heads)) {
+        // work items of up to 128 queries, heaviest first (longest key range)
+        std::vector<int32_t> items;
+        std::vector<std::pair<int32_t, int32_t>> order;  // (-n_keys, item)
+        int64_t q_off = 0;
+        for (int32_t b = 0; b < batch; ++b) {
+            const int32_t tok = ws.h_ctx[static_cast<size_t>(b)];
+            for (int32_t t0 = 0; t0 < q_len[b]; t0 += kPrefillRows) {
+                const int32_t nq = std::min(kPrefillRows, q_len[b] - t0);
+                const int64_t last = static_cast<int64_t>(q_start[b]) + t0 + nq - 1;
+                const int32_t n_keys = static_cast<int32_t>(std::min<int64_t>(tok, last + 1));
+                if (n_keys <= 0) continue;  // no keys: the reference leaves these rows alone
+                const int32_t id = static_cast<int32_t>(order.size());
+                order.emplace_back(-n_keys, id);
+                const int32_t rec[kPrefillItemInts] = {b, q_start[b] + t0, static_cast<int32_t>(q_off + t0), nq,
+                                                       n_keys, tok, 0, 0};
+                items.insert(items.end(), rec, rec + kPrefillItemInts);
+            }
+            q_off += q_len[b];
+        }
+        std::stable_sort(order.begin(), order.end());
+        std::vector<char> host(order.size() * kPrefillItemInts * 4);
+        for (size_t i = 0; i < order.size(); ++i)
+            memcpy(host.data() + i * kPrefillItemInts * 4,
+                   items.data() + static_cast<size_t>(order[i].second) * kPrefillItemInts, kPrefillItemInts * 4);
+        rc = stage_prefill(p, host, st);
+        if (rc != GKV_OK) return rc;
+        const void* qb = d_q;
+        int launches = 0;
+        if (q_dtype == GKV_DTYPE_F32) {
+            rc = ensure_qconv(p, static_cast<size_t>(q_elems) * 2);
+            if (rc != GKV_OK) return rc;
+            cudaError_t e = launch_f32_to_bf16(static_cast<const float*>(d_q), ws.d_qconv, q_elems, st);
+            if (e != cudaSuccess) return cuda_fail(e, "prefill q conversion");
+            qb = ws.d_qconv;
+            ++launches;
+        } else if (reinterpret_cast<uintptr_t>(d_q) & 15) {
+            return set_error(GKV_EINVAL, "bf16 q must be 16-byte aligned");
+        }
+        PrefillArgs a{};
+        a.items = reinterpret_cast<const int32_t*>(ws.d_pre);
+        a.n_items = static_cast<int32_t>(order.size());
+        a.tables = ws.work.tables;
+        a.max_blocks = ws.up_max_blocks;
+        a.layer = layer;
+        a.n_heads = n_heads;
+        a.scale = scale;
+        a.out = d_out;
+        a.err = ws.d_err;
+        if (a.n_items > 0) {
+            cudaError_t e = launch_paged_prefill_tc(p->geom, a, qb, total_q, st);
+            if (e != cudaSuccess) return cuda_fail(e, "paged_prefill launch");
+            ++launches;
+        }
+        p->last_launches += launches;
+        return GKV_OK;
+    }
+
+    // Any other pool: the split-KV decode kernel with one segment per query, all on the
+    // sequence's table row, each with its causal length.
+    std::vector<int32_t> ctx_e, row_e;
+    ctx_e.reserve(static_cast<size_t>(total_q));
+    row_e.reserve(static_cast<size_t>(total_q));
+    for (int32_t b = 0; b < batch; ++b)
+        for (int32_t t = 0; t < q_len[b]; ++t) {
+            ctx_e.push_back(static_cast<int32_t>(
+                std::min<int64_t>(ws.h_ctx[static_cast<size_t>(b)], static_cast<int64_t>(q_start[b]) + t + 1)));
+            row_e.push_back(b);
+        }
+    const int32_t n_e = static_cast<int32_t>(total_q);
+    rc = decode_buffers(p, n_heads, 0, 0);
+    if (rc != GKV_OK) return rc;
+    if (!ws.cfg.supported)
+        return set_error(GKV_EUNSUPPORTED, "prefill not built for head_dim %d / v_head_dim %d", p->desc.head_dim,
+                         p->desc.v_head_dim);
+    const int32_t bs = p->desc.block_size;
+    int64_t chunks = 0;
+    for (int32_t c : ctx_e) chunks += chunks_of(c, bs);
+    chunks *= p->desc.heads_kv;
+    const int warps = ws.cfg.warps;
+    int64_t ctas = ((chunks + kMinChunksPerWorker - 1) / kMinChunksPerWorker + warps - 1) / warps;
+    if (ctas > ws.n_ctas_max) ctas = ws.n_ctas_max;
+    if (ctas < 1) ctas = 1;
+    WorkList W;
+    build_work_list(ctx_e.data(), n_e, p->desc.heads_kv, bs, static_cast<int32_t>(ctas * warps), &W);
+    const int64_t n_pieces = static_cast<int64_t>(W.piece_seg.size());
+    const int64_t n_merge = static_cast<int64_t>(W.merge_seg.size());
+    rc = decode_buffers(p, n_heads, W.n_slots, n_merge);
+    if (rc != GKV_OK) return rc;
+    const MetaLayout L = meta_layout(0, n_e, 0, n_pieces, ctas * warps, n_merge);
+    const size_t rows_off = L.total;
+    std::vector<char> host(rows_off + align_up(static_cast<size_t>(n_e) * 4, 16));
+    put_vec(host, L.ctx, ctx_e);
+    put_vec(host, L.pseg, W.piece_seg);
+    put_vec(host, L.pc0, W.piece_c0);
+    put_vec(host, L.pc1, W.piece_c1);
+    put_vec(host, L.pslot, W.piece_slot);
+    put_vec(host, L.pmerge, W.piece_merge);
+    put_vec(host, L.wbeg, W.worker_begin);
+    put_vec(host, L.mseg, W.merge_seg);
+    put_vec(host, L.ms0, W.merge_slot0);
+    put_vec(host, L.mns, W.merge_nslots);
+    put_vec(host, L.mdef, W.merge_deferred);
+    put_vec(host, rows_off, row_e);
+    rc = stage_prefill(p, host, st);
+    if (rc != GKV_OK) return rc;
+    const char* d = ws.d_pre;
+    auto at = [&](size_t off) { return reinterpret_cast<const int32_t*>(d + off); };
+    DecodeWork w{};
+    w.tables = ws.work.tables;
+    w.ctx_lens = at(L.ctx);
+    w.max_blocks = ws.up_max_blocks;
+    w.piece_seg = at(L.pseg);
+    w.piece_c0 = at(L.pc0);
+    w.piece_c1 = at(L.pc1);
+    w.piece_slot = at(L.pslot);
+    w.worker_piece_begin = at(L.wbeg);
+    w.n_ctas = chunks > 0 ? static_cast<int32_t>(ctas) : 0;
+    w.n_slots = W.n_slots;
+    w.merge_seg = at(L.mseg);
+    w.merge_slot0 = at(L.ms0);
+    w.merge_nslots = at(L.mns);
+    w.piece_merge = at(L.pmerge);
+    w.n_merge = static_cast<int32_t>(n_merge);
+    w.merge_deferred = at(L.mdef);
+    w.n_deferred = static_cast<int32_t>(W.merge_deferred.size());
+    w.merge_count = ws.d_merge_count;
+    w.table_row = at(rows_off);
+    const float* qf = static_cast<const float*>(d_q);
+    int launches = 0;
+    if (q_dtype == GKV_DTYPE_BF16) {
+        rc = ensure_qconv(p, static_cast<size_t>(q_elems) * 4);
+        if (rc != GKV_OK) return rc;
+        cudaError_t e = launch_bf16_to_f32(d_q, static_cast<float*>(ws.d_qconv), q_elems, st);
+        if (e != cudaSuccess) return cuda_fail(e, "prefill q conversion");
+        qf = static_cast<const float*>(ws.d_qconv);
+        ++launches;
+    }
+    DecodeArgs a{};
+    a.layer = layer;
+    a.q = qf;
+    a.out = d_out;
+    a.n_heads = n_heads;
+    a.scale = scale;
+    a.part_acc = ws.d_part_acc;
+    a.part_ml = ws.d_part_ml;
+    a.err = ws.d_err;
+    int dl = 0;
+    if (w.n_ctas > 0) {
+        cudaError_t e = launch_paged_decode(p->geom, w, a, &dl, st);
+        if (e != cudaSuccess) return cuda_fail(e, "prefill (decode kernel) launch");
+    }
+    p->last_launches += launches + dl;
+    return GKV_OK;
+}
+
 }  // namespace gkv
 
 using gkv::Pool;
@@ -512,6 +769,16 @@ int gkv_paged_decode(gkv_pool* pool, int32_t layer, const float* d_q, float* d_o
     pool->impl.last_launches = 0;
     return gkv::step_decode(&pool->impl, layer, d_q, d_out, n_heads, scale, d_sinks,
                             static_cast<cudaStream_t>(stream));
+}
+
+int gkv_paged_prefill(gkv_pool* pool, int32_t layer, const void* d_q, int32_t q_dtype, float* d_out,
+                      const int32_t* h_q_start, const int32_t* h_q_len, int32_t n_heads, float scale,
+                      void* stream) {
+    GKV_DEVICE_POOL(pool);
+    gkv::DeviceGuard guard(pool->impl.desc.device);
+    pool->impl.last_launches = 0;
+    return gkv::step_prefill(&pool->impl, layer, d_q, q_dtype, d_out, h_q_start, h_q_len, n_heads, scale,
+                             static_cast<cudaStream_t>(stream));
 }
 
 int gkv_compute_attention(gkv_pool* pool, int32_t stage_layer, int32_t model_layer, int32_t pos,

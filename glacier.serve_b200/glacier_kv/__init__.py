@@ -327,6 +327,22 @@ class PagedBlockPool:
                                     float(scale), None if sinks is None else _f32_dev(sinks, "sinks"),
                                     _stream(stream, self.device)))
 
+    def paged_prefill(self, layer: int, q, out, q_start, q_len, n_heads: int, scale: float, stream=None) -> None:
+        """Chunked causal prefill of the uploaded step: q [sum q_len, n_heads, head_dim] float32 or
+        bfloat16 CUDA, packed by sequence; out [sum q_len, n_heads, v_head_dim] float32.  Query t
+        of sequence b sits at position q_start[b] + t and attends keys
+        [0, min(ctx_lens[b], q_start[b] + t + 1))."""
+        import torch
+
+        if not (isinstance(q, torch.Tensor) and q.is_cuda and q.is_contiguous()
+                and q.dtype in (torch.float32, torch.bfloat16)):
+            raise ValueError("q must be a contiguous float32 or bfloat16 CUDA tensor")
+        qs = np.ascontiguousarray(q_start, dtype=np.int32)
+        ql = np.ascontiguousarray(q_len, dtype=np.int32)
+        qd = GKV_DTYPE_BF16 if q.dtype == torch.bfloat16 else GKV_DTYPE_F32
+        _check(lib.gkv_paged_prefill(self._h, layer, q.data_ptr(), qd, _f32_dev(out, "out"), _ptr(qs), _ptr(ql),
+                                     n_heads, float(scale), _stream(stream, self.device)))
+
     def decode_step_host(self, layer: int, block_tables, ctx_lens, slot_mapping, k_new, v_new, q, out,
                          n_heads: int, scale: float, sinks=None, stream=None) -> None:
         """One append+decode iteration from host buffers (pinned torch tensors or numpy)."""

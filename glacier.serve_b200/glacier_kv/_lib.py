@@ -120,6 +120,7 @@ SIGNATURES = {
     "gkv_upload_step_tables": (C.c_int, [P, P, I32, P, P, I32, P]),
     "gkv_kv_append": (C.c_int, [P, I32, P, P, I32, P]),
     "gkv_paged_decode": (C.c_int, [P, I32, P, P, I32, F32, P, P]),
+    "gkv_paged_prefill": (C.c_int, [P, I32, P, I32, P, P, P, I32, F32, P]),
     "gkv_compute_attention": (
         C.c_int,
         [P, I32, I32, I32, P, P, P, I32, I32, I32, I32, F32, I32, I32, F32, P],

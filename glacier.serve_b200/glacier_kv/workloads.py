@@ -8,6 +8,8 @@ what the free list produces), and N(0,1) values for Q, K and V.
     cfg2  append + decode, 64 seqs x (2048 cached + 1 new), 32q/8kv, d 128, fp32, pool 16384
     cfg3  decode, 256 seqs, ctx ~ lognormal(ln 1500, 1) in [16, 32768], 28q/4kv, d 128,
           fp32 or bf16, pool 65536 after a 10k-op admit/evict churn
+    cfg4  chunked causal prefill, 8 seqs x (prefix ~ U{0..4096} + 2048-token chunk),
+          28q/4kv, d 128, bf16
     cfg5  long-context decode, 4 seqs x 131072, 64q/8kv, d 128, bf16, split by block range
 """
 from __future__ import annotations
@@ -171,6 +173,72 @@ def cfg5_local(rank: int, world: int, seed: int = SEED, batch: int = 4, ctx: int
     ctx_local = np.full(batch, per * bs, np.int32)
     return DecodeWorkload("cfg5", 64, 8, 128, 128, bs, total_blocks, "bf16", ctx_local, np.ascontiguousarray(tables),
                           np.zeros(0, np.int64), np.zeros(0, np.int32), 1.0 / math.sqrt(128), seed)
+
+
+@dataclasses.dataclass
+class PrefillWorkload:
+    """Chunked causal prefill: every sequence has `prefix[b]` cached tokens, `chunk` new tokens
+    are appended after them and attend causally over prefix + chunk."""
+    name: str
+    n_heads: int
+    heads_kv: int
+    head_dim: int
+    v_head_dim: int
+    block_size: int
+    total_blocks: int
+    dtype: str
+    prefix: np.ndarray            # [B] cached tokens before the chunk
+    chunk: int                    # queries (= appended tokens) per sequence
+    tables: np.ndarray            # [B, max_blocks] int32, -1 padded
+    slot_mapping: np.ndarray      # [B * chunk] int64 slots of the chunk tokens, sequence-major
+    scale: float
+    seed: int
+
+    @property
+    def batch(self) -> int:
+        return int(self.prefix.shape[0])
+
+    @property
+    def token_counts(self) -> np.ndarray:
+        return (self.prefix + self.chunk).astype(np.int32)
+
+    @property
+    def q_lens(self) -> np.ndarray:
+        return np.full(self.batch, self.chunk, np.int32)
+
+    @property
+    def n_queries(self) -> int:
+        return self.batch * self.chunk
+
+    def flops(self) -> int:
+        """Causal-only count: 2 * (d + dv) * n_heads per visible (query, key) pair."""
+        pairs = sum(self.chunk * (int(p) + 1) + self.chunk * (self.chunk - 1) // 2 for p in self.prefix)
+        return 2 * (self.head_dim + self.v_head_dim) * self.n_heads * pairs
+
+    def append_bytes(self) -> int:
+        eb = 2 if self.dtype == "bf16" else 4
+        return self.n_queries * self.heads_kv * (self.head_dim + self.v_head_dim) * eb
+
+
+def cfg4(seed: int = SEED, batch: int = 8, chunk: int = 2048, max_prefix: int = 4096) -> PrefillWorkload:
+    """8 sequences, prefix ~ U{0..4096}, a 2048-token chunk each; 28q/4kv, d 128, bf16."""
+    rng = np.random.default_rng(seed)
+    bs = 16
+    prefix = rng.integers(0, max_prefix, size=batch, endpoint=True).astype(np.int32)
+    n_blocks = [(int(p) + chunk + bs - 1) // bs for p in prefix]
+    total_blocks = sum(n_blocks) + 64
+    perm = rng.permutation(total_blocks).astype(np.int32)
+    tables, at = [], 0
+    for n in n_blocks:
+        tables.append(perm[at: at + n].tolist())
+        at += n
+    packed = _pack(tables)
+    slots = []
+    for b, p in enumerate(prefix):
+        pos = np.arange(int(p), int(p) + chunk)
+        slots.append(packed[b, pos // bs].astype(np.int64) * bs + pos % bs)
+    return PrefillWorkload("cfg4", 28, 4, 128, 128, bs, total_blocks, "bf16", prefix, chunk, packed,
+                           np.concatenate(slots).astype(np.int64), 1.0 / math.sqrt(128), seed)
 
 
 def make_pool(w: DecodeWorkload, device: int = 0, layers: int = 1) -> PagedBlockPool:

@@ -210,6 +210,22 @@ GKV_API int gkv_kv_append(gkv_pool* pool, int32_t layer, const float* d_k, const
  * PagedAttentionKernel.ComputeAttention, PagedAttentionKernel.cs:17-372, for a batch. */
 GKV_API int gkv_paged_decode(gkv_pool* pool, int32_t layer, const float* d_q, float* d_out,
                              int32_t n_heads, float scale, const float* d_sinks, void* stream);
+/* Chunked causal prefill of the uploaded step for `layer`.  Sequence b (row b of the
+ * uploaded tables, ctx_lens[b] = its TokenCount with the chunk's K/V already appended) has
+ * h_q_len[b] queries at positions h_q_start[b] .. h_q_start[b] + h_q_len[b] - 1; query t
+ * attends keys [0, min(ctx_lens[b], h_q_start[b] + t + 1)) and a sequence with no keys
+ * leaves its rows of d_out untouched.  Queries are packed by sequence in batch order:
+ * d_q [sum q_len][n_heads][head_dim], q_dtype GKV_DTYPE_F32 or GKV_DTYPE_BF16;
+ * d_out [sum q_len][n_heads][v_head_dim] fp32.  Same result as one
+ * PagedAttentionKernel.ComputeAttention per chunk token with pos = start + t
+ * (PagedTransformerRunner.ForwardPrefillSubBatch, PagedTransformerRunner.cs:424-471).
+ * bf16 pools with head_dim = v_head_dim = 128 run on the tensor cores (tcgen05, bf16
+ * operands: an fp32 q is rounded to bf16 first); every other pool runs the split-KV decode
+ * kernel over one segment per query.  GKV_EINVAL when a position reaches
+ * max_blocks * block_size of the upload (ComputeAttention's pos < maxSeqLen check). */
+GKV_API int gkv_paged_prefill(gkv_pool* pool, int32_t layer, const void* d_q, int32_t q_dtype,
+                              float* d_out, const int32_t* h_q_start, const int32_t* h_q_len,
+                              int32_t n_heads, float scale, void* stream);
 /* ComputeAttention for ONE sequence with the reference's argument checks
  * (PagedAttentionKernel.cs:17-42): GKV_EINVAL when max_seq_len <= 0, pos outside
  * [0, max_seq_len) or TokenCount > max_seq_len; a no-op when min(TokenCount, pos+1) == 0.
