@@ -46,18 +46,19 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def workload(name: str, rank: int, world: int = 1):
+def workload(name: str, rank: int, world: int = 1, batch: int = 0):
+    """batch > 0 shrinks cfg2 / cfg3 to that many sequences (small cases for profiler captures)."""
     from glacier_kv import workloads as W
 
     seed = W.SEED + 1000003 * rank
     if name == "cfg1":
         return W.cfg1(seed)
     if name == "cfg2":
-        return W.cfg2(seed)
+        return W.cfg2(seed, batch=batch or 64)
     if name == "cfg3":
-        return W.cfg3(seed, "f32")
+        return W.cfg3(seed, "f32", batch=batch or 256)
     if name == "cfg3-bf16":
-        return W.cfg3(seed, "bf16")
+        return W.cfg3(seed, "bf16", batch=batch or 256)
     if name == "cfg5":  # this rank's block range of the 4 x 131072 sequences
         return W.cfg5_local(rank, world, W.SEED)
     raise SystemExit(f"unknown config {name}")
@@ -424,6 +425,8 @@ def main():
     ap.add_argument("--config", default="cfg2")
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="sequences of cfg2/cfg3 (default: the config's own); for small profiler captures")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -463,7 +466,7 @@ def main():
             dist.destroy_process_group()
         return
 
-    w = workload(args.config, rank, world)
+    w = workload(args.config, rank, world, args.batch)
     pool = W.make_pool(w, device=local)
     W.fill_arena_randn(pool, seed=w.seed)
     stream = torch.cuda.current_stream(dev)

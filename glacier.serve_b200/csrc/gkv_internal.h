@@ -134,6 +134,9 @@ struct Pool {
     // TMA maps of the arena for the tensor-core decode, encoded once at creation
     alignas(64) unsigned char tmap_k[128];
     alignas(64) unsigned char tmap_v[128];
+    // the same views with 16-slot boxes, for the prefill kernel
+    alignas(64) unsigned char tmap_pk[128];
+    alignas(64) unsigned char tmap_pv[128];
 
     bool in_range(int32_t b) const {
         return static_cast<uint32_t>(b) < static_cast<uint32_t>(desc.total_blocks);

@@ -19,6 +19,9 @@ struct ArenaGeom {
     // the tensor-core decode; nullptr means "encode at launch".  Never read on the device.
     const void* tmap_k = nullptr;
     const void* tmap_v = nullptr;
+    // The same with boxes of 16 slots (block sizes that are multiples of 16), for the prefill.
+    const void* tmap_pk = nullptr;
+    const void* tmap_pv = nullptr;
 };
 
 // ---- kv append ----
@@ -119,11 +122,11 @@ bool decode_tc_eligible(const ArenaGeom& g, int n_heads);
 bool encode_decode_tmaps(const ArenaGeom& g, void* tmap_k, void* tmap_v);
 // Tiled TMA maps (bf16, 128-byte swizzle, no interleave; `map` is a 64-byte aligned
 // 128-byte CUtensorMap).  encode_arena_map: the 3-D view [block*layer*head][slot][dim] of
-// one arena with boxes of 8 slots x 64 dims.
+// one arena with boxes of `rows` slots x 64 dims.
 bool tmap_encoder_available();
 bool encode_bf16_map3(void* map, const void* base, const uint64_t dims[3], const uint64_t strides[2],
                       const uint32_t box[3]);
-bool encode_arena_map(void* map, void* base, const ArenaGeom& g, int dim);
+bool encode_arena_map(void* map, void* base, const ArenaGeom& g, int dim, int rows = kDecodeChunk);
 void decode_tc_config(DecodeConfig& c);
 cudaError_t launch_paged_decode_tc(const ArenaGeom& g, const DecodeWork& w, const DecodeArgs& a,
                                    int group, int head_groups, int* launches, cudaStream_t st);

@@ -376,12 +376,13 @@ bool encode_bf16_map3(void* map, const void* base, const uint64_t dims[3], const
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// 3-D view [block * layer * head][slot][dim] of one bf16 arena, boxes of 8 slots x 64 dims.
-bool encode_arena_map(void* map, void* base, const ArenaGeom& g, int dim) {
+// 3-D view [block * layer * head][slot][dim] of one bf16 arena, boxes of `rows` slots x 64 dims.
+bool encode_arena_map(void* map, void* base, const ArenaGeom& g, int dim, int rows) {
+    if (rows <= 0 || g.block_size % rows != 0) return false;
     const uint64_t dims[3] = {static_cast<uint64_t>(dim), static_cast<uint64_t>(g.block_size),
                               static_cast<uint64_t>(g.total_blocks) * g.layers * g.heads_kv};
     const uint64_t strides[2] = {static_cast<uint64_t>(dim) * 2, static_cast<uint64_t>(g.block_size) * dim * 2};
-    const uint32_t box[3] = {64, static_cast<uint32_t>(kDecodeChunk), 1};
+    const uint32_t box[3] = {64, static_cast<uint32_t>(rows), 1};
     return encode_bf16_map3(map, base, dims, strides, box);
 }
 

@@ -9,9 +9,11 @@
 // sequence's pages in tiles of 64 keys:
 //
 //  * warp 4 (TMA producer): the Q tile once (two boxes of 128 rows x 64 dims), then per key
-//    tile 8 chunks of 8 keys x 2 dim halves of K, and the same of V, gathered from the arena
-//    through the block table with tiled cp.async.bulk.tensor (128-byte swizzle, no
-//    multicast) into 2-stage K and V rings.
+//    tile one box per page (16 slots; 8 when the block size is not a multiple of 16) and dim
+//    half, of K and of V, gathered from the arena through the block table with tiled
+//    cp.async.bulk.tensor (128-byte swizzle, no multicast) into 2-stage K and V rings.  Each
+//    lane issues one box: a TMA instruction occupies its issuing thread for on the order of
+//    a hundred cycles, so one thread alone starves the tensor cores.
 //  * warp 5 (one thread issues): S = Q K^T (M=128, N=64, K=128: 8 tcgen05.mma kind::f16,
 //    both operands K-major in shared memory) into one of two TMEM S buffers, then
 //    O += P V (M=128, N=128, K=64: 4 MMAs, P read from TMEM, V MN-major in shared memory).
@@ -59,29 +61,46 @@ constexpr uint32_t idesc_bf16(int m, int n, bool b_mn_major) {
            (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
-// One key tile (64 keys from key0, fewer at the end) of K or V: chunk c of 8 keys lands at
-// dst + c*1 KB (dims 0-63) and dst + 8 KB + c*1 KB (dims 64-127); 1 KB = one swizzle atom.
-__device__ __forceinline__ void load_kv_tile(uint8_t* dst, const CUtensorMap* tm, uint64_t* full, int key0,
-                                             int n_keys, const int32_t* trow, const ArenaGeom& g, int layer,
-                                             int hkv, int* err) {
-    int nch = (n_keys - key0 + 7) >> 3;
-    if (nch > kBN / 8) nch = kBN / 8;
-    mbar_arrive_expect_tx(full, static_cast<uint32_t>(nch) * 2048u);
-    for (int c = 0; c < nch; ++c) {
-        const int key = key0 + c * 8;
-        const int page = key / g.block_size;
-        const int slot = key - page * g.block_size;
-        int blk = __ldg(trow + page);
-        if (blk < 0 || blk >= g.total_blocks) {  // validated on the host; never dereference it
-            atomicOr(err, kErrBadBlock);
-            blk = 0;
-        }
-        const int z = static_cast<int>((static_cast<int64_t>(blk) * g.layers + layer) * g.heads_kv + hkv);
-        tma_load_3d(dst + c * 1024, tm, 0, slot, z, full);
-        tma_load_3d(dst + kHalf + c * 1024, tm, 64, slot, z, full);
+// One lane of the producer warp per TMA box.  A key tile is 64 / R boxes of R keys (R = 16:
+// a whole 16-slot page; R = 8 otherwise) for each dim half, of K and of V: lanes
+// [0, 2*64/R) load K, the next 2*64/R lanes load V.  A TMA instruction costs its issuing
+// thread on the order of a hundred cycles, so one issuing thread cannot feed the tensor
+// cores; 8 or 16 lanes in parallel can.
+template <int R>
+struct BoxLane {
+    static constexpr int kBoxes = kBN / R;        // boxes per dim half per tile
+    static constexpr int kPerOperand = 2 * kBoxes;
+    int chunk, half;  // this lane's box: rows [chunk*R, chunk*R + R) of dims [half*64, half*64 + 64)
+    bool is_k, active;
+    __device__ __forceinline__ explicit BoxLane(int lane) {
+        const int l = lane % kPerOperand;
+        chunk = l >> 1;
+        half = l & 1;
+        is_k = lane < kPerOperand;
+        active = lane < 2 * kPerOperand;
     }
-}
+    // Arena row (block*layers + layer)*heads_kv + hkv of this lane's box in tile j, or -1 past
+    // the keys of the item.
+    __device__ __forceinline__ int row_of(int j, int n_keys, const int32_t* trow, const ArenaGeom& g, int layer,
+                                          int hkv, int* err) const {
+        const int key = j * kBN + chunk * R;
+        if (!active || key >= n_keys) return -1;
+        int b = __ldg(trow + key / g.block_size);
+        if (b < 0 || b >= g.total_blocks) {  // validated on the host; never dereference it
+            atomicOr(err, kErrBadBlock);
+            b = 0;
+        }
+        return static_cast<int>((static_cast<int64_t>(b) * g.layers + layer) * g.heads_kv + hkv);
+    }
+    // Bytes a tile with keys [key0, n_keys) delivers to one operand's barrier.
+    static __device__ __forceinline__ uint32_t tile_bytes(int key0, int n_keys) {
+        int n = (n_keys - key0 + R - 1) / R;
+        if (n > kBoxes) n = kBoxes;
+        return static_cast<uint32_t>(n) * 2u * R * 128u;
+    }
+};
 
+template <int R>
 __global__ void __launch_bounds__(kThreads, 2)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                             const __grid_constant__ CUtensorMap tmv, const ArenaGeom g, const PrefillArgs a) {
@@ -134,38 +153,62 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint32_t tbase = *tmem_slot;
 
     if (warp == 4) {
-        // ---------------- TMA producer ----------------
+        // ---------------- TMA producer: the whole warp, one box per lane ----------------
+        using BL = BoxLane<R>;
+        const BL bl(lane);
+        const int32_t* trow = a.tables + static_cast<int64_t>(seq) * a.max_blocks;
+        uint32_t armed_k0 = 0, armed_k1 = 0, armed_v0 = 0, armed_v1 = 0;  // lane 0's expect_tx count
         if (lane == 0) {
-            uint32_t armed_k[2] = {0, 0}, armed_v[2] = {0, 0};
-            const int32_t* trow = a.tables + static_cast<int64_t>(seq) * a.max_blocks;
             mbar_arrive_expect_tx(q_full, kQBytes);
             tma_load_3d(sQ, &tmq, 0, h, qrow0, q_full);
             tma_load_3d(sQ + kQHalf, &tmq, 64, h, qrow0, q_full);
-            for (int j = 0; j < n_tiles; ++j) {
-                const int s = j & 1;
-                const uint32_t par = ((j >> 1) & 1) ^ 1;
-                if (j >= 2 && !mbar_wait(k_empty + s, par)) {
-                    atomicOr(a.err, kErrWaitTimeout);
-                    *abort_flag = 1;
-                }
-                if (*abort_flag) break;
-                load_kv_tile(sK + s * kTile, &tmk, k_full + s, j * kBN, n_keys, trow, g, a.layer, hkv, a.err);
-                ++armed_k[s];
-                if (j >= 2 && !mbar_wait(v_empty + s, par)) {
-                    atomicOr(a.err, kErrWaitTimeout);
-                    *abort_flag = 1;
-                }
-                if (*abort_flag) break;
-                load_kv_tile(sV + s * kTile, &tmv, v_full + s, j * kBN, n_keys, trow, g, a.layer, hkv, a.err);
-                ++armed_v[s];
+        }
+        int row = bl.row_of(0, n_keys, trow, g, a.layer, hkv, a.err);
+        bool ok = true;
+        for (int j = 0; j < n_tiles; ++j) {
+            const int s = j & 1;
+            const uint32_t par = ((j >> 1) & 1) ^ 1;
+            // the next tile's table read is in flight while this tile waits for its stages
+            const int row_next = j + 1 < n_tiles ? bl.row_of(j + 1, n_keys, trow, g, a.layer, hkv, a.err) : -1;
+            const uint32_t bytes = BL::tile_bytes(j * kBN, n_keys);
+            const uint32_t dst = s * kTile + bl.half * kHalf + bl.chunk * R * 128;
+            const int slot = (j * kBN + bl.chunk * R) % g.block_size;
+            if (j >= 2 && !__all_sync(~0u, mbar_wait(k_empty + s, par))) {
+                ok = false;
+                break;
+            }
+            if (__any_sync(~0u, *abort_flag != 0)) break;
+            if (lane == 0) {
+                mbar_arrive_expect_tx(k_full + s, bytes);
+                if (s) ++armed_k1; else ++armed_k0;
+            }
+            __syncwarp();  // expect_tx precedes every complete_tx of this stage
+            if (bl.is_k && row >= 0) tma_load_3d(sK + dst, &tmk, bl.half * 64, slot, row, k_full + s);
+            if (j >= 2 && !__all_sync(~0u, mbar_wait(v_empty + s, par))) {
+                ok = false;
+                break;
+            }
+            if (__any_sync(~0u, *abort_flag != 0)) break;
+            if (lane == 0) {
+                mbar_arrive_expect_tx(v_full + s, bytes);
+                if (s) ++armed_v1; else ++armed_v0;
+            }
+            __syncwarp();
+            if (!bl.is_k && bl.active && row >= 0) tma_load_3d(sV + dst, &tmv, bl.half * 64, slot, row, v_full + s);
+            row = row_next;
+        }
+        if (lane == 0) {
+            if (!ok) {
+                atomicOr(a.err, kErrWaitTimeout);
+                *abort_flag = 1;
             }
             if (*abort_flag) {
                 // every armed copy must land before the CTA's shared memory goes away
                 mbar_wait(q_full, 0);
-                for (int s = 0; s < 2; ++s) {
-                    if (armed_k[s]) mbar_wait(k_full + s, (armed_k[s] - 1) & 1);
-                    if (armed_v[s]) mbar_wait(v_full + s, (armed_v[s] - 1) & 1);
-                }
+                if (armed_k0) mbar_wait(k_full, (armed_k0 - 1) & 1);
+                if (armed_k1) mbar_wait(k_full + 1, (armed_k1 - 1) & 1);
+                if (armed_v0) mbar_wait(v_full, (armed_v0 - 1) & 1);
+                if (armed_v1) mbar_wait(v_full + 1, (armed_v1 - 1) & 1);
             }
         }
         __syncwarp();
@@ -246,20 +289,25 @@ __global__ void __launch_bounds__(kThreads, 2)
             tmem_ld32(t_lane + b * kBN, s0);
             tmem_ld32(t_lane + b * kBN + 32, s1);
             tmem_wait_ld();
+            // raw scores; masked keys become -inf (sl > 0, so the max commutes with the scale)
             float x[kBN];
 #pragma unroll
             for (int c = 0; c < 32; ++c) {
-                x[c] = __uint_as_float(s0[c]) * sl;
-                x[c + 32] = __uint_as_float(s1[c]) * sl;
+                x[c] = __uint_as_float(s0[c]);
+                x[c + 32] = __uint_as_float(s1[c]);
             }
             const int kb = j * kBN;
             if (kb + kBN > limit) {
 #pragma unroll
                 for (int c = 0; c < kBN; ++c) x[c] = (kb + c < limit) ? x[c] : -INFINITY;
             }
-            float mt = x[0];
+            float mx0 = x[0], mx1 = x[1];
 #pragma unroll
-            for (int c = 1; c < kBN; ++c) mt = fmaxf(mt, x[c]);
+            for (int c = 2; c < kBN; c += 2) {
+                mx0 = fmaxf(mx0, x[c]);
+                mx1 = fmaxf(mx1, x[c + 1]);
+            }
+            const float mt = fmaxf(mx0, mx1) * sl;
             const bool need = mt > m_run + kRescaleLog2;
             float alpha = 1.f;
             if (need) {
@@ -267,16 +315,18 @@ __global__ void __launch_bounds__(kThreads, 2)
                 m_run = mt;
                 l_run *= alpha;
             }
+            // p = 2^(s * sl - m): one packed FMA per key pair, then the SFU
             uint32_t pk[32];
-            float sum = 0.f;
+            float2 sum2 = make_float2(0.f, 0.f);
+            const float2 sl2 = make_float2(sl, sl), nm2 = make_float2(-m_run, -m_run);
 #pragma unroll
             for (int c = 0; c < 32; ++c) {
-                const float p0 = fast_exp2(x[2 * c] - m_run);
-                const float p1 = fast_exp2(x[2 * c + 1] - m_run);
-                sum += p0 + p1;
-                pk[c] = pack_bf16x2(p0, p1);
+                const float2 e = __ffma2_rn(make_float2(x[2 * c], x[2 * c + 1]), sl2, nm2);
+                const float2 p = make_float2(fast_exp2(e.x), fast_exp2(e.y));
+                sum2 = __fadd2_rn(sum2, p);
+                pk[c] = pack_bf16x2(p.x, p.y);
             }
-            l_run += sum;
+            l_run += sum2.x + sum2.y;
             if (j == n_tiles - 1 && tail < kBN) {
                 // keys past n_keys were never loaded (or are unwritten slots): zero their V
                 // rows so that P = 0 never meets a non-finite value in the MMA
@@ -386,8 +436,11 @@ cudaError_t prefill_prepare() {
     if (e != cudaSuccess) return e;
     const uint64_t bit = 1ull << (dev & 63);
     if (done_mask.load(std::memory_order_acquire) & bit) return cudaSuccess;
-    e = cudaFuncSetAttribute(paged_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(paged_prefill_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kSmem));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(paged_prefill_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kSmem));
     if (e == cudaSuccess) done_mask.fetch_or(bit, std::memory_order_acq_rel);
     return e;
 }
@@ -428,10 +481,14 @@ cudaError_t launch_paged_prefill_tc(const ArenaGeom& g, const PrefillArgs& a, co
     const uint64_t strides[2] = {static_cast<uint64_t>(kD) * 2, static_cast<uint64_t>(a.n_heads) * kD * 2};
     const uint32_t box[3] = {64, 1, static_cast<uint32_t>(kBM)};
     if (!encode_bf16_map3(&mq, q_bf16, dims, strides, box)) return cudaErrorInvalidValue;
-    const CUtensorMap* tk = static_cast<const CUtensorMap*>(g.tmap_k);
-    const CUtensorMap* tv = static_cast<const CUtensorMap*>(g.tmap_v);
+    // whole 16-slot pages per box when the block size allows, else 8-slot boxes; the pool
+    // caches both map pairs
+    const int rows = g.block_size % 16 == 0 ? 16 : 8;
+    const CUtensorMap* tk = static_cast<const CUtensorMap*>(rows == 16 ? g.tmap_pk : g.tmap_k);
+    const CUtensorMap* tv = static_cast<const CUtensorMap*>(rows == 16 ? g.tmap_pv : g.tmap_v);
     if (!tk || !tv) {
-        if (!encode_arena_map(&ek, g.k, g, kD) || !encode_arena_map(&ev, g.v, g, kD)) return cudaErrorInvalidValue;
+        if (!encode_arena_map(&ek, g.k, g, kD, rows) || !encode_arena_map(&ev, g.v, g, kD, rows))
+            return cudaErrorInvalidValue;
         tk = &ek;
         tv = &ev;
     }
@@ -439,7 +496,10 @@ cudaError_t launch_paged_prefill_tc(const ArenaGeom& g, const PrefillArgs& a, co
     if (e != cudaSuccess) return e;
     const int64_t grid = static_cast<int64_t>(a.n_items) * a.n_heads;
     if (grid > 0x7fffffff) return cudaErrorInvalidValue;
-    paged_prefill_tc_kernel<<<static_cast<unsigned>(grid), kThreads, kSmem, st>>>(mq, *tk, *tv, g, a);
+    if (rows == 16)
+        paged_prefill_tc_kernel<16><<<static_cast<unsigned>(grid), kThreads, kSmem, st>>>(mq, *tk, *tv, g, a);
+    else
+        paged_prefill_tc_kernel<8><<<static_cast<unsigned>(grid), kThreads, kSmem, st>>>(mq, *tk, *tv, g, a);
     return cudaGetLastError();
 }
 

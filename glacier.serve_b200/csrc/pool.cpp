@@ -343,6 +343,12 @@ int gkv_pool_create(const gkv_pool_desc* desc, gkv_pool** out_pool) {
             gkv::encode_decode_tmaps(g, P.tmap_k, P.tmap_v)) {
             g.tmap_k = P.tmap_k;
             g.tmap_v = P.tmap_v;
+            // whole-page boxes (16 slots) for the prefill kernel when the block size allows
+            if (d.block_size % 16 == 0 && gkv::encode_arena_map(P.tmap_pk, g.k, g, 128, 16) &&
+                gkv::encode_arena_map(P.tmap_pv, g.v, g, 128, 16)) {
+                g.tmap_pk = P.tmap_pk;
+                g.tmap_pv = P.tmap_pv;
+            }
         }
     }
     *out_pool = p;

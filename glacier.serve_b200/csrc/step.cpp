@@ -544,7 +544,8 @@ int step_prefill(Pool* p, int32_t layer, const void* d_q, int32_t q_dtype, float
     if (total_q == 0) return GKV_OK;
     const int64_t q_elems = total_q * n_heads * p->desc.head_dim;
 
-    if (prefill_tc_eligible(p->geom, n_heads)) {
+    // the tensor-core kernel takes the row max on unscaled scores: it needs scale > 0
+    if (prefill_tc_eligible(p->geom, n_heads) && scale > 0.f) {
         // work items of up to 128 queries, heaviest first (longest key range)
         std::vector<int32_t> items;
         std::vector<std::pair<int32_t, int32_t>> order;  // (-n_keys, item)
