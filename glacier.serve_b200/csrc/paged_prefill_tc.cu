@@ -43,7 +43,9 @@ namespace {
 constexpr int kBM = 128;                           // query rows per CTA
 constexpr int kBN = 64;                            // keys per tile
 constexpr int kD = 128;                            // head_dim = v_head_dim
-constexpr int kThreads = 192;                      // 4 softmax warps, producer, MMA
+constexpr int kSoftmaxWarps = 8;                   // two threads per query row
+constexpr int kKWarp = 8, kVWarp = 9, kMmaWarp = 10;  // K producer, V producer, MMA issuer
+constexpr int kThreads = 352;
 constexpr uint32_t kQBytes = kBM * kD * 2;         // 32 KB
 constexpr uint32_t kQHalf = kQBytes / 2;           // 128 rows x 128 B (64 dims)
 constexpr uint32_t kTile = kBN * kD * 2;           // 16 KB: one K or V tile
@@ -61,38 +63,28 @@ constexpr uint32_t idesc_bf16(int m, int n, bool b_mn_major) {
            (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
-// One lane of the producer warp per TMA box.  A key tile is 64 / R boxes of R keys (R = 16:
-// a whole 16-slot page; R = 8 otherwise) for each dim half, of K and of V: lanes
-// [0, 2*64/R) load K, the next 2*64/R lanes load V.  A TMA instruction costs its issuing
-// thread on the order of a hundred cycles, so one issuing thread cannot feed the tensor
-// cores; 8 or 16 lanes in parallel can.
+// One lane of a producer warp per TMA box.  A key tile of K (or of V) is 64 / R boxes of R
+// keys (R = 16: a whole 16-slot page; R = 8 otherwise) for each dim half: lane l < 2*64/R
+// loads rows [chunk*R, chunk*R + R) of dims [half*64, half*64 + 64), chunk = l/2, half = l%2.
+// A TMA instruction costs its issuing thread on the order of a hundred cycles, so one thread
+// cannot feed the tensor cores; 8 or 16 lanes in parallel can.
 template <int R>
 struct BoxLane {
-    static constexpr int kBoxes = kBN / R;        // boxes per dim half per tile
-    static constexpr int kPerOperand = 2 * kBoxes;
-    int chunk, half;  // this lane's box: rows [chunk*R, chunk*R + R) of dims [half*64, half*64 + 64)
-    bool is_k, active;
+    static constexpr int kBoxes = kBN / R;  // boxes per dim half per tile
+    int chunk, half;
+    bool active;
     __device__ __forceinline__ explicit BoxLane(int lane) {
-        const int l = lane % kPerOperand;
-        chunk = l >> 1;
-        half = l & 1;
-        is_k = lane < kPerOperand;
-        active = lane < 2 * kPerOperand;
+        chunk = (lane >> 1) % kBoxes;
+        half = lane & 1;
+        active = lane < 2 * kBoxes;
     }
-    // Arena row (block*layers + layer)*heads_kv + hkv of this lane's box in tile j, or -1 past
-    // the keys of the item.
-    __device__ __forceinline__ int row_of(int j, int n_keys, const int32_t* trow, const ArenaGeom& g, int layer,
-                                          int hkv, int* err) const {
+    // Block-table entry of this lane's box in tile j (raw: checked where it is used, so the
+    // load can be issued a tile ahead without stalling), or -1 past the item's keys.
+    __device__ __forceinline__ int block_of(int j, int n_keys, const int32_t* trow, int block_size) const {
         const int key = j * kBN + chunk * R;
-        if (!active || key >= n_keys) return -1;
-        int b = __ldg(trow + key / g.block_size);
-        if (b < 0 || b >= g.total_blocks) {  // validated on the host; never dereference it
-            atomicOr(err, kErrBadBlock);
-            b = 0;
-        }
-        return static_cast<int>((static_cast<int64_t>(b) * g.layers + layer) * g.heads_kv + hkv);
+        return (active && key < n_keys) ? __ldg(trow + key / block_size) : -1;
     }
-    // Bytes a tile with keys [key0, n_keys) delivers to one operand's barrier.
+    // Bytes a tile with keys [key0, n_keys) delivers to its operand's barrier.
     static __device__ __forceinline__ uint32_t tile_bytes(int key0, int n_keys) {
         int n = (n_keys - key0 + R - 1) / R;
         if (n > kBoxes) n = kBoxes;
@@ -139,63 +131,64 @@ __global__ void __launch_bounds__(kThreads, 2)
             mbar_init(v_full + s, 1);
             mbar_init(v_empty + s, 1);
             mbar_init(s_full + s, 1);
-            mbar_init(p_full + s, kBM);
+            mbar_init(p_full + s, kSoftmaxWarps * 32);
             mbar_init(pv_done + s, 1);
         }
         mbar_init(drained, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
-    if (warp == 5) tmem_alloc(tmem_slot, kTmemCols);
+    if (warp == kMmaWarp) tmem_alloc(tmem_slot, kTmemCols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *tmem_slot;
 
-    if (warp == 4) {
-        // ---------------- TMA producer: the whole warp, one box per lane ----------------
+    if (warp == kKWarp || warp == kVWarp) {
+        // ------------- TMA producers: one warp for K, one for V, one box per lane -------------
+        // Separate warps: V of tile j waits for P V of tile j-2, which must not hold back K.
         using BL = BoxLane<R>;
         const BL bl(lane);
+        const bool is_k = warp == kKWarp;
+        uint64_t* full = is_k ? k_full : v_full;
+        uint64_t* empty = is_k ? k_empty : v_empty;
+        uint8_t* ring = is_k ? sK : sV;
+        const CUtensorMap* tm = is_k ? &tmk : &tmv;
         const int32_t* trow = a.tables + static_cast<int64_t>(seq) * a.max_blocks;
-        uint32_t armed_k0 = 0, armed_k1 = 0, armed_v0 = 0, armed_v1 = 0;  // lane 0's expect_tx count
-        if (lane == 0) {
+        uint32_t armed0 = 0, armed1 = 0;  // lane 0's expect_tx count per stage
+        if (is_k && lane == 0) {
             mbar_arrive_expect_tx(q_full, kQBytes);
             tma_load_3d(sQ, &tmq, 0, h, qrow0, q_full);
             tma_load_3d(sQ + kQHalf, &tmq, 64, h, qrow0, q_full);
         }
-        int row = bl.row_of(0, n_keys, trow, g, a.layer, hkv, a.err);
+        int blk = bl.block_of(0, n_keys, trow, g.block_size);
         bool ok = true;
         for (int j = 0; j < n_tiles; ++j) {
             const int s = j & 1;
-            const uint32_t par = ((j >> 1) & 1) ^ 1;
-            // the next tile's table read is in flight while this tile waits for its stages
-            const int row_next = j + 1 < n_tiles ? bl.row_of(j + 1, n_keys, trow, g, a.layer, hkv, a.err) : -1;
-            const uint32_t bytes = BL::tile_bytes(j * kBN, n_keys);
-            const uint32_t dst = s * kTile + bl.half * kHalf + bl.chunk * R * 128;
-            const int slot = (j * kBN + bl.chunk * R) % g.block_size;
-            if (j >= 2 && !__all_sync(~0u, mbar_wait(k_empty + s, par))) {
+            // the next tile's table read is in flight while this tile waits for its stage
+            const int blk_next = j + 1 < n_tiles ? bl.block_of(j + 1, n_keys, trow, g.block_size) : -1;
+            if (j >= 2 && !__all_sync(~0u, mbar_wait(empty + s, ((j >> 1) & 1) ^ 1))) {
                 ok = false;
                 break;
             }
             if (__any_sync(~0u, *abort_flag != 0)) break;
             if (lane == 0) {
-                mbar_arrive_expect_tx(k_full + s, bytes);
-                if (s) ++armed_k1; else ++armed_k0;
+                mbar_arrive_expect_tx(full + s, BL::tile_bytes(j * kBN, n_keys));
+                if (s) ++armed1; else ++armed0;
             }
             __syncwarp();  // expect_tx precedes every complete_tx of this stage
-            if (bl.is_k && row >= 0) tma_load_3d(sK + dst, &tmk, bl.half * 64, slot, row, k_full + s);
-            if (j >= 2 && !__all_sync(~0u, mbar_wait(v_empty + s, par))) {
-                ok = false;
-                break;
+            if (blk >= 0 || (bl.active && j * kBN + bl.chunk * R < n_keys)) {
+                int b = blk;
+                if (b < 0 || b >= g.total_blocks) {  // validated on the host; never dereference it
+                    atomicOr(a.err, kErrBadBlock);
+                    b = 0;
+                }
+                const int z = static_cast<int>((static_cast<int64_t>(b) * g.layers + a.layer) * g.heads_kv + hkv);
+                const int slot = (j * kBN + bl.chunk * R) % g.block_size;
+                tma_load_3d(ring + s * kTile + bl.half * kHalf + bl.chunk * R * 128, tm, bl.half * 64, slot, z,
+                            full + s);
             }
-            if (__any_sync(~0u, *abort_flag != 0)) break;
-            if (lane == 0) {
-                mbar_arrive_expect_tx(v_full + s, bytes);
-                if (s) ++armed_v1; else ++armed_v0;
-            }
-            __syncwarp();
-            if (!bl.is_k && bl.active && row >= 0) tma_load_3d(sV + dst, &tmv, bl.half * 64, slot, row, v_full + s);
-            row = row_next;
+            blk = blk_next;
         }
         if (lane == 0) {
             if (!ok) {
@@ -204,15 +197,13 @@ __global__ void __launch_bounds__(kThreads, 2)
             }
             if (*abort_flag) {
                 // every armed copy must land before the CTA's shared memory goes away
-                mbar_wait(q_full, 0);
-                if (armed_k0) mbar_wait(k_full, (armed_k0 - 1) & 1);
-                if (armed_k1) mbar_wait(k_full + 1, (armed_k1 - 1) & 1);
-                if (armed_v0) mbar_wait(v_full, (armed_v0 - 1) & 1);
-                if (armed_v1) mbar_wait(v_full + 1, (armed_v1 - 1) & 1);
+                if (is_k) mbar_wait(q_full, 0);
+                if (armed0) mbar_wait(full, (armed0 - 1) & 1);
+                if (armed1) mbar_wait(full + 1, (armed1 - 1) & 1);
             }
         }
         __syncwarp();
-    } else if (warp == 5) {
+    } else if (warp == kMmaWarp) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             constexpr uint32_t kIdS = idesc_bf16(kBM, kBN, false);
@@ -224,8 +215,9 @@ __global__ void __launch_bounds__(kThreads, 2)
                 if (*abort_flag) break;
                 if (j < n_tiles) {
                     const int b = j & 1;
-                    // S buffer b last held P of tile j-2: its P V must be complete
-                    if (j >= 2 && !(ok = mbar_wait(pv_done + b, ((j - 2) >> 1) & 1))) break;
+                    // S buffer b last held P of tile j-2, read by the P V issued before this
+                    // point: tcgen05.mma from one thread execute in issue order, so the write of
+                    // S_j cannot overtake that read and the issuer never waits for its own MMAs.
                     if (!(ok = mbar_wait(k_full + b, (j >> 1) & 1))) break;
                     tc_fence_after();
                     const uint32_t kb = k_addr + b * kTile;
@@ -265,14 +257,20 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         __syncwarp();
     } else {
-        // ---------------- softmax + epilogue (row r) ----------------
-        const int r = threadIdx.x;
-        const uint32_t t_lane = tbase + (static_cast<uint32_t>(warp * 32) << 16);
+        // ---------------- softmax + epilogue: two threads per query row ----------------
+        // Warp w owns TMEM lanes [row0, row0 + 16), row0 = 32*(w%4) + 16*(w/4) (its own lane
+        // quarter); lane l takes row row0 + l%16 and key columns [32*(l/16), +32) of each tile
+        // (the 16x32bx2 TMEM shape), so the two halves of a row meet in one warp (shfl 16).
+        const int hc = lane >> 4;
+        const int r16 = lane & 15;
+        const int row0 = 32 * (warp & 3) + 16 * (warp >> 2);
+        const int r = row0 + r16;
+        const uint32_t t_w = tbase + (static_cast<uint32_t>(row0) << 16);
         const int qpos = qpos0 + r;
         const int limit = min(tok, qpos + 1);  // keys [0, limit) are visible to this row
         const float sl = a.scale * kLog2e;
         const int tail = n_keys - (n_tiles - 1) * kBN;  // valid keys of the last tile
-        float m_run = -INFINITY, l_run = 0.f;
+        float m_run = -INFINITY, l_run = 0.f;           // l_run: this thread's half of the row sum
         bool ok = true;
         for (int j = 0; j < n_tiles; ++j) {
             if (__any_sync(~0u, *abort_flag != 0)) {
@@ -285,29 +283,29 @@ __global__ void __launch_bounds__(kThreads, 2)
                 break;
             }
             tc_fence_after();
-            uint32_t s0[32], s1[32];
-            tmem_ld32(t_lane + b * kBN, s0);
-            tmem_ld32(t_lane + b * kBN + 32, s1);
+            uint32_t sv[32];
+            tmem_ld16x2_32<32>(t_w + b * kBN, sv);
             tmem_wait_ld();
             // raw scores; masked keys become -inf (sl > 0, so the max commutes with the scale)
-            float x[kBN];
+            float x[32];
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
-                x[c] = __uint_as_float(s0[c]);
-                x[c + 32] = __uint_as_float(s1[c]);
+            for (int c = 0; c < 32; ++c) x[c] = __uint_as_float(sv[c]);
+            const int kb = j * kBN + hc * 32;
+            if (kb + 32 > limit) {
+#pragma unroll
+                for (int c = 0; c < 32; ++c) x[c] = (kb + c < limit) ? x[c] : -INFINITY;
             }
-            const int kb = j * kBN;
-            if (kb + kBN > limit) {
+            float mx0 = x[0], mx1 = x[1], mx2 = x[2], mx3 = x[3];
 #pragma unroll
-                for (int c = 0; c < kBN; ++c) x[c] = (kb + c < limit) ? x[c] : -INFINITY;
-            }
-            float mx0 = x[0], mx1 = x[1];
-#pragma unroll
-            for (int c = 2; c < kBN; c += 2) {
+            for (int c = 4; c < 32; c += 4) {
                 mx0 = fmaxf(mx0, x[c]);
                 mx1 = fmaxf(mx1, x[c + 1]);
+                mx2 = fmaxf(mx2, x[c + 2]);
+                mx3 = fmaxf(mx3, x[c + 3]);
             }
-            const float mt = fmaxf(mx0, mx1) * sl;
+            float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+            mx = fmaxf(mx, __shfl_xor_sync(~0u, mx, 16));  // the row's other half
+            const float mt = mx * sl;
             const bool need = mt > m_run + kRescaleLog2;
             float alpha = 1.f;
             if (need) {
@@ -316,11 +314,11 @@ __global__ void __launch_bounds__(kThreads, 2)
                 l_run *= alpha;
             }
             // p = 2^(s * sl - m): one packed FMA per key pair, then the SFU
-            uint32_t pk[32];
+            uint32_t pk[16];
             float2 sum2 = make_float2(0.f, 0.f);
             const float2 sl2 = make_float2(sl, sl), nm2 = make_float2(-m_run, -m_run);
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
+            for (int c = 0; c < 16; ++c) {
                 const float2 e = __ffma2_rn(make_float2(x[2 * c], x[2 * c + 1]), sl2, nm2);
                 const float2 p = make_float2(fast_exp2(e.x), fast_exp2(e.y));
                 sum2 = __fadd2_rn(sum2, p);
@@ -334,16 +332,18 @@ __global__ void __launch_bounds__(kThreads, 2)
                     ok = false;
                     break;
                 }
-                const int row = r & (kBN - 1);
-                if (row >= tail) {
-                    uint4* dst = reinterpret_cast<uint4*>(sV + b * kTile + (r >> 6) * kHalf + (row >> 3) * 1024 +
+                const int t = threadIdx.x;  // 0..255: (dim half, key) = (t / 64, t % 64) for t < 128
+                const int row = t & (kBN - 1);
+                if (t < 2 * kBN && row >= tail) {
+                    uint4* dst = reinterpret_cast<uint4*>(sV + b * kTile + (t >> 6) * kHalf + (row >> 3) * 1024 +
                                                           (row & 7) * 128);
 #pragma unroll
                     for (int i = 0; i < 8; ++i) dst[i] = make_uint4(0, 0, 0, 0);
                 }
                 fence_proxy_async_smem();
             }
-            tmem_st32(t_lane + b * kBN, pk);  // P over the first 32 columns of its S buffer
+            // P over the first 32 columns of its S buffer: keys 0-31 -> cols 0-15, 32-63 -> 16-31
+            tmem_st16x2_16<16>(t_w + b * kBN, pk);
             if (j > 0 && __any_sync(~0u, need)) {
                 // O holds P V up to tile j-1: wait for it, then rescale the rows that need it
                 if (!__all_sync(~0u, mbar_wait(pv_done + ((j - 1) & 1), ((j - 1) >> 1) & 1))) {
@@ -353,13 +353,13 @@ __global__ void __launch_bounds__(kThreads, 2)
                 }
                 tc_fence_after();
 #pragma unroll 1
-                for (int c4 = 0; c4 < kD / 32; ++c4) {
+                for (int c2 = 0; c2 < 2; ++c2) {  // this thread's 64 of the 128 O columns
                     uint32_t o[32];
-                    tmem_ld32(t_lane + kColO + c4 * 32, o);
+                    tmem_ld16x2_32<64>(t_w + kColO + c2 * 32, o);
                     tmem_wait_ld();
 #pragma unroll
                     for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                    tmem_st32(t_lane + kColO + c4 * 32, o);
+                    tmem_st16x2_32<64>(t_w + kColO + c2 * 32, o);
                 }
             }
             tmem_wait_st();
@@ -375,27 +375,27 @@ __global__ void __launch_bounds__(kThreads, 2)
         } else {
             tc_fence_after();
             // all MMAs and copies are complete: the K/V rings (64 KB) become the staging area,
-            // 16 KB = 32 rows x 512 B per warp, 16-byte chunks XOR-swizzled by row
-            const float inv = 1.f / l_run;
-            uint8_t* stage = sK + warp * (32 * 512);
+            // 8 KB = 16 rows x 512 B per warp, 16-byte chunks XOR-swizzled by row
+            const float inv = 1.f / (l_run + __shfl_xor_sync(~0u, l_run, 16));
+            uint8_t* stage = sK + warp * (16 * 512);
 #pragma unroll 1
-            for (int c4 = 0; c4 < kD / 32; ++c4) {
+            for (int c2 = 0; c2 < 2; ++c2) {
                 uint32_t o[32];
-                tmem_ld32(t_lane + kColO + c4 * 32, o);
+                tmem_ld16x2_32<64>(t_w + kColO + c2 * 32, o);
                 tmem_wait_ld();
+                const int ch0 = (hc * 64 + c2 * 32) / 4;
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
-                    const int ch = c4 * 8 + q;
                     const float4 v = make_float4(__uint_as_float(o[4 * q]) * inv, __uint_as_float(o[4 * q + 1]) * inv,
                                                  __uint_as_float(o[4 * q + 2]) * inv,
                                                  __uint_as_float(o[4 * q + 3]) * inv);
-                    *reinterpret_cast<float4*>(stage + lane * 512 + ((ch ^ (lane & 7)) << 4)) = v;
+                    *reinterpret_cast<float4*>(stage + r16 * 512 + (((ch0 + q) ^ (r16 & 7)) << 4)) = v;
                 }
             }
             __syncwarp();
 #pragma unroll 4
-            for (int rr = 0; rr < 32; ++rr) {
-                const int t = warp * 32 + rr;
+            for (int rr = 0; rr < 16; ++rr) {
+                const int t = row0 + rr;
                 if (t < n_q) {
                     const float4 v = *reinterpret_cast<const float4*>(stage + rr * 512 + ((lane ^ (rr & 7)) << 4));
                     float* dst = a.out + (static_cast<int64_t>(qrow0 + t) * a.n_heads + h) * kD + lane * 4;
@@ -406,7 +406,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == kMmaWarp) {
         tc_fence_after();
         tmem_dealloc(tbase, kTmemCols);
     }
