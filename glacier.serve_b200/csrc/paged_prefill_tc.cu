@@ -8,25 +8,28 @@
 // CTA takes 128 consecutive queries of one (sequence, query head) and streams the
 // sequence's pages in tiles of 64 keys:
 //
-//  * warp 4 (TMA producer): the Q tile once (two boxes of 128 rows x 64 dims), then per key
-//    tile one box per page (16 slots; 8 when the block size is not a multiple of 16) and dim
-//    half, of K and of V, gathered from the arena through the block table with tiled
+//  * warps 8 and 9 (TMA producers, K and V): the Q tile once (two boxes of 128 rows x 64
+//    dims), then per key tile one box per page (16 slots; 8 when the block size is not a
+//    multiple of 16) and dim half, gathered from the arena through the block table with tiled
 //    cp.async.bulk.tensor (128-byte swizzle, no multicast) into 2-stage K and V rings.  Each
 //    lane issues one box: a TMA instruction occupies its issuing thread for on the order of
-//    a hundred cycles, so one thread alone starves the tensor cores.
-//  * warp 5 (one thread issues): S = Q K^T (M=128, N=64, K=128: 8 tcgen05.mma kind::f16,
+//    a hundred cycles, so one thread alone starves the tensor cores.  K and V have their own
+//    warps so that V (which waits for P V two tiles back) never holds back K.
+//  * warp 10 (one thread issues): S = Q K^T (M=128, N=64, K=128: 8 tcgen05.mma kind::f16,
 //    both operands K-major in shared memory) into one of two TMEM S buffers, then
 //    O += P V (M=128, N=128, K=64: 4 MMAs, P read from TMEM, V MN-major in shared memory).
 //    S of tile j+1 is issued before P V of tile j, so the tensor pipe works while the
-//    softmax runs.
-//  * warps 0-3 (query row r = thread r = TMEM lane r): load S, causal mask, base-2 online
-//    softmax with lazy rescaling (O in TMEM is rescaled only when the running max grows by
-//    more than 8, so P stays <= 2^8), P as bf16 written back over its own S columns.
-//    Epilogue: O / l through shared memory as coalesced fp32 rows.
+//    softmax runs; the issuer never waits for its own MMAs (they execute in issue order).
+//  * warps 0-7 (two threads per query row through the 16x32bx2 TMEM shape): load S, causal
+//    mask, base-2 online softmax with lazy rescaling (O in TMEM is rescaled only when the
+//    running max grows by more than 8, so P stays <= 2^8), P as bf16 written back over its
+//    own S columns.  Epilogue: O / l through shared memory as coalesced fp32 rows.
 //
 // Two CTAs share an SM (96 KB shared memory and 256 TMEM columns each), so one CTA's softmax
-// overlaps the other's MMAs.  Every mbarrier wait is bounded: on expiry the CTA raises
-// kErrWaitTimeout, lets its copies and MMAs finish and frees its TMEM.
+// overlaps the other's MMAs; one CTA with two Q tiles sharing K/V measured slower (its
+// single issuer waits on whichever tile's softmax is late), and so did a third K stage.
+// Every mbarrier wait is bounded: on expiry the CTA raises kErrWaitTimeout, lets its copies
+// and MMAs finish and frees its TMEM.
 #include <cuda.h>
 
 #include <atomic>
