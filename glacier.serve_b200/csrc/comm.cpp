@@ -92,7 +92,9 @@ int nccl_wait(gkv_comm* c, const char* what) {
             return set_error(GKV_ETIMEDOUT, "%s: no progress after %d ms; communicator aborted", what,
                              c->timeout_ms);
         }
-        std::this_thread::sleep_for(std::chrono::microseconds(100));
+        // A data-path call finishes enqueueing within microseconds: poll without sleeping
+        // first (a sleep here delays every later launch of the step), then back off.
+        if (ms >= 2) std::this_thread::sleep_for(std::chrono::microseconds(50));
     }
 }
 
