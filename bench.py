@@ -46,8 +46,15 @@ def peaks():
     return 6650.0, "fallback"
 
 
+# Configs whose sequences are one fixed global batch split over the GPUs (strong scaling):
+# cfg3 by longest-first partitioning, cfg5 by block range.  cfg1 / cfg2 give every GPU its own
+# batch (weak scaling).
+STRONG = ("cfg3", "cfg3-bf16", "cfg5")
+
+
 def workload(name: str, rank: int, world: int = 1, batch: int = 0):
-    """batch > 0 shrinks cfg2 / cfg3 to that many sequences (small cases for profiler captures)."""
+    """This rank's workload.  batch > 0 shrinks cfg2 / cfg3 to that many sequences (small cases
+    for profiler captures)."""
     from glacier_kv import workloads as W
 
     seed = W.SEED + 1000003 * rank
@@ -55,10 +62,9 @@ def workload(name: str, rank: int, world: int = 1, batch: int = 0):
         return W.cfg1(seed)
     if name == "cfg2":
         return W.cfg2(seed, batch=batch or 64)
-    if name == "cfg3":
-        return W.cfg3(seed, "f32", batch=batch or 256)
-    if name == "cfg3-bf16":
-        return W.cfg3(seed, "bf16", batch=batch or 256)
+    if name in ("cfg3", "cfg3-bf16"):  # the same 256 sequences everywhere, LPT share per rank
+        w = W.cfg3(W.SEED, "f32" if name == "cfg3" else "bf16", batch=batch or 256)
+        return w if world == 1 else W.lpt_share(w, rank, world)
     if name == "cfg5":  # this rank's block range of the 4 x 131072 sequences
         return W.cfg5_local(rank, world, W.SEED)
     raise SystemExit(f"unknown config {name}")
@@ -467,6 +473,7 @@ def main():
         return
 
     w = workload(args.config, rank, world, args.batch)
+    global_batch = (args.batch or 256) if args.config in ("cfg3", "cfg3-bf16") else w.batch
     pool = W.make_pool(w, device=local)
     W.fill_arena_randn(pool, seed=w.seed)
     stream = torch.cuda.current_stream(dev)
@@ -544,7 +551,8 @@ def main():
     span_ms = t0.elapsed_time(t1) / args.steps
     ms = max_over_ranks(step_ms if flush is not None else span_ms)
     dec_ms = sum(a.elapsed_time(b) for a, b in dec_events) / args.steps
-    seqs_per_step = w.batch if split_kv else world * w.batch  # split-KV: ranks share sequences
+    # strong-scaled configs split one global batch over the ranks; the others add a batch per rank
+    seqs_per_step = global_batch if args.config in STRONG else world * w.batch
     value = seqs_per_step / (ms / 1e3)
 
     # ---- end-to-end through the C ABI with host buffers ----
@@ -588,13 +596,17 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "strong" if args.config == "cfg5" else "weak",
+            "scaling": "strong" if args.config in STRONG else "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) Q/K/V, seeded block tables)",
             "config": {"workload": describe(w),
                        "l2": "L2 flushed (256 MiB write) before every step" if small else
                              f"inputs larger than L2 ({kv_bytes / 1e9:.2f} GB of KV read per step)",
-                       "parallelism": (f"split-KV: each sequence's blocks split over {world} GPU(s), NCCL all-gather "
-                                       "of (out, lse) + LSE merge") if split_kv else
+                       "parallelism": (f"split-KV: each sequence's blocks split over {world} GPU(s), (out, lse) "
+                                       "exchanged through peer-memory mailboxes (NCCL all-gather fallback) + LSE "
+                                       "merge") if split_kv else
+                                      (f"sequence-sharded: the {global_batch} sequences split over {world} GPU(s) by "
+                                       "longest-first partitioning, one pool each, no collective")
+                                      if args.config in STRONG else
                                       f"sequence-sharded: {world} GPU(s), one pool each, no collective",
                        "step": "upload tables+slots (1 H2D) + kv_append + paged_decode (+ LSE merge)"},
             "kv_gbs_per_gpu": kv_bytes / (ms / 1e3) / 1e9,

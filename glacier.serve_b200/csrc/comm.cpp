@@ -7,8 +7,15 @@
 // those (rows * (dv + 1) floats each) with NCCL over NVLink, and every rank merges them:
 // out = sum_r exp(lse_r - LSE) * out_r, LSE = ln(sum_r exp(lse_r) [+ exp(sink)]).
 //
+// The exchange itself goes through peer memory when the ranks can map each other's HBM (CUDA
+// IPC over NVLink, set up once with two small NCCL all-gathers): each rank stores its block
+// straight into every rank's mailbox and the merge waits on epoch flags (exchange.cu).  That
+// replaces a ring all-gather whose N-1 latency-bound steps cost more than the decode itself
+// at 8 ranks.  Without peer mappings the ranks agree to use ncclAllGather instead.
+//
 // Every NCCL wait is bounded: the communicator is created non-blocking and polled against a
-// host timeout, and a timeout aborts it (ncclCommAbort) and returns GKV_ETIMEDOUT.
+// host timeout, and a timeout aborts it (ncclCommAbort) and returns GKV_ETIMEDOUT.  The merge
+// kernel's wait on peer flags is bounded too (kErrWaitTimeout in the pool's error word).
 #include <dlfcn.h>
 #include <nccl.h>
 
@@ -19,6 +26,7 @@
 #include <mutex>
 #include <thread>
 #include <type_traits>
+#include <vector>
 
 #include "gkv_internal.h"
 
@@ -29,6 +37,12 @@ struct gkv_comm {
     float* d_recv = nullptr;
     size_t cap_floats = 0;  // per rank
     bool aborted = false;
+    // peer-memory exchange: 0 = not set up yet, 1 = NCCL all-gather, 2 = peer mailboxes
+    int kind = 0;
+    void* d_mbox = nullptr;                     // this rank's mailbox (floats, then flags)
+    void* peer_base[gkv::kMaxExchangeRanks] = {};  // IPC mappings of the other ranks' mailboxes
+    gkv::ExchangePeers peers{};
+    unsigned epoch = 0;
 };
 
 namespace {
@@ -98,6 +112,93 @@ int nccl_wait(gkv_comm* c, const char* what) {
     }
 }
 
+// NCCL all-gather of `bytes` per rank through device buffers, completed before returning.
+int allgather_host(gkv_comm* c, const void* mine, void* all, size_t bytes, cudaStream_t st) {
+    void* d = nullptr;
+    cudaError_t e = cudaMalloc(&d, bytes * (c->n_ranks + 1));
+    if (e != cudaSuccess) return gkv::cuda_fail(e, "cudaMalloc(exchange set-up)");
+    char* send = static_cast<char*>(d) + bytes * c->n_ranks;
+    int rc = GKV_OK;
+    e = cudaMemcpyAsync(send, mine, bytes, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) rc = gkv::cuda_fail(e, "cudaMemcpyAsync(exchange set-up)");
+    if (rc == GKV_OK) {
+        ncclResult_t r = nccl().AllGather(send, d, bytes, ncclChar, c->comm, st);
+        if (r == ncclInProgress) rc = nccl_wait(c, "ncclAllGather(exchange set-up)");
+        else if (r != ncclSuccess) rc = nccl_fail(r, "ncclAllGather(exchange set-up)");
+    }
+    if (rc == GKV_OK) {
+        e = cudaMemcpyAsync(all, d, bytes * c->n_ranks, cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) rc = gkv::cuda_fail(e, "exchange set-up copy");
+    }
+    cudaFree(d);
+    return rc;
+}
+
+void release_p2p(gkv_comm* c) {
+    for (int r = 0; r < gkv::kMaxExchangeRanks; ++r)
+        if (c->peer_base[r]) {
+            cudaIpcCloseMemHandle(c->peer_base[r]);
+            c->peer_base[r] = nullptr;
+        }
+    if (c->d_mbox) cudaFree(c->d_mbox);
+    c->d_mbox = nullptr;
+}
+
+// Collective: every rank calls it on its first split-KV decode with the same slot size.
+// Sets c->kind to 2 when every rank mapped every other rank's mailbox, else to 1.
+int setup_exchange(gkv_comm* c, int64_t per, cudaStream_t st) {
+    const int n = c->n_ranks;
+    const int64_t slot = (per + 3) / 4 * 4 * 2;  // room for twice the first call's rows
+    const size_t floats_bytes = static_cast<size_t>(2) * n * slot * sizeof(float);
+    const size_t bytes = floats_bytes + static_cast<size_t>(2) * n * sizeof(unsigned);
+    struct Entry {
+        cudaIpcMemHandle_t handle;
+        int32_t ok;
+    } mine{};
+    mine.ok = n <= gkv::kMaxExchangeRanks;
+    if (mine.ok && cudaMalloc(&c->d_mbox, bytes) != cudaSuccess) mine.ok = 0;
+    if (mine.ok && cudaMemset(c->d_mbox, 0, bytes) != cudaSuccess) mine.ok = 0;
+    if (mine.ok && cudaIpcGetMemHandle(&mine.handle, c->d_mbox) != cudaSuccess) mine.ok = 0;
+    cudaGetLastError();
+    std::vector<Entry> all(static_cast<size_t>(n));
+    int rc = allgather_host(c, &mine, all.data(), sizeof(Entry), st);
+    if (rc != GKV_OK) return rc;
+    int32_t ok = 1;
+    for (const Entry& en : all) ok &= en.ok;
+    if (ok) {
+        for (int r = 0; r < n; ++r) {
+            if (r == c->rank) continue;
+            if (cudaIpcOpenMemHandle(&c->peer_base[r], all[static_cast<size_t>(r)].handle,
+                                     cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                c->peer_base[r] = nullptr;
+                ok = 0;
+                break;
+            }
+        }
+        cudaGetLastError();
+    }
+    // every rank must take the same path
+    std::vector<int32_t> oks(static_cast<size_t>(n));
+    rc = allgather_host(c, &ok, oks.data(), sizeof(int32_t), st);
+    if (rc != GKV_OK) return rc;
+    for (int32_t v : oks) ok &= v;
+    if (!ok) {
+        release_p2p(c);
+        c->kind = 1;
+        return GKV_OK;
+    }
+    c->peers.n_ranks = n;
+    c->peers.slot = slot;
+    for (int r = 0; r < n; ++r) {
+        char* base = static_cast<char*>(r == c->rank ? c->d_mbox : c->peer_base[r]);
+        c->peers.mbox[r] = reinterpret_cast<float*>(base);
+        c->peers.flags[r] = reinterpret_cast<unsigned*>(base + floats_bytes);
+    }
+    c->kind = 2;
+    return GKV_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -163,11 +264,15 @@ int gkv_comm_destroy(gkv_comm* c) {
         nccl_wait(c, "ncclCommFinalize");
         if (c->comm) nccl().CommDestroy(c->comm);
     }
+    cudaDeviceSynchronize();  // the last merge has read every peer's block
+    release_p2p(c);
     if (c->d_send) cudaFree(c->d_send);
     if (c->d_recv) cudaFree(c->d_recv);
     delete c;
     return GKV_OK;
 }
+
+int gkv_comm_exchange_kind(const gkv_comm* c) { return c ? c->kind : 0; }
 
 int gkv_paged_decode_lse(gkv_pool* pool, int32_t layer, const float* d_q, float* d_out,
                          float* d_lse, int32_t n_heads, float scale, const float* d_sinks,
@@ -207,16 +312,17 @@ int gkv_paged_decode_splitkv_dist(gkv_pool* pool, gkv_comm* c, int32_t layer, co
     const int32_t dv = P.desc.v_head_dim;
     const int64_t rows = static_cast<int64_t>(P.ws.batch) * n_heads;
     const size_t per = static_cast<size_t>(rows) * (dv + 1);
-    if (per > c->cap_floats) {
+    const size_t per4 = (per + 3) / 4 * 4;  // the push moves whole float4s
+    if (per4 > c->cap_floats) {
         cudaDeviceSynchronize();
         if (c->d_send) cudaFree(c->d_send);
         if (c->d_recv) cudaFree(c->d_recv);
         c->d_send = c->d_recv = nullptr;
         c->cap_floats = 0;
-        cudaError_t e = cudaMalloc(&c->d_send, per * sizeof(float));
-        if (e == cudaSuccess) e = cudaMalloc(&c->d_recv, per * sizeof(float) * c->n_ranks);
+        cudaError_t e = cudaMalloc(&c->d_send, per4 * sizeof(float));
+        if (e == cudaSuccess) e = cudaMalloc(&c->d_recv, per4 * sizeof(float) * c->n_ranks);
         if (e != cudaSuccess) return gkv::cuda_fail(e, "cudaMalloc(split-KV exchange)");
-        c->cap_floats = per;
+        c->cap_floats = per4;
     }
     float* send_out = c->d_send;
     float* send_lse = c->d_send + rows * dv;
@@ -227,6 +333,24 @@ int gkv_paged_decode_splitkv_dist(gkv_pool* pool, gkv_comm* c, int32_t layer, co
     int rc = gkv::step_decode_lse(&P, layer, d_q, send_out, send_lse, n_heads, scale, nullptr, st);
     if (rc != GKV_OK) return rc;
     const int launches = P.last_launches + 1;
+    if (c->kind == 0) {
+        rc = setup_exchange(c, static_cast<int64_t>(per), st);
+        if (rc != GKV_OK) return rc;
+    }
+    // the slot size is fixed at set-up; every rank sees the same rows, so all take the same path
+    if (c->kind == 2 && static_cast<int64_t>(per4) <= c->peers.slot) {
+        const unsigned ep = ++c->epoch;
+        const int parity = static_cast<int>(ep & 1u);
+        e = gkv::launch_exchange_push(c->d_send, static_cast<int64_t>(per), c->peers, c->rank, ep, parity, st);
+        if (e != cudaSuccess) return gkv::cuda_fail(e, "exchange push launch");
+        const float* mb = c->peers.mbox[c->rank] + static_cast<int64_t>(parity) * c->n_ranks * c->peers.slot;
+        const unsigned* fl = c->peers.flags[c->rank] + parity * c->n_ranks;
+        e = gkv::launch_exchange_merge(mb, fl, c->n_ranks, c->peers.slot, static_cast<int>(rows), dv, d_sinks, n_heads,
+                                       d_out, ep, P.ws.d_err, st);
+        if (e != cudaSuccess) return gkv::cuda_fail(e, "exchange merge launch");
+        P.last_launches = launches + 2;
+        return GKV_OK;
+    }
     ncclResult_t r = nccl().AllGather(c->d_send, c->d_recv, per, ncclFloat, c->comm, st);
     if (r == ncclInProgress) {
         rc = nccl_wait(c, "ncclAllGather");

@@ -99,6 +99,26 @@ cudaError_t launch_lse_merge(const float* parts, int n_parts, int rows, int dv, 
 // x[0..n) = value
 cudaError_t launch_fill(float* x, int64_t n, float value, cudaStream_t st);
 
+// ---- peer-memory exchange of split-KV partials (exchange.cu) ----
+// Mailbox of rank r, as this rank addresses it: mbox[r] = [2][n_ranks][slot] floats,
+// flags[r] = [2][n_ranks] epoch words (own rank: local pointers; peers: CUDA IPC mappings).
+constexpr int kMaxExchangeRanks = 16;
+struct ExchangePeers {
+    float* mbox[kMaxExchangeRanks];
+    unsigned* flags[kMaxExchangeRanks];
+    int n_ranks;
+    int64_t slot;  // floats per slot, a multiple of 4
+};
+// Stores this rank's n_floats (rounded up to whole float4s; src must hold them) into slot
+// [parity][me] of every rank's mailbox, then publishes `epoch` in its flag [parity][me].
+cudaError_t launch_exchange_push(const float* src, int64_t n_floats, const ExchangePeers& p, int me, unsigned epoch,
+                                 int parity, cudaStream_t st);
+// Waits (bounded) until all n_parts flags of this rank's mailbox parity read `epoch`, then
+// merges the n_parts (out, lse) blocks as launch_lse_merge.
+cudaError_t launch_exchange_merge(const float* mbox_parity, const unsigned* flags_parity, int n_parts, int64_t slot,
+                                  int rows, int dv, const float* sinks, int n_heads, float* out, unsigned epoch,
+                                  int* err, cudaStream_t st);
+
 // Launch configuration the decode kernel uses for this geometry and query-head count.
 struct DecodeConfig {
     bool supported;

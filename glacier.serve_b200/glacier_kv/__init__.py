@@ -488,6 +488,11 @@ class Comm:
     def handle(self):
         return self._h
 
+    @property
+    def exchange_kind(self) -> int:
+        """0 = undecided (the first split-KV decode decides), 1 = NCCL all-gather, 2 = peer mailboxes."""
+        return lib.gkv_comm_exchange_kind(self._h) if self._h else 0
+
     def abort(self) -> None:
         if self._h:
             lib.gkv_comm_abort(self._h)

@@ -142,6 +142,7 @@ SIGNATURES = {
     "gkv_comm_init": (C.c_int, [P, I32, I32, I32, I32, C.POINTER(P)]),
     "gkv_comm_abort": (C.c_int, [P]),
     "gkv_comm_destroy": (C.c_int, [P]),
+    "gkv_comm_exchange_kind": (C.c_int, [P]),
     "gkv_paged_decode_splitkv_dist": (C.c_int, [P, P, I32, P, P, I32, F32, P, P]),
     "gkv_partition_lpt": (C.c_int, [P, I32, I32, P]),
     "gkv_split_block_range": (C.c_int, [I32, I32, I32, PI32, PI32]),

@@ -158,6 +158,18 @@ def cfg3(seed: int = SEED, dtype: str = "f32", batch: int = 256, total_blocks: i
                           np.zeros(0, np.int64), np.zeros(0, np.int32), 1.0 / math.sqrt(128), seed)
 
 
+def lpt_share(w: DecodeWorkload, rank: int, world: int) -> DecodeWorkload:
+    """This rank's sequences of `w` under longest-first partitioning (gkv_partition_lpt): the
+    same global batch split over `world` GPUs, each with the whole pool geometry."""
+    from . import partition_lpt
+
+    rows = np.nonzero(partition_lpt(w.ctx_lens, world) == rank)[0]
+    ctx = w.ctx_lens[rows]
+    nb = max(1, max((int(c) + w.block_size - 1) // w.block_size for c in ctx)) if rows.size else 1
+    tables = np.ascontiguousarray(w.tables[rows, :nb])
+    return dataclasses.replace(w, ctx_lens=ctx, tables=tables)
+
+
 def cfg5_local(rank: int, world: int, seed: int = SEED, batch: int = 4, ctx: int = 131072) -> DecodeWorkload:
     """Rank `rank`'s contiguous block range of each long sequence (split-KV across GPUs)."""
     from . import split_block_range

@@ -151,12 +151,20 @@ def _dist_worker(rank, world, q_uid, ret):
             q_uid.put(uid)
     comm = G2.Comm(uid, world, rank, rank, timeout_ms=60_000)
     pool.upload_step(local, lens)
-    out = torch.zeros((3, nH, d), device=dev)
-    pool.paged_decode_splitkv_dist(comm, 0, torch.from_numpy(q).to(dev), out, nH, 1 / math.sqrt(d))
-    torch.cuda.synchronize(dev)
     g = O2.geom(total, 1, nKv, d, d, bs, O2.BF16)
-    ref = O2.decode_batch(np.ascontiguousarray(Kb), np.ascontiguousarray(Vb), g, 0, tables, ctx, q, nH, 1 / math.sqrt(d))
-    ret[rank] = float(np.abs(out.cpu().numpy() - ref).max())
+    err = 0.0
+    # several decodes: the peer mailboxes alternate parity every call
+    for step in range(4):
+        qs = q if step == 0 else np.random.default_rng(100 + step).standard_normal(q.shape).astype(np.float32)
+        out = torch.zeros((3, nH, d), device=dev)
+        pool.paged_decode_splitkv_dist(comm, 0, torch.from_numpy(qs).to(dev), out, nH, 1 / math.sqrt(d))
+        torch.cuda.synchronize(dev)
+        ref = O2.decode_batch(np.ascontiguousarray(Kb), np.ascontiguousarray(Vb), g, 0, tables, ctx, qs, nH,
+                              1 / math.sqrt(d))
+        err = max(err, float(np.abs(out.cpu().numpy() - ref).max()))
+    pool.sync()
+    ret[rank] = err
+    ret[f"kind{rank}"] = comm.exchange_kind
     comm.close()
     pool.close()
 
@@ -175,3 +183,5 @@ def test_two_gpu_nccl_split_kv(cuda):
     [p.join(timeout=300) for p in procs]
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert ret[0] < TOL["bf16"] and ret[1] < TOL["bf16"], dict(ret)
+    # NVLink peers map each other's mailboxes: the exchange must not fall back to NCCL
+    assert ret["kind0"] == 2 and ret["kind1"] == 2, dict(ret)

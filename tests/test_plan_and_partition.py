@@ -99,3 +99,20 @@ def test_workload_generators_match_the_configs():
     assert np.mean(first[:, 1] - first[:, 0] != 1) > 0.2
     w5 = W.cfg5_local(3, 8)
     assert w5.batch == 4 and np.all(w5.ctx_lens == 131072 // 8)
+
+
+def test_lpt_shares_cover_the_global_batch_once():
+    w = W.cfg3(ops=2000)
+    for world in (1, 2, 8):
+        shares = [W.lpt_share(w, r, world) for r in range(world)]
+        assert sum(s.batch for s in shares) == w.batch
+        assert sum(int(s.ctx_lens.sum()) for s in shares) == int(w.ctx_lens.sum())
+        # every share keeps its sequences' own table rows
+        rank = G.partition_lpt(w.ctx_lens, world)
+        for r, s in enumerate(shares):
+            rows = np.nonzero(rank == r)[0]
+            assert np.array_equal(s.ctx_lens, w.ctx_lens[rows])
+            assert np.array_equal(s.tables, w.tables[rows, : s.tables.shape[1]])
+            assert np.all(w.tables[rows, s.tables.shape[1]:] < 0)
+        loads = [int(s.ctx_lens.sum()) for s in shares]
+        assert max(loads) <= int(w.ctx_lens.sum()) / world + int(w.ctx_lens.max())
