@@ -87,11 +87,21 @@ struct StepWorkspace {
     // device error word shared by every kernel of this pool
     int* d_err = nullptr;
     // e2e staging for gkv_decode_step_host
-    float* d_q = nullptr;
-    float* d_out = nullptr;
-    float* d_knew = nullptr;
-    float* d_vnew = nullptr;
-    size_t io_cap_q = 0, io_cap_out = 0, io_cap_k = 0, io_cap_v = 0;
+    // Two slots, used by consecutive calls in turn: the inputs of call k+1 travel on io_in and
+    // the output of call k on io_out while the caller's stream computes.
+    struct IoSlot {
+        float* d_q = nullptr;
+        float* d_out = nullptr;
+        float* d_knew = nullptr;
+        float* d_vnew = nullptr;
+        size_t cap_q = 0, cap_out = 0, cap_k = 0, cap_v = 0;
+        cudaEvent_t in_done = nullptr;    // inputs copied
+        cudaEvent_t used = nullptr;       // append + decode finished reading inputs, writing out
+        cudaEvent_t out_done = nullptr;   // output copied back
+        bool used_pending = false, out_pending = false;
+    } io[2];
+    cudaStream_t io_in = nullptr, io_out = nullptr;
+    int io_next = 0;
     // the uploaded step
     int32_t batch = 0, n_tok = 0, up_max_blocks = 0;
     DecodeWork work{};

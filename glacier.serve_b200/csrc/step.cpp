@@ -247,10 +247,21 @@ void step_free(Pool* p) {
     if (ws.d_part_ml) cudaFree(ws.d_part_ml);
     if (ws.d_merge_count) cudaFree(ws.d_merge_count);
     ws.d_merge_count = nullptr;
-    if (ws.d_q) cudaFree(ws.d_q);
-    if (ws.d_out) cudaFree(ws.d_out);
-    if (ws.d_knew) cudaFree(ws.d_knew);
-    if (ws.d_vnew) cudaFree(ws.d_vnew);
+    if (ws.io_in) cudaStreamSynchronize(ws.io_in);
+    if (ws.io_out) cudaStreamSynchronize(ws.io_out);
+    for (auto& io : ws.io) {
+        if (io.d_q) cudaFree(io.d_q);
+        if (io.d_out) cudaFree(io.d_out);
+        if (io.d_knew) cudaFree(io.d_knew);
+        if (io.d_vnew) cudaFree(io.d_vnew);
+        if (io.in_done) cudaEventDestroy(io.in_done);
+        if (io.used) cudaEventDestroy(io.used);
+        if (io.out_done) cudaEventDestroy(io.out_done);
+        io = StepWorkspace::IoSlot{};
+    }
+    if (ws.io_in) cudaStreamDestroy(ws.io_in);
+    if (ws.io_out) cudaStreamDestroy(ws.io_out);
+    ws.io_in = ws.io_out = nullptr;
     if (ws.pre_copied) cudaEventDestroy(ws.pre_copied);
     if (ws.h_pre) cudaFreeHost(ws.h_pre);
     if (ws.d_pre) cudaFree(ws.d_pre);
@@ -261,7 +272,6 @@ void step_free(Pool* p) {
     ws.meta_copied = nullptr;
     ws.h_meta = ws.d_meta = nullptr;
     ws.d_part_acc = ws.d_part_ml = nullptr;
-    ws.d_q = ws.d_out = ws.d_knew = ws.d_vnew = nullptr;
 }
 
 int step_upload(Pool* p, const int32_t* tables, int32_t batch, int32_t max_blocks,
@@ -839,24 +849,60 @@ int gkv_decode_step_host(gkv_pool* pool, int32_t layer, const int32_t* h_block_t
     const size_t ob = static_cast<size_t>(batch) * n_heads * P.desc.v_head_dim * sizeof(float);
     const size_t kb = static_cast<size_t>(n_tok) * P.desc.heads_kv * P.desc.head_dim * sizeof(float);
     const size_t vb = static_cast<size_t>(n_tok) * P.desc.heads_kv * P.desc.v_head_dim * sizeof(float);
-    int rc = gkv::grow_device(reinterpret_cast<void**>(&ws.d_q), &ws.io_cap_q, qb, "cudaMalloc(q)");
-    if (rc == GKV_OK) rc = gkv::grow_device(reinterpret_cast<void**>(&ws.d_out), &ws.io_cap_out, ob, "cudaMalloc(out)");
-    if (rc == GKV_OK) rc = gkv::grow_device(reinterpret_cast<void**>(&ws.d_knew), &ws.io_cap_k, kb, "cudaMalloc(k_new)");
-    if (rc == GKV_OK) rc = gkv::grow_device(reinterpret_cast<void**>(&ws.d_vnew), &ws.io_cap_v, vb, "cudaMalloc(v_new)");
-    if (rc != GKV_OK) return rc;
     cudaError_t e = cudaSuccess;
-    if (qb) e = cudaMemcpyAsync(ws.d_q, h_q, qb, cudaMemcpyHostToDevice, st);
-    if (e == cudaSuccess && kb) e = cudaMemcpyAsync(ws.d_knew, h_k_new, kb, cudaMemcpyHostToDevice, st);
-    if (e == cudaSuccess && vb) e = cudaMemcpyAsync(ws.d_vnew, h_v_new, vb, cudaMemcpyHostToDevice, st);
+    if (!ws.io_in) e = cudaStreamCreateWithFlags(&ws.io_in, cudaStreamNonBlocking);
+    if (e == cudaSuccess && !ws.io_out) e = cudaStreamCreateWithFlags(&ws.io_out, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return gkv::cuda_fail(e, "cudaStreamCreate(step copies)");
+    // Slot of this call; the call two back used it last.
+    auto& io = ws.io[ws.io_next];
+    auto& prev = ws.io[ws.io_next ^ 1];
+    for (cudaEvent_t* ev : {&io.in_done, &io.used, &io.out_done})
+        if (!*ev && (e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming)) != cudaSuccess)
+            return gkv::cuda_fail(e, "cudaEventCreate(step copies)");
+    if (qb > io.cap_q || ob > io.cap_out || kb > io.cap_k || vb > io.cap_v) {
+        // growing frees buffers the earlier calls' copies may still use
+        cudaStreamSynchronize(ws.io_in);
+        cudaStreamSynchronize(ws.io_out);
+        cudaStreamSynchronize(st);
+    }
+    int rc = gkv::grow_device(reinterpret_cast<void**>(&io.d_q), &io.cap_q, qb, "cudaMalloc(q)");
+    if (rc == GKV_OK) rc = gkv::grow_device(reinterpret_cast<void**>(&io.d_out), &io.cap_out, ob, "cudaMalloc(out)");
+    if (rc == GKV_OK) rc = gkv::grow_device(reinterpret_cast<void**>(&io.d_knew), &io.cap_k, kb, "cudaMalloc(k_new)");
+    if (rc == GKV_OK) rc = gkv::grow_device(reinterpret_cast<void**>(&io.d_vnew), &io.cap_v, vb, "cudaMalloc(v_new)");
+    if (rc != GKV_OK) return rc;
+    // inputs: on the copy stream, once the call two back has finished reading this slot
+    if (io.used_pending) e = cudaStreamWaitEvent(ws.io_in, io.used, 0);
+    if (e == cudaSuccess && qb) e = cudaMemcpyAsync(io.d_q, h_q, qb, cudaMemcpyHostToDevice, ws.io_in);
+    if (e == cudaSuccess && kb) e = cudaMemcpyAsync(io.d_knew, h_k_new, kb, cudaMemcpyHostToDevice, ws.io_in);
+    if (e == cudaSuccess && vb) e = cudaMemcpyAsync(io.d_vnew, h_v_new, vb, cudaMemcpyHostToDevice, ws.io_in);
+    if (e == cudaSuccess) e = cudaEventRecord(io.in_done, ws.io_in);
     if (e != cudaSuccess) return gkv::cuda_fail(e, "cudaMemcpyAsync(step inputs)");
     rc = gkv::step_upload(&P, h_block_tables, batch, max_blocks, h_ctx_lens, h_slot_mapping, n_tok, st);
     if (rc != GKV_OK) return rc;
-    rc = gkv::step_append(&P, layer, ws.d_knew, ws.d_vnew, n_tok, st);
+    // compute on the caller's stream once the inputs are in and this slot's previous output
+    // has been copied out
+    e = cudaStreamWaitEvent(st, io.in_done, 0);
+    if (e == cudaSuccess && io.out_pending) e = cudaStreamWaitEvent(st, io.out_done, 0);
+    if (e != cudaSuccess) return gkv::cuda_fail(e, "cudaStreamWaitEvent(step inputs)");
+    rc = gkv::step_append(&P, layer, io.d_knew, io.d_vnew, n_tok, st);
     if (rc != GKV_OK) return rc;
-    rc = gkv::step_decode(&P, layer, ws.d_q, ws.d_out, n_heads, scale, d_sinks, st);
+    rc = gkv::step_decode(&P, layer, io.d_q, io.d_out, n_heads, scale, d_sinks, st);
     if (rc != GKV_OK) return rc;
-    if (ob) e = cudaMemcpyAsync(h_out, ws.d_out, ob, cudaMemcpyDeviceToHost, st);
+    e = cudaEventRecord(io.used, st);
+    io.used_pending = e == cudaSuccess;
+    // output: on the other copy stream, overlapping the next call's compute
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(ws.io_out, io.used, 0);
+    if (e == cudaSuccess && ob) e = cudaMemcpyAsync(h_out, io.d_out, ob, cudaMemcpyDeviceToHost, ws.io_out);
+    if (e == cudaSuccess) e = cudaEventRecord(io.out_done, ws.io_out);
     if (e != cudaSuccess) return gkv::cuda_fail(e, "cudaMemcpyAsync(step output)");
+    io.out_pending = true;
+    // the caller's stream passes this point only after the previous call's output arrived, so
+    // completing call k on `stream` means h_out of call k-1 is there; gkv_sync covers call k
+    if (prev.out_pending) {
+        e = cudaStreamWaitEvent(st, prev.out_done, 0);
+        if (e != cudaSuccess) return gkv::cuda_fail(e, "cudaStreamWaitEvent(previous output)");
+    }
+    ws.io_next ^= 1;
     return GKV_OK;
 }
 
@@ -896,8 +942,11 @@ int gkv_sync(gkv_pool* pool, void* stream, int32_t timeout_ms) {
     std::unique_ptr<gkv::DeviceGuard> guard;
     if (pool && pool->impl.has_arena) guard.reset(new gkv::DeviceGuard(pool->impl.desc.device));
     const auto t0 = std::chrono::steady_clock::now();
+    // the host-buffer step copies its output back on an internal stream
+    const cudaStream_t io_out = (pool && pool->impl.has_arena) ? pool->impl.ws.io_out : nullptr;
     for (;;) {
-        const cudaError_t e = cudaStreamQuery(st);
+        cudaError_t e = cudaStreamQuery(st);
+        if (e == cudaSuccess && io_out) e = cudaStreamQuery(io_out);
         if (e == cudaSuccess) break;
         if (e != cudaErrorNotReady) return gkv::cuda_fail(e, "cudaStreamQuery");
         const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(

@@ -241,7 +241,10 @@ GKV_API int gkv_compute_attention(gkv_pool* pool, int32_t stage_layer, int32_t m
  * CudaPagedTransformerRunner.ForwardBatch (CudaPagedTransformerRunner.cs:307-364) for the
  * attention part: copies h_q, h_k_new, h_v_new and the packed metadata to the device,
  * appends the new tokens, decodes every sequence and copies the output back to h_out.
- * Everything is enqueued on `stream`; call gkv_sync before reading h_out. */
+ * Consecutive calls overlap: the host-to-device copies of a call and the device-to-host
+ * copy of the previous one run on the pool's own copy streams while `stream` computes.  The
+ * compute is enqueued on `stream`, which also waits for the previous call's output copy;
+ * call gkv_sync(pool, stream, ...) before reading h_out or reusing the host inputs. */
 GKV_API int gkv_decode_step_host(gkv_pool* pool, int32_t layer, const int32_t* h_block_tables,
                                  int32_t batch, int32_t max_blocks, const int32_t* h_ctx_lens,
                                  const int64_t* h_slot_mapping, int32_t n_tok,

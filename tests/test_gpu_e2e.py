@@ -93,3 +93,24 @@ def test_cfg5_local_shard_parity(cuda):
     ref = O.decode_batch(K, V, g, 0, sub, w.ctx_lens[:2], q[:2], w.n_heads, w.scale)
     np.testing.assert_allclose(out[:2], ref, atol=TOL["bf16"], rtol=0)
     pool.close()
+
+
+def test_consecutive_host_steps_overlap_and_stay_exact(cuda):
+    """Back-to-back host-buffer calls (copies of one call overlap the neighbours' compute):
+    every call's output equals the device path for its own q, bit for bit."""
+    import torch
+
+    w, pool = _cfg2_pool()
+    rng = np.random.default_rng(w.seed + 3)
+    kn = torch.from_numpy(rng.standard_normal((w.batch, w.heads_kv, w.head_dim)).astype(np.float32)).pin_memory()
+    vn = torch.from_numpy(rng.standard_normal((w.batch, w.heads_kv, w.v_head_dim)).astype(np.float32)).pin_memory()
+    qs = [rng.standard_normal((w.batch, w.n_heads, w.head_dim)).astype(np.float32) for _ in range(5)]
+    hqs = [torch.from_numpy(q).pin_memory() for q in qs]
+    houts = [torch.full((w.batch, w.n_heads, w.v_head_dim), np.nan, dtype=torch.float32).pin_memory() for _ in qs]
+    for hq, hout in zip(hqs, houts):  # no sync between the calls
+        pool.decode_step_host(0, w.tables, w.ctx_lens, w.slot_mapping, kn, vn, hq, hout, w.n_heads, w.scale)
+    pool.sync()
+    for q, hout in zip(qs, houts):
+        dev = gpu_decode(pool, 0, w.tables, w.ctx_lens, q, w.n_heads, w.scale)
+        assert np.array_equal(hout.numpy(), dev)
+    pool.close()
