@@ -71,12 +71,15 @@ struct StepWorkspace {
     int32_t max_batch = 0, max_blocks = 0, max_tokens = 0, n_heads = 0;
     DecodeConfig cfg{};
     int32_t n_ctas_max = 0;   // persistent grid size for this geometry
-    // packed metadata: one pinned staging buffer, one device buffer, one copy per step
-    char* h_meta = nullptr;
+    // packed metadata: one device buffer and one copy per step, from two pinned staging
+    // buffers used in turn, so the host fills step k+1's while step k's copy may still be in
+    // flight
+    char* h_meta[2] = {nullptr, nullptr};
     char* d_meta = nullptr;
     size_t meta_cap = 0;
-    cudaEvent_t meta_copied = nullptr;  // staging buffer may be rewritten once this fires
-    bool meta_pending = false;
+    cudaEvent_t meta_copied[2] = {nullptr, nullptr};  // staging i may be rewritten once this fires
+    bool meta_pending[2] = {false, false};
+    int meta_flip = 0;
     // partial results of split segments
     float* d_part_acc = nullptr;
     float* d_part_ml = nullptr;

@@ -150,21 +150,25 @@ void build_work_list(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, i
 // (cudaFree synchronises the device).
 static int ensure_meta(Pool* p, size_t bytes) {
     StepWorkspace& ws = p->ws;
-    if (!ws.meta_copied) {
-        cudaError_t e = cudaEventCreateWithFlags(&ws.meta_copied, cudaEventDisableTiming);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
-    }
+    for (int i = 0; i < 2; ++i)
+        if (!ws.meta_copied[i]) {
+            cudaError_t e = cudaEventCreateWithFlags(&ws.meta_copied[i], cudaEventDisableTiming);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
+        }
     if (bytes <= ws.meta_cap) return GKV_OK;
-    if (ws.meta_pending) cudaEventSynchronize(ws.meta_copied);
-    ws.meta_pending = false;
-    if (ws.h_meta) cudaFreeHost(ws.h_meta);
+    for (int i = 0; i < 2; ++i) {
+        if (ws.meta_pending[i]) cudaEventSynchronize(ws.meta_copied[i]);
+        ws.meta_pending[i] = false;
+        if (ws.h_meta[i]) cudaFreeHost(ws.h_meta[i]);
+        ws.h_meta[i] = nullptr;
+    }
     if (ws.d_meta) cudaFree(ws.d_meta);
-    ws.h_meta = nullptr;
     ws.d_meta = nullptr;
     ws.meta_cap = 0;
     ws.uploaded = false;  // the previous step's metadata is gone
     const size_t cap = align_up(bytes, 4096);
-    cudaError_t e = cudaMallocHost(&ws.h_meta, cap);
+    cudaError_t e = cudaSuccess;
+    for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = cudaMallocHost(&ws.h_meta[i], cap);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMallocHost(step metadata)");
     e = cudaMalloc(&ws.d_meta, cap);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(step metadata)");
@@ -240,8 +244,12 @@ int step_reserve(Pool* p, int32_t max_batch, int32_t max_blocks, int32_t max_tok
 
 void step_free(Pool* p) {
     StepWorkspace& ws = p->ws;
-    if (ws.meta_copied) cudaEventDestroy(ws.meta_copied);
-    if (ws.h_meta) cudaFreeHost(ws.h_meta);
+    for (int i = 0; i < 2; ++i) {
+        if (ws.meta_copied[i]) cudaEventDestroy(ws.meta_copied[i]);
+        if (ws.h_meta[i]) cudaFreeHost(ws.h_meta[i]);
+        ws.meta_copied[i] = nullptr;
+        ws.h_meta[i] = nullptr;
+    }
     if (ws.d_meta) cudaFree(ws.d_meta);
     if (ws.d_part_acc) cudaFree(ws.d_part_acc);
     if (ws.d_part_ml) cudaFree(ws.d_part_ml);
@@ -269,8 +277,7 @@ void step_free(Pool* p) {
     ws.pre_copied = nullptr;
     ws.h_pre = ws.d_pre = nullptr;
     ws.d_qconv = nullptr;
-    ws.meta_copied = nullptr;
-    ws.h_meta = ws.d_meta = nullptr;
+    ws.d_meta = nullptr;
     ws.d_part_acc = ws.d_part_ml = nullptr;
 }
 
@@ -327,13 +334,14 @@ int step_upload(Pool* p, const int32_t* tables, int32_t batch, int32_t max_block
     int mrc = ensure_meta(p, L.total);
     if (mrc != GKV_OK) return mrc;
 
-    // The pinned staging buffer may still feed the previous step's copy.
-    if (ws.meta_pending) {
-        cudaError_t e = cudaEventSynchronize(ws.meta_copied);
+    // This staging buffer fed the copy two uploads ago, normally long finished.
+    const int mi = ws.meta_flip;
+    if (ws.meta_pending[mi]) {
+        cudaError_t e = cudaEventSynchronize(ws.meta_copied[mi]);
         if (e != cudaSuccess) return cuda_fail(e, "cudaEventSynchronize(step metadata)");
-        ws.meta_pending = false;
+        ws.meta_pending[mi] = false;
     }
-    char* h = ws.h_meta;
+    char* h = ws.h_meta[mi];
     if (n_tok) memcpy(h + L.slots, slots, static_cast<size_t>(n_tok) * 8);
     if (batch && max_blocks) memcpy(h + L.tables, tables, static_cast<size_t>(batch) * max_blocks * 4);
     if (batch) memcpy(h + L.ctx, ctx_lens, static_cast<size_t>(batch) * 4);
@@ -350,11 +358,12 @@ int step_upload(Pool* p, const int32_t* tables, int32_t batch, int32_t max_block
     put(L.ms0, W.merge_slot0);
     put(L.mns, W.merge_nslots);
     put(L.mdef, W.merge_deferred);
-    cudaError_t e = cudaMemcpyAsync(ws.d_meta, ws.h_meta, L.total, cudaMemcpyHostToDevice, st);
+    cudaError_t e = cudaMemcpyAsync(ws.d_meta, h, L.total, cudaMemcpyHostToDevice, st);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(step metadata)");
-    e = cudaEventRecord(ws.meta_copied, st);
+    e = cudaEventRecord(ws.meta_copied[mi], st);
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord(step metadata)");
-    ws.meta_pending = true;
+    ws.meta_pending[mi] = true;
+    ws.meta_flip ^= 1;
 
     char* d = ws.d_meta;
     DecodeWork& w = ws.work;
