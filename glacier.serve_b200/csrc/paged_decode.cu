@@ -278,7 +278,8 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
             int page, tok0, ntok;
             chunk_geom(c0 + j, ctx, page, tok0, ntok);
             const int64_t blk = __ldg(w.tables + table_row(w, b) * w.max_blocks + page);
-            if (!dead && !mbar_wait(&my_bars[st], ph)) {
+            // warp-uniform: the transpose-reduce below is warp-collective
+            if (!dead && !__all_sync(0xffffffffu, mbar_wait(&my_bars[st], ph))) {
                 dead = true;
                 if (lane == 0 && a.err) atomicOr(a.err, kErrWaitTimeout);
             }
