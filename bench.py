@@ -271,6 +271,22 @@ def run_reference(args):
         print(json.dumps(line), flush=True)
         return
 
+    if args.config in BANDWIDTH_CONFIGS:
+        res = bandwidth_cpu_baseline(args.config, max(args.steps, 1), budget_s=120.0)
+        line = {
+            "metric": f"{'KV append' if args.config.startswith('append') else 'block copy'} GB/s per B200 vs HBM peak",
+            "value": res["value"], "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": res["ms_per_sample"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16" if args.config.endswith("bf16") else "f32",
+            "data": "synthetic (seeded N(0,1))",
+            "config": {"workload": args.config, "l2": "n/a (CPU)",
+                       "implementation": "C restatement of PagedBlockPool.Store / CopyBlockData and the runner loop"},
+            "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": res["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
+        return
+
     w = workload(args.config, 0)
     threads = O.max_threads()
     res = cpu_baseline_run(w, max(args.steps, 1), budget_s=120.0, threads=threads, seed=w.seed)
@@ -423,6 +439,182 @@ def run_prefill(args, world, rank, local, dev, barrier, max_over_ranks):
     pool.close()
 
 
+BANDWIDTH_CONFIGS = ("append", "append-bf16", "copy", "copy-bf16")
+
+
+def bandwidth_workload(config: str, rank: int = 0):
+    """Seeded inputs of the append / copy configs on the cfg2 arena geometry."""
+    nb, hkv, d, bs = 16384, 8, 128, 16
+    rng = np.random.default_rng(0x61AC1E5 + 1000003 * rank)
+    perm = rng.permutation(nb).astype(np.int32)
+    if config.startswith("append"):
+        seqs, chunk = 32, 2048
+        tables = perm[: seqs * chunk // bs].reshape(seqs, chunk // bs)
+        j = np.arange(chunk)
+        slots = (tables[:, j // bs].astype(np.int64) * bs + j % bs).reshape(-1)
+        return dict(nb=nb, hkv=hkv, d=d, bs=bs, rng=rng, tables=tables, slots=slots, seqs=seqs, chunk=chunk)
+    n_ops = 4096
+    return dict(nb=nb, hkv=hkv, d=d, bs=bs, rng=rng, src=perm[:n_ops].copy(), dst=perm[n_ops:2 * n_ops].copy(),
+                valid=np.full(n_ops, bs, np.int32))
+
+
+def bandwidth_cpu_baseline(config: str, steps: int, budget_s: float):
+    """The reference's own loops on one host core: the runner's per-token Store loop
+    (PagedTransformerRunner.cs:450) or CopyBlockData per fork (PagedBlockPool.cs:304-342), as
+    restated in oracle/, on a bounded prefix of the same inputs."""
+    from oracle import pyoracle as O
+
+    w = bandwidth_workload(config)
+    bf16 = config.endswith("bf16")
+    eb = 2 if bf16 else 4
+    g = O.geom(w["nb"], 1, w["hkv"], w["d"], block_size=w["bs"], dtype=O.BF16 if bf16 else O.F32)
+    K, V = O.new_arena(g)
+    if config.startswith("append"):
+        n = 8192
+        slots = w["slots"][:n]
+        k = w["rng"].standard_normal((n, w["hkv"], w["d"]), dtype=np.float32)
+        v = w["rng"].standard_normal((n, w["hkv"], w["d"]), dtype=np.float32)
+        alg = n * w["hkv"] * 2 * w["d"] * (4 + eb)
+        run = lambda: O.store_many(K, V, g, 0, slots, k, v)  # noqa: E731
+        sample = f"first {n} of the 65536 tokens, per-token Store loop, 1 thread (the reference's loop is serial)"
+    else:
+        n = 512
+        alg = n * w["hkv"] * w["bs"] * 2 * w["d"] * eb * 2
+        run = lambda: O.copy_many(K, V, g, w["src"][:n], w["dst"][:n], w["valid"][:n])  # noqa: E731
+        sample = f"first {n} of the 4096 forks, CopyBlockData per fork, 1 thread (the reference's copy is serial)"
+    run()  # touch the pages once
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < steps and time.perf_counter() < t_end:
+        t0 = time.perf_counter()
+        assert run() == 0
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": alg / med / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": sample + f", median of {len(times)} runs", "ms_per_sample": med * 1e3}
+
+
+def run_bandwidth(args, world, rank, local, dev, barrier, max_over_ranks):
+    """The two data-movement kernels of the pool on their own, each against the HBM roofline, on
+    the cfg2 arena geometry (16384 blocks x 8 kv heads x 16 slots x d 128, one layer).
+
+    append: one kv_append of 65536 tokens (32 sequences x 2048 prefill tokens; every sequence's
+        slots follow its seeded block table), fp32 sources, fp32 or bf16 arena.
+    copy:   one block_copy of 4096 full blocks (seeded distinct src / dst), K and V.
+    Both move about 1 GB per launch, more than L2.  Weak scaling: every rank owns a pool."""
+    import torch
+
+    import glacier_kv as G
+
+    dtype = "bf16" if args.config.endswith("bf16") else "f32"
+    eb = 2 if dtype == "bf16" else 4
+    w = bandwidth_workload(args.config, rank)
+    nb, hkv, d, bs, rng = w["nb"], w["hkv"], w["d"], w["bs"], w["rng"]
+    pool = G.PagedBlockPool(nb, 1, hkv, d, bs, d, device=local, dtype=dtype)
+    stream = torch.cuda.current_stream(dev)
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    if args.config.startswith("append"):
+        seqs, chunk, tables, slots = w["seqs"], w["chunk"], w["tables"], w["slots"]
+        n_tok = slots.size
+        pool.reserve_step(seqs, tables.shape[1], n_tok, hkv)
+        pool.upload_step(tables, np.full(seqs, chunk, np.int32), slots, stream=stream)
+        kn = torch.from_numpy(rng.standard_normal((n_tok, hkv, d), dtype=np.float32)).to(dev)
+        vn = torch.from_numpy(rng.standard_normal((n_tok, hkv, d), dtype=np.float32)).to(dev)
+        alg = n_tok * hkv * 2 * d * (4 + eb)  # fp32 rows read, arena rows written
+
+        def launch():
+            pool.kv_append(0, kn, vn, stream=stream)
+            return pool.last_launch_count
+
+        hk, hv = kn.cpu().pin_memory(), vn.cpu().pin_memory()
+        h2d, d2h = hk.numel() * 4 * 2, 0
+
+        def e2e():
+            kn.copy_(hk, non_blocking=True)
+            vn.copy_(hv, non_blocking=True)
+            launch()
+
+        kernel = f"kv_append_kernel<{'bf16' if eb == 2 else 'float'}> (65536 tokens x 8 heads, K and V rows)"
+        work = (f"{args.config}: kv_append of {n_tok} tokens ({seqs} seqs x {chunk}), {hkv} kv heads, d {d}, "
+                f"fp32 sources, {dtype} arena, block {bs}, pool {nb} blocks")
+    else:
+        src, dst, valid = w["src"], w["dst"], w["valid"]
+        n_ops = src.size
+        alg = n_ops * hkv * bs * 2 * d * eb * 2  # K and V spans, read + written
+
+        def launch():
+            pool.block_copy(src, dst, valid, stream=stream)
+            return pool.last_launch_count
+
+        h2d, d2h = n_ops * 3 * 4, 0
+        e2e = launch
+        kernel = f"block_copy_kernel ({n_ops} full blocks, K and V)"
+        work = (f"{args.config}: block_copy of {n_ops} full blocks (seeded distinct src/dst), {hkv} kv heads, "
+                f"d {d}, {dtype} arena, block {bs}, pool {nb} blocks")
+
+    clk = Clocks(dev)
+    clk.__enter__()
+    for _ in range(args.warmup):
+        launch()
+    torch.cuda.synchronize(dev)
+    events = [(ev(), ev()) for _ in range(args.steps)]
+    launches = 0
+    barrier()
+    torch.cuda.synchronize(dev)
+    clk.mark(0)
+    for i in range(args.steps):
+        events[i][0].record(stream)
+        launches += launch()
+        events[i][1].record(stream)
+    torch.cuda.synchronize(dev)
+    clk.mark(1)
+    clk.__exit__()
+    pool.sync()
+    barrier()
+    ms_local = sum(a.elapsed_time(b) for a, b in events) / args.steps
+    ms = max_over_ranks(ms_local)
+    for _ in range(args.warmup):
+        e2e()
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0, e1 = ev(), ev()
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    pool.sync()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    barrier()
+    if rank == 0:
+        peak, peak_kind = peaks()
+        achieved = alg / (ms_local / 1e3) / 1e9
+        line = {
+            "metric": f"{'KV append' if args.config.startswith('append') else 'block copy'} GB/s per B200 vs HBM peak",
+            "value": world * alg / (ms / 1e3) / 1e9, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": dtype, "data": "synthetic (seeded N(0,1) rows, seeded block tables)",
+            "config": {"workload": work, "l2": f"inputs larger than L2 ({alg / 1e9:.2f} GB moved per launch)",
+                       "parallelism": f"{world} GPU(s), one pool each, no collective",
+                       "bytes_per_step_per_gpu": alg},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic_from_profiles(args.config),
+                         "kernel": kernel, "bytes_per_launch": alg, "avg_launch_ms": ms_local,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s"},
+            "e2e": {"value": world * alg / (e2e_ms / 1e3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms,
+                    "path": ("pinned host K/V rows copied in, then gkv_kv_append" if args.config.startswith("append")
+                             else "gkv_block_copy from host op lists (ops copied in by the call)")},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+        }
+        if not args.no_cpu_baseline and world == 1:
+            line["cpu_baseline"] = {k: v for k, v in bandwidth_cpu_baseline(
+                args.config, steps=max(5, args.steps), budget_s=20.0).items() if k != "ms_per_sample"}
+        print(json.dumps(line), flush=True)
+    pool.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -466,8 +658,9 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    if args.config == "cfg4":
-        run_prefill(args, world, rank, local, dev, barrier, max_over_ranks)
+    if args.config == "cfg4" or args.config in BANDWIDTH_CONFIGS:
+        run = run_prefill if args.config == "cfg4" else run_bandwidth
+        run(args, world, rank, local, dev, barrier, max_over_ranks)
         if world > 1:
             dist.destroy_process_group()
         return

@@ -96,6 +96,33 @@ int oracle_copy_block_data(void* kpool, void* vpool, const oracle_geom* g, int32
     return ORACLE_OK;
 }
 
+int oracle_store_many(void* kpool, void* vpool, const oracle_geom* g, int32_t layer,
+                      const int64_t* slots, int32_t n_tok, const float* k, const float* v) {
+    /* The runners' per-token Store loop (PagedTransformerRunner.cs:450: pool.Store(blockId,
+     * layer, offset, k, v) for each token of the chunk), with (block, offset) taken from the
+     * flat slot index; negative slots are padding and skipped. */
+    const int64_t kstride = (int64_t)g->heads_kv * g->head_dim;
+    const int64_t vstride = (int64_t)g->heads_kv * g->v_head_dim;
+    for (int32_t i = 0; i < n_tok; ++i) {
+        if (slots[i] < 0) continue;
+        const int rc = oracle_store(kpool, vpool, g, (int32_t)(slots[i] / g->block_size), layer,
+                                    (int32_t)(slots[i] % g->block_size), k + i * kstride,
+                                    v + i * vstride);
+        if (rc != ORACLE_OK) return rc;
+    }
+    return ORACLE_OK;
+}
+
+int oracle_copy_many(void* kpool, void* vpool, const oracle_geom* g, const int32_t* src,
+                     const int32_t* dst, const int32_t* valid, int32_t n) {
+    /* One CopyBlockData per queued fork (TryForkBlock, PagedBlockPool.cs:332-342). */
+    for (int32_t i = 0; i < n; ++i) {
+        const int rc = oracle_copy_block_data(kpool, vpool, g, src[i], dst[i], valid[i]);
+        if (rc != ORACLE_OK) return rc;
+    }
+    return ORACLE_OK;
+}
+
 /* QuantKernels.VecDotF32 (NuGet Glacier.Inference 1.7.0, called at
  * PagedAttentionKernel.cs:64): source absent.  Restated as an in-order fp32 fused
  * multiply-add chain; the reference's lane order is unpinned. */

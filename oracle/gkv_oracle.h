@@ -46,6 +46,15 @@ int oracle_store(void* kpool, void* vpool, const oracle_geom* g, int32_t block, 
 int oracle_copy_block_data(void* kpool, void* vpool, const oracle_geom* g, int32_t src,
                            int32_t dst, int32_t valid_tokens);
 
+/* The runners' per-token Store loop (PagedTransformerRunner.cs:450) over flat slot indices
+ * (slot = block * block_size + offset; negative = padding); k, v are [n_tok][heads][dim]. */
+int oracle_store_many(void* kpool, void* vpool, const oracle_geom* g, int32_t layer,
+                      const int64_t* slots, int32_t n_tok, const float* k, const float* v);
+
+/* CopyBlockData for each of n (src, dst, valid) forks. */
+int oracle_copy_many(void* kpool, void* vpool, const oracle_geom* g, const int32_t* src,
+                     const int32_t* dst, const int32_t* valid, int32_t n);
+
 /* PagedAttentionKernel.ComputeAttention, PagedAttentionKernel.cs:17-372, for one sequence
  * whose table holds n_block_ids ids and token_count tokens.  head_scores: scratch of
  * n_heads * max_seq_len floats (the reference's headScores).  n_threads <= 0 uses OpenMP's

@@ -30,12 +30,15 @@ def _load() -> C.CDLL:
     lib.oracle_bf16_to_f32.argtypes = [C.c_uint16]
     lib.oracle_store.argtypes = [P, P, P, I, I, I, P, P]
     lib.oracle_copy_block_data.argtypes = [P, P, P, I, I, I]
+    lib.oracle_store_many.argtypes = [P, P, P, I, P, I, P, P]
+    lib.oracle_copy_many.argtypes = [P, P, P, P, P, P, I]
     lib.oracle_compute_attention.argtypes = [P, P, P, I, I, P, P, P, I, I, I, I, I, I, F, P, I, I, F, I]
     lib.oracle_decode_batch.argtypes = [P, P, P, I, P, I, I, P, P, P, I, F, I, F, I]
     lib.oracle_decode_batch_parallel.argtypes = [P, P, P, I, P, I, I, P, P, P, I, F, I]
     lib.oracle_prefill_chunk.argtypes = [P, P, P, I, P, I, I, I, I, P, P, I, F, I]
     lib.oracle_max_threads.restype = C.c_int
-    for n in ("oracle_store", "oracle_copy_block_data", "oracle_compute_attention",
+    for n in ("oracle_store", "oracle_copy_block_data", "oracle_store_many", "oracle_copy_many",
+              "oracle_compute_attention",
               "oracle_decode_batch", "oracle_decode_batch_parallel", "oracle_prefill_chunk"):
         getattr(lib, n).restype = C.c_int
     return lib
@@ -89,6 +92,20 @@ def store(K, V, g: Geom, block, layer, slot, k: np.ndarray, v: np.ndarray) -> in
 
 def copy_block_data(K, V, g: Geom, src, dst, valid) -> int:
     return lib.oracle_copy_block_data(_p(K), _p(V), C.byref(g), src, dst, valid)
+
+
+def store_many(K, V, g: Geom, layer, slots: np.ndarray, k: np.ndarray, v: np.ndarray) -> int:
+    slots = np.ascontiguousarray(slots, np.int64)
+    k = np.ascontiguousarray(k, np.float32)
+    v = np.ascontiguousarray(v, np.float32)
+    return lib.oracle_store_many(_p(K), _p(V), C.byref(g), layer, _p(slots), int(slots.size), _p(k), _p(v))
+
+
+def copy_many(K, V, g: Geom, src, dst, valid) -> int:
+    src = np.ascontiguousarray(src, np.int32)
+    dst = np.ascontiguousarray(dst, np.int32)
+    valid = np.ascontiguousarray(valid, np.int32)
+    return lib.oracle_copy_many(_p(K), _p(V), C.byref(g), _p(src), _p(dst), _p(valid), int(src.size))
 
 
 def compute_attention(K, V, g: Geom, stage_layer, pos, q, block_ids, token_count, n_heads, n_heads_kv,

@@ -99,6 +99,51 @@ def test_append_matches_oracle_store_random_slots(cuda):
     assert np.array_equal(Vg.view(np.uint32), V.view(np.uint32))
 
 
+@pytest.mark.parametrize("heads,d,dv,dtype", [(3, 128, 128, "f32"), (3, 128, 64, "bf16"), (1, 30, 18, "f32")])
+def test_large_append_matches_oracle_store_loop(cuda, heads, d, dv, dtype):
+    """An odd number of (token, head) rows, more than one pass of the grid-stride loop, with
+    padding slots; the scalar path (d not a multiple of 4) included.  Bit-exact against the
+    runner's per-token Store loop."""
+    import torch
+
+    rng = np.random.default_rng(24)
+    bs, nb, n = 16, 1400, 20001
+    pool = G.PagedBlockPool(nb, 1, heads, d, bs, v_head_dim=dv, dtype=dtype)
+    K, V = random_arena(pool, rng)
+    g = geom_of(pool)
+    slots = rng.choice(nb * bs, size=n, replace=False).astype(np.int64)
+    slots[rng.choice(n, 37, replace=False)] = -1
+    k = rng.standard_normal((n, heads, d)).astype(np.float32)
+    v = rng.standard_normal((n, heads, dv)).astype(np.float32)
+    pool.reserve_step(1, 1, n, heads)
+    pool.upload_step(np.zeros((1, 1), np.int32), np.zeros(1, np.int32), slots)
+    pool.kv_append(0, torch.from_numpy(k).to(cuda), torch.from_numpy(v).to(cuda))
+    pool.sync()
+    assert O.store_many(K, V, g, 0, slots, k, v) == 0
+    Kg, Vg = arena_to_host(pool)
+    assert np.array_equal(Kg, K) and np.array_equal(Vg, V)
+
+
+@pytest.mark.parametrize("d,dv", [(128, 128), (30, 18)])
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_large_block_copy_matches_oracle(cuda, dtype, d, dv):
+    """More 2 KB chunks than one pass of the grid-stride loop; ragged valid counts; spans that
+    end in a tail shorter than 16 bytes (d 30 / dv 18)."""
+    rng = np.random.default_rng(25)
+    nb, n = 3000, 1400
+    pool = G.PagedBlockPool(nb, 1, 4, d, 16, v_head_dim=dv, dtype=dtype)
+    K, V = random_arena(pool, rng)
+    g = geom_of(pool)
+    perm = rng.permutation(nb)
+    src, dst = perm[:n], perm[n:2 * n]
+    valid = rng.integers(-2, 20, n).astype(np.int32)
+    pool.block_copy(src, dst, valid)
+    pool.sync()
+    assert O.copy_many(K, V, g, src, dst, valid) == 0
+    Kg, Vg = arena_to_host(pool)
+    assert np.array_equal(Kg, K) and np.array_equal(Vg, V)
+
+
 def test_cow_fork_preserves_data(cuda):
     """PrefixHashKvCacheTests.cs:134-181 with the arena on the device."""
     pool = G.PagedBlockPool(16, 2, 2, 32, 16)

@@ -76,6 +76,30 @@ def test_oracle_copy_block_data_sentinels():
     assert O.copy_block_data(K, V, g, 0, 3, 0) == 0 and np.all(K[3] == 0)
 
 
+@pytest.mark.parametrize("dtype", [O.F32, O.BF16])
+def test_oracle_batch_loops_equal_single_calls(dtype):
+    """store_many / copy_many (the bench's CPU baseline loops) are one Store / CopyBlockData
+    per entry; padding slots are skipped and a bad slot or block is rejected."""
+    rng = np.random.default_rng(5)
+    g = O.geom(20, 2, 3, 8, 4, 4, dtype)
+    K1, V1 = O.new_arena(g)
+    K2, V2 = O.new_arena(g)
+    slots = np.array([5, -1, 79, 0, 33], np.int64)
+    k = rng.standard_normal((5, 3, 8)).astype(np.float32)
+    v = rng.standard_normal((5, 3, 4)).astype(np.float32)
+    assert O.store_many(K1, V1, g, 1, slots, k, v) == 0
+    for i, s in enumerate(slots):
+        if s >= 0:
+            assert O.store(K2, V2, g, int(s) // 4, 1, int(s) % 4, k[i], v[i]) == 0
+    assert np.array_equal(K1, K2) and np.array_equal(V1, V2) and K1.any()
+    assert O.copy_many(K1, V1, g, [1, 19, 8], [2, 3, 4], [4, 2, 0]) == 0
+    for s, d, n in ((1, 2, 4), (19, 3, 2), (8, 4, 0)):
+        assert O.copy_block_data(K2, V2, g, s, d, n) == 0
+    assert np.array_equal(K1, K2) and np.array_equal(V1, V2)
+    assert O.store_many(K1, V1, g, 0, np.array([80], np.int64), k[:1], v[:1]) != 0  # block 20 of 20
+    assert O.copy_many(K1, V1, g, [0], [20], [4]) != 0
+
+
 @pytest.mark.parametrize("pos", [16, -1])
 def test_oracle_rejects_out_of_bounds_position(pos):
     """PhaseCServeRemediationTests.cs:117-174: pos outside [0, maxSeqLen) throws."""
