@@ -121,17 +121,27 @@ void build_work_list(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, i
     }
     W.worker_begin[static_cast<size_t>(n_workers)] = static_cast<int32_t>(W.piece_seg.size());
     // Pieces of one segment are adjacent; a segment cut into several pieces gets
-    // contiguous partial slots and one merge entry.
+    // contiguous partial slots and one merge entry.  A segment of more than
+    // kFusedMergeMaxSlots pieces is merged by the second launch; once that launch is needed,
+    // it takes every split segment, so that no warp of the decode merges at its tail (on a
+    // 20-sequence GQA-7 batch those fused merges made the slowest warps 10 us late).
     const size_t np = W.piece_seg.size();
     W.piece_slot.assign(np, -1);
     W.piece_merge.assign(np, -1);
+    bool defer_all = false;
+    for (size_t i = 0; i < np && !defer_all;) {
+        size_t j = i + 1;
+        while (j < np && W.piece_seg[j] == W.piece_seg[i]) ++j;
+        defer_all = (j - i) > static_cast<size_t>(kFusedMergeMaxSlots);
+        i = j;
+    }
     size_t i = 0;
     while (i < np) {
         size_t j = i + 1;
         while (j < np && W.piece_seg[j] == W.piece_seg[i]) ++j;
         if (j - i > 1) {
             const int32_t mi = static_cast<int32_t>(W.merge_seg.size());
-            const bool deferred = (j - i) > static_cast<size_t>(kFusedMergeMaxSlots);
+            const bool deferred = defer_all;
             W.merge_seg.push_back(W.piece_seg[i]);
             W.merge_slot0.push_back(W.n_slots);
             W.merge_nslots.push_back(static_cast<int32_t>(j - i));
