@@ -133,6 +133,10 @@ __global__ void __launch_bounds__(256) deferred_merge_kernel(ArenaGeom g, Decode
     const int h = seg - b * g.heads_kv;
     const int q_head0 = h * group + hg * GP;
     const int gcount = min(GP, group - hg * GP);
+    // the merge list above comes from the step's host copy; the partials are the previous
+    // (decode) kernel's output
+    pdl_launch_dependents();
+    pdl_wait();
     if (gg >= gcount) return;
     const int64_t base = (static_cast<int64_t>(hg) * w.n_slots + s0) * GP + gg;  // + s * GP
     auto block_reduce = [&](float v, bool is_max) {

@@ -6,6 +6,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace gkv {
 
 // Bits OR-ed into the step workspace's device error word.
@@ -33,6 +35,18 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
 __device__ __forceinline__ void fence_mbar_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
+
+// Programmatic dependent launch.  A kernel launched with programmatic stream serialization
+// (launch_pdl) may start while the kernel before it on the stream is still running:
+// pdl_launch_dependents() lets the NEXT kernel start once every CTA of this grid has issued
+// it (or exited), and pdl_wait() blocks until the PREVIOUS kernel has completed and its
+// memory is visible.  A kernel that runs pdl_wait() before every read of the previous
+// kernel's output and every global write, and on every exit path, is correct whether or not
+// it was launched that way (without the attribute the wait returns at once).
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // Orders this thread's earlier generic-proxy shared-memory accesses before later
 // async-proxy (bulk copy) accesses of the same memory.
@@ -336,5 +350,24 @@ struct SmemVec<__nv_bfloat16, EPL> {
         }
     }
 };
+
+// Launches `kernel` with programmatic stream serialization (see pdl_wait): its CTAs may start
+// while the previous kernel on `st` drains, once that kernel has called
+// pdl_launch_dependents() in every CTA.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace gkv

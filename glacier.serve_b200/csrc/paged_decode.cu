@@ -158,10 +158,17 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
     if (lane < S) mbar_init(&my_bars[lane], 1);
     fence_mbar_init();
     __syncwarp();
+    // the next kernel (the deferred merge) may be scheduled as soon as this grid is resident
+    pdl_launch_dependents();
 
+    // the work list comes from a host copy ordered before the previous kernel, so it is read
+    // before pdl_wait; the arena (which a preceding append writes) only after it
     const int pb = __ldg(w.worker_piece_begin + worker);
     const int pe = __ldg(w.worker_piece_begin + worker + 1);
-    if (pb >= pe) return;
+    if (pb >= pe) {
+        pdl_wait();
+        return;
+    }
 
     const char* Kb = static_cast<const char*>(g.k);
     const char* Vb = static_cast<const char*>(g.v);
@@ -194,6 +201,7 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
         p_ctx = __ldg(w.ctx_lens + p_b);
     };
     p_load();
+    pdl_wait();
     auto issue = [&](int st) {
         int page, tok0, ntok;
         chunk_geom(p_c0 + p_j, p_ctx, page, tok0, ntok);
@@ -505,8 +513,8 @@ struct Inst {
         cudaError_t e = prepare();
         if (e != cudaSuccess) return e;
         dim3 grid(static_cast<unsigned>(w.n_ctas), static_cast<unsigned>(head_groups));
-        paged_decode_kernel<KV, D, DV, GP, NW, S><<<grid, NW * 32, Tr::SMEM, st>>>(g, w, a, group, cpp);
-        e = cudaGetLastError();
+        e = launch_pdl(paged_decode_kernel<KV, D, DV, GP, NW, S>, grid, dim3(NW * 32), Tr::SMEM, st, g, w,
+                       a, group, cpp);
         if (e != cudaSuccess) return e;
         *launches = 1;
         if (w.n_deferred > 0) {
@@ -602,10 +610,7 @@ cudaError_t launch_deferred_merge(const ArenaGeom& g, const DecodeWork& w, const
                                   int group, int gp, int head_groups, cudaStream_t st) {
     if (w.n_deferred <= 0) return cudaSuccess;
     const dim3 grid(static_cast<unsigned>(w.n_deferred), static_cast<unsigned>(head_groups * gp));
-    auto go = [&](auto kern) {
-        kern<<<grid, 256, 0, st>>>(g, w, a, group);
-        return cudaGetLastError();
-    };
+    auto go = [&](auto kern) { return launch_pdl(kern, grid, dim3(256), 0, st, g, w, a, group); };
 #define GKV_MERGE_DV(GPV)                                                                  \
     switch (g.v_head_dim) {                                                               \
         case 32: return go(deferred_merge_kernel<GPV, 32>);                               \

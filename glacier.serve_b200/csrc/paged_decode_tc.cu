@@ -67,10 +67,17 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_tc_kernel(
     if (lane < S) mbar_init(&my_bars[lane], 1);
     fence_mbar_init();
     __syncwarp();
+    // the next kernel (the deferred merge) may be scheduled as soon as this grid is resident
+    pdl_launch_dependents();
 
+    // the work list comes from a host copy ordered before the previous kernel, so it is read
+    // before pdl_wait; the arena (which a preceding append writes) only after it
     const int pb = __ldg(w.worker_piece_begin + worker);
     const int pe = __ldg(w.worker_piece_begin + worker + 1);
-    if (pb >= pe) return;
+    if (pb >= pe) {
+        pdl_wait();
+        return;
+    }
 
     const int bs = g.block_size;
     const bool cpp2 = (cpp == 2);
@@ -99,6 +106,7 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_tc_kernel(
         p_ctx = __ldg(w.ctx_lens + p_b);
     };
     p_load();
+    pdl_wait();
     auto issue = [&](int st) {
         int page, tok0, ntok;
         chunk_geom(p_c0 + p_j, p_ctx, page, tok0, ntok);
@@ -434,8 +442,8 @@ cudaError_t launch_paged_decode_tc(const ArenaGeom& g, const DecodeWork& w, cons
     if (e != cudaSuccess) return e;
     const int cpp = (g.block_size + kChunk - 1) / kChunk;
     dim3 grid(static_cast<unsigned>(w.n_ctas), static_cast<unsigned>(head_groups));
-    paged_decode_tc_kernel<kNW, kS><<<grid, kNW * 32, kTcSmem, st>>>(*tk, *tv, g, w, a, group, cpp);
-    e = cudaGetLastError();
+    e = launch_pdl(paged_decode_tc_kernel<kNW, kS>, grid, dim3(kNW * 32), kTcSmem, st, *tk, *tv, g, w, a,
+                   group, cpp);
     if (e != cudaSuccess) return e;
     *launches = 1;
     if (w.n_deferred > 0) {
