@@ -66,6 +66,15 @@ class PrefixMap {
     static int shard_of(uint64_t h) { return static_cast<int>((h ^ (h >> 29) ^ (h >> 47)) & (kShards - 1)); }
 };
 
+// Work-list construction (host only; unit-tested through the C ABI helpers).
+struct WorkList {
+    std::vector<int32_t> piece_seg, piece_c0, piece_c1, piece_slot, piece_merge, merge_deferred;
+    std::vector<int32_t> worker_begin;  // n_workers + 1
+    std::vector<int32_t> merge_seg, merge_slot0, merge_nslots;
+    int32_t n_slots = 0;
+    int64_t total_chunks = 0;
+};
+
 // Device + pinned buffers of one step (block tables, ctx lens, slot mapping, work list).
 struct StepWorkspace {
     int32_t max_batch = 0, max_blocks = 0, max_tokens = 0, n_heads = 0;
@@ -111,6 +120,7 @@ struct StepWorkspace {
     const int64_t* d_slots = nullptr;
     bool uploaded = false;
     std::vector<int32_t> h_ctx;  // ctx_lens of the uploaded step
+    WorkList wl;                 // the uploaded step's work list (kept for its capacity)
     // chunked prefill: pinned + device buffer of its work items / work list, and q in the
     // dtype its kernel reads
     char* h_pre = nullptr;
@@ -188,14 +198,6 @@ int step_prefill(Pool* p, int32_t layer, const void* d_q, int32_t q_dtype, float
                  cudaStream_t st);
 void step_free(Pool* p);
 
-// Work-list construction (host only; unit-tested through the C ABI helpers).
-struct WorkList {
-    std::vector<int32_t> piece_seg, piece_c0, piece_c1, piece_slot, piece_merge, merge_deferred;
-    std::vector<int32_t> worker_begin;  // n_workers + 1
-    std::vector<int32_t> merge_seg, merge_slot0, merge_nslots;
-    int32_t n_slots = 0;
-    int64_t total_chunks = 0;
-};
 int32_t chunks_of(int32_t ctx, int32_t block_size);
 void build_work_list(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, int32_t block_size,
                      int32_t n_workers, WorkList* out);

@@ -90,7 +90,11 @@ int32_t chunks_of(int32_t ctx, int32_t block_size) {
 void build_work_list(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, int32_t block_size,
                      int32_t n_workers, WorkList* out) {
     WorkList& W = *out;
-    W = WorkList{};
+    // cleared, not reassigned: a work list kept across steps keeps its capacity
+    for (auto* v : {&W.piece_seg, &W.piece_c0, &W.piece_c1, &W.piece_slot, &W.piece_merge,
+                    &W.merge_deferred, &W.merge_seg, &W.merge_slot0, &W.merge_nslots})
+        v->clear();
+    W.n_slots = 0;
     const int64_t n_seg = static_cast<int64_t>(batch) * heads_kv;
     std::vector<int64_t> seg_start(static_cast<size_t>(n_seg) + 1, 0);
     for (int32_t b = 0; b < batch; ++b) {
@@ -104,22 +108,44 @@ void build_work_list(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, i
     W.total_chunks = total;
     W.worker_begin.assign(static_cast<size_t>(n_workers) + 1, 0);
     int64_t seg = 0;
+    // Worker w covers chunks [total*w/n, total*(w+1)/n), stepped without divisions; every
+    // worker range is cut at segment ends, so there are at most n_workers + n_seg pieces.
+    const int64_t q = n_workers > 0 ? total / n_workers : 0;  // no workers: an empty step
+    const int64_t r = n_workers > 0 ? total % n_workers : 0;
+    int64_t hi = 0, frac = 0;
+    const size_t cap = static_cast<size_t>(n_workers) + static_cast<size_t>(n_seg);
+    W.piece_seg.resize(cap);
+    W.piece_c0.resize(cap);
+    W.piece_c1.resize(cap);
+    int32_t* ps = W.piece_seg.data();
+    int32_t* pc0 = W.piece_c0.data();
+    int32_t* pc1 = W.piece_c1.data();
+    size_t np_ = 0;
     for (int32_t w = 0; w < n_workers; ++w) {
-        W.worker_begin[static_cast<size_t>(w)] = static_cast<int32_t>(W.piece_seg.size());
-        int64_t lo = total * w / n_workers;
-        const int64_t hi = total * (w + 1) / n_workers;
+        W.worker_begin[static_cast<size_t>(w)] = static_cast<int32_t>(np_);
+        int64_t lo = hi;
+        hi += q;
+        frac += r;
+        if (frac >= n_workers) {
+            frac -= n_workers;
+            ++hi;
+        }
         while (lo < hi) {
             while (seg_start[static_cast<size_t>(seg) + 1] <= lo) ++seg;
             const int64_t s0 = seg_start[static_cast<size_t>(seg)];
             const int64_t s1 = seg_start[static_cast<size_t>(seg) + 1];
             const int64_t end = hi < s1 ? hi : s1;
-            W.piece_seg.push_back(static_cast<int32_t>(seg));
-            W.piece_c0.push_back(static_cast<int32_t>(lo - s0));
-            W.piece_c1.push_back(static_cast<int32_t>(end - s0));
+            ps[np_] = static_cast<int32_t>(seg);
+            pc0[np_] = static_cast<int32_t>(lo - s0);
+            pc1[np_] = static_cast<int32_t>(end - s0);
+            ++np_;
             lo = end;
         }
     }
-    W.worker_begin[static_cast<size_t>(n_workers)] = static_cast<int32_t>(W.piece_seg.size());
+    W.piece_seg.resize(np_);
+    W.piece_c0.resize(np_);
+    W.piece_c1.resize(np_);
+    W.worker_begin[static_cast<size_t>(n_workers)] = static_cast<int32_t>(np_);
     // Pieces of one segment are adjacent; a segment cut into several pieces gets
     // contiguous partial slots and one merge entry.  A segment of more than
     // kFusedMergeMaxSlots pieces is merged by the second launch; once that launch is needed,
@@ -326,17 +352,16 @@ int step_upload(Pool* p, const int32_t* tables, int32_t batch, int32_t max_block
         if (rc != GKV_OK) return rc;
     }
     // Work list over a persistent grid: enough workers for the chunks, at most one wave.
-    std::vector<int32_t> ctx_v(ctx_lens, ctx_lens + batch);
     int64_t total = 0;
-    for (int32_t b = 0; b < batch; ++b) total += chunks_of(ctx_v[static_cast<size_t>(b)], bs);
+    for (int32_t b = 0; b < batch; ++b) total += chunks_of(ctx_lens[b], bs);
     total *= p->desc.heads_kv;
     const int warps = ws.cfg.supported ? ws.cfg.warps : 4;
     int64_t want_workers = (total + kMinChunksPerWorker - 1) / kMinChunksPerWorker;
     int64_t ctas = (want_workers + warps - 1) / warps;
     if (ctas > ws.n_ctas_max) ctas = ws.n_ctas_max;
     if (ctas < 1 && total > 0) ctas = 1;
-    WorkList W;
-    build_work_list(ctx_v.data(), batch, p->desc.heads_kv, bs, static_cast<int32_t>(ctas * warps), &W);
+    WorkList& W = ws.wl;
+    build_work_list(ctx_lens, batch, p->desc.heads_kv, bs, static_cast<int32_t>(ctas * warps), &W);
     const int64_t n_pieces = static_cast<int64_t>(W.piece_seg.size());
     const int64_t n_workers = static_cast<int64_t>(ctas) * warps;
     const int64_t n_merge = static_cast<int64_t>(W.merge_seg.size());
