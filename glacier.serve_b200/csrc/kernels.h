@@ -38,7 +38,18 @@ cudaError_t launch_block_copy(const ArenaGeom& g, const int32_t* ops, int n, int
 
 // ---- paged decode ----
 constexpr int kDecodeChunk = 8;  // tokens per decode work chunk
-constexpr int kFusedMergeMaxSlots = 8;  // segments split into more pieces use the merge kernel
+// Segments split into more pieces than this are merged by the merge kernel, the others by the
+// decode warp that completes them.  0: the merge kernel takes every split segment.  In-kernel
+// merging costs each arriving warp a fence + atomic round trip (~4 us under full HBM load)
+// and puts merges on the decode's tail; with the merge launch overlapped (programmatic
+// dependent launch) the merge kernel measured 2 % faster on cfg2 and equal elsewhere.
+constexpr int kFusedMergeMaxSlots = 0;
+// Chunks' worth of time charged to every segment when the chunk stream is cut into equal
+// worker ranges, so a warp that starts more segments (a q load, a new table row, a partial
+// per piece) gets fewer chunks.  Measured on the lognormal 256-sequence batch: 0 -> 4 took the
+// fp32 decode from 0.782 to 0.807 of HBM and bf16 from 0.727 to 0.774; 8 was worse than 4;
+// the uniform 64 x 2049 batch was unchanged.
+constexpr int64_t kSegmentCost = 4;
 
 // Work list of one step, built on the host (all pointers are device pointers).
 //  segment s = b * heads_kv + h; its chunks are k = 0 .. n_chunks(ctx_b) - 1, chunk k
@@ -60,8 +71,8 @@ struct DecodeWork {
     const int32_t* merge_slot0;        // their first partial slot (slots are contiguous)
     const int32_t* merge_nslots;
     // [n_pieces] merge entry of a split piece whose segment is merged inside the decode
-    // kernel (few pieces); -1 for an unsplit piece; -2 when the segment is merged afterwards
-    // by the deferred-merge kernel (many pieces: one warp would serialise the merge).
+    // kernel (at most kFusedMergeMaxSlots pieces); -1 for an unsplit piece; -2 when the
+    // segment is merged afterwards by the deferred-merge kernel.
     const int32_t* piece_merge;
     int32_t n_merge;
     const int32_t* merge_deferred;     // [n_deferred] merge entries left to the merge kernel

@@ -87,24 +87,35 @@ void plan_fixed(const int32_t* ctx, int32_t batch, int32_t heads_kv, int32_t bs,
                 int64_t total, int32_t* pseg, int32_t* pc0, int32_t* pc1, int32_t* pslot,
                 int32_t* pmerge, int32_t* wbeg, int32_t* mseg, int32_t* ms0, int32_t* mns, int32_t* mdef,
                 int32_t* n_pieces, int32_t* n_slots, int32_t* n_merge, int32_t* n_deferred) {
+    // the charged stream: every non-empty segment spans kSegmentCost units, then its chunks
     const int64_t n_seg = static_cast<int64_t>(batch) * heads_kv;
-    int64_t s = 0, s0 = 0, s1 = n_seg > 0 ? chunks_of(ctx[0], bs) : 0;
+    auto span = [&](int64_t seg) {
+        const int64_t c = chunks_of(ctx[seg / heads_kv], bs);
+        return c > 0 ? c + kSegmentCost : 0;
+    };
+    int64_t vtotal = 0;
+    for (int64_t seg = 0; seg < n_seg; ++seg) vtotal += span(seg);
+    (void)total;
+    int64_t s = 0, s0 = 0, s1 = n_seg > 0 ? span(0) : 0;
     int32_t np = 0;
     for (int32_t w = 0; w < n_workers; ++w) {
         wbeg[w] = np;
-        int64_t lo = total * w / n_workers;
-        const int64_t hi = total * (w + 1) / n_workers;
+        int64_t lo = vtotal * w / n_workers;
+        const int64_t hi = vtotal * (w + 1) / n_workers;
         while (lo < hi) {
             while (s1 <= lo) {
                 ++s;
                 s0 = s1;
-                s1 = s0 + chunks_of(ctx[s / heads_kv], bs);
+                s1 = s0 + span(s);
             }
             const int64_t end = hi < s1 ? hi : s1;
-            pseg[np] = static_cast<int32_t>(s);
-            pc0[np] = static_cast<int32_t>(lo - s0);
-            pc1[np] = static_cast<int32_t>(end - s0);
-            ++np;
+            const int64_t c0 = lo - s0 - kSegmentCost, c1 = end - s0 - kSegmentCost;
+            if (c1 > 0) {  // a range inside the overhead units holds no chunk
+                pseg[np] = static_cast<int32_t>(s);
+                pc0[np] = static_cast<int32_t>(c0 > 0 ? c0 : 0);
+                pc1[np] = static_cast<int32_t>(c1);
+                ++np;
+            }
             lo = end;
         }
     }

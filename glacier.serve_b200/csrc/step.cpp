@@ -23,6 +23,7 @@ namespace {
 // 16 -> 52 us, 4 -> 43 us; cfg2 / cfg3 unchanged.
 constexpr int kMinChunksPerWorker = 4;
 
+
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 int sm_count(int device) {
@@ -96,16 +97,21 @@ void build_work_list(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, i
         v->clear();
     W.n_slots = 0;
     const int64_t n_seg = static_cast<int64_t>(batch) * heads_kv;
+    // segment s spans [seg_start[s], seg_start[s+1]) of the split line: kSegmentCost units of
+    // per-piece overhead, then its chunks
     std::vector<int64_t> seg_start(static_cast<size_t>(n_seg) + 1, 0);
+    int64_t real_total = 0;
     for (int32_t b = 0; b < batch; ++b) {
         const int32_t c = chunks_of(ctx_lens[b], block_size);
+        const int64_t span = c > 0 ? c + kSegmentCost : 0;
         for (int32_t h = 0; h < heads_kv; ++h) {
             const int64_t s = static_cast<int64_t>(b) * heads_kv + h;
-            seg_start[static_cast<size_t>(s) + 1] = seg_start[static_cast<size_t>(s)] + c;
+            seg_start[static_cast<size_t>(s) + 1] = seg_start[static_cast<size_t>(s)] + span;
         }
+        real_total += static_cast<int64_t>(c) * heads_kv;
     }
     const int64_t total = seg_start[static_cast<size_t>(n_seg)];
-    W.total_chunks = total;
+    W.total_chunks = real_total;
     W.worker_begin.assign(static_cast<size_t>(n_workers) + 1, 0);
     int64_t seg = 0;
     // Worker w covers chunks [total*w/n, total*(w+1)/n), stepped without divisions; every
@@ -135,10 +141,13 @@ void build_work_list(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, i
             const int64_t s0 = seg_start[static_cast<size_t>(seg)];
             const int64_t s1 = seg_start[static_cast<size_t>(seg) + 1];
             const int64_t end = hi < s1 ? hi : s1;
-            ps[np_] = static_cast<int32_t>(seg);
-            pc0[np_] = static_cast<int32_t>(lo - s0);
-            pc1[np_] = static_cast<int32_t>(end - s0);
-            ++np_;
+            const int64_t c0 = lo - s0 - kSegmentCost, c1 = end - s0 - kSegmentCost;
+            if (c1 > 0) {  // a range inside the overhead units holds no chunk
+                ps[np_] = static_cast<int32_t>(seg);
+                pc0[np_] = static_cast<int32_t>(c0 > 0 ? c0 : 0);
+                pc1[np_] = static_cast<int32_t>(c1);
+                ++np_;
+            }
             lo = end;
         }
     }
@@ -966,6 +975,7 @@ int gkv_plan_decode(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, in
         info->n_slots = W.n_slots;
         info->n_merge = static_cast<int32_t>(W.merge_seg.size());
         info->n_workers = n_workers;
+        info->segment_cost = static_cast<int32_t>(gkv::kSegmentCost);
     }
     if (piece_seg || piece_c0 || piece_c1 || piece_slot) {
         if (cap_pieces < np) return set_error(GKV_EINVAL, "cap_pieces %d < %d pieces", cap_pieces, np);

@@ -557,7 +557,7 @@ def plan_decode(ctx_lens: Sequence[int], heads_kv: int, block_size: int, n_worke
                                C.byref(info), _ptr(seg), _ptr(c0), _ptr(c1), _ptr(slot), _ptr(wb), n))
     k = info.n_pieces
     return {"total_chunks": info.total_chunks, "n_pieces": k, "n_slots": info.n_slots,
-            "n_merge": info.n_merge, "piece_seg": seg[:k], "piece_c0": c0[:k], "piece_c1": c1[:k],
+            "n_merge": info.n_merge, "segment_cost": info.segment_cost, "piece_seg": seg[:k], "piece_c0": c0[:k], "piece_c1": c1[:k],
             "piece_slot": slot[:k], "worker_begin": wb}
 
 

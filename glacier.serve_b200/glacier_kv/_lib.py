@@ -47,6 +47,7 @@ class gkv_plan_info(C.Structure):
         ("n_slots", C.c_int32),
         ("n_merge", C.c_int32),
         ("n_workers", C.c_int32),
+        ("segment_cost", C.c_int32),
     ]
 
 

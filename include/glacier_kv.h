@@ -290,9 +290,11 @@ typedef struct gkv_plan_info {
     int32_t n_slots;       /* pieces that write a partial (segment split over workers)  */
     int32_t n_merge;       /* segments merged by the log-sum-exp kernel                 */
     int32_t n_workers;
+    int32_t segment_cost;  /* chunks' worth of time charged to each segment in the split */
 } gkv_plan_info;
 /* Builds the decode work list for n_workers warp workers without touching a GPU: the
- * flattened chunk stream of all segments is split into n_workers equal contiguous ranges.
+ * flattened stream of all segments, each charged segment_cost chunks for its per-piece
+ * overhead ahead of its chunks, is split into n_workers equal contiguous ranges.
  * The piece arrays (cap_pieces entries each) and worker_begin (n_workers + 1) are optional;
  * pass NULL to query sizes only.  (No reference counterpart: the reference runs one
  * sequence per call, PagedTransformerRunner.cs:605-656.) */

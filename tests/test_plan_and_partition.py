@@ -35,9 +35,17 @@ def test_work_list_covers_every_chunk_once_and_balances(ctx, heads, bs, workers)
     assert len(seen) == total
     wb = plan["worker_begin"]
     assert wb[0] == 0 and wb[-1] == plan["n_pieces"] and np.all(np.diff(wb) >= 0)
-    per_worker = [int((plan["piece_c1"][wb[w]:wb[w + 1]] - plan["piece_c0"][wb[w]:wb[w + 1]]).sum())
-                  for w in range(workers)]
-    assert max(per_worker) - min(per_worker) <= 1  # equal contiguous ranges
+    # equal contiguous ranges of the charged stream: a worker's chunks plus segment_cost for
+    # every segment it starts agree to within one chunk plus the charge of a segment whose
+    # start another worker's range cut
+    cost = plan["segment_cost"]
+    assert cost >= 0
+    load = []
+    for w in range(workers):
+        c0 = plan["piece_c0"][wb[w]:wb[w + 1]]
+        c1 = plan["piece_c1"][wb[w]:wb[w + 1]]
+        load.append(int((c1 - c0).sum()) + cost * int((c0 == 0).sum()))
+    assert max(load) - min(load) <= 1 + 2 * cost
     # a segment split over several workers gets contiguous partial slots
     slots = plan["piece_slot"]
     split = [s for s in set(plan["piece_seg"].tolist()) if (plan["piece_seg"] == s).sum() > 1]
