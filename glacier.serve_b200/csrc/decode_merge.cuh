@@ -110,11 +110,95 @@ __device__ __forceinline__ void merge_segment(const DecodeArgs& a, const DecodeW
 }
 
 // Merge of the segments split into more than kFusedMergeMaxSlots pieces, run as a second
-// launch so that the merge of a long segment is spread over a whole CTA instead of one warp
-// at the tail of the decode.  One CTA per (deferred segment, head group x head); its 256
-// threads are SL slot lanes x DV dims (SL = 256 / DV).
+// launch, when no segment has more than kWarpMergeMaxSlots slots.  One warp per (deferred
+// segment, head of a head group), eight per CTA: lane l owns
+// dims [l*DV/32, (l+1)*DV/32) and makes ONE online pass over the segment's partial slots,
+// keeping the running (max, sum) itself.  A slot's loads do not depend on the running state,
+// so the loads of consecutive slots overlap, and no block reduction is needed.
 template <int GP, int DV>
-__global__ void __launch_bounds__(256) deferred_merge_kernel(ArenaGeom g, DecodeWork w,
+__global__ void __launch_bounds__(256) deferred_merge_warp_kernel(ArenaGeom g, DecodeWork w,
+                                                             DecodeArgs a, int group,
+                                                             int head_groups) {
+    constexpr int EPLV = DV / 32;
+    static_assert(DV % 32 == 0, "DV must be a multiple of 32");
+    constexpr float kL2e = 1.4426950408889634f;
+    const int lane = threadIdx.x & 31;
+    const int per_entry = head_groups * GP;
+    const int item = static_cast<int>(blockIdx.x) * 8 + static_cast<int>(threadIdx.x >> 5);
+    const bool live = item < w.n_deferred * per_entry;
+    const int di = live ? item / per_entry : 0;
+    const int y = item - di * per_entry;
+    const int hg = y / GP;
+    const int gg = y - hg * GP;
+    // the merge list comes from the step's host copy; the partials are the previous
+    // (decode) kernel's output
+    const int mi = live ? __ldg(w.merge_deferred + di) : 0;
+    const int seg = live ? __ldg(w.merge_seg + mi) : 0;
+    const int s0 = live ? __ldg(w.merge_slot0 + mi) : 0;
+    const int ns = live ? __ldg(w.merge_nslots + mi) : 0;
+    const int b = seg / g.heads_kv;
+    const int h = seg - b * g.heads_kv;
+    const int q_head0 = h * group + hg * GP;
+    const int gcount = min(GP, group - hg * GP);
+    pdl_launch_dependents();
+    pdl_wait();
+    if (!live || gg >= gcount) return;
+    const int64_t base = (static_cast<int64_t>(hg) * w.n_slots + s0) * GP + gg;  // + s * GP
+    float M = -INFINITY, L = 0.f, A[EPLV];
+#pragma unroll
+    for (int e = 0; e < EPLV; ++e) A[e] = 0.f;
+#pragma unroll 4
+    for (int s = 0; s < ns; ++s) {
+        const int64_t ps = base + static_cast<int64_t>(s) * GP;
+        const float2 st = __ldcg(reinterpret_cast<const float2*>(a.part_ml + ps * 2));
+        const float* ap = a.part_acc + ps * DV + lane * EPLV;
+        float v[EPLV];
+        if constexpr (EPLV % 4 == 0) {
+#pragma unroll
+            for (int e = 0; e < EPLV; e += 4) {
+                const float4 x = __ldcg(reinterpret_cast<const float4*>(ap + e));
+                v[e] = x.x;
+                v[e + 1] = x.y;
+                v[e + 2] = x.z;
+                v[e + 3] = x.w;
+            }
+        } else if constexpr (EPLV == 2) {
+            const float2 x = __ldcg(reinterpret_cast<const float2*>(ap));
+            v[0] = x.x;
+            v[1] = x.y;
+        } else {
+#pragma unroll
+            for (int e = 0; e < EPLV; ++e) v[e] = __ldcg(ap + e);
+        }
+        if (st.x == -INFINITY) continue;  // a piece with no scores
+        const float mn = fmaxf(M, st.x);
+        const float fo = exp2f(M - mn), fn = exp2f(st.x - mn);
+        L = fmaf(L, fo, st.y * fn);
+#pragma unroll
+        for (int e = 0; e < EPLV; ++e) A[e] = fmaf(A[e], fo, v[e] * fn);
+        M = mn;
+    }
+    const int qh = q_head0 + gg;
+    float f = 1.f, Mref = M;
+    if (a.sinks || a.has_sink_all) {
+        const float sk = (a.sinks ? __ldg(a.sinks + qh) : a.sink_all) * kL2e;
+        const float M2 = fmaxf(M, sk);
+        f = (M == -INFINITY) ? 0.f : exp2f(M - M2);
+        L = L * f + exp2f(sk - M2);
+        Mref = M2;
+    }
+    const float inv = L > 0.f ? f / L : 0.f;
+    float* op = a.out + (static_cast<int64_t>(b) * a.n_heads + qh) * DV + lane * EPLV;
+#pragma unroll
+    for (int e = 0; e < EPLV; ++e) op[e] = A[e] * inv;
+    if (a.lse && lane == 0) a.lse[static_cast<int64_t>(b) * a.n_heads + qh] = lse_ln(Mref, L);
+}
+
+// The same merge for long segments (more than kWarpMergeMaxSlots slots): one CTA per
+// (deferred segment, head group x head), whose 256 threads are SL slot lanes x DV dims
+// (SL = 256 / DV), so a long segment's slots are read by SL lanes at once.
+template <int GP, int DV>
+__global__ void __launch_bounds__(256) deferred_merge_cta_kernel(ArenaGeom g, DecodeWork w,
                                                              DecodeArgs a, int group) {
     constexpr int T = 256;
     constexpr int SL = T / DV;

@@ -50,6 +50,11 @@ constexpr int kFusedMergeMaxSlots = 0;
 // fp32 decode from 0.782 to 0.807 of HBM and bf16 from 0.727 to 0.774; 8 was worse than 4;
 // the uniform 64 x 2049 batch was unchanged.
 constexpr int64_t kSegmentCost = 4;
+// Deferred merges run one warp per (segment, head) when the deferred segments average at most
+// this many slots, else one CTA per (segment, head) with several slot lanes.  Measured: the
+// warp form saved 1-2 % of the decode on batches averaging 3-6 slots per segment (a few longer
+// segments included) and cost 30 % on a batch of 15-slot segments and 6 % on 37-slot ones.
+constexpr int kWarpMergeMaxSlots = 8;
 
 // Work list of one step, built on the host (all pointers are device pointers).
 //  segment s = b * heads_kv + h; its chunks are k = 0 .. n_chunks(ctx_b) - 1, chunk k
@@ -77,6 +82,7 @@ struct DecodeWork {
     int32_t n_merge;
     const int32_t* merge_deferred;     // [n_deferred] merge entries left to the merge kernel
     int32_t n_deferred;
+    int32_t deferred_avg_slots;        // mean slots of the deferred entries, rounded up (merge form)
     // Arrival counters of the fused merge, [head_groups][n_merge] ints.  They must be zero
     // when a launch starts; the worker that completes a segment resets its counter, so they
     // are zero again after every launch that ran to completion.

@@ -280,6 +280,9 @@ extern "C" int gkv_paged_decode_noalloc(const gkv_arena_desc* arena, int32_t lay
     w.merge_count = reinterpret_cast<int32_t*>(dbase + L.counters);
     w.merge_deferred = dp(L.mdef);
     w.n_deferred = ndef;
+    int64_t def_slots = 0;  // mean slots of the deferred entries (selects the merge form)
+    for (int32_t k = 0; k < ndef; ++k) def_slots += at(L.mns)[at(L.mdef)[k]];
+    w.deferred_avg_slots = ndef > 0 ? static_cast<int32_t>((def_slots + ndef - 1) / ndef) : 0;
 
     DecodeArgs a{};
     a.layer = layer;

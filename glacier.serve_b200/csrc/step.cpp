@@ -190,6 +190,15 @@ void build_work_list(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, i
     }
 }
 
+// Mean partial slots of the segments the merge kernel takes, rounded up (selects its warp or
+// CTA form).
+static int32_t deferred_avg_slots(const WorkList& W) {
+    int64_t sum = 0;
+    for (int32_t mi : W.merge_deferred) sum += W.merge_nslots[static_cast<size_t>(mi)];
+    const int64_t n = static_cast<int64_t>(W.merge_deferred.size());
+    return n > 0 ? static_cast<int32_t>((sum + n - 1) / n) : 0;
+}
+
 // Sizes the pinned + device metadata buffers for `bytes`.  Only called while no step of
 // this pool is in use by a kernel that has not been ordered before the next upload
 // (cudaFree synchronises the device).
@@ -428,6 +437,7 @@ int step_upload(Pool* p, const int32_t* tables, int32_t batch, int32_t max_block
     w.n_merge = static_cast<int32_t>(n_merge);
     w.merge_deferred = reinterpret_cast<const int32_t*>(d + L.mdef);
     w.n_deferred = static_cast<int32_t>(W.merge_deferred.size());
+    w.deferred_avg_slots = deferred_avg_slots(W);
     w.merge_count = ws.d_merge_count;
     w.table_row = nullptr;
     ws.d_slots = reinterpret_cast<const int64_t*>(d + L.slots);
@@ -737,6 +747,7 @@ int step_prefill(Pool* p, int32_t layer, const void* d_q, int32_t q_dtype, float
     w.n_merge = static_cast<int32_t>(n_merge);
     w.merge_deferred = at(L.mdef);
     w.n_deferred = static_cast<int32_t>(W.merge_deferred.size());
+    w.deferred_avg_slots = deferred_avg_slots(W);
     w.merge_count = ws.d_merge_count;
     w.table_row = at(rows_off);
     const float* qf = static_cast<const float*>(d_q);
