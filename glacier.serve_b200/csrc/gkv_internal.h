@@ -80,14 +80,19 @@ struct StepWorkspace {
     int32_t max_batch = 0, max_blocks = 0, max_tokens = 0, n_heads = 0;
     DecodeConfig cfg{};
     int32_t n_ctas_max = 0;   // persistent grid size for this geometry
-    // packed metadata: one device buffer and one copy per step, from two pinned staging
-    // buffers used in turn, so the host fills step k+1's while step k's copy may still be in
-    // flight
+    // Packed metadata: one copy per step, from two pinned staging buffers into two device
+    // buffers used in turn.  The copy runs on meta_stream as soon as the step that last used
+    // its buffer (two uploads ago) has finished, so it overlaps the previous step's kernels;
+    // the caller's stream then waits for it.
     char* h_meta[2] = {nullptr, nullptr};
-    char* d_meta = nullptr;
+    char* d_meta[2] = {nullptr, nullptr};
     size_t meta_cap = 0;
-    cudaEvent_t meta_copied[2] = {nullptr, nullptr};  // staging i may be rewritten once this fires
+    cudaEvent_t meta_copied[2] = {nullptr, nullptr};  // staging + device buffer i filled
     bool meta_pending[2] = {false, false};
+    // recorded on the caller's stream at upload time: everything queued before that upload
+    cudaEvent_t meta_mark[2] = {nullptr, nullptr};
+    bool meta_marked[2] = {false, false};
+    cudaStream_t meta_stream = nullptr;
     int meta_flip = 0;
     // partial results of split segments
     float* d_part_acc = nullptr;

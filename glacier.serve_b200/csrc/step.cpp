@@ -204,27 +204,34 @@ static int32_t deferred_avg_slots(const WorkList& W) {
 // (cudaFree synchronises the device).
 static int ensure_meta(Pool* p, size_t bytes) {
     StepWorkspace& ws = p->ws;
-    for (int i = 0; i < 2; ++i)
-        if (!ws.meta_copied[i]) {
-            cudaError_t e = cudaEventCreateWithFlags(&ws.meta_copied[i], cudaEventDisableTiming);
-            if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
-        }
+    for (int i = 0; i < 2; ++i) {
+        for (cudaEvent_t* ev : {&ws.meta_copied[i], &ws.meta_mark[i]})
+            if (!*ev) {
+                cudaError_t e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming);
+                if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
+            }
+    }
+    if (!ws.meta_stream) {
+        cudaError_t e = cudaStreamCreateWithFlags(&ws.meta_stream, cudaStreamNonBlocking);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaStreamCreate(step metadata)");
+    }
     if (bytes <= ws.meta_cap) return GKV_OK;
     for (int i = 0; i < 2; ++i) {
         if (ws.meta_pending[i]) cudaEventSynchronize(ws.meta_copied[i]);
         ws.meta_pending[i] = false;
+        ws.meta_marked[i] = false;
         if (ws.h_meta[i]) cudaFreeHost(ws.h_meta[i]);
         ws.h_meta[i] = nullptr;
+        if (ws.d_meta[i]) cudaFree(ws.d_meta[i]);
+        ws.d_meta[i] = nullptr;
     }
-    if (ws.d_meta) cudaFree(ws.d_meta);
-    ws.d_meta = nullptr;
     ws.meta_cap = 0;
     ws.uploaded = false;  // the previous step's metadata is gone
     const size_t cap = align_up(bytes, 4096);
     cudaError_t e = cudaSuccess;
     for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = cudaMallocHost(&ws.h_meta[i], cap);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMallocHost(step metadata)");
-    e = cudaMalloc(&ws.d_meta, cap);
+    for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = cudaMalloc(&ws.d_meta[i], cap);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(step metadata)");
     ws.meta_cap = cap;
     return GKV_OK;
@@ -298,13 +305,19 @@ int step_reserve(Pool* p, int32_t max_batch, int32_t max_blocks, int32_t max_tok
 
 void step_free(Pool* p) {
     StepWorkspace& ws = p->ws;
+    if (ws.meta_stream) cudaStreamSynchronize(ws.meta_stream);
     for (int i = 0; i < 2; ++i) {
         if (ws.meta_copied[i]) cudaEventDestroy(ws.meta_copied[i]);
+        if (ws.meta_mark[i]) cudaEventDestroy(ws.meta_mark[i]);
         if (ws.h_meta[i]) cudaFreeHost(ws.h_meta[i]);
-        ws.meta_copied[i] = nullptr;
+        if (ws.d_meta[i]) cudaFree(ws.d_meta[i]);
+        ws.meta_copied[i] = ws.meta_mark[i] = nullptr;
         ws.h_meta[i] = nullptr;
+        ws.d_meta[i] = nullptr;
+        ws.meta_marked[i] = false;
     }
-    if (ws.d_meta) cudaFree(ws.d_meta);
+    if (ws.meta_stream) cudaStreamDestroy(ws.meta_stream);
+    ws.meta_stream = nullptr;
     if (ws.d_part_acc) cudaFree(ws.d_part_acc);
     if (ws.d_part_ml) cudaFree(ws.d_part_ml);
     if (ws.d_merge_count) cudaFree(ws.d_merge_count);
@@ -331,7 +344,6 @@ void step_free(Pool* p) {
     ws.pre_copied = nullptr;
     ws.h_pre = ws.d_pre = nullptr;
     ws.d_qconv = nullptr;
-    ws.d_meta = nullptr;
     ws.d_part_acc = ws.d_part_ml = nullptr;
 }
 
@@ -411,14 +423,23 @@ int step_upload(Pool* p, const int32_t* tables, int32_t batch, int32_t max_block
     put(L.ms0, W.merge_slot0);
     put(L.mns, W.merge_nslots);
     put(L.mdef, W.merge_deferred);
-    cudaError_t e = cudaMemcpyAsync(ws.d_meta, h, L.total, cudaMemcpyHostToDevice, st);
+    // Device buffer mi last served the step uploaded two calls ago, whose kernels were queued
+    // before the previous upload: the copy waits for the mark that upload recorded, then the
+    // caller's stream waits for the copy.
+    cudaError_t e = cudaSuccess;
+    if (ws.meta_marked[mi ^ 1]) e = cudaStreamWaitEvent(ws.meta_stream, ws.meta_mark[mi ^ 1], 0);
+    if (e == cudaSuccess) e = cudaEventRecord(ws.meta_mark[mi], st);
+    if (e != cudaSuccess) return cuda_fail(e, "step metadata ordering");
+    ws.meta_marked[mi] = true;
+    e = cudaMemcpyAsync(ws.d_meta[mi], h, L.total, cudaMemcpyHostToDevice, ws.meta_stream);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(step metadata)");
-    e = cudaEventRecord(ws.meta_copied[mi], st);
+    e = cudaEventRecord(ws.meta_copied[mi], ws.meta_stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(st, ws.meta_copied[mi], 0);
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord(step metadata)");
     ws.meta_pending[mi] = true;
     ws.meta_flip ^= 1;
 
-    char* d = ws.d_meta;
+    char* d = ws.d_meta[mi];
     DecodeWork& w = ws.work;
     w.tables = reinterpret_cast<const int32_t*>(d + L.tables);
     w.ctx_lens = reinterpret_cast<const int32_t*>(d + L.ctx);
