@@ -179,7 +179,8 @@ GKV_API int gkv_table_release_all(gkv_table* table);
  * the device block-table buffer of CudaPagedTransformerRunner.cs:115-120,143. */
 GKV_API int gkv_step_reserve(gkv_pool* pool, int32_t max_batch, int32_t max_blocks_per_seq,
                              int32_t max_tokens, int32_t n_heads);
-/* Uploads one step's packed metadata with ONE host-to-device copy on `stream`:
+/* Uploads one step's packed metadata with ONE host-to-device copy, ordered before the rest
+ * of `stream`:
  *   h_block_tables [batch][max_blocks] int32 (unused entries may hold -1),
  *   h_ctx_lens     [batch] tokens each sequence attends (0 = skip, output untouched,
  *                  PagedAttentionKernel.cs:42),
@@ -187,7 +188,11 @@ GKV_API int gkv_step_reserve(gkv_pool* pool, int32_t max_batch, int32_t max_bloc
  *                  token (-1 = skip).
  * Validates every referenced block id and every ctx_len <= max_blocks * block_size on the
  * host (GKV_EINVAL), then builds the split-KV work list.  Replaces the per-sequence
- * UploadBlockTable, CudaPagedTransformerRunner.cs:344,367-379. */
+ * UploadBlockTable, CudaPagedTransformerRunner.cs:344,367-379.
+ * The copy runs on a stream of the pool's own, into one of two device buffers used in turn,
+ * once the work queued on `stream` before the PREVIOUS upload has finished; `stream` then
+ * waits for it.  So the launches of a step (append, decode, prefill) belong on the stream of
+ * its upload, or must be ordered before the next-but-one upload by the caller. */
 GKV_API int gkv_upload_step(gkv_pool* pool, const int32_t* h_block_tables, int32_t batch,
                             int32_t max_blocks, const int32_t* h_ctx_lens,
                             const int64_t* h_slot_mapping, int32_t n_tok, void* stream);
