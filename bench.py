@@ -3,18 +3,22 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2] [--impl reference]
 
-Default workload: BASELINE config 2 -- one continuous-batching iteration of 64 sequences x
-2048 cached tokens (32 query / 8 kv heads, d 128, fp32 KV, 16-token blocks, 16384-block
-pool): upload the step's tables + slot mapping, append one new K/V row per sequence, decode
-every sequence.  A "step" is that iteration; tokens/s = sequences decoded per second.
+Default workload: BASELINE config 3, the config the metric's 1/2/4/8-GPU reading is quoted on --
+one decode step of 256 sequences with lognormal context lengths (median 1500, sigma 1, clipped to
+16..32768) whose block tables come from a seeded 10k-operation admit/evict churn of a 65536-block
+pool (28 query / 4 kv heads, d 128, fp32 KV, 16-token blocks).  The 256 sequences are ONE global
+batch split over the GPUs by longest-first partitioning (strong scaling): every rank owns a pool
+and decodes its share, with no collective.  A "step" is: upload the step's tables (one host-to-
+device copy), decode every sequence; tokens/s = sequences decoded per second.  cfg2 (append +
+decode of 64 x 2048 tokens, weak-scaled), cfg1, cfg3-bf16, cfg4 (prefill), cfg5 (split-KV over
+GPUs) and the append / copy kernels run with --config.
 
 `value` times the step with inputs resident in HBM (CUDA events, max over ranks).  `e2e`
 times the same iteration through gkv_decode_step_host with pinned HOST buffers (q, new K/V,
-tables in; attention output out), copies included.  Multi-GPU runs are weak-scaled: every
-rank owns its own pool and its own 64 sequences (sequence partitioning, no collective).
+tables in; attention output out), every copy included, the last output copy too.
 
 `--impl reference` times the CPU restatement of the reference's PagedAttentionKernel
-(oracle/, faithful threading: sequences serial, OpenMP over query heads) on the host cores;
+(oracle/, faithful threading: sequences serial, OpenMP over query heads) on all host cores;
 the reference itself is C# and cannot be built in this image.
 """
 from __future__ import annotations
@@ -246,17 +250,36 @@ def prefill_cpu_baseline(w, steps: int, budget_s: float, threads: int, seed: int
     }
 
 
+def mapped_native_libs():
+    """Shared objects of this repository mapped into the process (from /proc/self/maps)."""
+    out = set()
+    try:
+        with open("/proc/self/maps") as f:
+            for ln in f:
+                path = ln.split()[-1] if len(ln.split()) >= 6 else ""
+                if path.endswith(".so") and os.path.realpath(path).startswith(os.path.realpath(ROOT)):
+                    out.add(os.path.relpath(os.path.realpath(path), os.path.realpath(ROOT)))
+    except OSError:
+        pass
+    return sorted(out)
+
+
 def run_reference(args):
+    """The reference arm: the CPU restatement (oracle/) of the reference's own code for the path,
+    timed on the host cores with the thread count passed explicitly (a torchrun launch sets
+    OMP_NUM_THREADS=1, which must not shrink the baseline).  Maps no native code of the product:
+    the workload generators are numpy only and glacier_kv's library loads on first use."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     from oracle import pyoracle as O
 
+    cores = O.host_cores()
     if args.config == "cfg4":
         from glacier_kv import workloads as W
 
         w = W.cfg4(W.SEED)
-        res = prefill_cpu_baseline(w, max(args.steps, 1), budget_s=120.0, threads=O.max_threads(), seed=w.seed)
+        res = prefill_cpu_baseline(w, max(args.steps, 1), budget_s=120.0, threads=cores, seed=w.seed)
         line = {
             "metric": PREFILL_METRIC, "value": res["value"], "unit": "TFLOP/s", "impl": "reference",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -268,10 +291,7 @@ def run_reference(args):
             "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": res["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }
-        print(json.dumps(line), flush=True)
-        return
-
-    if args.config in BANDWIDTH_CONFIGS:
+    elif args.config in BANDWIDTH_CONFIGS:
         res = bandwidth_cpu_baseline(args.config, max(args.steps, 1), budget_s=120.0)
         line = {
             "metric": f"{'KV append' if args.config.startswith('append') else 'block copy'} GB/s per B200 vs HBM peak",
@@ -280,27 +300,28 @@ def run_reference(args):
             "vs_baseline": None, "dtype": "bf16" if args.config.endswith("bf16") else "f32",
             "data": "synthetic (seeded N(0,1))",
             "config": {"workload": args.config, "l2": "n/a (CPU)",
-                       "implementation": "C restatement of PagedBlockPool.Store / CopyBlockData and the runner loop"},
+                       "implementation": "C restatement of PagedBlockPool.Store / CopyBlockData and the runner loop "
+                                         "(serial in the reference, so one thread)"},
             "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": res["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }
-        print(json.dumps(line), flush=True)
-        return
-
-    w = workload(args.config, 0)
-    threads = O.max_threads()
-    res = cpu_baseline_run(w, max(args.steps, 1), budget_s=120.0, threads=threads, seed=w.seed)
-    line = {
-        "metric": METRIC, "value": res["value"], "unit": UNIT, "impl": "reference",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": res["ms_per_sample"], "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
-        "config": {"workload": describe(w), "l2": "n/a (CPU)",
-                   "implementation": "C restatement of PagedAttentionKernel.ComputeAttention "
-                                     "(the C# reference needs .NET 10 + un-vendored NuGet; not buildable here)"},
-        "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
-        "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
+    else:
+        w = workload(args.config, 0)
+        res = cpu_baseline_run(w, max(args.steps, 1), budget_s=120.0, threads=cores, seed=w.seed)
+        line = {
+            "metric": METRIC, "value": res["value"], "unit": UNIT, "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": res["ms_per_sample"], "higher_is_better": True,
+            "scaling": "strong" if args.config in STRONG else "weak",
+            "vs_baseline": None, "dtype": "f32", "kv_dtype": w.dtype, "data": "synthetic (seeded N(0,1))",
+            "config": {"workload": describe(w), "l2": "n/a (CPU)",
+                       "implementation": "C restatement of PagedAttentionKernel.ComputeAttention "
+                                         "(the C# reference needs .NET 10 + un-vendored NuGet; not buildable here)"},
+            "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+    line["host_cores"] = cores
+    line["native_so_loaded"] = mapped_native_libs()
     print(json.dumps(line), flush=True)
 
 
@@ -636,11 +657,14 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="cfg2")
+    ap.add_argument("--config", default="cfg3")
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=0,
                     help="sequences of cfg2/cfg3 (default: the config's own); for small profiler captures")
+    ap.add_argument("--share", type=int, default=0,
+                    help="cfg3 on one GPU: decode only rank 0's longest-first share of an N-GPU split "
+                         "(the per-rank step of the N-GPU run, for profiling it on one GPU)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -683,6 +707,11 @@ def main():
 
     w = workload(args.config, rank, world, args.batch)
     global_batch = (args.batch or 256) if args.config in ("cfg3", "cfg3-bf16") else w.batch
+    if args.share > 1 and world == 1 and args.config in ("cfg3", "cfg3-bf16"):
+        from glacier_kv import workloads as W
+
+        w = W.lpt_share(w, 0, args.share)
+        global_batch = w.batch  # this GPU decodes its share only
     pool = W.make_pool(w, device=local)
     W.fill_arena_randn(pool, seed=w.seed)
     stream = torch.cuda.current_stream(dev)
@@ -798,6 +827,8 @@ def main():
             flush.zero_()
             fl[i][1].record(stream)
         e2e_step()
+    if not split_kv:  # the last call's output copy runs on the pool's copy stream
+        pool.wait_host_outputs(stream)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     flush_ms = sum(a.elapsed_time(b) for a, b in fl)
@@ -812,18 +843,25 @@ def main():
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong" if args.config in STRONG else "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) Q/K/V, seeded block tables)",
+            "vs_baseline": None, "dtype": "f32", "kv_dtype": w.dtype,
+            "data": "synthetic (seeded N(0,1) Q/K/V, seeded block tables)",
             "config": {"workload": describe(w),
                        "l2": "L2 flushed (256 MiB write) before every step" if small else
                              f"inputs larger than L2 ({kv_bytes / 1e9:.2f} GB of KV read per step)",
                        "parallelism": (f"split-KV: each sequence's blocks split over {world} GPU(s), (out, lse) "
                                        "exchanged through peer-memory mailboxes (NCCL all-gather fallback) + LSE "
                                        "merge") if split_kv else
+                                      (f"rank 0's share ({w.batch} sequences) of the 256 split over {args.share} GPUs "
+                                       "by longest-first partitioning, run alone on one GPU")
+                                      if args.share > 1 else
                                       (f"sequence-sharded: the {global_batch} sequences split over {world} GPU(s) by "
                                        "longest-first partitioning, one pool each, no collective")
                                       if args.config in STRONG else
                                       f"sequence-sharded: {world} GPU(s), one pool each, no collective",
-                       "step": "upload tables+slots (1 H2D) + kv_append + paged_decode (+ LSE merge)"},
+                       "step": ("upload tables (1 H2D) + split-KV decode with lse + peer exchange + LSE merge"
+                                if split_kv else
+                                "upload tables+slots (1 H2D) + kv_append + paged_decode (+ merge kernel)"
+                                if n_tok else "upload tables (1 H2D) + paged_decode (+ merge kernel)")},
             "kv_gbs_per_gpu": kv_bytes / (ms / 1e3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic_from_profiles(args.config),
@@ -832,7 +870,9 @@ def main():
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s"},
             "e2e": {"value": seqs_per_step / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms,
-                    "path": "gkv_decode_step_host (pinned host q/K/V/tables in, output out)",
+                    "path": ("pinned host q copied in, gkv_upload_step + gkv_paged_decode_splitkv_dist, "
+                             "output copied out (both copies on the step's stream)") if split_kv else
+                            "gkv_decode_step_host (pinned host q/K/V/tables in, output out)",
                     "l2": ("the L2 flush between steps is outside the timed span (its device time is "
                            "subtracted)") if flush is not None else "no flush (inputs larger than L2)"},
             "gpu_launches": launches,

@@ -67,6 +67,28 @@ class PrefixMap {
 };
 
 // Work-list construction (host only; unit-tested through the C ABI helpers).
+//
+// plan_work_into is the one planner of the decode work list.  It writes into caller-owned
+// arrays (no heap), sized for n_workers + batch * heads_kv pieces and batch * heads_kv merge
+// entries; build_work_list wraps it with vectors, and the allocation-free decode calls it on its
+// static staging buffer.
+struct PlanArrays {
+    int32_t *piece_seg, *piece_c0, *piece_c1, *piece_slot, *piece_merge;
+    int32_t* worker_begin;  // n_workers + 1
+    int32_t *merge_seg, *merge_slot0, *merge_nslots, *merge_deferred;
+    // results
+    int32_t n_pieces, n_slots, n_merge, n_deferred;
+    int64_t total_chunks;
+};
+void plan_work_into(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, int32_t block_size,
+                    int32_t n_workers, PlanArrays* out);
+// Persistent-grid size of a decode over `total_chunks` chunks: enough warp workers for
+// kMinChunksPerWorker chunks each, at most max_ctas CTAs of `warps` workers, >= 1 CTA when
+// there is work.
+int64_t decode_grid_ctas(int64_t total_chunks, int warps, int64_t max_ctas);
+// Mean partial slots of the deferred merge entries, rounded up (selects the merge form).
+int32_t deferred_avg_slots(const int32_t* merge_nslots, const int32_t* merge_deferred, int32_t n_deferred);
+
 struct WorkList {
     std::vector<int32_t> piece_seg, piece_c0, piece_c1, piece_slot, piece_merge, merge_deferred;
     std::vector<int32_t> worker_begin;  // n_workers + 1

@@ -22,7 +22,13 @@
 //  * The first call on each device resolves the array's device address with
 //    cudaGetSymbolAddress (with that device current) and caches it; make that first call
 //    before any stream capture.
+//  * A kernel that meets a bad block id or gives up a bounded wait ORs a bit into an error word
+//    at the end of the array.  Calls never clear it; gkv_paged_decode_noalloc_status waits for
+//    the caller's stream, reads the word and clears it, so bits of every call since the last
+//    check are reported.
+#include <chrono>
 #include <mutex>
+#include <thread>
 
 #include "gkv_device.cuh"
 #include "gkv_internal.h"
@@ -36,7 +42,6 @@ constexpr size_t kMetaBytes = 4u << 20;       // tables, context lengths, work l
 constexpr size_t kErrOffset = kScratchBytes - 256;
 constexpr size_t kPartBytes = kErrOffset - kMetaBytes;
 constexpr int kMaxDevices = 64;
-constexpr int kMinChunks = 16;
 
 }  // namespace
 
@@ -80,71 +85,6 @@ Layout layout_for(int64_t batch, int64_t max_blocks, int64_t max_pieces, int64_t
     L.counters = take(max_merge * head_groups * 4);  // merge arrival counters, staged as zeros
     L.total = o;
     return L;
-}
-
-// The work list of step.cpp's build_work_list, written into fixed arrays (no heap).
-void plan_fixed(const int32_t* ctx, int32_t batch, int32_t heads_kv, int32_t bs, int32_t n_workers,
-                int64_t total, int32_t* pseg, int32_t* pc0, int32_t* pc1, int32_t* pslot,
-                int32_t* pmerge, int32_t* wbeg, int32_t* mseg, int32_t* ms0, int32_t* mns, int32_t* mdef,
-                int32_t* n_pieces, int32_t* n_slots, int32_t* n_merge, int32_t* n_deferred) {
-    // the charged stream: every non-empty segment spans kSegmentCost units, then its chunks
-    const int64_t n_seg = static_cast<int64_t>(batch) * heads_kv;
-    auto span = [&](int64_t seg) {
-        const int64_t c = chunks_of(ctx[seg / heads_kv], bs);
-        return c > 0 ? c + kSegmentCost : 0;
-    };
-    int64_t vtotal = 0;
-    for (int64_t seg = 0; seg < n_seg; ++seg) vtotal += span(seg);
-    (void)total;
-    int64_t s = 0, s0 = 0, s1 = n_seg > 0 ? span(0) : 0;
-    int32_t np = 0;
-    for (int32_t w = 0; w < n_workers; ++w) {
-        wbeg[w] = np;
-        int64_t lo = vtotal * w / n_workers;
-        const int64_t hi = vtotal * (w + 1) / n_workers;
-        while (lo < hi) {
-            while (s1 <= lo) {
-                ++s;
-                s0 = s1;
-                s1 = s0 + span(s);
-            }
-            const int64_t end = hi < s1 ? hi : s1;
-            const int64_t c0 = lo - s0 - kSegmentCost, c1 = end - s0 - kSegmentCost;
-            if (c1 > 0) {  // a range inside the overhead units holds no chunk
-                pseg[np] = static_cast<int32_t>(s);
-                pc0[np] = static_cast<int32_t>(c0 > 0 ? c0 : 0);
-                pc1[np] = static_cast<int32_t>(c1);
-                ++np;
-            }
-            lo = end;
-        }
-    }
-    wbeg[n_workers] = np;
-    int32_t slots = 0, merges = 0, deferred = 0, i = 0;
-    while (i < np) {
-        int32_t j = i + 1;
-        while (j < np && pseg[j] == pseg[i]) ++j;
-        if (j - i > 1) {
-            const bool defer = (j - i) > kFusedMergeMaxSlots;
-            mseg[merges] = pseg[i];
-            ms0[merges] = slots;
-            mns[merges] = j - i;
-            if (defer) mdef[deferred++] = merges;
-            for (int32_t k = i; k < j; ++k) {
-                pslot[k] = slots++;
-                pmerge[k] = defer ? -2 : merges;
-            }
-            ++merges;
-        } else {
-            pslot[i] = -1;
-            pmerge[i] = -1;
-        }
-        i = j;
-    }
-    *n_pieces = np;
-    *n_slots = slots;
-    *n_merge = merges;
-    *n_deferred = deferred;
 }
 
 }  // namespace
@@ -227,10 +167,8 @@ extern "C" int gkv_paged_decode_noalloc(const gkv_arena_desc* arena, int32_t lay
 
     int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) sms = 148;
-    const int64_t max_ctas = static_cast<int64_t>(sms) * cfg.ctas_per_sm;
-    int64_t ctas = ((total + kMinChunks - 1) / kMinChunks + cfg.warps - 1) / cfg.warps;
-    if (ctas > max_ctas) ctas = max_ctas;
-    if (ctas < 1) ctas = 1;
+    // the same grid and work list as the pool's decode (gkv_upload_step + gkv_paged_decode)
+    const int64_t ctas = decode_grid_ctas(total, cfg.warps, static_cast<int64_t>(sms) * cfg.ctas_per_sm);
     const int32_t n_workers = static_cast<int32_t>(ctas * cfg.warps);
     const int64_t n_seg = static_cast<int64_t>(batch) * A.heads_kv;
     const int64_t max_pieces = n_workers + n_seg;
@@ -241,24 +179,28 @@ extern "C" int gkv_paged_decode_noalloc(const gkv_arena_desc* arena, int32_t lay
     unsigned char* h = g_stage;
     if (batch && max_blocks) memcpy(h + L.tables, h_block_tables, static_cast<size_t>(batch) * max_blocks * 4);
     memcpy(h + L.ctx, h_ctx_lens, static_cast<size_t>(batch) * 4);
-    int32_t np = 0, nslots = 0, nmerge = 0, ndef = 0;
     auto at = [&](size_t off) { return reinterpret_cast<int32_t*>(h + off); };
-    plan_fixed(h_ctx_lens, batch, A.heads_kv, bs, n_workers, total, at(L.pseg), at(L.pc0), at(L.pc1),
-               at(L.pslot), at(L.pmerge), at(L.wbeg), at(L.mseg), at(L.ms0), at(L.mns), at(L.mdef), &np,
-               &nslots, &nmerge, &ndef);
+    PlanArrays P{at(L.pseg), at(L.pc0), at(L.pc1), at(L.pslot), at(L.pmerge), at(L.wbeg),
+                 at(L.mseg), at(L.ms0), at(L.mns), at(L.mdef), 0, 0, 0, 0, 0};
+    plan_work_into(h_ctx_lens, batch, A.heads_kv, bs, n_workers, &P);
+    const int32_t nslots = P.n_slots, nmerge = P.n_merge, ndef = P.n_deferred;
     // the fused merge's arrival counters must start at zero on every call
     memset(h + L.counters, 0, static_cast<size_t>(n_seg) * cfg.head_groups * 4);
-    const size_t part_floats =
-        static_cast<size_t>(nslots) * cfg.head_groups * cfg.gp * (static_cast<size_t>(dv) + 2);
-    if (part_floats * sizeof(float) > kPartBytes)
+    // partials: (max, sum) pairs, then the accumulators at a 256-byte boundary (the
+    // tensor-core decode reads them with 16-byte vectors)
+    const size_t ml_bytes = static_cast<size_t>(nslots) * cfg.head_groups * cfg.gp * 2 * sizeof(float);
+    const size_t acc_off = (ml_bytes + 255) & ~static_cast<size_t>(255);
+    const size_t part_bytes =
+        acc_off + static_cast<size_t>(nslots) * cfg.head_groups * cfg.gp * static_cast<size_t>(dv) * sizeof(float);
+    if (part_bytes > kPartBytes)
         return set_error(GKV_EINVAL, "decode partials need %zu bytes, more than the %zu-byte static scratch allows",
-                         part_floats * sizeof(float), kPartBytes);
+                         part_bytes, kPartBytes);
 
     e = cudaMemcpyAsync(dbase, h, L.total, cudaMemcpyHostToDevice, st);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(static scratch)");
+    // the error word starts at zero (static storage) and is read and cleared by
+    // gkv_paged_decode_noalloc_status; kernels only OR bits into it
     int* d_err = reinterpret_cast<int*>(dbase + kErrOffset);
-    e = cudaMemsetAsync(d_err, 0, sizeof(int), st);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(error word)");
 
     DecodeWork w{};
     auto dp = [&](size_t off) { return reinterpret_cast<const int32_t*>(dbase + off); };
@@ -280,9 +222,7 @@ extern "C" int gkv_paged_decode_noalloc(const gkv_arena_desc* arena, int32_t lay
     w.merge_count = reinterpret_cast<int32_t*>(dbase + L.counters);
     w.merge_deferred = dp(L.mdef);
     w.n_deferred = ndef;
-    int64_t def_slots = 0;  // mean slots of the deferred entries (selects the merge form)
-    for (int32_t k = 0; k < ndef; ++k) def_slots += at(L.mns)[at(L.mdef)[k]];
-    w.deferred_avg_slots = ndef > 0 ? static_cast<int32_t>((def_slots + ndef - 1) / ndef) : 0;
+    w.deferred_avg_slots = deferred_avg_slots(at(L.mns), at(L.mdef), ndef);
 
     DecodeArgs a{};
     a.layer = layer;
@@ -291,12 +231,48 @@ extern "C" int gkv_paged_decode_noalloc(const gkv_arena_desc* arena, int32_t lay
     a.n_heads = n_heads;
     a.scale = scale;
     a.sinks = d_sinks;
-    float* part = reinterpret_cast<float*>(dbase + kMetaBytes);
-    a.part_ml = part;
-    a.part_acc = part + static_cast<size_t>(nslots) * cfg.head_groups * cfg.gp * 2;
+    a.part_ml = reinterpret_cast<float*>(dbase + kMetaBytes);
+    a.part_acc = reinterpret_cast<float*>(dbase + kMetaBytes + acc_off);
     a.err = d_err;
     int launches = 0;
     e = launch_paged_decode(g, w, a, &launches, st);
     if (e != cudaSuccess) return cuda_fail(e, "paged_decode launch");
     return GKV_OK;
+}
+
+extern "C" int gkv_paged_decode_noalloc_status(void* stream, int32_t timeout_ms) {
+    using namespace gkv;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= kMaxDevices) return set_error(GKV_EINVAL, "device %d beyond %d", dev, kMaxDevices);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // bounded wait for the caller's stream (no call here may hang)
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        e = cudaStreamQuery(st);
+        if (e == cudaSuccess) break;
+        if (e != cudaErrorNotReady) return cuda_fail(e, "cudaStreamQuery");
+        const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                            std::chrono::steady_clock::now() - t0).count();
+        if (timeout_ms >= 0 && ms >= timeout_ms)
+            return set_error(GKV_ETIMEDOUT, "stream still busy after %d ms", timeout_ms);
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+    char* dbase = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        dbase = static_cast<char*>(g_scratch_dev[dev]);
+    }
+    if (!dbase) return GKV_OK;  // no allocation-free decode ran on this device yet
+    int* d_err = reinterpret_cast<int*>(dbase + kErrOffset);
+    int flag = 0;
+    e = cudaMemcpy(&flag, d_err, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(error word)");
+    if (flag == 0) return GKV_OK;
+    const int zero = 0;
+    e = cudaMemcpy(d_err, &zero, sizeof(int), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(error word)");
+    return set_error(GKV_EDEVICE,
+                     "an allocation-free decode reported error bits 0x%x (1 = bad block id, 2 = wait timeout)", flag);
 }

@@ -88,47 +88,32 @@ int32_t chunks_of(int32_t ctx, int32_t block_size) {
     return full * cpp + (rem + kDecodeChunk - 1) / kDecodeChunk;
 }
 
-void build_work_list(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, int32_t block_size,
-                     int32_t n_workers, WorkList* out) {
-    WorkList& W = *out;
-    // cleared, not reassigned: a work list kept across steps keeps its capacity
-    for (auto* v : {&W.piece_seg, &W.piece_c0, &W.piece_c1, &W.piece_slot, &W.piece_merge,
-                    &W.merge_deferred, &W.merge_seg, &W.merge_slot0, &W.merge_nslots})
-        v->clear();
-    W.n_slots = 0;
-    const int64_t n_seg = static_cast<int64_t>(batch) * heads_kv;
-    // segment s spans [seg_start[s], seg_start[s+1]) of the split line: kSegmentCost units of
-    // per-piece overhead, then its chunks
-    std::vector<int64_t> seg_start(static_cast<size_t>(n_seg) + 1, 0);
-    int64_t real_total = 0;
+void plan_work_into(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, int32_t block_size,
+                    int32_t n_workers, PlanArrays* out) {
+    PlanArrays& A = *out;
+    // The charged stream: every non-empty (sequence, kv head) segment spans kSegmentCost units
+    // of per-piece overhead, then its chunks.  All heads of a sequence have the same span, so
+    // the walk below keeps a (sequence, head) cursor and needs no per-segment table.
+    int64_t total = 0, real_total = 0;
     for (int32_t b = 0; b < batch; ++b) {
         const int32_t c = chunks_of(ctx_lens[b], block_size);
-        const int64_t span = c > 0 ? c + kSegmentCost : 0;
-        for (int32_t h = 0; h < heads_kv; ++h) {
-            const int64_t s = static_cast<int64_t>(b) * heads_kv + h;
-            seg_start[static_cast<size_t>(s) + 1] = seg_start[static_cast<size_t>(s)] + span;
-        }
+        total += (c > 0 ? c + kSegmentCost : 0) * static_cast<int64_t>(heads_kv);
         real_total += static_cast<int64_t>(c) * heads_kv;
     }
-    const int64_t total = seg_start[static_cast<size_t>(n_seg)];
-    W.total_chunks = real_total;
-    W.worker_begin.assign(static_cast<size_t>(n_workers) + 1, 0);
-    int64_t seg = 0;
-    // Worker w covers chunks [total*w/n, total*(w+1)/n), stepped without divisions; every
-    // worker range is cut at segment ends, so there are at most n_workers + n_seg pieces.
+    A.total_chunks = real_total;
+    // Worker w covers [total*w/n, total*(w+1)/n), stepped without divisions; every worker
+    // range is cut at segment ends, so there are at most n_workers + n_seg pieces.
     const int64_t q = n_workers > 0 ? total / n_workers : 0;  // no workers: an empty step
     const int64_t r = n_workers > 0 ? total % n_workers : 0;
     int64_t hi = 0, frac = 0;
-    const size_t cap = static_cast<size_t>(n_workers) + static_cast<size_t>(n_seg);
-    W.piece_seg.resize(cap);
-    W.piece_c0.resize(cap);
-    W.piece_c1.resize(cap);
-    int32_t* ps = W.piece_seg.data();
-    int32_t* pc0 = W.piece_c0.data();
-    int32_t* pc1 = W.piece_c1.data();
-    size_t np_ = 0;
+    // cursor: segment (b, h) = b * heads_kv + h spans [s0, s1) of the charged stream
+    int32_t cb = 0, ch = 0;
+    int64_t span = batch > 0 ? (chunks_of(ctx_lens[0], block_size) > 0
+                                    ? chunks_of(ctx_lens[0], block_size) + kSegmentCost : 0) : 0;
+    int64_t s0 = 0, s1 = span;
+    int32_t np = 0;
     for (int32_t w = 0; w < n_workers; ++w) {
-        W.worker_begin[static_cast<size_t>(w)] = static_cast<int32_t>(np_);
+        A.worker_begin[w] = np;
         int64_t lo = hi;
         hi += q;
         frac += r;
@@ -137,66 +122,104 @@ void build_work_list(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, i
             ++hi;
         }
         while (lo < hi) {
-            while (seg_start[static_cast<size_t>(seg) + 1] <= lo) ++seg;
-            const int64_t s0 = seg_start[static_cast<size_t>(seg)];
-            const int64_t s1 = seg_start[static_cast<size_t>(seg) + 1];
+            while (s1 <= lo) {  // advance to the segment holding unit `lo`
+                if (++ch == heads_kv) {
+                    ch = 0;
+                    ++cb;
+                    const int32_t c = chunks_of(ctx_lens[cb], block_size);
+                    span = c > 0 ? c + kSegmentCost : 0;
+                }
+                s0 = s1;
+                s1 = s0 + span;
+            }
             const int64_t end = hi < s1 ? hi : s1;
             const int64_t c0 = lo - s0 - kSegmentCost, c1 = end - s0 - kSegmentCost;
             if (c1 > 0) {  // a range inside the overhead units holds no chunk
-                ps[np_] = static_cast<int32_t>(seg);
-                pc0[np_] = static_cast<int32_t>(c0 > 0 ? c0 : 0);
-                pc1[np_] = static_cast<int32_t>(c1);
-                ++np_;
+                A.piece_seg[np] = cb * heads_kv + ch;
+                A.piece_c0[np] = static_cast<int32_t>(c0 > 0 ? c0 : 0);
+                A.piece_c1[np] = static_cast<int32_t>(c1);
+                ++np;
             }
             lo = end;
         }
     }
-    W.piece_seg.resize(np_);
-    W.piece_c0.resize(np_);
-    W.piece_c1.resize(np_);
-    W.worker_begin[static_cast<size_t>(n_workers)] = static_cast<int32_t>(np_);
-    // Pieces of one segment are adjacent; a segment cut into several pieces gets
-    // contiguous partial slots and one merge entry.  A segment of more than
-    // kFusedMergeMaxSlots pieces is merged by the second launch; once that launch is needed,
-    // it takes every split segment, so that no warp of the decode merges at its tail (on a
-    // 20-sequence GQA-7 batch those fused merges made the slowest warps 10 us late).
-    const size_t np = W.piece_seg.size();
-    W.piece_slot.assign(np, -1);
-    W.piece_merge.assign(np, -1);
+    A.worker_begin[n_workers > 0 ? n_workers : 0] = np;
+    A.n_pieces = np;
+    // Pieces of one segment are adjacent; a segment cut into several pieces gets contiguous
+    // partial slots and one merge entry.  A segment of more than kFusedMergeMaxSlots pieces is
+    // merged by the second launch; once that launch is needed, it takes every split segment,
+    // so that no warp of the decode merges at its tail (on a 20-sequence GQA-7 batch those
+    // fused merges made the slowest warps 10 us late).
     bool defer_all = false;
-    for (size_t i = 0; i < np && !defer_all;) {
-        size_t j = i + 1;
-        while (j < np && W.piece_seg[j] == W.piece_seg[i]) ++j;
-        defer_all = (j - i) > static_cast<size_t>(kFusedMergeMaxSlots);
+    for (int32_t i = 0; i < np && !defer_all;) {
+        int32_t j = i + 1;
+        while (j < np && A.piece_seg[j] == A.piece_seg[i]) ++j;
+        defer_all = (j - i) > kFusedMergeMaxSlots;
         i = j;
     }
-    size_t i = 0;
-    while (i < np) {
-        size_t j = i + 1;
-        while (j < np && W.piece_seg[j] == W.piece_seg[i]) ++j;
+    int32_t slots = 0, merges = 0, deferred = 0;
+    for (int32_t i = 0; i < np;) {
+        int32_t j = i + 1;
+        while (j < np && A.piece_seg[j] == A.piece_seg[i]) ++j;
         if (j - i > 1) {
-            const int32_t mi = static_cast<int32_t>(W.merge_seg.size());
-            const bool deferred = defer_all;
-            W.merge_seg.push_back(W.piece_seg[i]);
-            W.merge_slot0.push_back(W.n_slots);
-            W.merge_nslots.push_back(static_cast<int32_t>(j - i));
-            if (deferred) W.merge_deferred.push_back(mi);
-            for (size_t k = i; k < j; ++k) {
-                W.piece_slot[k] = W.n_slots++;
-                W.piece_merge[k] = deferred ? -2 : mi;
+            A.merge_seg[merges] = A.piece_seg[i];
+            A.merge_slot0[merges] = slots;
+            A.merge_nslots[merges] = j - i;
+            if (defer_all) A.merge_deferred[deferred++] = merges;
+            for (int32_t k = i; k < j; ++k) {
+                A.piece_slot[k] = slots++;
+                A.piece_merge[k] = defer_all ? -2 : merges;
             }
+            ++merges;
+        } else {
+            A.piece_slot[i] = -1;
+            A.piece_merge[i] = -1;
         }
         i = j;
     }
+    A.n_slots = slots;
+    A.n_merge = merges;
+    A.n_deferred = deferred;
 }
 
-// Mean partial slots of the segments the merge kernel takes, rounded up (selects its warp or
-// CTA form).
-static int32_t deferred_avg_slots(const WorkList& W) {
+void build_work_list(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, int32_t block_size,
+                     int32_t n_workers, WorkList* out) {
+    WorkList& W = *out;
+    const size_t n_seg = static_cast<size_t>(batch) * static_cast<size_t>(heads_kv > 0 ? heads_kv : 0);
+    const size_t cap = static_cast<size_t>(n_workers > 0 ? n_workers : 0) + n_seg;
+    // resized, not reassigned: a work list kept across steps keeps its capacity
+    for (auto* v : {&W.piece_seg, &W.piece_c0, &W.piece_c1, &W.piece_slot, &W.piece_merge}) v->resize(cap);
+    for (auto* v : {&W.merge_seg, &W.merge_slot0, &W.merge_nslots, &W.merge_deferred}) v->resize(n_seg);
+    W.worker_begin.resize(static_cast<size_t>(n_workers > 0 ? n_workers : 0) + 1);
+    PlanArrays A{W.piece_seg.data(), W.piece_c0.data(), W.piece_c1.data(), W.piece_slot.data(),
+                 W.piece_merge.data(), W.worker_begin.data(), W.merge_seg.data(), W.merge_slot0.data(),
+                 W.merge_nslots.data(), W.merge_deferred.data(), 0, 0, 0, 0, 0};
+    plan_work_into(ctx_lens, batch, heads_kv, block_size, n_workers, &A);
+    for (auto* v : {&W.piece_seg, &W.piece_c0, &W.piece_c1, &W.piece_slot, &W.piece_merge})
+        v->resize(static_cast<size_t>(A.n_pieces));
+    for (auto* v : {&W.merge_seg, &W.merge_slot0, &W.merge_nslots}) v->resize(static_cast<size_t>(A.n_merge));
+    W.merge_deferred.resize(static_cast<size_t>(A.n_deferred));
+    W.n_slots = A.n_slots;
+    W.total_chunks = A.total_chunks;
+}
+
+int32_t deferred_avg_slots(const int32_t* merge_nslots, const int32_t* merge_deferred, int32_t n_deferred) {
     int64_t sum = 0;
-    for (int32_t mi : W.merge_deferred) sum += W.merge_nslots[static_cast<size_t>(mi)];
-    const int64_t n = static_cast<int64_t>(W.merge_deferred.size());
-    return n > 0 ? static_cast<int32_t>((sum + n - 1) / n) : 0;
+    for (int32_t k = 0; k < n_deferred; ++k) sum += merge_nslots[merge_deferred[k]];
+    return n_deferred > 0 ? static_cast<int32_t>((sum + n_deferred - 1) / n_deferred) : 0;
+}
+
+int64_t decode_grid_ctas(int64_t total_chunks, int warps, int64_t max_ctas) {
+    if (total_chunks <= 0) return 0;
+    const int64_t want_workers = (total_chunks + kMinChunksPerWorker - 1) / kMinChunksPerWorker;
+    int64_t ctas = (want_workers + warps - 1) / warps;
+    if (ctas > max_ctas) ctas = max_ctas;
+    return ctas < 1 ? 1 : ctas;
+}
+
+static int32_t deferred_avg_slots(const WorkList& W) {
+    return deferred_avg_slots(W.merge_nslots.data(), W.merge_deferred.data(),
+                              static_cast<int32_t>(W.merge_deferred.size()));
 }
 
 // Sizes the pinned + device metadata buffers for `bytes`.  Only called while no step of
@@ -386,10 +409,7 @@ int step_upload(Pool* p, const int32_t* tables, int32_t batch, int32_t max_block
     for (int32_t b = 0; b < batch; ++b) total += chunks_of(ctx_lens[b], bs);
     total *= p->desc.heads_kv;
     const int warps = ws.cfg.supported ? ws.cfg.warps : 4;
-    int64_t want_workers = (total + kMinChunksPerWorker - 1) / kMinChunksPerWorker;
-    int64_t ctas = (want_workers + warps - 1) / warps;
-    if (ctas > ws.n_ctas_max) ctas = ws.n_ctas_max;
-    if (ctas < 1 && total > 0) ctas = 1;
+    const int64_t ctas = decode_grid_ctas(total, warps, ws.n_ctas_max);
     WorkList& W = ws.wl;
     build_work_list(ctx_lens, batch, p->desc.heads_kv, bs, static_cast<int32_t>(ctas * warps), &W);
     const int64_t n_pieces = static_cast<int64_t>(W.piece_seg.size());
@@ -722,8 +742,7 @@ int step_prefill(Pool* p, int32_t layer, const void* d_q, int32_t q_dtype, float
     for (int32_t c : ctx_e) chunks += chunks_of(c, bs);
     chunks *= p->desc.heads_kv;
     const int warps = ws.cfg.warps;
-    int64_t ctas = ((chunks + kMinChunksPerWorker - 1) / kMinChunksPerWorker + warps - 1) / warps;
-    if (ctas > ws.n_ctas_max) ctas = ws.n_ctas_max;
+    int64_t ctas = decode_grid_ctas(chunks, warps, ws.n_ctas_max);
     if (ctas < 1) ctas = 1;
     WorkList W;
     build_work_list(ctx_e.data(), n_e, p->desc.heads_kv, bs, static_cast<int32_t>(ctas * warps), &W);
@@ -988,6 +1007,18 @@ int gkv_decode_step_host(gkv_pool* pool, int32_t layer, const int32_t* h_block_t
         if (e != cudaSuccess) return gkv::cuda_fail(e, "cudaStreamWaitEvent(previous output)");
     }
     ws.io_next ^= 1;
+    return GKV_OK;
+}
+
+int gkv_wait_host_outputs(gkv_pool* pool, void* stream) {
+    GKV_DEVICE_POOL(pool);
+    Pool& P = pool->impl;
+    gkv::DeviceGuard guard(P.desc.device);
+    // the last call's slot; the output copies run in order on io_out, so its event covers all
+    auto& last = P.ws.io[P.ws.io_next ^ 1];
+    if (!last.out_pending) return GKV_OK;
+    cudaError_t e = cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), last.out_done, 0);
+    if (e != cudaSuccess) return gkv::cuda_fail(e, "cudaStreamWaitEvent(host outputs)");
     return GKV_OK;
 }
 

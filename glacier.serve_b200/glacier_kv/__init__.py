@@ -355,6 +355,10 @@ class PagedBlockPool:
             _ptr(k_new), _ptr(v_new), _ptr(q), _ptr(out), n_heads, float(scale),
             None if sinks is None else _f32_dev(sinks, "sinks"), _stream(stream, self.device)))
 
+    def wait_host_outputs(self, stream=None) -> None:
+        """Orders `stream` after the output copies of every decode_step_host call so far."""
+        _check(lib.gkv_wait_host_outputs(self._h, _stream(stream, self.device)))
+
     def paged_decode_lse(self, layer: int, q, out, lse, n_heads: int, scale: float, sinks=None, stream=None) -> None:
         """paged_decode plus lse [batch, n_heads] = ln(softmax denominator) of every row."""
         _check(lib.gkv_paged_decode_lse(self._h, layer, _f32_dev(q, "q"), _f32_dev(out, "out"),
@@ -530,18 +534,30 @@ def arena_desc(pool: PagedBlockPool) -> _lib.gkv_arena_desc:
 def paged_decode_noalloc(pool: PagedBlockPool, layer: int, block_tables, ctx_lens, q, out, n_heads: int,
                          scale: float, sinks=None, stream=None) -> None:
     """gkv_paged_decode_noalloc on the pool's arena: the same decode as upload_step +
-    paged_decode, with every scratch buffer in the library's fixed per-device array (nothing
-    is allocated).  Runs on the pool's device."""
+    paged_decode, with every scratch buffer in the library's fixed per-device array (the call
+    allocates nothing).  Runs on the pool's device.  Copy-on-write copies the pool has queued
+    are issued first on the same stream (the entry point sees only the raw arena)."""
     import torch
 
     desc = arena_desc(pool)
     bt = np.ascontiguousarray(block_tables, dtype=np.int32)
     cl = np.ascontiguousarray(ctx_lens, dtype=np.int32)
+    if pool.pending_copies:
+        pool.flush_copies(stream)
     with torch.cuda.device(pool.device):
         _check(lib.gkv_paged_decode_noalloc(
             C.byref(desc), layer, _ptr(bt), bt.shape[0], bt.shape[1], _ptr(cl), _f32_dev(q, "q"),
             _f32_dev(out, "out"), n_heads, float(scale), None if sinks is None else _f32_dev(sinks, "sinks"),
             _stream(stream, pool.device)))
+
+
+def paged_decode_noalloc_status(device: int = 0, stream=None, timeout_ms: int = 60_000) -> None:
+    """gkv_paged_decode_noalloc_status: raises DeviceError if an allocation-free decode on
+    `device` since the last check met a bad block id or an expired bounded wait."""
+    import torch
+
+    with torch.cuda.device(device):
+        _check(lib.gkv_paged_decode_noalloc_status(_stream(stream, device), timeout_ms))
 
 
 def plan_decode(ctx_lens: Sequence[int], heads_kv: int, block_size: int, n_workers: int) -> dict:

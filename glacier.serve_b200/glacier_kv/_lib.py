@@ -1,8 +1,9 @@
 """ctypes binding of libglacier_kv.so (the C ABI declared in include/glacier_kv.h).
 
 The shared library is built in-tree by ``make -C glacier.serve_b200/csrc`` (or
-``__graft_entry__.build()``).  Importing this module without it raises ImportError: there is
-no fallback implementation.
+``__graft_entry__.build()``).  It is mapped on the first call through ``lib`` (so importing the
+package, e.g. for its numpy-only workload generators, maps no native code); that first call
+raises ImportError when the library is missing: there is no fallback implementation.
 """
 from __future__ import annotations
 
@@ -134,6 +135,8 @@ SIGNATURES = {
         C.c_int,
         [C.POINTER(gkv_arena_desc), I32, P, I32, I32, P, P, P, I32, F32, P, P],
     ),
+    "gkv_paged_decode_noalloc_status": (C.c_int, [P, I32]),
+    "gkv_wait_host_outputs": (C.c_int, [P, P]),
     "gkv_pool_last_launch_count": (C.c_int, [P]),
     "gkv_sync": (C.c_int, [P, P, I32]),
     "gkv_plan_decode": (C.c_int, [P, I32, I32, I32, I32, C.POINTER(gkv_plan_info), P, P, P, P, P, I32]),
@@ -166,7 +169,22 @@ def _load() -> C.CDLL:
     return lib
 
 
-lib = _load()
+class _LazyLib:
+    """Loads libglacier_kv.so on first attribute access and forwards to the CDLL."""
+
+    _cdll = None
+
+    def __getattr__(self, name):
+        if _LazyLib._cdll is None:
+            _LazyLib._cdll = _load()
+        return getattr(_LazyLib._cdll, name)
+
+    @staticmethod
+    def loaded() -> bool:
+        return _LazyLib._cdll is not None
+
+
+lib = _LazyLib()
 
 
 def last_error() -> str:

@@ -1,8 +1,12 @@
 """Seeded synthetic workloads of the BASELINE configs (shapes, pools, value distributions).
 
 The reference publishes no dataset for this path; every input here is generated from a seed:
-context lengths, block tables (drawn from the shim's own allocator, so their fragmentation is
-what the free list produces), and N(0,1) values for Q, K and V.
+context lengths, block tables (drawn from a LIFO free list with the allocator's semantics, so
+their fragmentation is what the pool's free list produces), and N(0,1) values for Q, K and V.
+
+Table generation is numpy only: importing this module maps no native code (the benchmark's CPU
+reference arm uses it).  ``churn_tables`` replays the same churn on a real pool's allocator, and
+a CPU test checks that both give identical tables.
 
     cfg1  decode, 20 seqs, ctx ~ U{128..1024}, 28q/4kv, d 128, fp32, pool 1024 (permuted)
     cfg2  append + decode, 64 seqs x (2048 cached + 1 new), 32q/8kv, d 128, fp32, pool 16384
@@ -19,8 +23,6 @@ import math
 from typing import List, Optional
 
 import numpy as np
-
-from . import BlockTable, PagedBlockPool
 
 SEED = 0x61AC1E5
 
@@ -103,9 +105,31 @@ def cfg2(seed: int = SEED, batch: int = 64, cached: int = 2048) -> DecodeWorkloa
                           slots, np.arange(batch, dtype=np.int32), 1.0 / math.sqrt(128), seed)
 
 
-def churn_tables(pool: PagedBlockPool, ctx_lens: np.ndarray, rng: np.random.Generator, ops: int = 10_000,
+class LifoFreeList:
+    """The pool's free-list semantics in plain Python: block 0 is popped first
+    (PagedBlockPool.cs:116-120), pops take the most recently released block (ConcurrentStack,
+    PagedBlockPool.cs:39,178-189), and a block released with one reference returns to the top
+    (ReleaseBlock, :251-279).  Enough to replay an admit/evict trace without a pool."""
+
+    def __init__(self, total_blocks: int, block_size: int = 16):
+        self.total_blocks = total_blocks
+        self.block_size = block_size
+        self._stack = list(range(total_blocks - 1, -1, -1))
+
+    def try_allocate_block(self):
+        if not self._stack:
+            return False, -1
+        return True, self._stack.pop()
+
+    def release_block(self, block: int) -> int:
+        self._stack.append(block)
+        return 0
+
+
+def churn_tables(pool, ctx_lens: np.ndarray, rng: np.random.Generator, ops: int = 10_000,
                  max_live_frac: float = 0.4) -> np.ndarray:
-    """Admit/evict churn on the pool's real free list, then allocate one table per ctx."""
+    """Admit/evict churn on `pool`'s free list (a PagedBlockPool or a LifoFreeList), then
+    allocate one table per ctx."""
     bs = pool.block_size
     total = pool.total_blocks
     live: List[List[int]] = []
@@ -144,16 +168,16 @@ def churn_tables(pool: PagedBlockPool, ctx_lens: np.ndarray, rng: np.random.Gene
     return _pack(tables)
 
 
+def cfg3_ctx(rng: np.random.Generator, batch: int = 256) -> np.ndarray:
+    return np.clip(np.round(rng.lognormal(math.log(1500.0), 1.0, size=batch)), 16, 32768).astype(np.int32)
+
+
 def cfg3(seed: int = SEED, dtype: str = "f32", batch: int = 256, total_blocks: int = 65536,
          ops: int = 10_000) -> DecodeWorkload:
     rng = np.random.default_rng(seed)
-    ctx = np.clip(np.round(rng.lognormal(math.log(1500.0), 1.0, size=batch)), 16, 32768).astype(np.int32)
+    ctx = cfg3_ctx(rng, batch)
     bs = 16
-    meta = PagedBlockPool(total_blocks, 1, 4, 128, bs, allocate_device_arena=False)
-    try:
-        tables = churn_tables(meta, ctx, rng, ops=ops)
-    finally:
-        meta.close()
+    tables = churn_tables(LifoFreeList(total_blocks, bs), ctx, rng, ops=ops)
     return DecodeWorkload("cfg3", 28, 4, 128, 128, bs, total_blocks, dtype, ctx, tables,
                           np.zeros(0, np.int64), np.zeros(0, np.int32), 1.0 / math.sqrt(128), seed)
 
@@ -172,11 +196,14 @@ def lpt_share(w: DecodeWorkload, rank: int, world: int) -> DecodeWorkload:
 
 def cfg5_local(rank: int, world: int, seed: int = SEED, batch: int = 4, ctx: int = 131072) -> DecodeWorkload:
     """Rank `rank`'s contiguous block range of each long sequence (split-KV across GPUs)."""
-    from . import split_block_range
-
     bs = 16
     n_blocks = ctx // bs
-    b0, b1 = split_block_range(n_blocks, world, rank)
+    if world == 1:  # the whole sequences (no native call: the CPU reference arm uses this case)
+        b0, b1 = 0, n_blocks
+    else:
+        from . import split_block_range
+
+        b0, b1 = split_block_range(n_blocks, world, rank)
     per = b1 - b0
     rng = np.random.default_rng(seed + 7919 * rank)
     total_blocks = batch * per
@@ -253,12 +280,14 @@ def cfg4(seed: int = SEED, batch: int = 8, chunk: int = 2048, max_prefix: int = 
                            np.concatenate(slots).astype(np.int64), 1.0 / math.sqrt(128), seed)
 
 
-def make_pool(w: DecodeWorkload, device: int = 0, layers: int = 1) -> PagedBlockPool:
+def make_pool(w: DecodeWorkload, device: int = 0, layers: int = 1):
+    from . import PagedBlockPool
+
     return PagedBlockPool(w.total_blocks, layers, w.heads_kv, w.head_dim, w.block_size, w.v_head_dim,
                           allocate_device_arena=True, device=device, dtype=w.dtype)
 
 
-def fill_arena_randn(pool: PagedBlockPool, seed: int, blocks: Optional[np.ndarray] = None) -> None:
+def fill_arena_randn(pool, seed: int, blocks: Optional[np.ndarray] = None) -> None:
     """N(0,1) K and V (rounded to the storage type) written straight into the device arena."""
     import torch
 

@@ -256,6 +256,12 @@ GKV_API int gkv_decode_step_host(gkv_pool* pool, int32_t layer, const int32_t* h
                                  const float* h_k_new, const float* h_v_new, const float* h_q,
                                  float* h_out, int32_t n_heads, float scale,
                                  const float* d_sinks, void* stream);
+/* Makes `stream` wait (on the device, without blocking the host) for the device-to-host output
+ * copies of every gkv_decode_step_host call made on this pool so far, so that an event recorded
+ * on `stream` afterwards marks every h_out as written.  The reference's ForwardBatch returns
+ * with its logits on the host (CudaPagedTransformerRunner.cs:307-364); this is the
+ * asynchronous form of that guarantee. */
+GKV_API int gkv_wait_host_outputs(gkv_pool* pool, void* stream);
 /* A KV arena described by raw device pointers, in the same layout and meaning as a pool's
  * (gkv_pool_kv_ptrs returns a pool's pointers). */
 typedef struct gkv_arena_desc {
@@ -280,6 +286,14 @@ GKV_API int gkv_paged_decode_noalloc(const gkv_arena_desc* arena, int32_t layer,
                                      int32_t max_blocks, const int32_t* h_ctx_lens,
                                      const float* d_q, float* d_out, int32_t n_heads, float scale,
                                      const float* d_sinks, void* stream);
+/* Error check of gkv_paged_decode_noalloc on the calling thread's current device (no
+ * counterpart in the reference; the status half of the allocation-free decode).  Waits for
+ * `stream` with a bound (GKV_ETIMEDOUT after timeout_ms, < 0: no bound), then reads and clears
+ * the device's error word: GKV_EDEVICE if a decode since the last check met a bad block id or
+ * gave up a bounded wait (its output is then wrong), GKV_OK otherwise.  It allocates nothing.
+ * The arena is read as it is: copy-on-write copies queued on a pool (gkv_pool_try_fork_block)
+ * must have been issued (gkv_pool_flush_copies) on `stream` before the decode. */
+GKV_API int gkv_paged_decode_noalloc_status(void* stream, int32_t timeout_ms);
 /* Number of kernel launches the last gkv_kv_append / gkv_paged_decode /
  * gkv_decode_step_host / gkv_compute_attention call on this pool enqueued. */
 GKV_API int gkv_pool_last_launch_count(const gkv_pool* pool);

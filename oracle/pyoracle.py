@@ -156,4 +156,16 @@ def prefill_chunk(K, V, g: Geom, layer, block_ids, token_count, start_pos, q, n_
 
 
 def max_threads() -> int:
+    """OpenMP's default team size (honours OMP_NUM_THREADS)."""
     return lib.oracle_max_threads()
+
+
+def host_cores() -> int:
+    """Host cores this process may run on, whatever OMP_NUM_THREADS says (a torchrun launch sets
+    it to 1): the thread count the timed CPU baseline passes explicitly."""
+    import os
+
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return max(1, os.cpu_count() or 1)

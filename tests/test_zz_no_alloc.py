@@ -2,17 +2,20 @@
 memory on the decode path (hosts whose memory belongs to another allocator or to a fixed
 budget, serving loops that cannot take a call that may synchronize the device).
 
-It is checked through the C ABI against the allocating path (gkv_upload_step +
-gkv_paged_decode) on the same inputs, on two calls in a row with different batches, so
-that contents the first call leaves in the shared static scratch cannot leak into the
-second.  This file sorts last so that a run stopping at the first failure has already run
-every other test; it also passes alone in a fresh process.
+It is checked through the C ABI against the CPU oracle (the restatement of the reference's
+PagedAttentionKernel.ComputeAttention) and against the allocating path (gkv_upload_step +
+gkv_paged_decode) on the same inputs, on two calls in a row with different batches, so that
+contents the first call leaves in the shared static scratch cannot leak into the second; its
+error word is read back through gkv_paged_decode_noalloc_status.  This file sorts last so that a
+run stopping at the first failure has already run every other test; it also passes alone in a
+fresh process.
 """
 import numpy as np
 import pytest
 
 import glacier_kv as G
-from gpu_helpers import TOL, gpu_decode, random_arena, random_tables
+from gpu_helpers import TOL, geom_of, gpu_decode, random_arena, random_tables
+from oracle import pyoracle as O
 
 pytestmark = pytest.mark.gpu
 
@@ -40,7 +43,8 @@ def test_noalloc_matches_allocating_decode_on_two_calls(cuda, dtype):
 
     rng = np.random.default_rng(31)
     pool = G.PagedBlockPool(3000, 1, 8, 128, 16, dtype=dtype)
-    random_arena(pool, rng)
+    K, V = random_arena(pool, rng)
+    g = geom_of(pool)
     # call 1: many long sequences (most segments split over several warps -> partials)
     ctx1 = [2049] * 16 + [5, 1, 700]
     t1 = random_tables(rng, ctx1, 16, 3000)
@@ -50,6 +54,8 @@ def test_noalloc_matches_allocating_decode_on_two_calls(cuda, dtype):
     t2 = random_tables(rng, ctx2, 16, 3000)
     q2 = rng.standard_normal((len(ctx2), 64, 128)).astype(np.float32)
 
+    ora1 = O.decode_batch(K, V, g, 0, t1, np.asarray(ctx1, np.int32), q1, 32, 0.088)
+    ora2 = O.decode_batch(K, V, g, 0, t2, np.asarray(ctx2, np.int32), q2, 64, 0.088)
     ref1 = gpu_decode(pool, 0, t1, ctx1, q1, 32, 0.088)
     ref2 = gpu_decode(pool, 0, t2, ctx2, q2, 64, 0.088)
     b1 = _buffers(pool, ctx1, q1, 32, cuda)
@@ -58,11 +64,15 @@ def test_noalloc_matches_allocating_decode_on_two_calls(cuda, dtype):
     got1 = _noalloc(pool, t1, ctx1, *b1, 32, 0.088, cuda)
     free_after_first = torch.cuda.mem_get_info(cuda)[0]
     got2 = _noalloc(pool, t2, ctx2, *b2, 64, 0.088, cuda)
-    np.testing.assert_allclose(got1, ref1, atol=TOL[dtype], rtol=0)
-    np.testing.assert_allclose(got2, ref2, atol=TOL[dtype], rtol=0)
+    G.paged_decode_noalloc_status(pool.device)  # no error bits from either call
+    for got, ora, ref in ((got1, ora1, ref1), (got2, ora2, ref2)):
+        np.testing.assert_allclose(got, ora, atol=TOL[dtype], rtol=0)  # the reference's arithmetic
+        np.testing.assert_allclose(got, ref, atol=TOL[dtype], rtol=0)  # the allocating path
     # and once more with the first batch, after the second call overwrote the scratch
     got1b = _noalloc(pool, t1, ctx1, *b1, 32, 0.088, cuda)
+    np.testing.assert_allclose(got1b, ora1, atol=TOL[dtype], rtol=0)
     np.testing.assert_allclose(got1b, ref1, atol=TOL[dtype], rtol=0)
+    G.paged_decode_noalloc_status(pool.device)
     # the calls after the first one take no device memory
     assert torch.cuda.mem_get_info(cuda)[0] == free_after_first
     pool.close()
@@ -80,4 +90,31 @@ def test_noalloc_rejects_sizes_beyond_its_static_scratch(cuda):
         G.paged_decode_noalloc(pool, 0, huge, np.array(ctx, np.int32), q, out, 1, 1.0)
     with pytest.raises(G.ArgumentOutOfRangeError):
         G.paged_decode_noalloc(pool, 0, np.full((4, 1), 99, np.int32), np.array(ctx, np.int32), q, out, 1, 1.0)
+    pool.close()
+
+
+def test_noalloc_sees_a_fork_queued_on_the_pool(cuda):
+    """A copy-on-write fork only queues its block copy on the pool; the Python wrapper issues it
+    before the allocation-free decode, which reads the raw arena (TryForkBlock,
+    PagedBlockPool.cs:332-342, then ComputeAttention over the forked table)."""
+    import torch
+
+    rng = np.random.default_rng(5)
+    pool = G.PagedBlockPool(64, 1, 2, 128, 16)
+    K, V = random_arena(pool, rng)
+    src = 3
+    ok, dst = pool.try_fork_block(src, 11)
+    assert ok and pool.pending_copies == 1
+    # the fork's destination holds the first 11 slots of src once the copy has run
+    O.copy_block_data(K, V, geom_of(pool), src, dst, 11)
+    tables = np.array([[dst]], np.int32)
+    ctx = np.array([11], np.int32)
+    q_np = rng.standard_normal((1, 4, 128)).astype(np.float32)
+    q = torch.from_numpy(q_np).to(cuda)
+    out = torch.zeros((1, 4, 128), device=cuda)
+    G.paged_decode_noalloc(pool, 0, tables, ctx, q, out, 4, 0.088)
+    G.paged_decode_noalloc_status(pool.device)
+    assert pool.pending_copies == 0
+    ora = O.decode_batch(K, V, geom_of(pool), 0, tables, ctx, q_np, 4, 0.088)
+    np.testing.assert_allclose(out.cpu().numpy(), ora, atol=TOL["f32"], rtol=0)
     pool.close()
