@@ -103,7 +103,7 @@ __global__ void __launch_bounds__(256, 4) block_copy_kernel(ArenaGeom g, CopyArg
 cudaError_t launch_block_copy(const ArenaGeom& g, const int32_t* ops, int n, int* err,
                               cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;
-    const int eb = g.dtype == GKV_DTYPE_BF16 ? 2 : 4;
+    const int eb = elem_bytes_of(g.dtype);
     // Every span starts at a multiple of the head stride; vectors need it 16-byte aligned.
     const bool vec16 = ((g.k_head_stride * eb) % 16 == 0) && ((g.v_head_stride * eb) % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(g.k) % 16 == 0) &&

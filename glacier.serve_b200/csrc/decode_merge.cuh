@@ -110,16 +110,19 @@ __device__ __forceinline__ void merge_segment(const DecodeArgs& a, const DecodeW
 }
 
 // Merge of the segments split into more than kFusedMergeMaxSlots pieces, run as a second
-// launch, when no segment has more than kWarpMergeMaxSlots slots.  One warp per (deferred
-// segment, head of a head group), eight per CTA: lane l owns
-// dims [l*DV/32, (l+1)*DV/32) and makes ONE online pass over the segment's partial slots,
-// keeping the running (max, sum) itself.  A slot's loads do not depend on the running state,
-// so the loads of consecutive slots overlap, and no block reduction is needed.
+// launch, when the deferred segments average at most kWarpMergeMaxSlots slots.  One warp per
+// (deferred segment, head of a head group), eight per CTA; lane l owns dims
+// [l*DV/32, (l+1)*DV/32).  The merge is two-phase so that nothing waits on a running state:
+// lane s reads slot s's (max, sum) while the first eight slots' accumulators are already in
+// flight, one warp reduction gives the segment's max M, every slot's weight 2^(m_s - M) stays
+// in its own lane, and the accumulators are summed in batches of eight independent loads,
+// each weight fetched from its lane with one shuffle.
 template <int GP, int DV>
 __global__ void __launch_bounds__(256) deferred_merge_warp_kernel(ArenaGeom g, DecodeWork w,
                                                              DecodeArgs a, int group,
                                                              int head_groups) {
     constexpr int EPLV = DV / 32;
+    constexpr int kBatch = 8;
     static_assert(DV % 32 == 0, "DV must be a multiple of 32");
     constexpr float kL2e = 1.4426950408889634f;
     const int lane = threadIdx.x & 31;
@@ -144,15 +147,12 @@ __global__ void __launch_bounds__(256) deferred_merge_warp_kernel(ArenaGeom g, D
     pdl_wait();
     if (!live || gg >= gcount) return;
     const int64_t base = (static_cast<int64_t>(hg) * w.n_slots + s0) * GP + gg;  // + s * GP
-    float M = -INFINITY, L = 0.f, A[EPLV];
-#pragma unroll
-    for (int e = 0; e < EPLV; ++e) A[e] = 0.f;
-#pragma unroll 4
-    for (int s = 0; s < ns; ++s) {
-        const int64_t ps = base + static_cast<int64_t>(s) * GP;
-        const float2 st = __ldcg(reinterpret_cast<const float2*>(a.part_ml + ps * 2));
-        const float* ap = a.part_acc + ps * DV + lane * EPLV;
-        float v[EPLV];
+    auto ml_of = [&](int s) {
+        return s < ns ? __ldcg(reinterpret_cast<const float2*>(a.part_ml + (base + static_cast<int64_t>(s) * GP) * 2))
+                      : make_float2(-INFINITY, 0.f);
+    };
+    auto acc_of = [&](int s, float (&v)[EPLV]) {
+        const float* ap = a.part_acc + (base + static_cast<int64_t>(s) * GP) * DV + lane * EPLV;
         if constexpr (EPLV % 4 == 0) {
 #pragma unroll
             for (int e = 0; e < EPLV; e += 4) {
@@ -170,14 +170,50 @@ __global__ void __launch_bounds__(256) deferred_merge_warp_kernel(ArenaGeom g, D
 #pragma unroll
             for (int e = 0; e < EPLV; ++e) v[e] = __ldcg(ap + e);
         }
-        if (st.x == -INFINITY) continue;  // a piece with no scores
-        const float mn = fmaxf(M, st.x);
-        const float fo = exp2f(M - mn), fn = exp2f(st.x - mn);
-        L = fmaf(L, fo, st.y * fn);
+    };
+    // phase 1: the segment max, with the first batch of accumulators already requested
+    float v0[kBatch][EPLV];
 #pragma unroll
-        for (int e = 0; e < EPLV; ++e) A[e] = fmaf(A[e], fo, v[e] * fn);
-        M = mn;
+    for (int k = 0; k < kBatch; ++k)
+        if (k < ns) acc_of(k, v0[k]);
+    float2 st = ml_of(lane);
+    float M = st.x;
+    for (int c0 = 32; c0 < ns; c0 += 32) M = fmaxf(M, ml_of(c0 + lane).x);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    // phase 2: weights per slot lane, the sum, and the weighted accumulators
+    float L = 0.f, A[EPLV];
+#pragma unroll
+    for (int e = 0; e < EPLV; ++e) A[e] = 0.f;
+    for (int c0 = 0; c0 < ns; c0 += 32) {
+        if (c0 > 0) st = ml_of(c0 + lane);
+        const float wgt = (st.x == -INFINITY || M == -INFINITY) ? 0.f : exp2f(st.x - M);
+        L = fmaf(st.y, wgt, L);
+        const int n = ns - c0 < 32 ? ns - c0 : 32;
+        for (int k0 = 0; k0 < n; k0 += kBatch) {
+            float v[kBatch][EPLV];
+            if (c0 == 0 && k0 == 0) {
+#pragma unroll
+                for (int k = 0; k < kBatch; ++k)
+#pragma unroll
+                    for (int e = 0; e < EPLV; ++e) v[k][e] = v0[k][e];
+            } else {
+#pragma unroll
+                for (int k = 0; k < kBatch; ++k)
+                    if (k0 + k < n) acc_of(c0 + k0 + k, v[k]);
+            }
+#pragma unroll
+            for (int k = 0; k < kBatch; ++k) {
+                const float wk = __shfl_sync(0xffffffffu, wgt, (k0 + k) & 31);
+                if (k0 + k < n) {
+#pragma unroll
+                    for (int e = 0; e < EPLV; ++e) A[e] = fmaf(wk, v[k][e], A[e]);
+                }
+            }
+        }
     }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
     const int qh = q_head0 + gg;
     float f = 1.f, Mref = M;
     if (a.sinks || a.has_sink_all) {

@@ -4,6 +4,7 @@
 
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <stdint.h>
 
 #include <utility>
@@ -123,23 +124,40 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint3
                  : "r"(addr));
 }
 
-// D = A(16x16 bf16, row) * B(16x8 bf16, col) + C, fp32 accumulate.
+// D = A(16x16, row) * B(16x8, col) + C, fp32 accumulate; A and B both bf16 (F16 = false) or
+// both fp16 (F16 = true).
+template <bool F16 = false>
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                           uint32_t a3, uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
-        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    if constexpr (F16)
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
+            "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    else
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+            "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// D = A(16x8 bf16, row) * B(8x8 bf16, col) + C, fp32 accumulate.
+// D = A(16x8, row) * B(8x8, col) + C, fp32 accumulate (bf16 or fp16 operands, as above).
+template <bool F16 = false>
 __device__ __forceinline__ void mma_1688(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k8.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
-        "{%4, %5}, {%6}, {%0, %1, %2, %3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(b0));
+    if constexpr (F16)
+        asm volatile(
+            "mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
+            "{%4, %5}, {%6}, {%0, %1, %2, %3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a0), "r"(a1), "r"(b0));
+    else
+        asm volatile(
+            "mma.sync.aligned.m16n8k8.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+            "{%4, %5}, {%6}, {%0, %1, %2, %3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a0), "r"(a1), "r"(b0));
 }
 
 // Two fp32 values as one bf16x2 word (lo in bits 0-15), round to nearest even.
@@ -148,10 +166,34 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Two fp32 values as one fp16x2 word (lo in bits 0-15), round to nearest even.
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <bool F16>
+__device__ __forceinline__ uint32_t pack_16x2(float lo, float hi) {
+    if constexpr (F16) return pack_f16x2(lo, hi);
+    else return pack_bf16x2(lo, hi);
+}
+
 // Splits x into bf16 hi + lo with x ~= hi + lo to about 16 mantissa bits.
 __device__ __forceinline__ void split_bf16(float x, float& hi, float& lo) {
     hi = __bfloat162float(__float2bfloat16_rn(x));
     lo = x - hi;
+}
+
+// Splits x into hi + lo of the 16-bit type (fp16: about 22 mantissa bits for |x| within the
+// fp16 range; callers scale x there first).
+template <bool F16>
+__device__ __forceinline__ void split_16(float x, float& hi, float& lo) {
+    if constexpr (F16) {
+        hi = __half2float(__float2half_rn(x));
+        lo = x - hi;
+    } else {
+        split_bf16(x, hi, lo);
+    }
 }
 
 // ---- tcgen05 (5th-generation tensor core, accumulators in tensor memory) ----------------
@@ -299,57 +341,6 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr, uint32_t lbo
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t lo16) {
     return __uint_as_float(lo16 << 16);
 }
-
-// Loads EPL consecutive KV elements from shared memory as fp32.
-template <typename KV, int EPL>
-struct SmemVec;
-
-template <int EPL>
-struct SmemVec<float, EPL> {
-    static __device__ __forceinline__ void load(const float* p, float (&x)[EPL]) {
-        if constexpr (EPL == 1) {
-            x[0] = p[0];
-        } else if constexpr (EPL == 2) {
-            float2 v = *reinterpret_cast<const float2*>(p);
-            x[0] = v.x; x[1] = v.y;
-        } else {
-            static_assert(EPL % 4 == 0, "EPL");
-#pragma unroll
-            for (int i = 0; i < EPL; i += 4) {
-                float4 v = *reinterpret_cast<const float4*>(p + i);
-                x[i] = v.x; x[i + 1] = v.y; x[i + 2] = v.z; x[i + 3] = v.w;
-            }
-        }
-    }
-};
-
-template <int EPL>
-struct SmemVec<__nv_bfloat16, EPL> {
-    static __device__ __forceinline__ void load(const __nv_bfloat16* p, float (&x)[EPL]) {
-        const uint16_t* u = reinterpret_cast<const uint16_t*>(p);
-        if constexpr (EPL == 1) {
-            x[0] = bf16_bits_to_f32(u[0]);
-        } else if constexpr (EPL == 2) {
-            uint32_t w = *reinterpret_cast<const uint32_t*>(u);
-            x[0] = __uint_as_float(w << 16);
-            x[1] = __uint_as_float(w & 0xffff0000u);
-        } else if constexpr (EPL == 4) {
-            uint2 w = *reinterpret_cast<const uint2*>(u);
-            x[0] = __uint_as_float(w.x << 16); x[1] = __uint_as_float(w.x & 0xffff0000u);
-            x[2] = __uint_as_float(w.y << 16); x[3] = __uint_as_float(w.y & 0xffff0000u);
-        } else {
-            static_assert(EPL % 8 == 0, "EPL");
-#pragma unroll
-            for (int i = 0; i < EPL; i += 8) {
-                uint4 w = *reinterpret_cast<const uint4*>(u + i);
-                x[i + 0] = __uint_as_float(w.x << 16); x[i + 1] = __uint_as_float(w.x & 0xffff0000u);
-                x[i + 2] = __uint_as_float(w.y << 16); x[i + 3] = __uint_as_float(w.y & 0xffff0000u);
-                x[i + 4] = __uint_as_float(w.z << 16); x[i + 5] = __uint_as_float(w.z & 0xffff0000u);
-                x[i + 6] = __uint_as_float(w.w << 16); x[i + 7] = __uint_as_float(w.w & 0xffff0000u);
-            }
-        }
-    }
-};
 
 // Launches `kernel` with programmatic stream serialization (see pdl_wait): its CTAs may start
 // while the previous kernel on `st` drains, once that kernel has called

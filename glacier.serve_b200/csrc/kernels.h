@@ -7,6 +7,10 @@
 
 namespace gkv {
 
+// Bytes per stored KV element of a GKV_DTYPE_* (fp32: 4; bf16 and fp16: 2).
+inline int elem_bytes_of(int dtype) { return dtype == 0 ? 4 : 2; }
+inline bool valid_kv_dtype(int dtype) { return dtype >= 0 && dtype <= 2; }
+
 // Geometry of one pool's arenas, in ELEMENTS of the storage type.
 struct ArenaGeom {
     void* k;                 // K arena base
@@ -51,10 +55,8 @@ constexpr int kFusedMergeMaxSlots = 0;
 // the uniform 64 x 2049 batch was unchanged.
 constexpr int64_t kSegmentCost = 4;
 // Deferred merges run one warp per (segment, head) when the deferred segments average at most
-// this many slots, else one CTA per (segment, head) with several slot lanes.  Measured: the
-// warp form saved 1-2 % of the decode on batches averaging 3-6 slots per segment (a few longer
-// segments included) and cost 30 % on a batch of 15-slot segments and 6 % on 37-slot ones.
-constexpr int kWarpMergeMaxSlots = 8;
+// this many slots, else one CTA per (segment, head) with several slot lanes.
+constexpr int kWarpMergeMaxSlots = 32;
 
 // Work list of one step, built on the host (all pointers are device pointers).
 //  segment s = b * heads_kv + h; its chunks are k = 0 .. n_chunks(ctx_b) - 1, chunk k
@@ -185,13 +187,15 @@ struct PrefillArgs {
     float* out;              // [total_q][n_heads][v_head_dim] fp32
     int* err;
 };
-// bf16 KV, d = dv = 128, block size a multiple of 8.
+// bf16 or fp16 KV, d = dv = 128, block size a multiple of 8.
 bool prefill_tc_eligible(const ArenaGeom& g, int n_heads);
-// q_bf16: [total_q][n_heads][128] bf16, 16-byte aligned.
-cudaError_t launch_paged_prefill_tc(const ArenaGeom& g, const PrefillArgs& a, const void* q_bf16,
+// q16: [total_q][n_heads][128] in the arena's 16-bit type, 16-byte aligned.
+cudaError_t launch_paged_prefill_tc(const ArenaGeom& g, const PrefillArgs& a, const void* q16,
                                     int64_t total_q, cudaStream_t st);
-cudaError_t launch_f32_to_bf16(const float* src, void* dst, int64_t n, cudaStream_t st);
-cudaError_t launch_bf16_to_f32(const void* src, float* dst, int64_t n, cudaStream_t st);
+// n elements of GKV_DTYPE_* src_dtype -> dst_dtype (different types), round to nearest even;
+// fp16 results saturate at +-65504.
+cudaError_t launch_convert(const void* src, int32_t src_dtype, void* dst, int32_t dst_dtype, int64_t n,
+                           cudaStream_t st);
 
 // Enqueues the split-KV decode (the cross-worker merge is fused into it).  *launches
 // receives the number of kernels enqueued.

@@ -5,8 +5,8 @@
 // (PagedTransformerRunner.cs:267,450,634).  One launch writes every token of the step:
 // token i's row for kv head h is copied from the contiguous source [n_tok][heads_kv][dim]
 // into arena element (block, layer, h, offset) with block = slot / block_size,
-// offset = slot % block_size.  fp32 storage is a bit copy; bf16 storage rounds to nearest
-// even.  HBM-bound: each (token, head) row is one warp moving 16-byte vectors, two rows per
+// offset = slot % block_size.  fp32 storage is a bit copy; bf16 and fp16 storage round to
+// nearest even.  HBM-bound: each (token, head) row is one warp moving 16-byte vectors, two rows per
 // warp iteration.
 #include "gkv_device.cuh"
 #include "kernels.h"
@@ -34,6 +34,16 @@ __device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* dst, float4
     *reinterpret_cast<uint2*>(dst) = w;
 }
 
+template <>
+__device__ __forceinline__ void store4<__half>(__half* dst, float4 v) {
+    __half2 a = __floats2half2_rn(v.x, v.y);
+    __half2 b = __floats2half2_rn(v.z, v.w);
+    uint2 w;
+    w.x = *reinterpret_cast<uint32_t*>(&a);
+    w.y = *reinterpret_cast<uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(dst) = w;
+}
+
 template <typename KV>
 __device__ __forceinline__ void store1(KV* dst, float v);
 template <>
@@ -41,6 +51,10 @@ __device__ __forceinline__ void store1<float>(float* dst, float v) { *dst = v; }
 template <>
 __device__ __forceinline__ void store1<__nv_bfloat16>(__nv_bfloat16* dst, float v) {
     *dst = __float2bfloat16_rn(v);
+}
+template <>
+__device__ __forceinline__ void store1<__half>(__half* dst, float v) {
+    *dst = __float2half_rn(v);
 }
 
 // x / d and x % d for the non-negative row and slot indices; `shift` >= 0 when d is a power of
@@ -208,6 +222,7 @@ cudaError_t launch_kv_append(const ArenaGeom& g, int layer, const float* k, cons
     if (n_tok <= 0) return cudaSuccess;
     AppendArgs a{layer, k, v, k_tok_stride, v_tok_stride, slots, single_slot, n_tok, -1, -1, err};
     if (g.dtype == GKV_DTYPE_BF16) return launch_typed<__nv_bfloat16>(g, a, stream);
+    if (g.dtype == GKV_DTYPE_F16) return launch_typed<__half>(g, a, stream);
     return launch_typed<float>(g, a, stream);
 }
 

@@ -80,6 +80,25 @@ __device__ __forceinline__ void load_pairs(const KV* p, float2 (&o)[(EPL + 1) / 
                 o[i / 2 + 1] = make_float2(v.z, v.w);
             }
         }
+    } else if constexpr (std::is_same<KV, __half>::value) {
+        if constexpr (EPL == 1) {
+            o[0] = make_float2(__half2float(p[0]), 0.f);
+        } else if constexpr (EPL == 2) {
+            o[0] = __half22float2(*reinterpret_cast<const __half2*>(p));
+        } else if constexpr (EPL == 4) {
+            const uint2 w = *reinterpret_cast<const uint2*>(p);
+            o[0] = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
+            o[1] = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
+        } else {
+#pragma unroll
+            for (int i = 0; i < EPL; i += 8) {
+                const uint4 w = *reinterpret_cast<const uint4*>(p + i);
+                o[i / 2 + 0] = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
+                o[i / 2 + 1] = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
+                o[i / 2 + 2] = __half22float2(*reinterpret_cast<const __half2*>(&w.z));
+                o[i / 2 + 3] = __half22float2(*reinterpret_cast<const __half2*>(&w.w));
+            }
+        }
     } else {
         const uint16_t* u = reinterpret_cast<const uint16_t*>(p);
         if constexpr (EPL == 1) {
@@ -554,6 +573,7 @@ bool dispatch(const ArenaGeom& g, int gp, F&& f) {
         return false;
     };
     if (g.dtype == GKV_DTYPE_BF16) return by_dims(__nv_bfloat16{});
+    if (g.dtype == GKV_DTYPE_F16) return by_dims(__half{});
     return by_dims(float{});
 }
 

@@ -104,7 +104,7 @@ extern "C" int gkv_paged_decode_noalloc(const gkv_arena_desc* arena, int32_t lay
     const int32_t bs = A.block_size > 0 ? A.block_size : 16;
     const int32_t dv = A.v_head_dim > 0 ? A.v_head_dim : A.head_dim;
     if (A.total_blocks < 1 || A.layers < 1 || A.heads_kv < 1 || A.head_dim < 1 ||
-        (A.dtype != GKV_DTYPE_F32 && A.dtype != GKV_DTYPE_BF16))
+        !valid_kv_dtype(A.dtype))
         return set_error(GKV_EINVAL, "invalid arena description");
     if (layer < 0 || layer >= A.layers) return set_error(GKV_EINVAL, "layer %d outside [0, %d)", layer, A.layers);
     if (n_heads <= 0 || n_heads % A.heads_kv != 0)

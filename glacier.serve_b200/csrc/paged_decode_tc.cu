@@ -1,8 +1,9 @@
-// Tensor-core variant of the split-KV paged decode for bf16 KV with wide GQA groups.
+// Tensor-core variant of the split-KV paged decode for 16-bit KV (bf16 or fp16) with wide GQA
+// groups.
 //
 // Same work decomposition, work list, partial layout and fused merge as paged_decode.cu
-// (warp-level stream-K over 8-token chunks of (sequence, kv head) segments), for bf16 KV,
-// d = dv = 128, block size a multiple of 8 and a query group of 5..8 heads (gp = 8): the
+// (warp-level stream-K over 8-token chunks of (sequence, kv head) segments), for bf16 or fp16
+// KV, d = dv = 128, block size a multiple of 8 and a query group of 5..8 heads (gp = 8): the
 // configurations where the CUDA-core kernel is limited by the FP32 pipe, not by HBM
 // (arithmetic intensity 2 * group / 2 bytes = 7-8 FLOP per KV byte).  Per chunk:
 //
@@ -10,9 +11,12 @@
 //    chunk's K rows and two bring its V rows: boxes of 8 tokens x 64 dims (1 KB each) from
 //    a 3-D view [block*layer*head][slot][dim] of this GPU's own arena.  The swizzle makes the
 //    ldmatrix reads below bank-conflict free.
-//  * S^T[8 heads x 8 tokens] = Q . K^T with mma.m16n8k16 (bf16 in, fp32 accumulate; rows
-//    8..15 of the A operand are zero).  Q is split into bf16 hi + lo parts (two MMAs), so the
-//    scores carry ~16 mantissa bits of q; K is exact bf16.  The accumulator fragment leaves
+//  * S^T[8 heads x 8 tokens] = Q . K^T with mma.m16n8k16 (16-bit in, fp32 accumulate; rows
+//    8..15 of the A operand are zero).  Q is split into hi + lo parts of the arena's type (two
+//    MMAs), so the scores carry ~16 (bf16) or ~22 (fp16) mantissa bits of q; K is exact.  For
+//    fp16, q is first scaled by a power of two that brings the head group's largest |q| into
+//    [2^13, 2^14) (exact; the scores are scaled back through the softmax scale), so any fp32 q
+//    fits the fp16 range.  The accumulator fragment leaves
 //    lane L holding head L/4 for tokens 2*(L%4) and 2*(L%4)+1.
 //  * Online softmax on those fragments (base 2, max/sum over the 4 lanes of a head).
 //  * O^T[128 dv x 8 heads] += V^T . P^T with mma.m16n8k8: the B fragment is exactly the
@@ -46,7 +50,7 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk16) {
     return static_cast<uint32_t>(row * 128 + ((chunk16 ^ row) << 4));
 }
 
-template <int NW, int S>
+template <int NW, int S, bool F16>
 __global__ void __launch_bounds__(NW * 32) paged_decode_tc_kernel(
     const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
     ArenaGeom g, DecodeWork w, DecodeArgs a, int group, int cpp) {
@@ -154,21 +158,46 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_tc_kernel(
 
         // Q A-fragments (rows = heads; rows 8..15 are zero), hi and lo parts per k-step
         uint32_t qh[8][2], ql[8][2];
+        float piece_scale_log2 = scale_log2;
         {
             const bool live = gq < gcount;
             const float* qp = a.q + (static_cast<int64_t>(b) * a.n_heads + q_head0 + gq) * kD;
+            float qv[8][2][2];
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
                     const int d0 = ks * 16 + half * 8 + tig * 2;
-                    const float x0 = live ? __ldg(qp + d0) : 0.f;
-                    const float x1 = live ? __ldg(qp + d0 + 1) : 0.f;
+                    qv[ks][half][0] = live ? __ldg(qp + d0) : 0.f;
+                    qv[ks][half][1] = live ? __ldg(qp + d0 + 1) : 0.f;
+                }
+            }
+            float qs = 1.f;
+            if constexpr (F16) {
+                // power-of-two scale 2^-e with max|q| * 2^-e in [2^13, 2^14)
+                float mx = 0.f;
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks)
+#pragma unroll
+                    for (int half = 0; half < 2; ++half)
+                        mx = fmaxf(mx, fmaxf(fabsf(qv[ks][half][0]), fabsf(qv[ks][half][1])));
+#pragma unroll
+                for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                const int ef = static_cast<int>((__float_as_uint(mx) >> 23) & 0xffu);
+                int e = (ef == 0 || ef == 0xff) ? 0 : ef - 126 - 14;  // mx < 2^(ef-126)
+                e = e < -100 ? -100 : (e > 100 ? 100 : e);
+                qs = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);
+                piece_scale_log2 = scale_log2 * __uint_as_float(static_cast<uint32_t>(127 + e) << 23);
+            }
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
                     float h0, l0, h1, l1;
-                    split_bf16(x0, h0, l0);
-                    split_bf16(x1, h1, l1);
-                    qh[ks][half] = pack_bf16x2(h0, h1);
-                    ql[ks][half] = pack_bf16x2(l0, l1);
+                    split_16<F16>(qv[ks][half][0] * qs, h0, l0);
+                    split_16<F16>(qv[ks][half][1] * qs, h1, l1);
+                    qh[ks][half] = pack_16x2<F16>(h0, h1);
+                    ql[ks][half] = pack_16x2<F16>(l0, l1);
                 }
             }
         }
@@ -202,18 +231,18 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_tc_kernel(
                     const uint32_t addr = sb + (dbase >> 6) * kBox + swz(rr, (dbase & 63) >> 3);
                     uint32_t b0, b1, b2, b3;
                     ldsm_x4(addr, b0, b1, b2, b3);
-                    mma_16816(sa[0], qh[2 * jj][0], 0u, qh[2 * jj][1], 0u, b0, b1);
-                    mma_16816(sa[1], ql[2 * jj][0], 0u, ql[2 * jj][1], 0u, b0, b1);
-                    mma_16816(sa[2], qh[2 * jj + 1][0], 0u, qh[2 * jj + 1][1], 0u, b2, b3);
-                    mma_16816(sa[3], ql[2 * jj + 1][0], 0u, ql[2 * jj + 1][1], 0u, b2, b3);
+                    mma_16816<F16>(sa[0], qh[2 * jj][0], 0u, qh[2 * jj][1], 0u, b0, b1);
+                    mma_16816<F16>(sa[1], ql[2 * jj][0], 0u, ql[2 * jj][1], 0u, b0, b1);
+                    mma_16816<F16>(sa[2], qh[2 * jj + 1][0], 0u, qh[2 * jj + 1][1], 0u, b2, b3);
+                    mma_16816<F16>(sa[3], ql[2 * jj + 1][0], 0u, ql[2 * jj + 1][1], 0u, b2, b3);
                 }
                 float s[2];
                 s[0] = (sa[0][0] + sa[2][0]) + (sa[1][0] + sa[3][0]);
                 s[1] = (sa[0][1] + sa[2][1]) + (sa[1][1] + sa[3][1]);
                 // ---- online softmax of head gq over tokens 2*tig, 2*tig+1 ----
                 const bool v0 = 2 * tig < ntok, v1 = 2 * tig + 1 < ntok;
-                const float s0 = v0 ? s[0] * scale_log2 : -INFINITY;
-                const float s1 = v1 ? s[1] * scale_log2 : -INFINITY;
+                const float s0 = v0 ? s[0] * piece_scale_log2 : -INFINITY;
+                const float s1 = v1 ? s[1] * piece_scale_log2 : -INFINITY;
                 float cmax = fmaxf(s0, s1);
                 cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 1));
                 cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 2));
@@ -241,10 +270,10 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_tc_kernel(
                 }
                 // ---- O^T += V^T . P^T ----
                 float ph0, pl0, ph1, pl1;
-                split_bf16(p0, ph0, pl0);
-                split_bf16(p1, ph1, pl1);
-                const uint32_t bh = pack_bf16x2(ph0, ph1);
-                const uint32_t bl = pack_bf16x2(pl0, pl1);
+                split_16<F16>(p0, ph0, pl0);
+                split_16<F16>(p1, ph1, pl1);
+                const uint32_t bh = pack_16x2<F16>(ph0, ph1);
+                const uint32_t bl = pack_16x2<F16>(pl0, pl1);
                 // zero the V^T elements of tokens past the chunk's end (stale slots)
                 const uint32_t vmask = (v0 ? 0x0000ffffu : 0u) | (v1 ? 0xffff0000u : 0u);
 #pragma unroll
@@ -257,10 +286,10 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_tc_kernel(
                     r1 &= vmask;
                     r2 &= vmask;
                     r3 &= vmask;
-                    mma_1688(acc[2 * pp], r0, r1, bh);
-                    mma_1688(acc[2 * pp], r0, r1, bl);
-                    mma_1688(acc[2 * pp + 1], r2, r3, bh);
-                    mma_1688(acc[2 * pp + 1], r2, r3, bl);
+                    mma_1688<F16>(acc[2 * pp], r0, r1, bh);
+                    mma_1688<F16>(acc[2 * pp], r0, r1, bl);
+                    mma_1688<F16>(acc[2 * pp + 1], r2, r3, bh);
+                    mma_1688<F16>(acc[2 * pp + 1], r2, r3, bl);
                 }
             }
             __syncwarp();
@@ -347,8 +376,11 @@ cudaError_t tc_prepare() {
     if (e != cudaSuccess) return e;
     const uint64_t bit = 1ull << (dev & 63);
     if (done_mask.load(std::memory_order_acquire) & bit) return cudaSuccess;
-    e = cudaFuncSetAttribute(paged_decode_tc_kernel<kNW, kS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(paged_decode_tc_kernel<kNW, kS, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kTcSmem));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(paged_decode_tc_kernel<kNW, kS, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kTcSmem));
     if (e == cudaSuccess) done_mask.fetch_or(bit, std::memory_order_acq_rel);
     return e;
 }
@@ -372,6 +404,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 bool tmap_encoder_available() { return encode_fn() != nullptr; }
 
+// The element type only sets the element size here (2 bytes): TMA copies bf16 and fp16 tiles
+// alike, so one encoder serves both arenas.
 bool encode_bf16_map3(void* map, const void* base, const uint64_t dims[3], const uint64_t strides[2],
                       const uint32_t box[3]) {
     auto fn = encode_fn();
@@ -385,7 +419,7 @@ bool encode_bf16_map3(void* map, const void* base, const uint64_t dims[3], const
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// 3-D view [block * layer * head][slot][dim] of one bf16 arena, boxes of `rows` slots x 64 dims.
+// 3-D view [block * layer * head][slot][dim] of one 16-bit arena, boxes of `rows` slots x 64 dims.
 bool encode_arena_map(void* map, void* base, const ArenaGeom& g, int dim, int rows) {
     if (rows <= 0 || g.block_size % rows != 0) return false;
     const uint64_t dims[3] = {static_cast<uint64_t>(dim), static_cast<uint64_t>(g.block_size),
@@ -401,7 +435,8 @@ bool encode_decode_tmaps(const ArenaGeom& g, void* tmap_k, void* tmap_v) {
 }
 
 bool decode_tc_eligible(const ArenaGeom& g, int n_heads) {
-    if (g.dtype != GKV_DTYPE_BF16 || g.head_dim != kD || g.v_head_dim != kDV) return false;
+    if ((g.dtype != GKV_DTYPE_BF16 && g.dtype != GKV_DTYPE_F16) || g.head_dim != kD || g.v_head_dim != kDV)
+        return false;
     if (g.block_size % kChunk != 0 || g.heads_kv <= 0 || n_heads % g.heads_kv != 0) return false;
     const int group = n_heads / g.heads_kv;
     if (group < 5) return false;  // gp 8 only; smaller groups are HBM-bound on the FP32 pipe
@@ -416,7 +451,7 @@ void decode_tc_config(DecodeConfig& c) {
     c.smem = kTcSmem;
     int per_sm = 1;
     if (tc_prepare() != cudaSuccess ||
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, paged_decode_tc_kernel<kNW, kS>, c.threads,
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, paged_decode_tc_kernel<kNW, kS, false>, c.threads,
                                                       kTcSmem) != cudaSuccess ||
         per_sm < 1) {
         cudaGetLastError();
@@ -442,8 +477,11 @@ cudaError_t launch_paged_decode_tc(const ArenaGeom& g, const DecodeWork& w, cons
     if (e != cudaSuccess) return e;
     const int cpp = (g.block_size + kChunk - 1) / kChunk;
     dim3 grid(static_cast<unsigned>(w.n_ctas), static_cast<unsigned>(head_groups));
-    e = launch_pdl(paged_decode_tc_kernel<kNW, kS>, grid, dim3(kNW * 32), kTcSmem, st, *tk, *tv, g, w, a,
-                   group, cpp);
+    e = g.dtype == GKV_DTYPE_F16
+            ? launch_pdl(paged_decode_tc_kernel<kNW, kS, true>, grid, dim3(kNW * 32), kTcSmem, st, *tk, *tv, g, w,
+                         a, group, cpp)
+            : launch_pdl(paged_decode_tc_kernel<kNW, kS, false>, grid, dim3(kNW * 32), kTcSmem, st, *tk, *tv, g, w,
+                         a, group, cpp);
     if (e != cudaSuccess) return e;
     *launches = 1;
     if (w.n_deferred > 0) {

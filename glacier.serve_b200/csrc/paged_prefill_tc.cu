@@ -22,8 +22,8 @@
 //    softmax runs; the issuer never waits for its own MMAs (they execute in issue order).
 //  * warps 0-7 (two threads per query row through the 16x32bx2 TMEM shape): load S, causal
 //    mask, base-2 online softmax with lazy rescaling (O in TMEM is rescaled only when the
-//    running max grows by more than 8, so P stays <= 2^8), P as bf16 written back over its
-//    own S columns.  Epilogue: O / l through shared memory as coalesced fp32 rows.
+//    running max grows by more than 8, so P stays <= 2^8), P in the arena's 16-bit type
+//    (bf16 or fp16; A and B of one MMA share it) written back over its own S columns.  Epilogue: O / l through shared memory as coalesced fp32 rows.
 //
 // Two CTAs share an SM (96 KB shared memory and 256 TMEM columns each), so one CTA's softmax
 // overlaps the other's MMAs; one CTA with two Q tiles sharing K/V measured slower (its
@@ -34,6 +34,7 @@
 
 #include <atomic>
 #include <cmath>
+#include <type_traits>
 
 #include "gkv_device.cuh"
 #include "kernels.h"
@@ -60,9 +61,11 @@ constexpr size_t kSmem = kSmemData + 256 + 1024;   // + barriers + 1024-byte ali
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.f;
 
-// Instruction descriptor of tcgen05.mma kind::f16 with bf16 A and B, fp32 D, A K-major.
-constexpr uint32_t idesc_bf16(int m, int n, bool b_mn_major) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+// Instruction descriptor of tcgen05.mma kind::f16 with fp32 D, A K-major, and A and B both
+// bf16 (format 1) or both fp16 (format 0).
+constexpr uint32_t idesc_16(int m, int n, bool b_mn_major, bool f16) {
+    const uint32_t fmt = f16 ? 0u : 1u;
+    return (1u << 4) | (fmt << 7) | (fmt << 10) | ((b_mn_major ? 1u : 0u) << 16) |
            (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
@@ -95,7 +98,7 @@ struct BoxLane {
     }
 };
 
-template <int R>
+template <int R, bool F16>
 __global__ void __launch_bounds__(kThreads, 2)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                             const __grid_constant__ CUtensorMap tmv, const ArenaGeom g, const PrefillArgs a) {
@@ -209,8 +212,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     } else if (warp == kMmaWarp) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            constexpr uint32_t kIdS = idesc_bf16(kBM, kBN, false);
-            constexpr uint32_t kIdO = idesc_bf16(kBM, kD, true);
+            constexpr uint32_t kIdS = idesc_16(kBM, kBN, false, F16);
+            constexpr uint32_t kIdO = idesc_16(kBM, kD, true, F16);
             const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
             bool ok = mbar_wait(q_full, 0);
             tc_fence_after();
@@ -325,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                 const float2 e = __ffma2_rn(make_float2(x[2 * c], x[2 * c + 1]), sl2, nm2);
                 const float2 p = make_float2(fast_exp2(e.x), fast_exp2(e.y));
                 sum2 = __fadd2_rn(sum2, p);
-                pk[c] = pack_bf16x2(p.x, p.y);
+                pk[c] = pack_16x2<F16>(p.x, p.y);
             }
             l_run += sum2.x + sum2.y;
             if (j == n_tiles - 1 && tail < kBN) {
@@ -415,21 +418,33 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
 }
 
-__global__ void f32_to_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, int64_t n) {
-    const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
-    if (i + 3 < n) {
-        const float4 v = *reinterpret_cast<const float4*>(src + i);
-        __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
-        *reinterpret_cast<__nv_bfloat162*>(dst + i) = lo;
-        *reinterpret_cast<__nv_bfloat162*>(dst + i + 2) = hi;
-    } else {
-        for (int64_t k = i; k < n; ++k) dst[k] = __float2bfloat16_rn(src[k]);
-    }
+// Element conversion of q between the three GKV_DTYPE_* types (round to nearest even; fp16
+// results saturate at +-65504 instead of rounding to infinity).
+template <typename T>
+__device__ __forceinline__ float to_f32(T x);
+template <>
+__device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float x);
+template <>
+__device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float x) {
+    return __float2half_rn(fminf(fmaxf(x, -65504.f), 65504.f));
 }
 
-__global__ void bf16_to_f32_kernel(const __nv_bfloat16* __restrict__ src, float* __restrict__ dst, int64_t n) {
-    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i < n) dst[i] = __bfloat162float(src[i]);
+template <typename S, typename D>
+__global__ void convert_kernel(const S* __restrict__ src, D* __restrict__ dst, int64_t n) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        dst[i] = from_f32<D>(to_f32<S>(src[i]));
 }
 
 cudaError_t prefill_prepare() {
@@ -439,11 +454,10 @@ cudaError_t prefill_prepare() {
     if (e != cudaSuccess) return e;
     const uint64_t bit = 1ull << (dev & 63);
     if (done_mask.load(std::memory_order_acquire) & bit) return cudaSuccess;
-    e = cudaFuncSetAttribute(paged_prefill_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kSmem));
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(paged_prefill_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(kSmem));
+    for (auto k : {paged_prefill_tc_kernel<8, false>, paged_prefill_tc_kernel<16, false>,
+                   paged_prefill_tc_kernel<8, true>, paged_prefill_tc_kernel<16, true>})
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmem));
     if (e == cudaSuccess) done_mask.fetch_or(bit, std::memory_order_acq_rel);
     return e;
 }
@@ -451,29 +465,39 @@ cudaError_t prefill_prepare() {
 }  // namespace
 
 bool prefill_tc_eligible(const ArenaGeom& g, int n_heads) {
-    if (g.dtype != GKV_DTYPE_BF16 || g.head_dim != kD || g.v_head_dim != kD) return false;
+    if ((g.dtype != GKV_DTYPE_BF16 && g.dtype != GKV_DTYPE_F16) || g.head_dim != kD || g.v_head_dim != kD)
+        return false;
     if (g.block_size % 8 != 0 || g.heads_kv <= 0 || n_heads <= 0 || n_heads % g.heads_kv != 0) return false;
     if ((reinterpret_cast<uintptr_t>(g.k) | reinterpret_cast<uintptr_t>(g.v)) & 15) return false;
     const int64_t rows = static_cast<int64_t>(g.total_blocks) * g.layers * g.heads_kv;
     return rows < (int64_t{1} << 31) && tmap_encoder_available();
 }
 
-cudaError_t launch_f32_to_bf16(const float* src, void* dst, int64_t n, cudaStream_t st) {
+cudaError_t launch_convert(const void* src, int32_t src_dtype, void* dst, int32_t dst_dtype, int64_t n,
+                           cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
-    const int64_t quads = (n + 3) / 4;
-    const unsigned grid = static_cast<unsigned>((quads + 255) / 256);
-    f32_to_bf16_kernel<<<grid, 256, 0, st>>>(src, static_cast<__nv_bfloat16*>(dst), n);
+    if (!valid_kv_dtype(src_dtype) || !valid_kv_dtype(dst_dtype) || src_dtype == dst_dtype)
+        return cudaErrorInvalidValue;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    const dim3 grid(static_cast<unsigned>(blocks));
+    auto go = [&](auto s_tag, auto d_tag) {
+        using S = decltype(s_tag);
+        using D = decltype(d_tag);
+        convert_kernel<S, D><<<grid, 256, 0, st>>>(static_cast<const S*>(src), static_cast<D*>(dst), n);
+    };
+    auto by_dst = [&](auto s_tag) {
+        if (dst_dtype == GKV_DTYPE_F32) go(s_tag, float{});
+        else if (dst_dtype == GKV_DTYPE_BF16) go(s_tag, __nv_bfloat16{});
+        else go(s_tag, __half{});
+    };
+    if (src_dtype == GKV_DTYPE_F32) by_dst(float{});
+    else if (src_dtype == GKV_DTYPE_BF16) by_dst(__nv_bfloat16{});
+    else by_dst(__half{});
     return cudaGetLastError();
 }
 
-cudaError_t launch_bf16_to_f32(const void* src, float* dst, int64_t n, cudaStream_t st) {
-    if (n <= 0) return cudaSuccess;
-    bf16_to_f32_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(src), dst, n);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_paged_prefill_tc(const ArenaGeom& g, const PrefillArgs& a, const void* q_bf16,
+cudaError_t launch_paged_prefill_tc(const ArenaGeom& g, const PrefillArgs& a, const void* q16,
                                     int64_t total_q, cudaStream_t st) {
     if (a.n_items <= 0) return cudaSuccess;
     alignas(64) CUtensorMap mq;
@@ -483,7 +507,7 @@ cudaError_t launch_paged_prefill_tc(const ArenaGeom& g, const PrefillArgs& a, co
                               static_cast<uint64_t>(total_q)};
     const uint64_t strides[2] = {static_cast<uint64_t>(kD) * 2, static_cast<uint64_t>(a.n_heads) * kD * 2};
     const uint32_t box[3] = {64, 1, static_cast<uint32_t>(kBM)};
-    if (!encode_bf16_map3(&mq, q_bf16, dims, strides, box)) return cudaErrorInvalidValue;
+    if (!encode_bf16_map3(&mq, q16, dims, strides, box)) return cudaErrorInvalidValue;
     // whole 16-slot pages per box when the block size allows, else 8-slot boxes; the pool
     // caches both map pairs
     const int rows = g.block_size % 16 == 0 ? 16 : 8;
@@ -499,10 +523,10 @@ cudaError_t launch_paged_prefill_tc(const ArenaGeom& g, const PrefillArgs& a, co
     if (e != cudaSuccess) return e;
     const int64_t grid = static_cast<int64_t>(a.n_items) * a.n_heads;
     if (grid > 0x7fffffff) return cudaErrorInvalidValue;
-    if (rows == 16)
-        paged_prefill_tc_kernel<16><<<static_cast<unsigned>(grid), kThreads, kSmem, st>>>(mq, *tk, *tv, g, a);
-    else
-        paged_prefill_tc_kernel<8><<<static_cast<unsigned>(grid), kThreads, kSmem, st>>>(mq, *tk, *tv, g, a);
+    const bool f16 = g.dtype == GKV_DTYPE_F16;
+    auto kern = rows == 16 ? (f16 ? paged_prefill_tc_kernel<16, true> : paged_prefill_tc_kernel<16, false>)
+                           : (f16 ? paged_prefill_tc_kernel<8, true> : paged_prefill_tc_kernel<8, false>);
+    kern<<<static_cast<unsigned>(grid), kThreads, kSmem, st>>>(mq, *tk, *tv, g, a);
     return cudaGetLastError();
 }
 

@@ -271,15 +271,15 @@ int gkv_pool_create(const gkv_pool_desc* desc, gkv_pool** out_pool) {
     if (d.heads_kv < 1) return set_error(GKV_EINVAL, "headsKv must be >= 1 (got %d)", d.heads_kv);
     if (d.head_dim < 1) return set_error(GKV_EINVAL, "headDim must be >= 1 (got %d)", d.head_dim);
     if (d.block_size < 1) return set_error(GKV_EINVAL, "blockSize must be >= 1 (got %d)", d.block_size);
-    if (d.dtype != GKV_DTYPE_F32 && d.dtype != GKV_DTYPE_BF16)
-        return set_error(GKV_EINVAL, "dtype %d is not GKV_DTYPE_F32 or GKV_DTYPE_BF16", d.dtype);
+    if (!gkv::valid_kv_dtype(d.dtype))
+        return set_error(GKV_EINVAL, "dtype %d is not GKV_DTYPE_F32, GKV_DTYPE_BF16 or GKV_DTYPE_F16", d.dtype);
     if (d.allocate_device_arena && d.device < 0) return set_error(GKV_EINVAL, "device %d < 0", d.device);
 
     gkv_pool* p = new (std::nothrow) gkv_pool();
     if (!p) return set_error(GKV_ENOMEM, "host allocation failed");
     Pool& P = p->impl;
     P.desc = d;
-    P.elem_bytes = d.dtype == GKV_DTYPE_BF16 ? 2 : 4;
+    P.elem_bytes = static_cast<size_t>(gkv::elem_bytes_of(d.dtype));
     // strides, PagedBlockPool.cs:77-83
     gkv::ArenaGeom& g = P.geom;
     g.k_head_stride = static_cast<int64_t>(d.block_size) * d.head_dim;
@@ -338,8 +338,9 @@ int gkv_pool_create(const gkv_pool_desc* desc, gkv_pool** out_pool) {
         g.k = k;
         g.v = v;
         P.has_arena = true;
-        // TMA maps for the tensor-core decode (bf16, d = dv = 128, 8-token-aligned blocks)
-        if (d.dtype == GKV_DTYPE_BF16 && d.head_dim == 128 && d.v_head_dim == 128 && d.block_size % 8 == 0 &&
+        // TMA maps for the tensor-core kernels (16-bit storage, d = dv = 128, 8-token-aligned
+        // blocks); the copies move 2-byte elements, whichever 16-bit format they hold
+        if (d.dtype != GKV_DTYPE_F32 && d.head_dim == 128 && d.v_head_dim == 128 && d.block_size % 8 == 0 &&
             gkv::encode_decode_tmaps(g, P.tmap_k, P.tmap_v)) {
             g.tmap_k = P.tmap_k;
             g.tmap_v = P.tmap_v;

@@ -638,8 +638,8 @@ int step_prefill(Pool* p, int32_t layer, const void* d_q, int32_t q_dtype, float
     if (n_heads <= 0 || n_heads % p->desc.heads_kv != 0)
         return set_error(GKV_EINVAL, "n_heads %d is not a positive multiple of heads_kv %d", n_heads,
                          p->desc.heads_kv);
-    if (q_dtype != GKV_DTYPE_F32 && q_dtype != GKV_DTYPE_BF16)
-        return set_error(GKV_EINVAL, "q_dtype %d is neither GKV_DTYPE_F32 nor GKV_DTYPE_BF16", q_dtype);
+    if (!valid_kv_dtype(q_dtype))
+        return set_error(GKV_EINVAL, "q_dtype %d is not GKV_DTYPE_F32, GKV_DTYPE_BF16 or GKV_DTYPE_F16", q_dtype);
     const int32_t batch = ws.batch;
     if (batch > 0 && (!q_start || !q_len)) return set_error(GKV_EINVAL, "q_start/q_len is NULL");
     const int64_t max_seq = static_cast<int64_t>(ws.up_max_blocks) * p->desc.block_size;
@@ -689,17 +689,18 @@ int step_prefill(Pool* p, int32_t layer, const void* d_q, int32_t q_dtype, float
                    items.data() + static_cast<size_t>(order[i].second) * kPrefillItemInts, kPrefillItemInts * 4);
         rc = stage_prefill(p, host, st);
         if (rc != GKV_OK) return rc;
+        // the MMAs take q in the arena's 16-bit type
         const void* qb = d_q;
         int launches = 0;
-        if (q_dtype == GKV_DTYPE_F32) {
+        if (q_dtype != p->desc.dtype) {
             rc = ensure_qconv(p, static_cast<size_t>(q_elems) * 2);
             if (rc != GKV_OK) return rc;
-            cudaError_t e = launch_f32_to_bf16(static_cast<const float*>(d_q), ws.d_qconv, q_elems, st);
+            cudaError_t e = launch_convert(d_q, q_dtype, ws.d_qconv, p->desc.dtype, q_elems, st);
             if (e != cudaSuccess) return cuda_fail(e, "prefill q conversion");
             qb = ws.d_qconv;
             ++launches;
         } else if (reinterpret_cast<uintptr_t>(d_q) & 15) {
-            return set_error(GKV_EINVAL, "bf16 q must be 16-byte aligned");
+            return set_error(GKV_EINVAL, "16-bit q must be 16-byte aligned");
         }
         PrefillArgs a{};
         a.items = reinterpret_cast<const int32_t*>(ws.d_pre);
@@ -792,10 +793,10 @@ int step_prefill(Pool* p, int32_t layer, const void* d_q, int32_t q_dtype, float
     w.table_row = at(rows_off);
     const float* qf = static_cast<const float*>(d_q);
     int launches = 0;
-    if (q_dtype == GKV_DTYPE_BF16) {
+    if (q_dtype != GKV_DTYPE_F32) {
         rc = ensure_qconv(p, static_cast<size_t>(q_elems) * 4);
         if (rc != GKV_OK) return rc;
-        cudaError_t e = launch_bf16_to_f32(d_q, static_cast<float*>(ws.d_qconv), q_elems, st);
+        cudaError_t e = launch_convert(d_q, q_dtype, ws.d_qconv, GKV_DTYPE_F32, q_elems, st);
         if (e != cudaSuccess) return cuda_fail(e, "prefill q conversion");
         qf = static_cast<const float*>(ws.d_qconv);
         ++launches;

@@ -18,7 +18,7 @@ from typing import Iterable, Optional, Sequence, Tuple
 import numpy as np
 
 from . import _lib
-from ._lib import (GKV_DTYPE_BF16, GKV_DTYPE_F32, GKV_EDEVICE, GKV_EINVAL, GKV_ESTATE,
+from ._lib import (DTYPES, GKV_DTYPE_BF16, GKV_DTYPE_F16, GKV_DTYPE_F32, GKV_EDEVICE, GKV_EINVAL, GKV_ESTATE,
                    GKV_ETIMEDOUT, GKV_EUNSUPPORTED, GKV_OK, LIB_PATH, last_error, lib)
 
 __all__ = [
@@ -140,7 +140,7 @@ class PagedBlockPool:
         d.head_dim = head_dim
         d.v_head_dim = v_head_dim
         d.block_size = block_size
-        d.dtype = {"f32": GKV_DTYPE_F32, "bf16": GKV_DTYPE_BF16}[dtype]
+        d.dtype = DTYPES[dtype]
         d.allocate_device_arena = 1 if allocate_device_arena else 0
         h = C.c_void_p()
         _check(lib.gkv_pool_create(C.byref(d), C.byref(h)))
@@ -226,9 +226,9 @@ class PagedBlockPool:
         if not ptr:
             raise InvalidOperationError(GKV_ESTATE, "Host KV buffers were omitted.")
         shape = (self.total_blocks, self._layers, self._heads_kv, self.block_size, dim)
-        if self.dtype == "bf16":
+        if self.dtype in ("bf16", "f16"):
             t = torch.as_tensor(_CudaArray(ptr, shape, "<i2"), device=f"cuda:{self.device}")
-            return t.view(torch.bfloat16)
+            return t.view(torch.bfloat16 if self.dtype == "bf16" else torch.float16)
         return torch.as_tensor(_CudaArray(ptr, shape, "<f4"), device=f"cuda:{self.device}")
 
     # ---- allocator, PagedBlockPool.cs:178-353 ----
@@ -334,12 +334,12 @@ class PagedBlockPool:
         [0, min(ctx_lens[b], q_start[b] + t + 1))."""
         import torch
 
-        if not (isinstance(q, torch.Tensor) and q.is_cuda and q.is_contiguous()
-                and q.dtype in (torch.float32, torch.bfloat16)):
-            raise ValueError("q must be a contiguous float32 or bfloat16 CUDA tensor")
+        qdt = {torch.float32: GKV_DTYPE_F32, torch.bfloat16: GKV_DTYPE_BF16, torch.float16: GKV_DTYPE_F16}
+        if not (isinstance(q, torch.Tensor) and q.is_cuda and q.is_contiguous() and q.dtype in qdt):
+            raise ValueError("q must be a contiguous float32, bfloat16 or float16 CUDA tensor")
         qs = np.ascontiguousarray(q_start, dtype=np.int32)
         ql = np.ascontiguousarray(q_len, dtype=np.int32)
-        qd = GKV_DTYPE_BF16 if q.dtype == torch.bfloat16 else GKV_DTYPE_F32
+        qd = qdt[q.dtype]
         _check(lib.gkv_paged_prefill(self._h, layer, q.data_ptr(), qd, _f32_dev(out, "out"), _ptr(qs), _ptr(ql),
                                      n_heads, float(scale), _stream(stream, self.device)))
 
@@ -527,8 +527,7 @@ def arena_desc(pool: PagedBlockPool) -> _lib.gkv_arena_desc:
     """The raw-pointer description of a pool's arena (for gkv_paged_decode_noalloc)."""
     k, v = pool._kv_ptrs()
     return _lib.gkv_arena_desc(k, v, pool.total_blocks, pool.layers, pool.heads_kv, pool.head_dim,
-                               pool.value_head_dim, pool.block_size,
-                               GKV_DTYPE_BF16 if pool.dtype == "bf16" else GKV_DTYPE_F32)
+                               pool.value_head_dim, pool.block_size, DTYPES[pool.dtype])
 
 
 def paged_decode_noalloc(pool: PagedBlockPool, layer: int, block_tables, ctx_lens, q, out, n_heads: int,

@@ -25,6 +25,8 @@ GKV_EUNSUPPORTED = -8
 
 GKV_DTYPE_F32 = 0
 GKV_DTYPE_BF16 = 1
+GKV_DTYPE_F16 = 2
+DTYPES = {"f32": GKV_DTYPE_F32, "bf16": GKV_DTYPE_BF16, "f16": GKV_DTYPE_F16}
 
 
 class gkv_pool_desc(C.Structure):

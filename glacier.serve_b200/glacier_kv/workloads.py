@@ -50,7 +50,7 @@ class DecodeWorkload:
 
     @property
     def elem_bytes(self) -> int:
-        return 2 if self.dtype == "bf16" else 4
+        return 4 if self.dtype == "f32" else 2
 
     def kv_bytes(self) -> int:
         """Algorithmic KV bytes one decode step reads (each K/V row once)."""

@@ -53,9 +53,10 @@ enum {
 };
 
 /* KV storage types of the device arena.  Sources handed to append/store are always fp32
- * (the reference stores fp32, PagedBlockPool.cs:151-161); bf16 storage rounds to nearest
- * even on append. */
-enum { GKV_DTYPE_F32 = 0, GKV_DTYPE_BF16 = 1 };
+ * (the reference stores fp32, PagedBlockPool.cs:151-161); bf16 and fp16 storage round to
+ * nearest even on append.  GKV_DTYPE_F16 is the precision of the reference's GPU pools
+ * (CudaPagedTransformerRunner.cs:118-119, KvCachePrecision.Fp16 at :139). */
+enum { GKV_DTYPE_F32 = 0, GKV_DTYPE_BF16 = 1, GKV_DTYPE_F16 = 2 };
 
 typedef struct gkv_pool gkv_pool;
 typedef struct gkv_table gkv_table;
@@ -71,7 +72,7 @@ typedef struct gkv_pool_desc {
     int32_t head_dim;
     int32_t v_head_dim;            /* <= 0 means head_dim (PagedBlockPool.cs:73)          */
     int32_t block_size;            /* tokens per block; 0 means 16 (PagedBlockPool.cs:18) */
-    int32_t dtype;                 /* GKV_DTYPE_F32 or GKV_DTYPE_BF16                     */
+    int32_t dtype;                 /* GKV_DTYPE_F32, GKV_DTYPE_BF16 or GKV_DTYPE_F16      */
     int32_t allocate_device_arena; /* 0 = metadata-only pool: allocator, tables and CoW
                                       bookkeeping without any CUDA call (the reference's
                                       allocateHostBuffers:false, PagedBlockPool.cs:61,106) */
@@ -220,13 +221,13 @@ GKV_API int gkv_paged_decode(gkv_pool* pool, int32_t layer, const float* d_q, fl
  * h_q_len[b] queries at positions h_q_start[b] .. h_q_start[b] + h_q_len[b] - 1; query t
  * attends keys [0, min(ctx_lens[b], h_q_start[b] + t + 1)) and a sequence with no keys
  * leaves its rows of d_out untouched.  Queries are packed by sequence in batch order:
- * d_q [sum q_len][n_heads][head_dim], q_dtype GKV_DTYPE_F32 or GKV_DTYPE_BF16;
+ * d_q [sum q_len][n_heads][head_dim], q_dtype GKV_DTYPE_F32, GKV_DTYPE_BF16 or GKV_DTYPE_F16;
  * d_out [sum q_len][n_heads][v_head_dim] fp32.  Same result as one
  * PagedAttentionKernel.ComputeAttention per chunk token with pos = start + t
  * (PagedTransformerRunner.ForwardPrefillSubBatch, PagedTransformerRunner.cs:424-471).
- * bf16 pools with head_dim = v_head_dim = 128 run on the tensor cores (tcgen05, bf16
- * operands: an fp32 q is rounded to bf16 first); every other pool runs the split-KV decode
- * kernel over one segment per query.  GKV_EINVAL when a position reaches
+ * bf16 and fp16 pools with head_dim = v_head_dim = 128 run on the tensor cores (tcgen05,
+ * operands in the arena's type: a q of another type is rounded to it first, fp16 saturating
+ * at +-65504); every other pool runs the split-KV decode kernel over one segment per query.  GKV_EINVAL when a position reaches
  * max_blocks * block_size of the upload (ComputeAttention's pos < maxSeqLen check). */
 GKV_API int gkv_paged_prefill(gkv_pool* pool, int32_t layer, const void* d_q, int32_t q_dtype,
                               float* d_out, const int32_t* h_q_start, const int32_t* h_q_len,

@@ -30,7 +30,64 @@ float oracle_bf16_to_f32(uint16_t h) {
     return f;
 }
 
-static size_t elem_size(const oracle_geom* g) { return g->dtype == ORACLE_BF16 ? 2 : 4; }
+/* IEEE 754 binary16: 1 sign bit, 5 exponent bits (bias 15), 10 fraction bits.  Rounding to
+ * nearest even is done on the integer significand: the bits shifted out are compared with
+ * half of the last kept unit, ties going to the even result; a carry out of the fraction
+ * moves into the exponent, which turns the largest finite value into infinity exactly when
+ * the input rounds past it. */
+uint16_t oracle_f32_to_f16(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    const uint16_t sign = (uint16_t)((u >> 16) & 0x8000u);
+    const int32_t e32 = (int32_t)((u >> 23) & 0xffu);
+    const uint32_t frac = u & 0x7fffffu;
+    if (e32 == 0xff) return (uint16_t)(sign | (frac ? 0x7e00u : 0x7c00u)); /* NaN / inf */
+    if (e32 == 0) return sign;              /* fp32 zero or subnormal: below half the fp16 minimum */
+    const int32_t e16 = e32 - 127 + 15;     /* biased binary16 exponent */
+    if (e16 >= 31) return (uint16_t)(sign | 0x7c00u);
+    const uint32_t sig = frac | 0x800000u;  /* 24-bit significand */
+    uint32_t shift, base;
+    if (e16 >= 1) {                         /* normal result: keep 11 significant bits */
+        shift = 13;
+        base = (uint32_t)e16 << 10;
+    } else {                                /* subnormal result: units of 2^-24 */
+        shift = (uint32_t)(14 - e16);
+        if (shift > 24) return sign;        /* below a quarter unit: rounds to zero */
+        base = 0;
+    }
+    const uint32_t kept = (e16 >= 1) ? (frac >> shift) : (sig >> shift);
+    const uint32_t rem = (e16 >= 1 ? frac : sig) & ((1u << shift) - 1u);
+    const uint32_t half = 1u << (shift - 1);
+    uint32_t r = base + kept;
+    if (rem > half || (rem == half && (kept & 1u))) ++r; /* may carry into the exponent */
+    return (uint16_t)(sign | r);
+}
+
+float oracle_f16_to_f32(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    const uint32_t e = (h >> 10) & 0x1fu;
+    const uint32_t frac = h & 0x3ffu;
+    uint32_t u;
+    if (e == 0x1f) {
+        u = sign | 0x7f800000u | (frac << 13);
+    } else if (e == 0) {
+        /* subnormal: frac * 2^-24, exact in fp32 */
+        const float v = (float)frac * 5.9604644775390625e-8f;
+        memcpy(&u, &v, 4);
+        u |= sign;
+    } else {
+        u = sign | ((e - 15 + 127) << 23) | (frac << 13);
+    }
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+void oracle_f32_to_f16_many(const float* src, uint16_t* dst, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) dst[i] = oracle_f32_to_f16(src[i]);
+}
+
+static size_t elem_size(const oracle_geom* g) { return g->dtype == ORACLE_F32 ? 4 : 2; }
 
 /* Element offsets of GetKeyPtr / GetValuePtr, PagedBlockPool.cs:124-145. */
 static int64_t k_off(const oracle_geom* g, int64_t blk, int64_t layer, int64_t h, int64_t slot) {
@@ -49,12 +106,15 @@ static int64_t v_off(const oracle_geom* g, int64_t blk, int64_t layer, int64_t h
 
 static inline float load_elem(const void* base, int dtype, int64_t i) {
     if (dtype == ORACLE_BF16) return oracle_bf16_to_f32(((const uint16_t*)base)[i]);
+    if (dtype == ORACLE_F16) return oracle_f16_to_f32(((const uint16_t*)base)[i]);
     return ((const float*)base)[i];
 }
 
 static inline void store_elem(void* base, int dtype, int64_t i, float v) {
     if (dtype == ORACLE_BF16)
         ((uint16_t*)base)[i] = oracle_f32_to_bf16(v);
+    else if (dtype == ORACLE_F16)
+        ((uint16_t*)base)[i] = oracle_f32_to_f16(v);
     else
         ((float*)base)[i] = v;
 }

@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-enum { ORACLE_F32 = 0, ORACLE_BF16 = 1 };
+enum { ORACLE_F32 = 0, ORACLE_BF16 = 1, ORACLE_F16 = 2 };
 enum { ORACLE_OK = 0, ORACLE_EINVAL = -1 };
 
 /* Geometry of a host copy of the arena, layout [block][layer][head_kv][slot][dim]
@@ -37,6 +37,12 @@ typedef struct oracle_geom {
 /* fp32 -> bf16 round to nearest even (storage rounding of the bf16 arena). */
 uint16_t oracle_f32_to_bf16(float f);
 float oracle_bf16_to_f32(uint16_t h);
+/* fp32 -> IEEE binary16 round to nearest even, overflow to infinity, subnormal results kept,
+ * NaN -> 0x7e00 (storage rounding of the fp16 arena, the reference GPU pools' precision,
+ * CudaPagedTransformerRunner.cs:118-119,139), and back (exact). */
+uint16_t oracle_f32_to_f16(float f);
+float oracle_f16_to_f32(uint16_t h);
+void oracle_f32_to_f16_many(const float* src, uint16_t* dst, int64_t n);
 
 /* PagedBlockPool.Store, PagedBlockPool.cs:151-161. */
 int oracle_store(void* kpool, void* vpool, const oracle_geom* g, int32_t block, int32_t layer,

@@ -28,6 +28,12 @@ def _load() -> C.CDLL:
     lib.oracle_f32_to_bf16.argtypes = [F]
     lib.oracle_bf16_to_f32.restype = F
     lib.oracle_bf16_to_f32.argtypes = [C.c_uint16]
+    lib.oracle_f32_to_f16.restype = C.c_uint16
+    lib.oracle_f32_to_f16.argtypes = [F]
+    lib.oracle_f16_to_f32.restype = F
+    lib.oracle_f16_to_f32.argtypes = [C.c_uint16]
+    lib.oracle_f32_to_f16_many.restype = None
+    lib.oracle_f32_to_f16_many.argtypes = [P, P, C.c_int64]
     lib.oracle_store.argtypes = [P, P, P, I, I, I, P, P]
     lib.oracle_copy_block_data.argtypes = [P, P, P, I, I, I]
     lib.oracle_store_many.argtypes = [P, P, P, I, P, I, P, P]
@@ -46,7 +52,7 @@ def _load() -> C.CDLL:
 
 lib = _load()
 
-F32, BF16 = 0, 1
+F32, BF16, F16 = 0, 1, 2
 
 
 class Geom(C.Structure):
@@ -66,7 +72,7 @@ def _p(a: np.ndarray) -> int:
 def new_arena(g: Geom):
     kshape = (g.total_blocks, g.layers, g.heads_kv, g.block_size, g.head_dim)
     vshape = (g.total_blocks, g.layers, g.heads_kv, g.block_size, g.v_head_dim)
-    dt = np.uint16 if g.dtype == BF16 else np.float32
+    dt = np.float32 if g.dtype == F32 else np.uint16
     return np.zeros(kshape, dt), np.zeros(vshape, dt)
 
 
@@ -78,6 +84,27 @@ def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
     r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
     r[nan] = 0x7FFF
     return r
+
+
+def f32_to_f16_bits(x: np.ndarray) -> np.ndarray:
+    """fp32 -> fp16 bit patterns through the oracle's own round-to-nearest-even conversion."""
+    src = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(src.shape, np.uint16)
+    lib.oracle_f32_to_f16_many(_p(src), _p(out), src.size)
+    return out
+
+
+def f16_bits_to_f32(h: np.ndarray) -> np.ndarray:
+    return np.asarray(h, dtype=np.uint16).view(np.float16).astype(np.float32)
+
+
+def to_storage_bits(x: np.ndarray, dtype: int) -> np.ndarray:
+    """fp32 values in an arena's storage representation (F32: unchanged)."""
+    if dtype == BF16:
+        return f32_to_bf16_bits(x)
+    if dtype == F16:
+        return f32_to_f16_bits(x)
+    return np.ascontiguousarray(x, dtype=np.float32)
 
 
 def bf16_bits_to_f32(h: np.ndarray) -> np.ndarray:

@@ -5,7 +5,8 @@ import numpy as np
 
 from oracle import pyoracle as O
 
-TOL = {"f32": 1e-4, "bf16": 2e-2}  # max-abs parity bars stated for this path
+TOL = {"f32": 1e-4, "bf16": 2e-2, "f16": 2e-2}  # max-abs parity bars: fp32 KV, 16-bit KV storage
+ODT = {"f32": O.F32, "bf16": O.BF16, "f16": O.F16}
 
 
 def torch():
@@ -16,14 +17,14 @@ def torch():
 
 def geom_of(pool):
     return O.geom(pool.total_blocks, pool.layers, pool.heads_kv, pool.head_dim, pool.value_head_dim,
-                  pool.block_size, O.BF16 if pool.dtype == "bf16" else O.F32)
+                  pool.block_size, ODT[pool.dtype])
 
 
 def arena_to_host(pool):
     """Host copies of the K and V arenas in the oracle's representation."""
     t = torch()
     k, v = pool.key_view(), pool.value_view()
-    if pool.dtype == "bf16":
+    if pool.dtype != "f32":
         return (k.view(t.int16).cpu().numpy().view(np.uint16), v.view(t.int16).cpu().numpy().view(np.uint16))
     return k.cpu().numpy(), v.cpu().numpy()
 
@@ -31,7 +32,7 @@ def arena_to_host(pool):
 def host_to_arena(pool, K, V):
     t = torch()
     for view, arr in ((pool.key_view(), K), (pool.value_view(), V)):
-        if pool.dtype == "bf16":
+        if pool.dtype != "f32":
             view.view(t.int16).copy_(t.from_numpy(np.ascontiguousarray(arr).view(np.int16)))
         else:
             view.copy_(t.from_numpy(np.ascontiguousarray(arr)))
@@ -42,12 +43,8 @@ def random_arena(pool, rng):
     K, V = O.new_arena(g)
     kf = rng.standard_normal(K.shape).astype(np.float32)
     vf = rng.standard_normal(V.shape).astype(np.float32)
-    if pool.dtype == "bf16":
-        K[...] = O.f32_to_bf16_bits(kf)
-        V[...] = O.f32_to_bf16_bits(vf)
-    else:
-        K[...] = kf
-        V[...] = vf
+    K[...] = O.to_storage_bits(kf, g.dtype)
+    V[...] = O.to_storage_bits(vf, g.dtype)
     host_to_arena(pool, K, V)
     return K, V
 
@@ -88,7 +85,7 @@ def compact(pool, tables, ctx, rows):
     idx = t.tensor(ids, dtype=t.long, device=f"cuda:{pool.device}")
     k = pool.key_view().index_select(0, idx)
     v = pool.value_view().index_select(0, idx)
-    if pool.dtype == "bf16":
+    if pool.dtype != "f32":
         K = k.view(t.int16).cpu().numpy().view(np.uint16)
         V = v.view(t.int16).cpu().numpy().view(np.uint16)
     else:
@@ -98,7 +95,7 @@ def compact(pool, tables, ctx, rows):
         n = (int(c) + pool.block_size - 1) // pool.block_size
         new[i, :n] = [remap[int(b)] for b in r[:n]]
     g = O.geom(len(ids), pool.layers, pool.heads_kv, pool.head_dim, pool.value_head_dim, pool.block_size,
-               O.BF16 if pool.dtype == "bf16" else O.F32)
+               ODT[pool.dtype])
     return g, np.ascontiguousarray(K), np.ascontiguousarray(V), new
 
 

@@ -8,7 +8,7 @@ import pytest
 
 import glacier_kv as G
 from conftest import ROOT
-from gpu_helpers import arena_to_host, geom_of, random_arena
+from gpu_helpers import ODT, arena_to_host, geom_of, random_arena
 from oracle import pyoracle as O
 
 pytestmark = pytest.mark.gpu
@@ -40,7 +40,7 @@ def test_arena_is_zeroed_and_aligned(cuda):
     assert pool.total_memory_bytes == 2 * 8 * 2 * 2 * 16 * 32 * 4
 
 
-@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("dtype", ["f32", "bf16", "f16"])
 def test_batched_append_bit_exact(cuda, dtype):
     """cfg2 shape: 64 tokens (one per sequence) scattered into a 16384-block pool, plus
     padding slots; every appended row matches the oracle's Store bit for bit and nothing
@@ -57,6 +57,9 @@ def test_batched_append_bit_exact(cuda, dtype):
     k = rng.standard_normal((n, w.heads_kv, w.head_dim)).astype(np.float32)
     v = rng.standard_normal((n, w.heads_kv, w.v_head_dim)).astype(np.float32)
     k[0, 0, :4] = [np.inf, -np.inf, -0.0, 1e-42]  # specials and a subnormal survive the copy
+    # fp16 edges: past the largest finite value (-> inf), just under the rounding threshold, an
+    # fp16 subnormal, a value that rounds to the smallest normal
+    k[1, 0, :5] = [1e5, 65519.0, 3e-6, 6.1033e-05, -65520.0]
     before_k = pool.key_view().clone()
     pool.upload_step(w.tables, w.ctx_lens, slots)
     pool.kv_append(0, torch.from_numpy(k).to(cuda), torch.from_numpy(v).to(cuda))
@@ -72,8 +75,9 @@ def test_batched_append_bit_exact(cuda, dtype):
                 assert np.array_equal(gk.cpu().numpy().view(np.uint32), k[i, h].view(np.uint32))
                 assert np.array_equal(gv.cpu().numpy().view(np.uint32), v[i, h].view(np.uint32))
             else:
-                assert np.array_equal(gk.view(torch.int16).cpu().numpy().view(np.uint16), O.f32_to_bf16_bits(k[i, h]))
-                assert np.array_equal(gv.view(torch.int16).cpu().numpy().view(np.uint16), O.f32_to_bf16_bits(v[i, h]))
+                bits = lambda x: O.to_storage_bits(x, ODT[dtype])  # noqa: E731
+                assert np.array_equal(gk.view(torch.int16).cpu().numpy().view(np.uint16), bits(k[i, h]))
+                assert np.array_equal(gv.view(torch.int16).cpu().numpy().view(np.uint16), bits(v[i, h]))
     changed = (K != before_k).reshape(w.total_blocks, -1).any(1).nonzero().flatten().cpu().numpy()
     assert set(changed.tolist()) <= {int(s) // 16 for s in slots if s >= 0}
     assert pool.last_launch_count == 1
@@ -99,7 +103,8 @@ def test_append_matches_oracle_store_random_slots(cuda):
     assert np.array_equal(Vg.view(np.uint32), V.view(np.uint32))
 
 
-@pytest.mark.parametrize("heads,d,dv,dtype", [(3, 128, 128, "f32"), (3, 128, 64, "bf16"), (1, 30, 18, "f32")])
+@pytest.mark.parametrize("heads,d,dv,dtype", [(3, 128, 128, "f32"), (3, 128, 64, "bf16"), (1, 30, 18, "f32"),
+                                              (3, 128, 128, "f16"), (1, 30, 18, "f16")])
 def test_large_append_matches_oracle_store_loop(cuda, heads, d, dv, dtype):
     """An odd number of (token, head) rows, more than one pass of the grid-stride loop, with
     padding slots; the scalar path (d not a multiple of 4) included.  Bit-exact against the
@@ -125,7 +130,7 @@ def test_large_append_matches_oracle_store_loop(cuda, heads, d, dv, dtype):
 
 
 @pytest.mark.parametrize("d,dv", [(128, 128), (30, 18)])
-@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("dtype", ["f32", "bf16", "f16"])
 def test_large_block_copy_matches_oracle(cuda, dtype, d, dv):
     """More 2 KB chunks than one pass of the grid-stride loop; ragged valid counts; spans that
     end in a tail shorter than 16 bytes (d 30 / dv 18)."""
@@ -202,7 +207,7 @@ def test_cow_16_concurrent_sequences_preserve_data(cuda):
     assert pool.free_blocks_count == 64
 
 
-@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("dtype", ["f32", "bf16", "f16"])
 def test_batched_block_copy_matches_oracle(cuda, dtype):
     rng = np.random.default_rng(23)
     pool = G.PagedBlockPool(40, 3, 2, 64, 16, v_head_dim=32, dtype=dtype)

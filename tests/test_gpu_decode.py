@@ -1,7 +1,7 @@
 """Parity of the sm_100a split-KV decode with the CPU oracle, through the C ABI.
 
-Bars: max-abs 1e-4 for fp32 KV and 2e-2 for bf16 KV storage (the oracle computes from the
-same bf16-rounded values in fp32).
+Bars: max-abs 1e-4 for fp32 KV and 2e-2 for bf16 and fp16 KV storage (the oracle computes from
+the same rounded values in fp32).
 """
 import glob
 import json
@@ -77,6 +77,13 @@ CASES = [
     (16, 2, 128, 128, 8, "bf16", [37, 8, 1, 100]),  # tensor-core kernel, block size 8
     (8, 1, 128, 128, 24, "bf16", [50, 24, 25, 3]),  # tensor-core kernel, block size 24
     (56, 8, 128, 128, 16, "bf16", [9000, 17]),      # group 7, long sequence: fused merge
+    # fp16 storage (the reference GPU pools' precision): tensor-core and CUDA-core kernels
+    (28, 4, 128, 128, 16, "f16", [1500, 16, 2, 333, 4097]),
+    (64, 8, 128, 128, 16, "f16", [5000, 3, 640]),
+    (12, 1, 128, 128, 8, "f16", [77, 400]),         # tensor-core kernel, two head groups
+    (32, 8, 128, 128, 16, "f16", [2049, 2049, 5]),  # group 4: CUDA-core kernel
+    (2, 1, 32, 64, 8, "f16", [20, 7, 1]),
+    (16, 1, 64, 64, 16, "f16", [300, 45]),
 ]
 
 
@@ -92,6 +99,24 @@ def test_decode_parity(cuda, case):
     out = gpu_decode(pool, 0, tables, ctx, q, nH, scale_of(d))
     ref = O.decode_batch(K, V, geom_of(pool), 0, tables, np.array(ctx, np.int32), q, nH, scale_of(d))
     np.testing.assert_allclose(out, ref, atol=TOL[dtype], rtol=0)
+
+
+@pytest.mark.parametrize("q_mag", [3e4, 1e-5])
+def test_f16_tensor_core_decode_takes_any_fp32_q(cuda, q_mag):
+    """The tensor-core decode of an fp16 arena splits q into fp16 hi + lo after a power-of-two
+    scale, so q components far outside fp16's range (or far below its normal range) still
+    give the oracle's result."""
+    rng = np.random.default_rng(77)
+    ctx = [700, 33]
+    pool = G.PagedBlockPool(60, 1, 4, 128, 16, dtype="f16")
+    K, V = random_arena(pool, rng)
+    tables = random_tables(rng, ctx, 16, 60)
+    q = (rng.standard_normal((2, 28, 128)) * q_mag).astype(np.float32)
+    scale = 1.0 / (q_mag * 30.0)  # scores of order one
+    out = gpu_decode(pool, 0, tables, ctx, q, 28, scale)
+    ref = O.decode_batch(K, V, geom_of(pool), 0, tables, np.array(ctx, np.int32), q, 28, scale)
+    np.testing.assert_allclose(out, ref, atol=TOL["f16"], rtol=0)
+    pool.close()
 
 
 def test_one_upload_serves_decodes_with_other_head_counts(cuda):

@@ -1,7 +1,7 @@
 """Chunked causal prefill (gkv_paged_prefill) against the oracle's restatement of
 PagedTransformerRunner.ForwardPrefillSubBatch (one ComputeAttention per chunk token,
-PagedTransformerRunner.cs:424-471).  bf16 pools with d = dv = 128 take the tcgen05 kernel;
-every other pool takes the decode kernel with one segment per query."""
+PagedTransformerRunner.cs:424-471).  bf16 and fp16 pools with d = dv = 128 take the tcgen05
+kernel; every other pool takes the decode kernel with one segment per query."""
 import math
 
 import numpy as np
@@ -16,6 +16,15 @@ pytestmark = pytest.mark.gpu
 
 def _bf16_round(x):
     return O.bf16_bits_to_f32(O.f32_to_bf16_bits(np.ascontiguousarray(x, np.float32)))
+
+
+def _round(x, dtype):
+    """x as the device sees it after rounding to `dtype` (fp16 saturating at +-65504)."""
+    if dtype == "bf16":
+        return _bf16_round(x)
+    if dtype == "f16":
+        return O.f16_bits_to_f32(O.f32_to_f16_bits(np.clip(x, -65504.0, 65504.0)))
+    return np.ascontiguousarray(x, np.float32)
 
 
 def _run(pool, rng, prefixes, q_lens, n_heads, layer=0, q_dtype="bf16", starts=None, toks=None,
@@ -34,13 +43,13 @@ def _run(pool, rng, prefixes, q_lens, n_heads, layer=0, q_dtype="bf16", starts=N
         K, V = random_arena(pool, rng)
     total_q = int(sum(q_lens))
     d = pool.head_dim
-    q = rng.standard_normal((total_q, n_heads, d)).astype(np.float32)
-    if q_dtype == "bf16" or pool.dtype == "bf16" and d == 128:
-        q = _bf16_round(q)  # the tensor-core path computes with bf16 q
+    q = _round(rng.standard_normal((total_q, n_heads, d)).astype(np.float32), q_dtype)
     dev = f"cuda:{pool.device}"
     qt = torch.from_numpy(q).to(dev)
-    if q_dtype == "bf16":
-        qt = qt.to(torch.bfloat16)
+    if q_dtype != "f32":
+        qt = qt.to(torch.bfloat16 if q_dtype == "bf16" else torch.float16)  # exact: q is rounded already
+    if pool.dtype != "f32" and d == 128:
+        q = _round(q, pool.dtype)  # the tensor-core path computes with q in the arena's type
     out = torch.full((total_q, n_heads, pool.value_head_dim), out_init, dtype=torch.float32, device=dev)
     pool.upload_step(tables, np.asarray(toks, np.int32))
     scale = 1 / math.sqrt(d)
@@ -81,6 +90,19 @@ def test_tc_prefill_parity(cuda, prefixes, q_lens, nH, nKv):
     pool = G.PagedBlockPool(need, 1, nKv, 128, 16, dtype="bf16")
     got, refs, _ = _run(pool, rng, prefixes, q_lens, nH)
     _assert_close(got, refs, TOL["bf16"])
+    pool.close()
+
+
+@pytest.mark.parametrize("q_dtype", ["f32", "bf16", "f16"])
+@pytest.mark.parametrize("prefixes,q_lens,nH,nKv", [([0, 5], [128, 129], 28, 4), ([37, 200, 0], [300, 17, 64], 28, 4)])
+def test_tc_prefill_f16_arena(cuda, prefixes, q_lens, nH, nKv, q_dtype):
+    """fp16 storage (the reference GPU pools' precision): both MMA operands fp16, q converted to
+    fp16 from whichever type it comes in."""
+    rng = np.random.default_rng(sum(prefixes) + sum(q_lens) + len(q_dtype))
+    need = sum((p + l + 15) // 16 for p, l in zip(prefixes, q_lens)) + 4
+    pool = G.PagedBlockPool(need, 1, nKv, 128, 16, dtype="f16")
+    got, refs, _ = _run(pool, rng, prefixes, q_lens, nH, q_dtype=q_dtype)
+    _assert_close(got, refs, TOL["f16"])
     pool.close()
 
 
@@ -154,6 +176,8 @@ def test_tc_prefill_ignores_non_finite_unwritten_slots(cuda):
     ("f32", 64, 8, 2, "f32"),
     ("bf16", 64, 16, 4, "bf16"),
     ("bf16", 256, 8, 1, "f32"),
+    ("f16", 64, 16, 4, "f16"),
+    ("f16", 32, 8, 8, "f32"),
 ])
 def test_decode_kernel_prefill_parity(cuda, dtype, d, nH, nKv, q_dtype):
     rng = np.random.default_rng(d + nH)
@@ -165,7 +189,7 @@ def test_decode_kernel_prefill_parity(cuda, dtype, d, nH, nKv, q_dtype):
     pool.close()
 
 
-@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+@pytest.mark.parametrize("dtype", ["bf16", "f32", "f16"])
 def test_empty_sequences_leave_rows_untouched(cuda, dtype):
     rng = np.random.default_rng(8)
     pool = G.PagedBlockPool(20, 1, 4, 128, 16, dtype=dtype)

@@ -206,3 +206,53 @@ def test_oracle_prefill_equals_per_token_compute():
     for t in range(10):
         _, o = O.compute_attention(K, V, g, 0, 30 + t, q[t], ids, 40, 4, 2, 32, 32, 0.25, 48)
         np.testing.assert_array_equal(out[t], o)
+
+
+def test_f16_storage_rounding_is_ieee_round_to_nearest_even():
+    """The oracle's fp32 -> fp16 rounding (the storage rounding of fp16 arenas) agrees with
+    IEEE 754 binary16 round-to-nearest-even as numpy implements it, over random bit patterns of
+    the whole fp32 range and the edge cases (overflow, subnormals, ties), and fp16 -> fp32 is
+    exact for all 65536 patterns."""
+    import numpy as np
+
+    from oracle import pyoracle as O
+
+    rng = np.random.default_rng(16)
+    x = rng.integers(0, 2**32, size=2_000_000, dtype=np.uint64).astype(np.uint32).view(np.float32)
+    edge = np.array([0.0, -0.0, 65504.0, 65519.99, 65520.0, 1e30, np.inf, -np.inf, 2.9802322e-08,
+                     2.9802326e-08, 5.9604645e-08, 6.1035156e-05, 6.1033e-05, 1.0009766, 1.0004883, -2.5],
+                    np.float32)
+    x = np.concatenate([x, edge])
+    with np.errstate(over="ignore"):
+        ref = x.astype(np.float16).view(np.uint16)
+    got = O.f32_to_f16_bits(x)
+    nan = np.isnan(x)
+    assert np.array_equal(got[~nan], ref[~nan])
+    assert np.isnan(got[nan].view(np.float16)).all()
+    h = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    back = np.array([O.lib.oracle_f16_to_f32(int(v)) for v in h], np.float32)
+    want = h.view(np.float16).astype(np.float32)
+    assert ((back == want) | (np.isnan(back) & np.isnan(want))).all()
+
+
+def test_f16_store_rounds_and_decodes_from_the_rounded_values():
+    """Store into an fp16 arena keeps the rounded bits; the decode reads them back exactly."""
+    import numpy as np
+
+    from oracle import pyoracle as O
+
+    rng = np.random.default_rng(17)
+    g = O.geom(4, 1, 2, 16, 16, 4, O.F16)
+    K, V = O.new_arena(g)
+    k = rng.standard_normal(32).astype(np.float32)
+    v = rng.standard_normal(32).astype(np.float32)
+    assert O.store(K, V, g, 2, 0, 1, k, v) == 0
+    assert np.array_equal(K[2, 0, :, 1].ravel(), O.f32_to_f16_bits(k))
+    assert np.array_equal(V[2, 0, :, 1].ravel(), O.f32_to_f16_bits(v))
+    # one token attended: the output is that token's (rounded) value row
+    q = rng.standard_normal((1, 2, 16)).astype(np.float32)
+    tables = np.array([[2]], np.int32)
+    K2, V2 = O.new_arena(g)
+    O.store(K2, V2, g, 2, 0, 0, k, v)
+    out = O.decode_batch(K2, V2, g, 0, tables, np.array([1], np.int32), q, 2, 0.25)
+    assert np.array_equal(out.reshape(-1), O.f16_bits_to_f32(O.f32_to_f16_bits(v)))

@@ -37,7 +37,7 @@ def _noalloc(pool, tables, ctx, q, out, n_heads, scale, cuda):
     return out.cpu().numpy()
 
 
-@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("dtype", ["f32", "bf16", "f16"])
 def test_noalloc_matches_allocating_decode_on_two_calls(cuda, dtype):
     import torch
 
