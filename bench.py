@@ -294,7 +294,7 @@ def run_reference(args):
     elif args.config in BANDWIDTH_CONFIGS:
         res = bandwidth_cpu_baseline(args.config, max(args.steps, 1), budget_s=120.0)
         line = {
-            "metric": f"{'KV append' if args.config.startswith('append') else 'block copy'} GB/s per B200 vs HBM peak",
+            "metric": f"{bandwidth_metric(args.config)} GB/s per B200 vs HBM peak",
             "value": res["value"], "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": res["ms_per_sample"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16" if args.config.endswith("bf16") else "f32",
@@ -467,7 +467,14 @@ def run_prefill(args, world, rank, local, dev, barrier, max_over_ranks):
     pool.close()
 
 
-BANDWIDTH_CONFIGS = ("append", "append-bf16", "copy", "copy-bf16")
+BANDWIDTH_CONFIGS = ("append", "append-bf16", "copy", "copy-bf16", "rope-append", "rope-append-bf16")
+ROPE_HEADS = 32  # query heads of the rope-append configs (cfg2's Llama-3-8B shape)
+
+
+def bandwidth_metric(config: str) -> str:
+    if config.startswith("rope"):
+        return "fused QK-norm + RoPE + KV append"
+    return "KV append" if config.startswith("append") else "block copy"
 
 
 def bandwidth_workload(config: str, rank: int = 0):
@@ -475,7 +482,7 @@ def bandwidth_workload(config: str, rank: int = 0):
     nb, hkv, d, bs = 16384, 8, 128, 16
     rng = np.random.default_rng(0x61AC1E5 + 1000003 * rank)
     perm = rng.permutation(nb).astype(np.int32)
-    if config.startswith("append"):
+    if config.startswith("append") or config.startswith("rope"):
         seqs, chunk = 32, 2048
         tables = perm[: seqs * chunk // bs].reshape(seqs, chunk // bs)
         j = np.arange(chunk)
@@ -498,8 +505,8 @@ def bandwidth_cpu_baseline(config: str, steps: int, budget_s: float):
     bs = w["bs"]
     # The sample's blocks are renumbered densely, so the host arena holds only the blocks it
     # touches (the bytes moved are the same; a sparse 2 GiB arena only costs page faults).
-    if config.startswith("append"):
-        n = 8192
+    if config.startswith("append") or config.startswith("rope"):
+        n = 8192 if config.startswith("append") else 2048
         blk = w["slots"][:n] // bs
         used, inv = np.unique(blk, return_inverse=True)
         slots = (inv.astype(np.int64) * bs + w["slots"][:n] % bs).astype(np.int64)
@@ -509,7 +516,21 @@ def bandwidth_cpu_baseline(config: str, steps: int, budget_s: float):
         src, dst = inv[:n].astype(np.int32), inv[n:].astype(np.int32)
     g = O.geom(int(used.size), 1, w["hkv"], w["d"], block_size=bs, dtype=O.BF16 if bf16 else O.F32)
     K, V = O.new_arena(g)
-    if config.startswith("append"):
+    if config.startswith("rope"):
+        k = w["rng"].standard_normal((n, w["hkv"], w["d"]), dtype=np.float32)
+        v = w["rng"].standard_normal((n, w["hkv"], w["d"]), dtype=np.float32)
+        q = w["rng"].standard_normal((n, ROPE_HEADS, w["d"]), dtype=np.float32)
+        pos = (np.arange(n) % 2048).astype(np.int32)
+        inv = (500000.0 ** (-2.0 * np.arange(w["d"] // 2) / w["d"])).astype(np.float32)
+        qn = np.ones(w["d"], np.float32)
+        alg = n * (ROPE_HEADS * w["d"] * 8 + w["hkv"] * 2 * w["d"] * (4 + eb))
+        def run():
+            O.rope_append(K, V, g, 0, q, k, v, pos, slots, inv, w["d"], 0, 1.0, q_norm=qn, k_norm=qn)
+            return 0
+
+        sample = (f"first {n} of the 65536 tokens, per-token bias + QK RMSNorm + RoPE + Store loop, 1 thread "
+                  "(the reference's loop is serial)")
+    elif config.startswith("append"):
         k = w["rng"].standard_normal((n, w["hkv"], w["d"]), dtype=np.float32)
         v = w["rng"].standard_normal((n, w["hkv"], w["d"]), dtype=np.float32)
         alg = n * w["hkv"] * 2 * w["d"] * (4 + eb)
@@ -550,7 +571,40 @@ def run_bandwidth(args, world, rank, local, dev, barrier, max_over_ranks):
     pool = G.PagedBlockPool(nb, 1, hkv, d, bs, d, device=local, dtype=dtype)
     stream = torch.cuda.current_stream(dev)
     ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
-    if args.config.startswith("append"):
+    if args.config.startswith("rope"):
+        seqs, chunk, tables, slots = w["seqs"], w["chunk"], w["tables"], w["slots"]
+        n_tok = slots.size
+        pool.reserve_step(seqs, tables.shape[1], n_tok, ROPE_HEADS)
+        pool.upload_step(tables, np.full(seqs, chunk, np.int32), slots, stream=stream)
+        kn = torch.from_numpy(rng.standard_normal((n_tok, hkv, d), dtype=np.float32)).to(dev)
+        vn = torch.from_numpy(rng.standard_normal((n_tok, hkv, d), dtype=np.float32)).to(dev)
+        q0 = torch.from_numpy(rng.standard_normal((n_tok, ROPE_HEADS, d), dtype=np.float32)).to(dev)
+        qn = torch.ones(d, device=dev)
+        pos = (np.arange(n_tok) % chunk).astype(np.int32)
+        # q read + written, k and v read as fp32 and written in the arena's type
+        alg = n_tok * (ROPE_HEADS * d * 8 + hkv * 2 * d * (4 + eb))
+
+        def launch():
+            pool.rope_append(0, q0, kn, vn, pos, ROPE_HEADS, freq_base=500000.0, q_norm=qn, k_norm=qn,
+                             stream=stream)
+            return pool.last_launch_count
+
+        hq, hk, hv = q0.cpu().pin_memory(), kn.cpu().pin_memory(), vn.cpu().pin_memory()
+        h2d, d2h = (hq.numel() + hk.numel() + hv.numel()) * 4, hq.numel() * 4
+        hq_out = torch.empty_like(hq).pin_memory()
+
+        def e2e():
+            q0.copy_(hq, non_blocking=True)
+            kn.copy_(hk, non_blocking=True)
+            vn.copy_(hv, non_blocking=True)
+            launch()
+            hq_out.copy_(q0, non_blocking=True)
+
+        kernel = (f"rope_append_kernel<{'bf16' if eb == 2 else 'float'}, 4> ({n_tok} tokens: {ROPE_HEADS} q rows "
+                  f"in place, {hkv} k and v rows into the arena)")
+        work = (f"{args.config}: bias-free QK RMSNorm + NEOX RoPE (base 5e5) of {n_tok} tokens ({seqs} seqs x "
+                f"{chunk}), {ROPE_HEADS}q/{hkv}kv heads, d {d}, fp32 q/k/v, {dtype} arena, block {bs}, pool {nb} blocks")
+    elif args.config.startswith("append"):
         seqs, chunk, tables, slots = w["seqs"], w["chunk"], w["tables"], w["slots"]
         n_tok = slots.size
         pool.reserve_step(seqs, tables.shape[1], n_tok, hkv)
@@ -627,7 +681,7 @@ def run_bandwidth(args, world, rank, local, dev, barrier, max_over_ranks):
         peak, peak_kind = peaks()
         achieved = alg / (ms_local / 1e3) / 1e9
         line = {
-            "metric": f"{'KV append' if args.config.startswith('append') else 'block copy'} GB/s per B200 vs HBM peak",
+            "metric": f"{bandwidth_metric(args.config)} GB/s per B200 vs HBM peak",
             "value": world * alg / (ms / 1e3) / 1e9, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": dtype, "data": "synthetic (seeded N(0,1) rows, seeded block tables)",
@@ -640,7 +694,9 @@ def run_bandwidth(args, world, rank, local, dev, barrier, max_over_ranks):
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s"},
             "e2e": {"value": world * alg / (e2e_ms / 1e3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms,
-                    "path": ("pinned host K/V rows copied in, then gkv_kv_append" if args.config.startswith("append")
+                    "path": ("pinned host q/K/V rows copied in, gkv_rope_append, rotated q copied out"
+                             if args.config.startswith("rope") else
+                             "pinned host K/V rows copied in, then gkv_kv_append" if args.config.startswith("append")
                              else "gkv_block_copy from host op lists (ops copied in by the call)")},
             "gpu_launches": launches,
             "clocks": clk.summary(),

@@ -97,6 +97,16 @@ struct WorkList {
     int64_t total_chunks = 0;
 };
 
+// A pinned staging buffer and its device twin for small per-call uploads: the host copy is
+// reused once the previous upload from it has landed; the device copy is ordered on the stream.
+struct StageBuf {
+    char* h = nullptr;
+    char* d = nullptr;
+    size_t cap = 0;
+    cudaEvent_t copied = nullptr;
+    bool pending = false;
+};
+
 // Device + pinned buffers of one step (block tables, ctx lens, slot mapping, work list).
 struct StepWorkspace {
     int32_t max_batch = 0, max_blocks = 0, max_tokens = 0, n_heads = 0;
@@ -150,11 +160,9 @@ struct StepWorkspace {
     WorkList wl;                 // the uploaded step's work list (kept for its capacity)
     // chunked prefill: pinned + device buffer of its work items / work list, and q in the
     // dtype its kernel reads
-    char* h_pre = nullptr;
-    char* d_pre = nullptr;
-    size_t pre_cap = 0;
-    cudaEvent_t pre_copied = nullptr;
-    bool pre_pending = false;
+    StageBuf pre;
+    // fused rope + append: positions and the inverse-frequency table
+    StageBuf rope;
     void* d_qconv = nullptr;
     size_t qconv_cap = 0;
 };
@@ -223,6 +231,10 @@ int step_reserve(Pool* p, int32_t max_batch, int32_t max_blocks, int32_t max_tok
 int step_prefill(Pool* p, int32_t layer, const void* d_q, int32_t q_dtype, float* d_out,
                  const int32_t* q_start, const int32_t* q_len, int32_t n_heads, float scale,
                  cudaStream_t st);
+int step_rope_append(Pool* p, int32_t layer, float* d_q, const float* d_k, const float* d_v, int32_t n_tok,
+                     int32_t n_heads, const int32_t* positions, const gkv_rope_desc* rope,
+                     const gkv_qkv_prologue* pro, cudaStream_t st);
+void rope_inv_freq(float freq_base, int32_t rope_dim, const float* factors, float* out);
 void step_free(Pool* p);
 
 int32_t chunks_of(int32_t ctx, int32_t block_size);

@@ -35,6 +35,26 @@ cudaError_t launch_kv_append(const ArenaGeom& g, int layer, const float* k, cons
                              int64_t k_tok_stride, int64_t v_tok_stride, const int64_t* slots,
                              int64_t single_slot, int n_tok, int* err, cudaStream_t stream);
 
+// ---- fused q/k/v prologue + KV append (rope_append.cu) ----
+struct RopeAppendParams {
+    int layer;
+    float* q;                  // [n_tok][n_heads][head_dim], rewritten in place
+    const float* k;            // [n_tok][heads_kv][head_dim]
+    const float* v;            // [n_tok][heads_kv][v_head_dim]
+    int n_tok, n_heads;
+    const int32_t* positions;  // device [n_tok]
+    const float* inv_freq;     // device [rope_dim / 2]
+    int rope_dim, style;       // style 0: pairs (i, i + rope_dim/2); 1: pairs (2i, 2i+1)
+    float mscale;
+    const float *q_bias, *k_bias, *v_bias, *q_norm, *k_norm;  // device or nullptr
+    float eps;
+    const int64_t* slots;      // device [n_tok]
+    int* err;
+};
+// head_dim in {32, 64, 128, 256}, rope_dim even, <= head_dim, (rope_dim/2) % (head_dim/32) == 0.
+bool rope_append_supported(const ArenaGeom& g, int rope_dim);
+cudaError_t launch_rope_append(const ArenaGeom& g, const RopeAppendParams& p, cudaStream_t st);
+
 // ---- block copy ----
 // ops: [n][3] int32 (src, dst, valid_tokens) in device memory.
 cudaError_t launch_block_copy(const ArenaGeom& g, const int32_t* ops, int n, int* err,

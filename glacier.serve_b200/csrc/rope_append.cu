@@ -1,0 +1,251 @@
+// Fused q/k/v prologue + KV append for sm_100a.
+//
+// Replaces the per-sequence steps that precede Store in the reference's batched runner
+// (PagedTransformerRunner.ForwardBatch, src/Glacier.Serve/Inference/PagedAttention/
+// PagedTransformerRunner.cs:612-634, and its prefill and single-token twins :431-450, :245-267):
+// AddVector of the q/k/v biases (:612-614), ApplyQkNorm, a per-head RMSNorm of q and k
+// (:616, :713-732), QuantKernels.RoPE with the YaRN inverse-frequency table and mscale
+// (:619-631), and pool.Store of k and v (:634).  One launch does all of it for every token of
+// the step: each warp takes one (token, head) row of q, k or v; q rows are written back in
+// place (ready for the decode or prefill that follows), k and v rows go straight into their
+// arena slots, so the rotated k never makes a round trip through HBM.
+//
+// The formulas of QuantKernels.RMSNorm and QuantKernels.RoPE are not in the reference tree
+// (NuGet Glacier.Inference 1.7.0); the ones computed here are stated next to each step, and
+// every step is an IEEE-rounded operation in a fixed order (no contraction by the compiler),
+// so a CPU restatement of the same steps gives the same bits.
+//
+// Roofline: HBM.  Bytes per token = (n_heads * d) * 8 (q read + written) + heads_kv * (d + dv)
+// * (4 + elem) (k, v read, arena written).
+#include "gkv_device.cuh"
+#include "kernels.h"
+#include "../../include/glacier_kv.h"
+
+namespace gkv {
+
+namespace {
+
+// sin and cos of a float angle: Cody-Waite reduction by pi/2 in double precision (pi/2 split
+// into two doubles, fused multiply-adds), then Taylor polynomials of sin and cos on |x| <= pi/4
+// in float (Horner with fused multiply-adds; truncation error below 2^-28).
+__device__ __forceinline__ void rope_sincos(float theta, float& s_out, float& c_out) {
+    const double t = static_cast<double>(theta);
+    const double k = rint(__dmul_rn(t, 0.63661977236758134308));  // 2/pi
+    double r = __fma_rn(-k, 1.5707963267948966192, t);              // pi/2, high part
+    r = __fma_rn(-k, 6.1232339957367660359e-17, r);                 // pi/2, low part
+    const float x = __double2float_rn(r);
+    const float x2 = __fmul_rn(x, x);
+    // sin x = x + x^3 (-1/3! + x^2 (1/5! + x^2 (-1/7! + x^2 (1/9! - x^2/11!))))
+    float ps = __fmaf_rn(x2, -2.5052108385441720e-8f, 2.7557319223985893e-6f);
+    ps = __fmaf_rn(x2, ps, -1.9841269841269841e-4f);
+    ps = __fmaf_rn(x2, ps, 8.3333333333333333e-3f);
+    ps = __fmaf_rn(x2, ps, -1.6666666666666667e-1f);
+    const float sn = __fmaf_rn(__fmul_rn(x, x2), ps, x);
+    // cos x = 1 + x^2 (-1/2! + x^2 (1/4! + x^2 (-1/6! + x^2 (1/8! - x^2/10!))))
+    float pc = __fmaf_rn(x2, -2.7557319223985891e-7f, 2.4801587301587302e-5f);
+    pc = __fmaf_rn(x2, pc, -1.3888888888888889e-3f);
+    pc = __fmaf_rn(x2, pc, 4.1666666666666667e-2f);
+    pc = __fmaf_rn(x2, pc, -0.5f);
+    const float cs = __fmaf_rn(x2, pc, 1.0f);
+    switch (static_cast<long long>(k) & 3) {
+        case 0: s_out = sn; c_out = cs; break;
+        case 1: s_out = cs; c_out = -sn; break;
+        case 2: s_out = -sn; c_out = -cs; break;
+        default: s_out = -cs; c_out = sn; break;
+    }
+}
+
+struct RopeArgs {
+    int layer;
+    float* q;                  // [n_tok][n_heads][d], rewritten in place
+    const float* k;            // [n_tok][heads_kv][d]
+    const float* v;            // [n_tok][heads_kv][dv]
+    int n_tok, n_heads;
+    const int32_t* positions;  // [n_tok]
+    const float* inv_freq;     // [rope_dim / 2]
+    int rope_dim, style;       // style 0: pairs (i, i + R/2); 1: pairs (2i, 2i + 1)
+    float mscale;
+    const float *q_bias, *k_bias, *v_bias, *q_norm, *k_norm;
+    float eps;
+    const int64_t* slots;      // [n_tok], -1 = padding (k/v not stored)
+    int* err;
+};
+
+template <typename KV>
+__device__ __forceinline__ void store_elem(KV* p, float x);
+template <>
+__device__ __forceinline__ void store_elem<float>(float* p, float x) { *p = x; }
+template <>
+__device__ __forceinline__ void store_elem<__nv_bfloat16>(__nv_bfloat16* p, float x) { *p = __float2bfloat16_rn(x); }
+template <>
+__device__ __forceinline__ void store_elem<__half>(__half* p, float x) { *p = __float2half_rn(x); }
+
+// One q or k head row of D = 32 * E elements, lane l holding elements [l*E, (l+1)*E): bias,
+// RMSNorm, rotation.  RMSNorm: lane l sums the squares of its elements in order (x*x, then
+// fused multiply-adds), a butterfly over lanes 16, 8, 4, 2, 1 adds the partial sums (every lane
+// ends with the same value), r = sqrt(sum / D + eps), y = (x / r) * w.  Rotation of pair
+// (a, b) by angle pos * inv_freq[i]: y_a = fma(x_a, c, -(x_b * s)), y_b = fma(x_b, c, x_a * s),
+// each times mscale.
+template <int E>
+__device__ __forceinline__ void prologue_row(float (&x)[E], const float* bias, const float* norm,
+                                             const RopeArgs& a, int pos, int lane) {
+    constexpr int D = 32 * E;
+    if (bias) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) x[e] = __fadd_rn(x[e], __ldg(bias + lane * E + e));
+    }
+    if (norm) {
+        float p = __fmul_rn(x[0], x[0]);
+#pragma unroll
+        for (int e = 1; e < E; ++e) p = __fmaf_rn(x[e], x[e], p);
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) p = __fadd_rn(p, __shfl_xor_sync(0xffffffffu, p, off));
+        const float r = __fsqrt_rn(__fadd_rn(__fdiv_rn(p, static_cast<float>(D)), a.eps));
+#pragma unroll
+        for (int e = 0; e < E; ++e) x[e] = __fmul_rn(__fdiv_rn(x[e], r), __ldg(norm + lane * E + e));
+    }
+    const int R = a.rope_dim;
+    if (R <= 0) return;
+    if (a.style == 0) {
+        // pairs (i, i + R/2): the partner of element j < R/2 sits (R/2)/E lanes up
+        const int half = R / 2;
+        const int dl = half / E;  // lanes between partners (the host checks half % E == 0)
+        const bool low = lane * E < half;
+        const int src = low ? lane + dl : lane - dl;
+        float y[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            const float other = __shfl_sync(0xffffffffu, x[e], src & 31);
+            const int j = lane * E + e;
+            y[e] = x[e];
+            if (j < R) {
+                const int i = low ? j : j - half;
+                float s, c;
+                rope_sincos(__fmul_rn(static_cast<float>(pos), __ldg(a.inv_freq + i)), s, c);
+                // low element: y = x*c - other*s; high element: y = x*c + other*s
+                y[e] = low ? __fmaf_rn(x[e], c, -__fmul_rn(other, s)) : __fmaf_rn(x[e], c, __fmul_rn(other, s));
+                y[e] = __fmul_rn(y[e], a.mscale);
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < E; ++e) x[e] = y[e];
+    } else {
+        // pairs (2i, 2i+1): within a lane for even E, across lanes l and l^1 for E == 1
+        if constexpr (E % 2 == 0) {
+#pragma unroll
+            for (int e = 0; e < E; e += 2) {
+                const int j = lane * E + e;
+                if (j < R) {
+                    float s, c;
+                    rope_sincos(__fmul_rn(static_cast<float>(pos), __ldg(a.inv_freq + j / 2)), s, c);
+                    const float x0 = x[e], x1 = x[e + 1];
+                    x[e] = __fmul_rn(__fmaf_rn(x0, c, -__fmul_rn(x1, s)), a.mscale);
+                    x[e + 1] = __fmul_rn(__fmaf_rn(x1, c, __fmul_rn(x0, s)), a.mscale);
+                }
+            }
+        } else {
+            const float other = __shfl_xor_sync(0xffffffffu, x[0], 1);
+            if (lane < R) {
+                float s, c;
+                rope_sincos(__fmul_rn(static_cast<float>(pos), __ldg(a.inv_freq + lane / 2)), s, c);
+                const bool even = (lane & 1) == 0;
+                x[0] = even ? __fmaf_rn(x[0], c, -__fmul_rn(other, s)) : __fmaf_rn(x[0], c, __fmul_rn(other, s));
+                x[0] = __fmul_rn(x[0], a.mscale);
+            }
+        }
+    }
+}
+
+// Rows per token: n_heads q rows, heads_kv k rows, heads_kv v rows; one warp per row.
+template <typename KV, int E>
+__global__ void __launch_bounds__(256) rope_append_kernel(ArenaGeom g, RopeArgs a) {
+    constexpr int D = 32 * E;
+    const int lane = threadIdx.x & 31;
+    const int per_tok = a.n_heads + 2 * g.heads_kv;
+    const int64_t total = static_cast<int64_t>(a.n_tok) * per_tok;
+    const int64_t n_warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; row < total;
+         row += n_warps) {
+        const int t = static_cast<int>(row / per_tok);
+        const int j = static_cast<int>(row - static_cast<int64_t>(t) * per_tok);
+        const int pos = __ldg(a.positions + t);
+        if (j < a.n_heads) {  // q head j: rewritten in place
+            float* qp = a.q + (static_cast<int64_t>(t) * a.n_heads + j) * D + lane * E;
+            float x[E];
+#pragma unroll
+            for (int e = 0; e < E; ++e) x[e] = qp[e];
+            prologue_row<E>(x, a.q_bias ? a.q_bias + j * D : nullptr, a.q_norm, a, pos, lane);
+#pragma unroll
+            for (int e = 0; e < E; ++e) qp[e] = x[e];
+            continue;
+        }
+        const int64_t slot = __ldg(a.slots + t);
+        if (slot < 0) continue;  // padding token: nothing to store
+        const int64_t blk = slot / g.block_size;
+        const int off = static_cast<int>(slot - blk * g.block_size);
+        if (blk >= g.total_blocks) {
+            if (lane == 0 && a.err) atomicOr(a.err, kErrBadSlot);
+            continue;
+        }
+        if (j < a.n_heads + g.heads_kv) {  // k head h: prologue, then the arena
+            const int h = j - a.n_heads;
+            const float* kp = a.k + (static_cast<int64_t>(t) * g.heads_kv + h) * D + lane * E;
+            float x[E];
+#pragma unroll
+            for (int e = 0; e < E; ++e) x[e] = __ldg(kp + e);
+            prologue_row<E>(x, a.k_bias ? a.k_bias + h * D : nullptr, a.k_norm, a, pos, lane);
+            KV* dst = static_cast<KV*>(g.k) + blk * g.k_block_stride + a.layer * g.k_layer_stride +
+                      h * g.k_head_stride + static_cast<int64_t>(off) * D + lane * E;
+#pragma unroll
+            for (int e = 0; e < E; ++e) store_elem<KV>(dst + e, x[e]);
+        } else {  // v head h: bias, then the arena
+            const int h = j - a.n_heads - g.heads_kv;
+            const int dv = g.v_head_dim;
+            const float* vp = a.v + (static_cast<int64_t>(t) * g.heads_kv + h) * dv;
+            KV* dst = static_cast<KV*>(g.v) + blk * g.v_block_stride + a.layer * g.v_layer_stride +
+                      h * g.v_head_stride + static_cast<int64_t>(off) * dv;
+            for (int e = lane; e < dv; e += 32) {
+                float x = __ldg(vp + e);
+                if (a.v_bias) x = __fadd_rn(x, __ldg(a.v_bias + h * dv + e));
+                store_elem<KV>(dst + e, x);
+            }
+        }
+    }
+}
+
+template <typename KV>
+cudaError_t launch_typed(const ArenaGeom& g, const RopeArgs& a, cudaStream_t st) {
+    const int64_t rows = static_cast<int64_t>(a.n_tok) * (a.n_heads + 2 * g.heads_kv);
+    int64_t blocks = (rows * 32 + 255) / 256;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    if (blocks < 1) blocks = 1;
+    const dim3 grid(static_cast<unsigned>(blocks));
+    switch (g.head_dim) {
+        case 32: rope_append_kernel<KV, 1><<<grid, 256, 0, st>>>(g, a); break;
+        case 64: rope_append_kernel<KV, 2><<<grid, 256, 0, st>>>(g, a); break;
+        case 128: rope_append_kernel<KV, 4><<<grid, 256, 0, st>>>(g, a); break;
+        case 256: rope_append_kernel<KV, 8><<<grid, 256, 0, st>>>(g, a); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+bool rope_append_supported(const ArenaGeom& g, int rope_dim) {
+    if (g.head_dim != 32 && g.head_dim != 64 && g.head_dim != 128 && g.head_dim != 256) return false;
+    if (rope_dim < 0 || rope_dim > g.head_dim || (rope_dim & 1)) return false;
+    const int E = g.head_dim / 32;
+    return (rope_dim / 2) % E == 0;  // NEOX partners a whole number of lanes apart
+}
+
+cudaError_t launch_rope_append(const ArenaGeom& g, const RopeAppendParams& p, cudaStream_t st) {
+    if (p.n_tok <= 0) return cudaSuccess;
+    RopeArgs a{p.layer, p.q, p.k, p.v, p.n_tok, p.n_heads, p.positions, p.inv_freq, p.rope_dim, p.style,
+               p.mscale, p.q_bias, p.k_bias, p.v_bias, p.q_norm, p.k_norm, p.eps, p.slots, p.err};
+    if (g.dtype == GKV_DTYPE_BF16) return launch_typed<__nv_bfloat16>(g, a, st);
+    if (g.dtype == GKV_DTYPE_F16) return launch_typed<__half>(g, a, st);
+    return launch_typed<float>(g, a, st);
+}
+
+}  // namespace gkv

@@ -26,6 +26,9 @@ constexpr int kMinChunksPerWorker = 4;
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+int stage_copy(StageBuf& sb, const void* host, size_t bytes, cudaStream_t st, const char* what);
+void stage_free(StageBuf& sb);
+
 int sm_count(int device) {
     int n = 0;
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n < 1) {
@@ -360,12 +363,9 @@ void step_free(Pool* p) {
     if (ws.io_in) cudaStreamDestroy(ws.io_in);
     if (ws.io_out) cudaStreamDestroy(ws.io_out);
     ws.io_in = ws.io_out = nullptr;
-    if (ws.pre_copied) cudaEventDestroy(ws.pre_copied);
-    if (ws.h_pre) cudaFreeHost(ws.h_pre);
-    if (ws.d_pre) cudaFree(ws.d_pre);
+    stage_free(ws.pre);
+    stage_free(ws.rope);
     if (ws.d_qconv) cudaFree(ws.d_qconv);
-    ws.pre_copied = nullptr;
-    ws.h_pre = ws.d_pre = nullptr;
     ws.d_qconv = nullptr;
     ws.d_part_acc = ws.d_part_ml = nullptr;
 }
@@ -575,38 +575,50 @@ namespace {
 
 constexpr int kPrefillRows = 128;  // queries per tensor-core work item
 
-// Copies `bytes` of host data into the prefill device buffer (one pinned staging copy).
-int stage_prefill(Pool* p, const std::vector<char>& host, cudaStream_t st) {
-    StepWorkspace& ws = p->ws;
-    if (!ws.pre_copied) {
-        cudaError_t e = cudaEventCreateWithFlags(&ws.pre_copied, cudaEventDisableTiming);
+// Copies `bytes` of host data into a staging buffer's device side (one pinned staging copy on
+// `st`).  The pinned side is reused once its previous copy has landed.
+int stage_copy(StageBuf& sb, const void* host, size_t bytes, cudaStream_t st, const char* what) {
+    if (!sb.copied) {
+        cudaError_t e = cudaEventCreateWithFlags(&sb.copied, cudaEventDisableTiming);
         if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
     }
-    if (ws.pre_pending) {
-        cudaError_t e = cudaEventSynchronize(ws.pre_copied);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaEventSynchronize(prefill metadata)");
-        ws.pre_pending = false;
+    if (sb.pending) {
+        cudaError_t e = cudaEventSynchronize(sb.copied);
+        if (e != cudaSuccess) return cuda_fail(e, what);
+        sb.pending = false;
     }
-    if (host.size() > ws.pre_cap) {
-        if (ws.h_pre) cudaFreeHost(ws.h_pre);
-        if (ws.d_pre) cudaFree(ws.d_pre);
-        ws.h_pre = ws.d_pre = nullptr;
-        ws.pre_cap = 0;
-        const size_t cap = align_up(host.size(), 4096);
-        cudaError_t e = cudaMallocHost(&ws.h_pre, cap);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaMallocHost(prefill metadata)");
-        e = cudaMalloc(&ws.d_pre, cap);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(prefill metadata)");
-        ws.pre_cap = cap;
+    if (bytes > sb.cap) {
+        if (sb.h) cudaFreeHost(sb.h);
+        if (sb.d) cudaFree(sb.d);
+        sb.h = sb.d = nullptr;
+        sb.cap = 0;
+        const size_t cap = align_up(bytes, 4096);
+        cudaError_t e = cudaMallocHost(&sb.h, cap);
+        if (e != cudaSuccess) return cuda_fail(e, what);
+        e = cudaMalloc(&sb.d, cap);
+        if (e != cudaSuccess) return cuda_fail(e, what);
+        sb.cap = cap;
     }
-    if (host.empty()) return GKV_OK;
-    memcpy(ws.h_pre, host.data(), host.size());
-    cudaError_t e = cudaMemcpyAsync(ws.d_pre, ws.h_pre, host.size(), cudaMemcpyHostToDevice, st);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(prefill metadata)");
-    e = cudaEventRecord(ws.pre_copied, st);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord(prefill metadata)");
-    ws.pre_pending = true;
+    if (bytes == 0) return GKV_OK;
+    memcpy(sb.h, host, bytes);
+    cudaError_t e = cudaMemcpyAsync(sb.d, sb.h, bytes, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    e = cudaEventRecord(sb.copied, st);
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    sb.pending = true;
     return GKV_OK;
+}
+
+void stage_free(StageBuf& sb) {
+    if (sb.pending && sb.copied) cudaEventSynchronize(sb.copied);
+    if (sb.copied) cudaEventDestroy(sb.copied);
+    if (sb.h) cudaFreeHost(sb.h);
+    if (sb.d) cudaFree(sb.d);
+    sb = StageBuf{};
+}
+
+int stage_prefill(Pool* p, const std::vector<char>& host, cudaStream_t st) {
+    return stage_copy(p->ws.pre, host.data(), host.size(), st, "prefill metadata upload");
 }
 
 int ensure_qconv(Pool* p, size_t bytes) {
@@ -703,7 +715,7 @@ int step_prefill(Pool* p, int32_t layer, const void* d_q, int32_t q_dtype, float
             return set_error(GKV_EINVAL, "16-bit q must be 16-byte aligned");
         }
         PrefillArgs a{};
-        a.items = reinterpret_cast<const int32_t*>(ws.d_pre);
+        a.items = reinterpret_cast<const int32_t*>(ws.pre.d);
         a.n_items = static_cast<int32_t>(order.size());
         a.tables = ws.work.tables;
         a.max_blocks = ws.up_max_blocks;
@@ -768,7 +780,7 @@ int step_prefill(Pool* p, int32_t layer, const void* d_q, int32_t q_dtype, float
     put_vec(host, rows_off, row_e);
     rc = stage_prefill(p, host, st);
     if (rc != GKV_OK) return rc;
-    const char* d = ws.d_pre;
+    const char* d = ws.pre.d;
     auto at = [&](size_t off) { return reinterpret_cast<const int32_t*>(d + off); };
     DecodeWork w{};
     w.tables = ws.work.tables;
@@ -816,6 +828,84 @@ int step_prefill(Pool* p, int32_t layer, const void* d_q, int32_t q_dtype, float
         if (e != cudaSuccess) return cuda_fail(e, "prefill (decode kernel) launch");
     }
     p->last_launches += launches + dl;
+    return GKV_OK;
+}
+
+void rope_inv_freq(float freq_base, int32_t rope_dim, const float* factors, float* out) {
+    for (int32_t i = 0; i < rope_dim / 2; ++i) {
+        float f = static_cast<float>(std::pow(static_cast<double>(freq_base), -2.0 * i / rope_dim));
+        if (factors) f = f / factors[i];
+        out[i] = f;
+    }
+}
+
+int step_rope_append(Pool* p, int32_t layer, float* d_q, const float* d_k, const float* d_v, int32_t n_tok,
+                     int32_t n_heads, const int32_t* positions, const gkv_rope_desc* rope,
+                     const gkv_qkv_prologue* pro, cudaStream_t st) {
+    StepWorkspace& ws = p->ws;
+    if (!ws.uploaded) return set_error(GKV_ESTATE, "no step uploaded (call gkv_upload_step first)");
+    if (!rope) return set_error(GKV_EINVAL, "rope description is NULL");
+    if (layer < 0 || layer >= p->desc.layers)
+        return set_error(GKV_EINVAL, "layer %d outside [0, %d)", layer, p->desc.layers);
+    if (n_tok < 0 || n_tok > ws.n_tok)
+        return set_error(GKV_EINVAL, "n_tok %d exceeds the uploaded slot mapping (%d)", n_tok, ws.n_tok);
+    if (n_heads <= 0 || n_heads % p->desc.heads_kv != 0)
+        return set_error(GKV_EINVAL, "n_heads %d is not a positive multiple of heads_kv %d", n_heads,
+                         p->desc.heads_kv);
+    const int32_t R = rope->rope_dim == 0 ? p->desc.head_dim : rope->rope_dim;
+    if (rope->style != GKV_ROPE_NEOX && rope->style != GKV_ROPE_INTERLEAVED)
+        return set_error(GKV_EINVAL, "rope style %d is neither GKV_ROPE_NEOX nor GKV_ROPE_INTERLEAVED", rope->style);
+    if (R < 0 || R > p->desc.head_dim || (R & 1))
+        return set_error(GKV_EINVAL, "rope_dim %d must be even and within [0, head_dim %d]", R, p->desc.head_dim);
+    if (!rope_append_supported(p->geom, R))
+        return set_error(GKV_EUNSUPPORTED, "fused rope append not built for head_dim %d / rope_dim %d",
+                         p->desc.head_dim, R);
+    if (!rope->h_inv_freq && !(rope->freq_base > 0.f))
+        return set_error(GKV_EINVAL, "freq_base must be positive when no inverse-frequency table is given");
+    if (n_tok > 0 && (!d_q || !d_k || !d_v || !positions)) return set_error(GKV_EINVAL, "q/k/v/positions is NULL");
+    for (int32_t i = 0; i < n_tok; ++i)
+        if (positions[i] < 0) return set_error(GKV_EINVAL, "positions[%d] = %d is negative", i, positions[i]);
+    int rc = p->flush_copies(st);
+    if (rc != GKV_OK) return rc;
+    if (n_tok == 0) return GKV_OK;
+    // one staged upload: positions, then the inverse-frequency table at a 16-byte boundary
+    const size_t pos_bytes = align_up(static_cast<size_t>(n_tok) * 4, 16);
+    std::vector<char> host(pos_bytes + static_cast<size_t>(R / 2 > 0 ? R / 2 : 1) * 4);
+    memcpy(host.data(), positions, static_cast<size_t>(n_tok) * 4);
+    float* tab = reinterpret_cast<float*>(host.data() + pos_bytes);
+    if (rope->h_inv_freq) {
+        for (int32_t i = 0; i < R / 2; ++i)
+            tab[i] = rope->h_freq_factors ? rope->h_inv_freq[i] / rope->h_freq_factors[i] : rope->h_inv_freq[i];
+    } else {
+        rope_inv_freq(rope->freq_base, R, rope->h_freq_factors, tab);
+    }
+    rc = stage_copy(ws.rope, host.data(), host.size(), st, "rope metadata upload");
+    if (rc != GKV_OK) return rc;
+    RopeAppendParams a{};
+    a.layer = layer;
+    a.q = d_q;
+    a.k = d_k;
+    a.v = d_v;
+    a.n_tok = n_tok;
+    a.n_heads = n_heads;
+    a.positions = reinterpret_cast<const int32_t*>(ws.rope.d);
+    a.inv_freq = reinterpret_cast<const float*>(ws.rope.d + pos_bytes);
+    a.rope_dim = R;
+    a.style = rope->style;
+    a.mscale = rope->mscale == 0.f ? 1.f : rope->mscale;
+    if (pro) {
+        a.q_bias = pro->d_q_bias;
+        a.k_bias = pro->d_k_bias;
+        a.v_bias = pro->d_v_bias;
+        a.q_norm = pro->d_q_norm;
+        a.k_norm = pro->d_k_norm;
+        a.eps = pro->eps;
+    }
+    a.slots = ws.d_slots;
+    a.err = ws.d_err;
+    cudaError_t e = launch_rope_append(p->geom, a, st);
+    if (e != cudaSuccess) return cuda_fail(e, "rope_append launch");
+    p->last_launches += 1;
     return GKV_OK;
 }
 
@@ -1008,6 +1098,23 @@ int gkv_decode_step_host(gkv_pool* pool, int32_t layer, const int32_t* h_block_t
         if (e != cudaSuccess) return gkv::cuda_fail(e, "cudaStreamWaitEvent(previous output)");
     }
     ws.io_next ^= 1;
+    return GKV_OK;
+}
+
+int gkv_rope_append(gkv_pool* pool, int32_t layer, float* d_q, const float* d_k, const float* d_v,
+                    int32_t n_tok, int32_t n_heads, const int32_t* h_positions, const gkv_rope_desc* rope,
+                    const gkv_qkv_prologue* prologue, void* stream) {
+    GKV_DEVICE_POOL(pool);
+    gkv::DeviceGuard guard(pool->impl.desc.device);
+    pool->impl.last_launches = 0;
+    return gkv::step_rope_append(&pool->impl, layer, d_q, d_k, d_v, n_tok, n_heads, h_positions, rope, prologue,
+                                 static_cast<cudaStream_t>(stream));
+}
+
+int gkv_rope_inv_freq(float freq_base, int32_t rope_dim, const float* h_freq_factors, float* out) {
+    if (rope_dim < 0 || (rope_dim & 1) || !(freq_base > 0.f) || (rope_dim > 0 && !out))
+        return set_error(GKV_EINVAL, "freq_base %g / rope_dim %d / out", static_cast<double>(freq_base), rope_dim);
+    gkv::rope_inv_freq(freq_base, rope_dim, h_freq_factors, out);
     return GKV_OK;
 }
 

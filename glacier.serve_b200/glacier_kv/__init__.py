@@ -21,6 +21,8 @@ from . import _lib
 from ._lib import (DTYPES, GKV_DTYPE_BF16, GKV_DTYPE_F16, GKV_DTYPE_F32, GKV_EDEVICE, GKV_EINVAL, GKV_ESTATE,
                    GKV_ETIMEDOUT, GKV_EUNSUPPORTED, GKV_OK, LIB_PATH, last_error, lib)
 
+GKV_ROPE_NEOX, GKV_ROPE_INTERLEAVED = 0, 1
+
 __all__ = [
     "PagedBlockPool", "BlockTable", "PagedAttentionKernel", "GkvError",
     "ArgumentOutOfRangeError", "InvalidOperationError", "DeviceError", "TimeoutError_",
@@ -321,6 +323,25 @@ class PagedBlockPool:
         _check(lib.gkv_kv_append(self._h, layer, _f32_dev(k, "k"), _f32_dev(v, "v"), n,
                                  _stream(stream, self.device)))
 
+    def rope_append(self, layer: int, q, k, v, positions, n_heads: int, rope_dim: int = 0, style: int = 0,
+                    freq_base: float = 10000.0, inv_freq=None, freq_factors=None, mscale: float = 1.0,
+                    q_bias=None, k_bias=None, v_bias=None, q_norm=None, k_norm=None, eps: float = 1e-6,
+                    stream=None) -> None:
+        """Bias + per-head RMSNorm + RoPE of q and k, then the append of k and v into the uploaded
+        step's slots (gkv_rope_append).  q [n_tok, n_heads, head_dim] float32 CUDA is rewritten
+        in place; k, v float32 CUDA; positions a host int array [n_tok]; inv_freq / freq_factors
+        host float arrays [rope_dim/2] or None; biases and norm weights float32 CUDA or None."""
+        pos = np.ascontiguousarray(positions, dtype=np.int32)
+        inv = None if inv_freq is None else np.ascontiguousarray(inv_freq, dtype=np.float32)
+        fac = None if freq_factors is None else np.ascontiguousarray(freq_factors, dtype=np.float32)
+        rd = _lib.gkv_rope_desc(rope_dim, style, float(freq_base), float(mscale), _ptr(inv), _ptr(fac))
+        opt = lambda t, n: None if t is None else _f32_dev(t, n)  # noqa: E731
+        pro = _lib.gkv_qkv_prologue(opt(q_bias, "q_bias"), opt(k_bias, "k_bias"), opt(v_bias, "v_bias"),
+                                    opt(q_norm, "q_norm"), opt(k_norm, "k_norm"), float(eps))
+        _check(lib.gkv_rope_append(self._h, layer, _f32_dev(q, "q"), _f32_dev(k, "k"), _f32_dev(v, "v"),
+                                   int(pos.size), n_heads, _ptr(pos), C.byref(rd), C.byref(pro),
+                                   _stream(stream, self.device)))
+
     def paged_decode(self, layer: int, q, out, n_heads: int, scale: float, sinks=None, stream=None) -> None:
         """q [batch, n_heads, head_dim] -> out [batch, n_heads, v_head_dim] float32 CUDA."""
         _check(lib.gkv_paged_decode(self._h, layer, _f32_dev(q, "q"), _f32_dev(out, "out"), n_heads,
@@ -574,6 +595,14 @@ def plan_decode(ctx_lens: Sequence[int], heads_kv: int, block_size: int, n_worke
     return {"total_chunks": info.total_chunks, "n_pieces": k, "n_slots": info.n_slots,
             "n_merge": info.n_merge, "segment_cost": info.segment_cost, "piece_seg": seg[:k], "piece_c0": c0[:k], "piece_c1": c1[:k],
             "piece_slot": slot[:k], "worker_begin": wb}
+
+
+def rope_inv_freq(freq_base: float, rope_dim: int, freq_factors=None) -> np.ndarray:
+    """The inverse-frequency table gkv_rope_append builds when none is given."""
+    fac = None if freq_factors is None else np.ascontiguousarray(freq_factors, dtype=np.float32)
+    out = np.zeros(max(rope_dim // 2, 1), np.float32)
+    _check(lib.gkv_rope_inv_freq(float(freq_base), rope_dim, _ptr(fac), _ptr(out)))
+    return out[: rope_dim // 2]
 
 
 def split_block_range(n_blocks: int, n_ranks: int, rank: int) -> Tuple[int, int]:

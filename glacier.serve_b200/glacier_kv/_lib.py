@@ -68,6 +68,28 @@ class gkv_arena_desc(C.Structure):
     ]
 
 
+class gkv_rope_desc(C.Structure):
+    _fields_ = [
+        ("rope_dim", C.c_int32),
+        ("style", C.c_int32),
+        ("freq_base", C.c_float),
+        ("mscale", C.c_float),
+        ("h_inv_freq", C.c_void_p),
+        ("h_freq_factors", C.c_void_p),
+    ]
+
+
+class gkv_qkv_prologue(C.Structure):
+    _fields_ = [
+        ("d_q_bias", C.c_void_p),
+        ("d_k_bias", C.c_void_p),
+        ("d_v_bias", C.c_void_p),
+        ("d_q_norm", C.c_void_p),
+        ("d_k_norm", C.c_void_p),
+        ("eps", C.c_float),
+    ]
+
+
 class gkv_pool_stats(C.Structure):
     _fields_ = [
         ("total_blocks", C.c_int32),
@@ -124,6 +146,9 @@ SIGNATURES = {
     "gkv_upload_step_tables": (C.c_int, [P, P, I32, P, P, I32, P]),
     "gkv_kv_append": (C.c_int, [P, I32, P, P, I32, P]),
     "gkv_paged_decode": (C.c_int, [P, I32, P, P, I32, F32, P, P]),
+    "gkv_rope_append": (C.c_int, [P, I32, P, P, P, I32, I32, P, C.POINTER(gkv_rope_desc),
+                                  C.POINTER(gkv_qkv_prologue), P]),
+    "gkv_rope_inv_freq": (C.c_int, [F32, I32, P, P]),
     "gkv_paged_prefill": (C.c_int, [P, I32, P, I32, P, P, P, I32, F32, P]),
     "gkv_compute_attention": (
         C.c_int,

@@ -208,6 +208,47 @@ GKV_API int gkv_upload_step_tables(gkv_pool* pool, gkv_table* const* tables, int
  * PagedBlockPool.cs:151-161.  Bit-exact for fp32 storage, RNE for bf16. */
 GKV_API int gkv_kv_append(gkv_pool* pool, int32_t layer, const float* d_k, const float* d_v,
                           int32_t n_tok, void* stream);
+/* Rotary position embedding of gkv_rope_append.  Pairs (i, i + rope_dim/2) for
+ * GKV_ROPE_NEOX (the half-split layout of Qwen2 / GPT-NeoX) or (2i, 2i+1) for
+ * GKV_ROPE_INTERLEAVED, i < rope_dim/2; elements from rope_dim on are not rotated. */
+enum { GKV_ROPE_NEOX = 0, GKV_ROPE_INTERLEAVED = 1 };
+typedef struct gkv_rope_desc {
+    int32_t rope_dim;              /* rotated dims per head: even, <= head_dim; 0 = head_dim      */
+    int32_t style;                 /* GKV_ROPE_NEOX or GKV_ROPE_INTERLEAVED                       */
+    float freq_base;               /* inv_freq[i] = freq_base^(-2i/rope_dim) when h_inv_freq = NULL */
+    float mscale;                  /* multiplies the rotated q and k (YaRN mscale); 0 means 1     */
+    const float* h_inv_freq;       /* [rope_dim/2] host table (the YaRN table) or NULL            */
+    const float* h_freq_factors;   /* [rope_dim/2] host divisors of the frequencies, or NULL      */
+} gkv_rope_desc;
+/* Optional per-layer terms applied before the rotation (device pointers, NULL = absent). */
+typedef struct gkv_qkv_prologue {
+    const float* d_q_bias;         /* [n_heads * head_dim]     AddVector(q, QBias)                */
+    const float* d_k_bias;         /* [heads_kv * head_dim]    AddVector(k, KBias)                */
+    const float* d_v_bias;         /* [heads_kv * v_head_dim]  AddVector(v, VBias)                */
+    const float* d_q_norm;         /* [head_dim] per-head RMSNorm weight of q (AttnQNormWeight)   */
+    const float* d_k_norm;         /* [head_dim] per-head RMSNorm weight of k (AttnKNormWeight)   */
+    float eps;                     /* RmsNormEps                                                  */
+} gkv_qkv_prologue;
+/* The steps between the q/k/v projections and Store, fused with the append, for the
+ * uploaded step's n_tok tokens at h_positions[n_tok]: bias add (PagedTransformerRunner.cs:
+ * 612-614), per-head RMSNorm of q and k (ApplyQkNorm, :616,713-732), rotary position embedding
+ * of q and k with the inverse-frequency table and mscale (QuantKernels.RoPE, :619-631), then
+ * Store of the rotated k and of v into each token's slot (:634), all in one launch.
+ * d_q [n_tok][n_heads][head_dim] fp32 is rewritten in place (ready for gkv_paged_decode /
+ * gkv_paged_prefill); d_k [n_tok][heads_kv][head_dim] and d_v [n_tok][heads_kv][v_head_dim]
+ * fp32 are read only.  Formulas (QuantKernels' own are not in the reference tree):
+ * RMSNorm y = (x / sqrt(sum(x^2) / head_dim + eps)) * w; rotation by angle pos * inv_freq[i]
+ * (one fp32 multiply): (a, b) -> (a cos - b sin, b cos + a sin), times mscale.  head_dim must
+ * be 32, 64, 128 or 256 (GKV_EUNSUPPORTED otherwise). */
+GKV_API int gkv_rope_append(gkv_pool* pool, int32_t layer, float* d_q, const float* d_k,
+                            const float* d_v, int32_t n_tok, int32_t n_heads,
+                            const int32_t* h_positions, const gkv_rope_desc* rope,
+                            const gkv_qkv_prologue* prologue, void* stream);
+/* The inverse-frequency table gkv_rope_append uses when rope->h_inv_freq is NULL:
+ * out[i] = (float)(freq_base^(-2i/rope_dim)) / h_freq_factors[i] (the divisor only when given),
+ * i < rope_dim/2.  Host only. */
+GKV_API int gkv_rope_inv_freq(float freq_base, int32_t rope_dim, const float* h_freq_factors,
+                              float* out);
 /* Split-KV GQA paged decode of the uploaded step for `layer`:
  * d_q [batch][n_heads][head_dim] fp32 -> d_out [batch][n_heads][v_head_dim] fp32.
  * out = softmax(scale * q.K^T [, sink]) . V over each sequence's ctx_len tokens, query

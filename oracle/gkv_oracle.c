@@ -373,3 +373,120 @@ int oracle_max_threads(void) {
     return 1;
 #endif
 }
+
+/* ---- the per-token prologue before Store: bias, QK RMSNorm, RoPE ---------------------------
+ * PagedTransformerRunner.ForwardBatch (PagedTransformerRunner.cs:612-634) runs, per sequence:
+ * AddVector of the q/k/v biases (:612-614, AddVector :735-752), ApplyQkNorm (per-head RMSNorm of
+ * q and k, :616 / :713-732), QuantKernels.RoPE with the YaRN inverse-frequency table and mscale
+ * (:619-631), then pool.Store of k and v (:634).  QuantKernels.RMSNorm and QuantKernels.RoPE
+ * live in the un-vendored NuGet Glacier.Inference 1.7.0: their exact formulas are UNPINNED and
+ * restated here as stated below; the CUDA kernel computes the same operations in the same order,
+ * so slot contents agree bit for bit. */
+
+/* sin and cos of a float angle: Cody-Waite reduction by pi/2 in double precision (pi/2 split
+ * into two doubles, fused multiply-adds), then Taylor polynomials of sin and cos on
+ * |x| <= pi/4 in float (Horner, fused multiply-adds; truncation error below 2^-28). */
+void oracle_sincos(float theta, float* s_out, float* c_out) {
+    const double t = (double)theta;
+    const double k = rint(t * 0.63661977236758134308);            /* 2/pi */
+    double r = fma(-k, 1.5707963267948966192, t);                  /* pi/2, high part */
+    r = fma(-k, 6.1232339957367660359e-17, r);                     /* pi/2, low part */
+    const float x = (float)r;
+    const float x2 = x * x;
+    /* sin x = x + x^3 (-1/3! + x^2 (1/5! + x^2 (-1/7! + x^2 (1/9! - x^2/11!)))) */
+    float ps = fmaf(x2, -2.5052108385441720e-8f, 2.7557319223985893e-6f);
+    ps = fmaf(x2, ps, -1.9841269841269841e-4f);
+    ps = fmaf(x2, ps, 8.3333333333333333e-3f);
+    ps = fmaf(x2, ps, -1.6666666666666667e-1f);
+    const float sn = fmaf(x * x2, ps, x);
+    /* cos x = 1 + x^2 (-1/2! + x^2 (1/4! + x^2 (-1/6! + x^2 (1/8! - x^2/10!)))) */
+    float pc = fmaf(x2, -2.7557319223985891e-7f, 2.4801587301587302e-5f);
+    pc = fmaf(x2, pc, -1.3888888888888889e-3f);
+    pc = fmaf(x2, pc, 4.1666666666666667e-2f);
+    pc = fmaf(x2, pc, -0.5f);
+    const float cs = fmaf(x2, pc, 1.0f);
+    switch (((long long)k) & 3) {
+        case 0: *s_out = sn; *c_out = cs; break;
+        case 1: *s_out = cs; *c_out = -sn; break;
+        case 2: *s_out = -sn; *c_out = -cs; break;
+        default: *s_out = -cs; *c_out = sn; break;
+    }
+}
+
+/* RMSNorm of one head row of length n = 32*E (E elements per lane of a 32-lane group): lane l
+ * sums the squares of its elements [l*E, (l+1)*E) in order (first x*x, then fused multiply-adds),
+ * the 32 partial sums are combined by a butterfly (lane l adds lane l^16's sum, then l^8, l^4,
+ * l^2, l^1); then r = sqrt(sum / n + eps) and y_i = (x_i / r) * w_i, each step rounded. */
+static void rmsnorm_row(float* x, const float* w, int32_t n, float eps) {
+    const int32_t E = n / 32;
+    float part[32];
+    for (int l = 0; l < 32; ++l) {
+        float p = x[l * E] * x[l * E];
+        for (int32_t e = 1; e < E; ++e) p = fmaf(x[l * E + e], x[l * E + e], p);
+        part[l] = p;
+    }
+    for (int off = 16; off >= 1; off >>= 1) {
+        float nxt[32];
+        for (int l = 0; l < 32; ++l) nxt[l] = part[l] + part[l ^ off];
+        memcpy(part, nxt, sizeof(part));
+    }
+    const float r = sqrtf(part[0] / (float)n + eps);
+    for (int32_t i = 0; i < n; ++i) x[i] = (x[i] / r) * w[i];
+}
+
+/* Rotation of one head row by position pos: pairs (i, i + R/2) (style 0, NEOX) or (2i, 2i+1)
+ * (style 1, interleaved) for i < R/2, angle pos * inv_freq[i] (one float multiply), then every
+ * rotated element times mscale; elements from R on pass through. */
+static void rope_row(float* x, int32_t pos, const float* inv_freq, int32_t R, int32_t style, float mscale) {
+    for (int32_t i = 0; i < R / 2; ++i) {
+        const int32_t a = style == 0 ? i : 2 * i;
+        const int32_t b = style == 0 ? i + R / 2 : 2 * i + 1;
+        float s, c;
+        oracle_sincos((float)pos * inv_freq[i], &s, &c);
+        const float x0 = x[a], x1 = x[b];
+        const float y0 = fmaf(x0, c, -(x1 * s));
+        const float y1 = fmaf(x1, c, x0 * s);
+        x[a] = y0 * mscale;
+        x[b] = y1 * mscale;
+    }
+}
+
+int oracle_rope_append(void* kpool, void* vpool, const oracle_geom* g, int32_t layer, float* q,
+                       const float* k, const float* v, int32_t n_tok, int32_t n_heads,
+                       const int32_t* positions, const int64_t* slots, const float* inv_freq,
+                       int32_t rope_dim, int32_t style, float mscale, const float* q_bias,
+                       const float* k_bias, const float* v_bias, const float* q_norm,
+                       const float* k_norm, float eps) {
+    const int32_t d = g->head_dim, dv = g->v_head_dim, hkv = g->heads_kv;
+    if (d % 32 != 0 || rope_dim < 0 || rope_dim > d || rope_dim % 2 != 0) return ORACLE_EINVAL;
+    float* kr = (float*)malloc(sizeof(float) * (size_t)hkv * (size_t)d);
+    float* vr = (float*)malloc(sizeof(float) * (size_t)hkv * (size_t)dv);
+    if (!kr || !vr) {
+        free(kr);
+        free(vr);
+        return ORACLE_EINVAL;
+    }
+    int rc = ORACLE_OK;
+    for (int32_t t = 0; t < n_tok && rc == ORACLE_OK; ++t) {
+        float* qt = q + (int64_t)t * n_heads * d;
+        memcpy(kr, k + (int64_t)t * hkv * d, sizeof(float) * (size_t)hkv * (size_t)d);
+        memcpy(vr, v + (int64_t)t * hkv * dv, sizeof(float) * (size_t)hkv * (size_t)dv);
+        /* AddVector, :612-614 */
+        if (q_bias) for (int32_t i = 0; i < n_heads * d; ++i) qt[i] = qt[i] + q_bias[i];
+        if (k_bias) for (int32_t i = 0; i < hkv * d; ++i) kr[i] = kr[i] + k_bias[i];
+        if (v_bias) for (int32_t i = 0; i < hkv * dv; ++i) vr[i] = vr[i] + v_bias[i];
+        /* ApplyQkNorm, :713-732 */
+        if (q_norm) for (int32_t h = 0; h < n_heads; ++h) rmsnorm_row(qt + (int64_t)h * d, q_norm, d, eps);
+        if (k_norm) for (int32_t h = 0; h < hkv; ++h) rmsnorm_row(kr + (int64_t)h * d, k_norm, d, eps);
+        /* QuantKernels.RoPE, :619-631 */
+        for (int32_t h = 0; h < n_heads; ++h) rope_row(qt + (int64_t)h * d, positions[t], inv_freq, rope_dim, style, mscale);
+        for (int32_t h = 0; h < hkv; ++h) rope_row(kr + (int64_t)h * d, positions[t], inv_freq, rope_dim, style, mscale);
+        /* pool.Store, :634 */
+        if (slots[t] >= 0)
+            rc = oracle_store(kpool, vpool, g, (int32_t)(slots[t] / g->block_size), layer,
+                              (int32_t)(slots[t] % g->block_size), kr, vr);
+    }
+    free(kr);
+    free(vr);
+    return rc;
+}

@@ -99,6 +99,17 @@ int oracle_prefill_chunk(const void* kpool, const void* vpool, const oracle_geom
 
 int oracle_max_threads(void);
 
+/* sin and cos of a float angle (Cody-Waite reduction in double, Taylor polynomials in float). */
+void oracle_sincos(float theta, float* s_out, float* c_out);
+/* Bias add, per-head RMSNorm of q and k, RoPE of q and k, then Store of the rotated k and v at
+ * slots[t] (< 0: skipped); q is rewritten in place.  PagedTransformerRunner.cs:612-634. */
+int oracle_rope_append(void* kpool, void* vpool, const oracle_geom* g, int32_t layer, float* q,
+                       const float* k, const float* v, int32_t n_tok, int32_t n_heads,
+                       const int32_t* positions, const int64_t* slots, const float* inv_freq,
+                       int32_t rope_dim, int32_t style, float mscale, const float* q_bias,
+                       const float* k_bias, const float* v_bias, const float* q_norm,
+                       const float* k_norm, float eps);
+
 #ifdef __cplusplus
 }
 #endif

@@ -43,6 +43,10 @@ def _load() -> C.CDLL:
     lib.oracle_decode_batch_parallel.argtypes = [P, P, P, I, P, I, I, P, P, P, I, F, I]
     lib.oracle_prefill_chunk.argtypes = [P, P, P, I, P, I, I, I, I, P, P, I, F, I]
     lib.oracle_max_threads.restype = C.c_int
+    lib.oracle_sincos.restype = None
+    lib.oracle_sincos.argtypes = [F, C.POINTER(F), C.POINTER(F)]
+    lib.oracle_rope_append.restype = C.c_int
+    lib.oracle_rope_append.argtypes = [P, P, P, I, P, P, P, I, I, P, P, P, I, I, F, P, P, P, P, P, F]
     for n in ("oracle_store", "oracle_copy_block_data", "oracle_store_many", "oracle_copy_many",
               "oracle_compute_attention",
               "oracle_decode_batch", "oracle_decode_batch_parallel", "oracle_prefill_chunk"):
@@ -196,3 +200,29 @@ def host_cores() -> int:
         return max(1, len(os.sched_getaffinity(0)))
     except (AttributeError, OSError):
         return max(1, os.cpu_count() or 1)
+
+
+def sincos(theta: float):
+    s, c = C.c_float(), C.c_float()
+    lib.oracle_sincos(float(theta), C.byref(s), C.byref(c))
+    return s.value, c.value
+
+
+def rope_append(K, V, g: Geom, layer, q, k, v, positions, slots, inv_freq, rope_dim, style=0, mscale=1.0,
+                q_bias=None, k_bias=None, v_bias=None, q_norm=None, k_norm=None, eps=1e-6):
+    """Restated prologue + Store (PagedTransformerRunner.cs:612-634); returns the rewritten q."""
+    q = np.array(q, dtype=np.float32, copy=True, order="C")
+    k = np.ascontiguousarray(k, np.float32)
+    v = np.ascontiguousarray(v, np.float32)
+    positions = np.ascontiguousarray(positions, np.int32)
+    slots = np.ascontiguousarray(slots, np.int64)
+    inv_freq = np.ascontiguousarray(inv_freq, np.float32)
+    terms = [None if a is None else np.ascontiguousarray(a, np.float32)
+             for a in (q_bias, k_bias, v_bias, q_norm, k_norm)]  # kept alive across the call
+    ptrs = [None if a is None else _p(a) for a in terms]
+    rc = lib.oracle_rope_append(_p(K), _p(V), C.byref(g), layer, _p(q), _p(k), _p(v), int(positions.size),
+                                int(q.shape[1]), _p(positions), _p(slots), _p(inv_freq), rope_dim, style,
+                                float(mscale), *ptrs, float(eps))
+    if rc != 0:
+        raise ValueError(f"oracle_rope_append failed ({rc})")
+    return q
