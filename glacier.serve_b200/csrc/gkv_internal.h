@@ -38,6 +38,9 @@ class DeviceGuard {
 class FreeStack {
    public:
     void init(int32_t n);  // pushes n-1 .. 0 so that 0 pops first
+    // Replaces the contents with pop_order (first element pops first).  Not safe against
+    // concurrent push/pop: the caller excludes every other allocator call.
+    void rebuild(const std::vector<int32_t>& pop_order);
     void push(int32_t idx);
     int32_t pop();         // -1 when empty
     int32_t count() const { return count_.load(std::memory_order_acquire); }
@@ -208,6 +211,10 @@ struct Pool {
     bool try_fork(int32_t src, int32_t valid, int32_t* out);
     // device helpers (caller holds a DeviceGuard)
     int flush_copies(cudaStream_t st);
+    // Moves movable live blocks into the lowest free ids (compact.cpp); returns the number of
+    // moves (src[i] -> dst[i]) or a negative code.  Excludes concurrent allocator calls.
+    int compact(struct Table* const* tables, int32_t n_tables, int32_t max_moves, std::vector<int32_t>* src,
+                std::vector<int32_t>* dst, cudaStream_t st);
     int launch_copies(const int32_t* h_ops, int n, cudaStream_t st);
 };
 

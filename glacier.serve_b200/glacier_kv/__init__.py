@@ -292,6 +292,17 @@ class PagedBlockPool:
         _check(lib.gkv_pool_store(self._h, block, layer, slot, _f32_dev(k, "k"), _f32_dev(v, "v"),
                                   _stream(stream, self.device)))
 
+    def compact(self, tables: Sequence["BlockTable"], max_moves: int = 0, stream=None) -> Tuple[np.ndarray, np.ndarray]:
+        """gkv_pool_compact: moves live blocks held only by `tables` into the lowest free ids
+        (one batched block copy), rewrites the tables; returns the moves (src ids, dst ids)."""
+        arr = (C.c_void_p * max(len(tables), 1))(*[t.handle.value for t in tables])
+        cap = max_moves if max_moves > 0 else self.total_blocks
+        src = np.zeros(max(cap, 1), np.int32)
+        dst = np.zeros(max(cap, 1), np.int32)
+        n = _check(lib.gkv_pool_compact(self._h, arr, len(tables), max_moves, _ptr(src), _ptr(dst), cap,
+                                        _stream(stream, self.device) if self.has_device_arena else None))
+        return src[:n], dst[:n]
+
     # ---- batched step ----
     def reserve_step(self, max_batch: int, max_blocks_per_seq: int, max_tokens: int, n_heads: int) -> None:
         _check(lib.gkv_step_reserve(self._h, max_batch, max_blocks_per_seq, max_tokens, n_heads))

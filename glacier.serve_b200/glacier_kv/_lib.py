@@ -131,6 +131,7 @@ SIGNATURES = {
     "gkv_pool_flush_copies": (C.c_int, [P, P]),
     "gkv_block_copy": (C.c_int, [P, P, P, P, I32, P]),
     "gkv_pool_store": (C.c_int, [P, I32, I32, I32, P, P, P]),
+    "gkv_pool_compact": (C.c_int, [P, P, I32, I32, P, P, I32, P]),
     "gkv_table_create": (C.c_int, [P, C.POINTER(P)]),
     "gkv_table_destroy": (C.c_int, [P]),
     "gkv_table_attach_prefix_blocks": (C.c_int, [P, P, I32, I32]),

@@ -172,6 +172,23 @@ GKV_API int gkv_table_block_ids(const gkv_table* table, int32_t* out, int32_t ca
 /* ReleaseAll, BlockTable.cs:108-116. */
 GKV_API int gkv_table_release_all(gkv_table* table);
 
+/* Compaction after evictions (the engine's evict loop, ContinuousBatchEngine.cs:498-512, frees
+ * blocks wherever they sit; the reference never moves a live block).  Moves live blocks into
+ * the lowest free ids: a block moves only if its reference count equals its number of
+ * occurrences in the n_tables tables passed (blocks also held elsewhere stay put).  Free ids
+ * are filled from the bottom with movable blocks taken from the top until the two meet, at most
+ * max_moves (<= 0: no limit; the capacity cap of out_src/out_dst when those are given).  ONE
+ * batched block copy (CopyBlockData of whole blocks, every layer and head, PagedBlockPool.cs:
+ * 304-327) runs on `stream` after the pool's queued copy-on-write copies; reference counts and
+ * prefix-cache bindings move with the blocks, the passed tables are rewritten, and the free list
+ * is rebuilt so that the lowest free id pops first.  out_src/out_dst (optional) receive the
+ * moves, for hosts that keep table copies of their own.  Returns the number of moves.  The
+ * caller excludes every other call on this pool while it runs, and orders the kernels that read
+ * the old ids before it on `stream`.  A metadata-only pool moves bookkeeping only. */
+GKV_API int gkv_pool_compact(gkv_pool* pool, gkv_table* const* tables, int32_t n_tables,
+                             int32_t max_moves, int32_t* out_src, int32_t* out_dst, int32_t cap,
+                             void* stream);
+
 /* ---- 3. one decode / append step ------------------------------------------------------ */
 
 /* Sizes the pool's step workspace (device + pinned staging) once, outside the hot loop:
