@@ -109,50 +109,26 @@ __device__ __forceinline__ void merge_segment(const DecodeArgs& a, const DecodeW
     }
 }
 
-// Merge of the segments split into more than kFusedMergeMaxSlots pieces, run as a second
-// launch, when the deferred segments average at most kWarpMergeMaxSlots slots.  One warp per
-// (deferred segment, head of a head group), eight per CTA; lane l owns dims
-// [l*DV/32, (l+1)*DV/32).  The merge is two-phase so that nothing waits on a running state:
-// lane s reads slot s's (max, sum) while the first eight slots' accumulators are already in
-// flight, one warp reduction gives the segment's max M, every slot's weight 2^(m_s - M) stays
-// in its own lane, and the accumulators are summed in batches of eight independent loads,
-// each weight fetched from its lane with one shuffle.
+// Unnormalised log-sum-exp merge of partial slots [s_lo, s_hi) of one (segment, head), by one
+// warp; lane l owns dims [l*DV/32, (l+1)*DV/32).  Slot s's (max, sum) sits at part_ml[(base +
+// s*GP)*2] (base 2), its accumulator at part_acc[(base + s*GP)*DV].  Two phases, so that nothing
+// waits on a running state: lane j reads slot s_lo + j's (max, sum) while the first eight slots'
+// accumulators are already in flight, one warp reduction gives the max M, each slot's weight
+// 2^(m_s - M) stays in its own lane, and the accumulators are summed in batches of eight
+// independent loads, each weight fetched from its lane with one shuffle.  On return every lane
+// holds M (-inf when no slot has scores), the sum L and its accumulator dims, both relative to M.
 template <int GP, int DV>
-__global__ void __launch_bounds__(256) deferred_merge_warp_kernel(ArenaGeom g, DecodeWork w,
-                                                             DecodeArgs a, int group,
-                                                             int head_groups) {
+__device__ __forceinline__ void merge_slots(const DecodeArgs& a, int64_t base, int s_lo, int s_hi, int lane,
+                                            float& M, float& L, float (&A)[DV / 32]) {
     constexpr int EPLV = DV / 32;
     constexpr int kBatch = 8;
-    static_assert(DV % 32 == 0, "DV must be a multiple of 32");
-    constexpr float kL2e = 1.4426950408889634f;
-    const int lane = threadIdx.x & 31;
-    const int per_entry = head_groups * GP;
-    const int item = static_cast<int>(blockIdx.x) * 8 + static_cast<int>(threadIdx.x >> 5);
-    const bool live = item < w.n_deferred * per_entry;
-    const int di = live ? item / per_entry : 0;
-    const int y = item - di * per_entry;
-    const int hg = y / GP;
-    const int gg = y - hg * GP;
-    // the merge list comes from the step's host copy; the partials are the previous
-    // (decode) kernel's output
-    const int mi = live ? __ldg(w.merge_deferred + di) : 0;
-    const int seg = live ? __ldg(w.merge_seg + mi) : 0;
-    const int s0 = live ? __ldg(w.merge_slot0 + mi) : 0;
-    const int ns = live ? __ldg(w.merge_nslots + mi) : 0;
-    const int b = seg / g.heads_kv;
-    const int h = seg - b * g.heads_kv;
-    const int q_head0 = h * group + hg * GP;
-    const int gcount = min(GP, group - hg * GP);
-    pdl_launch_dependents();
-    pdl_wait();
-    if (!live || gg >= gcount) return;
-    const int64_t base = (static_cast<int64_t>(hg) * w.n_slots + s0) * GP + gg;  // + s * GP
-    auto ml_of = [&](int s) {
-        return s < ns ? __ldcg(reinterpret_cast<const float2*>(a.part_ml + (base + static_cast<int64_t>(s) * GP) * 2))
+    const int ns = s_hi - s_lo;
+    auto ml_of = [&](int j) {
+        return j < ns ? __ldcg(reinterpret_cast<const float2*>(a.part_ml + (base + static_cast<int64_t>(s_lo + j) * GP) * 2))
                       : make_float2(-INFINITY, 0.f);
     };
-    auto acc_of = [&](int s, float (&v)[EPLV]) {
-        const float* ap = a.part_acc + (base + static_cast<int64_t>(s) * GP) * DV + lane * EPLV;
+    auto acc_of = [&](int j, float (&v)[EPLV]) {
+        const float* ap = a.part_acc + (base + static_cast<int64_t>(s_lo + j) * GP) * DV + lane * EPLV;
         if constexpr (EPLV % 4 == 0) {
 #pragma unroll
             for (int e = 0; e < EPLV; e += 4) {
@@ -171,18 +147,16 @@ __global__ void __launch_bounds__(256) deferred_merge_warp_kernel(ArenaGeom g, D
             for (int e = 0; e < EPLV; ++e) v[e] = __ldcg(ap + e);
         }
     };
-    // phase 1: the segment max, with the first batch of accumulators already requested
     float v0[kBatch][EPLV];
 #pragma unroll
     for (int k = 0; k < kBatch; ++k)
         if (k < ns) acc_of(k, v0[k]);
     float2 st = ml_of(lane);
-    float M = st.x;
+    M = st.x;
     for (int c0 = 32; c0 < ns; c0 += 32) M = fmaxf(M, ml_of(c0 + lane).x);
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    // phase 2: weights per slot lane, the sum, and the weighted accumulators
-    float L = 0.f, A[EPLV];
+    L = 0.f;
 #pragma unroll
     for (int e = 0; e < EPLV; ++e) A[e] = 0.f;
     for (int c0 = 0; c0 < ns; c0 += 32) {
@@ -214,7 +188,15 @@ __global__ void __launch_bounds__(256) deferred_merge_warp_kernel(ArenaGeom g, D
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-    const int qh = q_head0 + gg;
+}
+
+// Normalises one merged row (plus the optional sink) and writes it, and its natural-log
+// denominator when the caller asked for it.
+template <int DV>
+__device__ __forceinline__ void finish_row(const DecodeArgs& a, int b, int qh, float M, float L,
+                                           const float (&A)[DV / 32], int lane) {
+    constexpr int EPLV = DV / 32;
+    constexpr float kL2e = 1.4426950408889634f;
     float f = 1.f, Mref = M;
     if (a.sinks || a.has_sink_all) {
         const float sk = (a.sinks ? __ldg(a.sinks + qh) : a.sink_all) * kL2e;
@@ -230,19 +212,53 @@ __global__ void __launch_bounds__(256) deferred_merge_warp_kernel(ArenaGeom g, D
     if (a.lse && lane == 0) a.lse[static_cast<int64_t>(b) * a.n_heads + qh] = lse_ln(Mref, L);
 }
 
-// The same merge for long segments (more than kWarpMergeMaxSlots slots): one CTA per
-// (deferred segment, head group x head), whose 256 threads are SL slot lanes x DV dims
-// (SL = 256 / DV), so a long segment's slots are read by SL lanes at once.
+// Merge of the segments split into more than kFusedMergeMaxSlots pieces, run as a second
+// launch, when no deferred segment has more than kWarpMergeMaxSlots slots: one warp per
+// (deferred segment, head of a head group), eight per CTA.
+template <int GP, int DV>
+__global__ void __launch_bounds__(256) deferred_merge_warp_kernel(ArenaGeom g, DecodeWork w,
+                                                             DecodeArgs a, int group,
+                                                             int head_groups) {
+    static_assert(DV % 32 == 0, "DV must be a multiple of 32");
+    const int lane = threadIdx.x & 31;
+    const int per_entry = head_groups * GP;
+    const int item = static_cast<int>(blockIdx.x) * 8 + static_cast<int>(threadIdx.x >> 5);
+    const bool live = item < w.n_deferred * per_entry;
+    const int di = live ? item / per_entry : 0;
+    const int y = item - di * per_entry;
+    const int hg = y / GP;
+    const int gg = y - hg * GP;
+    // the merge list comes from the step's host copy; the partials are the previous
+    // (decode) kernel's output
+    const int mi = live ? __ldg(w.merge_deferred + di) : 0;
+    const int seg = live ? __ldg(w.merge_seg + mi) : 0;
+    const int s0 = live ? __ldg(w.merge_slot0 + mi) : 0;
+    const int ns = live ? __ldg(w.merge_nslots + mi) : 0;
+    const int b = seg / g.heads_kv;
+    const int h = seg - b * g.heads_kv;
+    const int q_head0 = h * group + hg * GP;
+    const int gcount = min(GP, group - hg * GP);
+    pdl_launch_dependents();
+    pdl_wait();
+    if (!live || gg >= gcount) return;
+    const int64_t base = (static_cast<int64_t>(hg) * w.n_slots + s0) * GP + gg;  // + s * GP
+    float M, L, A[DV / 32];
+    merge_slots<GP, DV>(a, base, 0, ns, lane, M, L, A);
+    finish_row<DV>(a, b, q_head0 + gg, M, L, A, lane);
+}
+
+// The same merge when some segment has more than kWarpMergeMaxSlots slots: one CTA of eight
+// warps per (deferred segment, head group x head).  Warp w merges an eighth of the slots as
+// above; the eight partial results are combined through shared memory by warp 0.
 template <int GP, int DV>
 __global__ void __launch_bounds__(256) deferred_merge_cta_kernel(ArenaGeom g, DecodeWork w,
                                                              DecodeArgs a, int group) {
-    constexpr int T = 256;
-    constexpr int SL = T / DV;
-    static_assert(SL >= 1 && DV * SL == T, "DV must divide 256");
-    constexpr float kL2e = 1.4426950408889634f;
-    __shared__ float red[T];
-    __shared__ float wred[T / 32];
-    const int t = threadIdx.x;
+    constexpr int EPLV = DV / 32;
+    constexpr int NW = 8;
+    __shared__ float sm_m[NW], sm_l[NW];
+    __shared__ __align__(16) float sm_a[NW][DV];
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
     const int hg = blockIdx.y / GP;
     const int gg = blockIdx.y - hg * GP;
     const int mi = __ldg(w.merge_deferred + blockIdx.x);
@@ -259,59 +275,32 @@ __global__ void __launch_bounds__(256) deferred_merge_cta_kernel(ArenaGeom g, De
     pdl_wait();
     if (gg >= gcount) return;
     const int64_t base = (static_cast<int64_t>(hg) * w.n_slots + s0) * GP + gg;  // + s * GP
-    auto block_reduce = [&](float v, bool is_max) {
+    const int per = (ns + NW - 1) / NW;
+    const int lo = min(ns, warp * per), hi = min(ns, lo + per);
+    float M, L, A[EPLV];
+    merge_slots<GP, DV>(a, base, lo, hi, lane, M, L, A);
+    if (lane == 0) {
+        sm_m[warp] = M;
+        sm_l[warp] = L;
+    }
 #pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) {
-            const float u = __shfl_xor_sync(0xffffffffu, v, o);
-            v = is_max ? fmaxf(v, u) : v + u;
-        }
-        if ((t & 31) == 0) wred[t >> 5] = v;
-        __syncthreads();
-        float r = wred[0];
+    for (int e = 0; e < EPLV; ++e) sm_a[warp][lane * EPLV + e] = A[e];
+    __syncthreads();
+    if (warp != 0) return;
+    float Mt = sm_m[0];
 #pragma unroll
-        for (int i = 1; i < T / 32; ++i) r = is_max ? fmaxf(r, wred[i]) : r + wred[i];
-        __syncthreads();
-        return r;
-    };
-    float M = -INFINITY;
-    for (int s = t; s < ns; s += T) M = fmaxf(M, __ldcg(a.part_ml + (base + s * GP) * 2));
-    M = block_reduce(M, true);
-    float L = 0.f;
-    if (M != -INFINITY) {
-        for (int s = t; s < ns; s += T) {
-            const int64_t ps = base + s * GP;
-            L += __ldcg(a.part_ml + ps * 2 + 1) * exp2f(__ldcg(a.part_ml + ps * 2) - M);
-        }
-    }
-    L = block_reduce(L, false);
-    const int d = t % DV;
-    const int sl = t / DV;
-    float A = 0.f;
-    if (M != -INFINITY) {
-#pragma unroll 4
-        for (int s = sl; s < ns; s += SL) {
-            const int64_t ps = base + s * GP;
-            A = fmaf(exp2f(__ldcg(a.part_ml + ps * 2) - M), __ldcg(a.part_acc + ps * DV + d), A);
-        }
-    }
-    if constexpr (SL > 1) {
-        red[t] = A;
-        __syncthreads();
-        if (sl != 0) return;
+    for (int k = 1; k < NW; ++k) Mt = fmaxf(Mt, sm_m[k]);
+    float Lt = 0.f, At[EPLV];
 #pragma unroll
-        for (int k = 1; k < SL; ++k) A += red[d + k * DV];
+    for (int e = 0; e < EPLV; ++e) At[e] = 0.f;
+#pragma unroll
+    for (int k = 0; k < NW; ++k) {
+        const float f = (sm_m[k] == -INFINITY || Mt == -INFINITY) ? 0.f : exp2f(sm_m[k] - Mt);
+        Lt = fmaf(sm_l[k], f, Lt);
+#pragma unroll
+        for (int e = 0; e < EPLV; ++e) At[e] = fmaf(f, sm_a[k][lane * EPLV + e], At[e]);
     }
-    const int qh = q_head0 + gg;
-    float f = 1.f, Mref = M;
-    if (a.sinks || a.has_sink_all) {
-        const float sk = (a.sinks ? __ldg(a.sinks + qh) : a.sink_all) * kL2e;
-        const float M2 = fmaxf(M, sk);
-        f = (M == -INFINITY) ? 0.f : exp2f(M - M2);
-        L = L * f + exp2f(sk - M2);
-        Mref = M2;
-    }
-    a.out[(static_cast<int64_t>(b) * a.n_heads + qh) * DV + d] = L > 0.f ? A * (f / L) : 0.f;
-    if (a.lse && d == 0) a.lse[static_cast<int64_t>(b) * a.n_heads + qh] = lse_ln(Mref, L);
+    finish_row<DV>(a, b, q_head0 + gg, Mt, Lt, At, lane);
 }
 
 // Cross-part merge of normalised outputs with their log-sum-exps (multi-GPU split-KV: the

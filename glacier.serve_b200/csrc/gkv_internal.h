@@ -89,8 +89,8 @@ void plan_work_into(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, in
 // kMinChunksPerWorker chunks each, at most max_ctas CTAs of `warps` workers, >= 1 CTA when
 // there is work.
 int64_t decode_grid_ctas(int64_t total_chunks, int warps, int64_t max_ctas);
-// Mean partial slots of the deferred merge entries, rounded up (selects the merge form).
-int32_t deferred_avg_slots(const int32_t* merge_nslots, const int32_t* merge_deferred, int32_t n_deferred);
+// Largest partial-slot count of the deferred merge entries (selects the merge form).
+int32_t deferred_max_slots(const int32_t* merge_nslots, const int32_t* merge_deferred, int32_t n_deferred);
 
 struct WorkList {
     std::vector<int32_t> piece_seg, piece_c0, piece_c1, piece_slot, piece_merge, merge_deferred;

@@ -629,7 +629,7 @@ cudaError_t launch_lse_merge(const float* parts, int n_parts, int rows, int dv, 
 cudaError_t launch_deferred_merge(const ArenaGeom& g, const DecodeWork& w, const DecodeArgs& a,
                                   int group, int gp, int head_groups, cudaStream_t st) {
     if (w.n_deferred <= 0) return cudaSuccess;
-    const bool warp_form = w.deferred_avg_slots <= kWarpMergeMaxSlots;
+    const bool warp_form = w.deferred_max_slots <= kWarpMergeMaxSlots;
     // warp form: one warp per (deferred segment, head), eight per CTA; CTA form: one CTA each
     const int64_t items = static_cast<int64_t>(w.n_deferred) * head_groups * gp;
     const dim3 wgrid(static_cast<unsigned>((items + 7) / 8));

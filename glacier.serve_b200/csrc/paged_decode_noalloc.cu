@@ -222,7 +222,7 @@ extern "C" int gkv_paged_decode_noalloc(const gkv_arena_desc* arena, int32_t lay
     w.merge_count = reinterpret_cast<int32_t*>(dbase + L.counters);
     w.merge_deferred = dp(L.mdef);
     w.n_deferred = ndef;
-    w.deferred_avg_slots = deferred_avg_slots(at(L.mns), at(L.mdef), ndef);
+    w.deferred_max_slots = deferred_max_slots(at(L.mns), at(L.mdef), ndef);
 
     DecodeArgs a{};
     a.layer = layer;

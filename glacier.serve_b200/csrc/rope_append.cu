@@ -6,9 +6,11 @@
 // AddVector of the q/k/v biases (:612-614), ApplyQkNorm, a per-head RMSNorm of q and k
 // (:616, :713-732), QuantKernels.RoPE with the YaRN inverse-frequency table and mscale
 // (:619-631), and pool.Store of k and v (:634).  One launch does all of it for every token of
-// the step: each warp takes one (token, head) row of q, k or v; q rows are written back in
-// place (ready for the decode or prefill that follows), k and v rows go straight into their
-// arena slots, so the rotated k never makes a round trip through HBM.
+// the step: each warp takes one token; q rows are written back in place (ready for the decode
+// or prefill that follows), k and v rows go straight into their arena slots, so the rotated k
+// never makes a round trip through HBM.  The rotation angles depend on the position only, so a
+// lane computes its few (sin, cos) pairs once and applies them to every q and k head of the
+// token.
 //
 // The formulas of QuantKernels.RMSNorm and QuantKernels.RoPE are not in the reference tree
 // (NuGet Glacier.Inference 1.7.0); the ones computed here are stated next to each step, and
@@ -80,15 +82,35 @@ __device__ __forceinline__ void store_elem<__nv_bfloat16>(__nv_bfloat16* p, floa
 template <>
 __device__ __forceinline__ void store_elem<__half>(__half* p, float x) { *p = __float2half_rn(x); }
 
+// Angles of the pairs this lane's E elements belong to, for position pos: (sin, cos) per element
+// (elements from rope_dim on get none).  NEOX pairs (i, i + R/2): element j < R/2 is pair j, and
+// j >= R/2 pair j - R/2; interleaved pairs (2i, 2i+1): element j is pair j/2.  The angle is
+// pos * inv_freq[i], one fp32 multiply.
+template <int E>
+__device__ __forceinline__ void lane_angles(const RopeArgs& a, int pos, int lane, float (&sn)[E], float (&cs)[E]) {
+    const int R = a.rope_dim;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const int j = lane * E + e;
+        sn[e] = 0.f;
+        cs[e] = 1.f;
+        if (j < R) {
+            const int i = a.style == 0 ? (j < R / 2 ? j : j - R / 2) : j / 2;
+            rope_sincos(__fmul_rn(static_cast<float>(pos), __ldg(a.inv_freq + i)), sn[e], cs[e]);
+        }
+    }
+}
+
 // One q or k head row of D = 32 * E elements, lane l holding elements [l*E, (l+1)*E): bias,
-// RMSNorm, rotation.  RMSNorm: lane l sums the squares of its elements in order (x*x, then
-// fused multiply-adds), a butterfly over lanes 16, 8, 4, 2, 1 adds the partial sums (every lane
-// ends with the same value), r = sqrt(sum / D + eps), y = (x / r) * w.  Rotation of pair
-// (a, b) by angle pos * inv_freq[i]: y_a = fma(x_a, c, -(x_b * s)), y_b = fma(x_b, c, x_a * s),
-// each times mscale.
+// RMSNorm, rotation with the lane's precomputed angles.  RMSNorm: lane l sums the squares of its
+// elements in order (x*x, then fused multiply-adds), a butterfly over lanes 16, 8, 4, 2, 1 adds
+// the partial sums (every lane ends with the same value), r = sqrt(sum / D + eps),
+// y = (x / r) * w.  Rotation of pair (a, b): y_a = fma(x_a, c, -(x_b * s)),
+// y_b = fma(x_b, c, x_a * s), each times mscale.
 template <int E>
 __device__ __forceinline__ void prologue_row(float (&x)[E], const float* bias, const float* norm,
-                                             const RopeArgs& a, int pos, int lane) {
+                                             const RopeArgs& a, const float (&sn)[E], const float (&cs)[E],
+                                             int lane) {
     constexpr int D = 32 * E;
     if (bias) {
 #pragma unroll
@@ -116,14 +138,11 @@ __device__ __forceinline__ void prologue_row(float (&x)[E], const float* bias, c
 #pragma unroll
         for (int e = 0; e < E; ++e) {
             const float other = __shfl_sync(0xffffffffu, x[e], src & 31);
-            const int j = lane * E + e;
             y[e] = x[e];
-            if (j < R) {
-                const int i = low ? j : j - half;
-                float s, c;
-                rope_sincos(__fmul_rn(static_cast<float>(pos), __ldg(a.inv_freq + i)), s, c);
+            if (lane * E + e < R) {
                 // low element: y = x*c - other*s; high element: y = x*c + other*s
-                y[e] = low ? __fmaf_rn(x[e], c, -__fmul_rn(other, s)) : __fmaf_rn(x[e], c, __fmul_rn(other, s));
+                y[e] = low ? __fmaf_rn(x[e], cs[e], -__fmul_rn(other, sn[e]))
+                           : __fmaf_rn(x[e], cs[e], __fmul_rn(other, sn[e]));
                 y[e] = __fmul_rn(y[e], a.mscale);
             }
         }
@@ -134,50 +153,83 @@ __device__ __forceinline__ void prologue_row(float (&x)[E], const float* bias, c
         if constexpr (E % 2 == 0) {
 #pragma unroll
             for (int e = 0; e < E; e += 2) {
-                const int j = lane * E + e;
-                if (j < R) {
-                    float s, c;
-                    rope_sincos(__fmul_rn(static_cast<float>(pos), __ldg(a.inv_freq + j / 2)), s, c);
+                if (lane * E + e < R) {
                     const float x0 = x[e], x1 = x[e + 1];
-                    x[e] = __fmul_rn(__fmaf_rn(x0, c, -__fmul_rn(x1, s)), a.mscale);
-                    x[e + 1] = __fmul_rn(__fmaf_rn(x1, c, __fmul_rn(x0, s)), a.mscale);
+                    x[e] = __fmul_rn(__fmaf_rn(x0, cs[e], -__fmul_rn(x1, sn[e])), a.mscale);
+                    x[e + 1] = __fmul_rn(__fmaf_rn(x1, cs[e], __fmul_rn(x0, sn[e])), a.mscale);
                 }
             }
         } else {
             const float other = __shfl_xor_sync(0xffffffffu, x[0], 1);
             if (lane < R) {
-                float s, c;
-                rope_sincos(__fmul_rn(static_cast<float>(pos), __ldg(a.inv_freq + lane / 2)), s, c);
                 const bool even = (lane & 1) == 0;
-                x[0] = even ? __fmaf_rn(x[0], c, -__fmul_rn(other, s)) : __fmaf_rn(x[0], c, __fmul_rn(other, s));
+                x[0] = even ? __fmaf_rn(x[0], cs[0], -__fmul_rn(other, sn[0]))
+                            : __fmaf_rn(x[0], cs[0], __fmul_rn(other, sn[0]));
                 x[0] = __fmul_rn(x[0], a.mscale);
             }
         }
     }
 }
 
-// Rows per token: n_heads q rows, heads_kv k rows, heads_kv v rows; one warp per row.
+template <int E>
+__device__ __forceinline__ void load_row(const float* p, float (&x)[E]) {
+    if constexpr (E % 4 == 0) {
+#pragma unroll
+        for (int e = 0; e < E; e += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(p + e);
+            x[e] = v.x;
+            x[e + 1] = v.y;
+            x[e + 2] = v.z;
+            x[e + 3] = v.w;
+        }
+    } else if constexpr (E == 2) {
+        const float2 v = *reinterpret_cast<const float2*>(p);
+        x[0] = v.x;
+        x[1] = v.y;
+    } else {
+        x[0] = *p;
+    }
+}
+
+template <int E>
+__device__ __forceinline__ void store_row(float* p, const float (&x)[E]) {
+    if constexpr (E % 4 == 0) {
+#pragma unroll
+        for (int e = 0; e < E; e += 4) *reinterpret_cast<float4*>(p + e) = make_float4(x[e], x[e + 1], x[e + 2], x[e + 3]);
+    } else if constexpr (E == 2) {
+        *reinterpret_cast<float2*>(p) = make_float2(x[0], x[1]);
+    } else {
+        *p = x[0];
+    }
+}
+
+// One warp per token: the lane's angles are computed once and serve every q and k head of the
+// token; q heads go U at a time (their loads issued together), then the k heads into the arena,
+// then the v heads.
 template <typename KV, int E>
 __global__ void __launch_bounds__(256) rope_append_kernel(ArenaGeom g, RopeArgs a) {
     constexpr int D = 32 * E;
+    constexpr int U = 4;
     const int lane = threadIdx.x & 31;
-    const int per_tok = a.n_heads + 2 * g.heads_kv;
-    const int64_t total = static_cast<int64_t>(a.n_tok) * per_tok;
-    const int64_t n_warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-    for (int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; row < total;
-         row += n_warps) {
-        const int t = static_cast<int>(row / per_tok);
-        const int j = static_cast<int>(row - static_cast<int64_t>(t) * per_tok);
+    const int n_warps = static_cast<int>((static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5);
+    for (int t = static_cast<int>((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5); t < a.n_tok;
+         t += n_warps) {
         const int pos = __ldg(a.positions + t);
-        if (j < a.n_heads) {  // q head j: rewritten in place
-            float* qp = a.q + (static_cast<int64_t>(t) * a.n_heads + j) * D + lane * E;
-            float x[E];
+        float sn[E], cs[E];
+        lane_angles<E>(a, pos, lane, sn, cs);
+        float* qt = a.q + static_cast<int64_t>(t) * a.n_heads * D + lane * E;
+        for (int h0 = 0; h0 < a.n_heads; h0 += U) {
+            float x[U][E];
 #pragma unroll
-            for (int e = 0; e < E; ++e) x[e] = qp[e];
-            prologue_row<E>(x, a.q_bias ? a.q_bias + j * D : nullptr, a.q_norm, a, pos, lane);
+            for (int u = 0; u < U; ++u)
+                if (h0 + u < a.n_heads) load_row<E>(qt + (h0 + u) * D, x[u]);
 #pragma unroll
-            for (int e = 0; e < E; ++e) qp[e] = x[e];
-            continue;
+            for (int u = 0; u < U; ++u) {
+                if (h0 + u < a.n_heads) {  // warp-uniform
+                    prologue_row<E>(x[u], a.q_bias ? a.q_bias + (h0 + u) * D : nullptr, a.q_norm, a, sn, cs, lane);
+                    store_row<E>(qt + (h0 + u) * D, x[u]);
+                }
+            }
         }
         const int64_t slot = __ldg(a.slots + t);
         if (slot < 0) continue;  // padding token: nothing to store
@@ -187,20 +239,25 @@ __global__ void __launch_bounds__(256) rope_append_kernel(ArenaGeom g, RopeArgs 
             if (lane == 0 && a.err) atomicOr(a.err, kErrBadSlot);
             continue;
         }
-        if (j < a.n_heads + g.heads_kv) {  // k head h: prologue, then the arena
-            const int h = j - a.n_heads;
-            const float* kp = a.k + (static_cast<int64_t>(t) * g.heads_kv + h) * D + lane * E;
-            float x[E];
+        const float* kt = a.k + static_cast<int64_t>(t) * g.heads_kv * D + lane * E;
+        for (int h0 = 0; h0 < g.heads_kv; h0 += U) {
+            float x[U][E];
 #pragma unroll
-            for (int e = 0; e < E; ++e) x[e] = __ldg(kp + e);
-            prologue_row<E>(x, a.k_bias ? a.k_bias + h * D : nullptr, a.k_norm, a, pos, lane);
-            KV* dst = static_cast<KV*>(g.k) + blk * g.k_block_stride + a.layer * g.k_layer_stride +
-                      h * g.k_head_stride + static_cast<int64_t>(off) * D + lane * E;
+            for (int u = 0; u < U; ++u)
+                if (h0 + u < g.heads_kv) load_row<E>(kt + (h0 + u) * D, x[u]);
 #pragma unroll
-            for (int e = 0; e < E; ++e) store_elem<KV>(dst + e, x[e]);
-        } else {  // v head h: bias, then the arena
-            const int h = j - a.n_heads - g.heads_kv;
-            const int dv = g.v_head_dim;
+            for (int u = 0; u < U; ++u) {
+                if (h0 + u < g.heads_kv) {
+                    prologue_row<E>(x[u], a.k_bias ? a.k_bias + (h0 + u) * D : nullptr, a.k_norm, a, sn, cs, lane);
+                    KV* dst = static_cast<KV*>(g.k) + blk * g.k_block_stride + a.layer * g.k_layer_stride +
+                              (h0 + u) * g.k_head_stride + static_cast<int64_t>(off) * D + lane * E;
+#pragma unroll
+                    for (int e = 0; e < E; ++e) store_elem<KV>(dst + e, x[u][e]);
+                }
+            }
+        }
+        const int dv = g.v_head_dim;
+        for (int h = 0; h < g.heads_kv; ++h) {
             const float* vp = a.v + (static_cast<int64_t>(t) * g.heads_kv + h) * dv;
             KV* dst = static_cast<KV*>(g.v) + blk * g.v_block_stride + a.layer * g.v_layer_stride +
                       h * g.v_head_stride + static_cast<int64_t>(off) * dv;
@@ -215,8 +272,7 @@ __global__ void __launch_bounds__(256) rope_append_kernel(ArenaGeom g, RopeArgs 
 
 template <typename KV>
 cudaError_t launch_typed(const ArenaGeom& g, const RopeArgs& a, cudaStream_t st) {
-    const int64_t rows = static_cast<int64_t>(a.n_tok) * (a.n_heads + 2 * g.heads_kv);
-    int64_t blocks = (rows * 32 + 255) / 256;
+    int64_t blocks = (static_cast<int64_t>(a.n_tok) * 32 + 255) / 256;  // a warp per token
     if (blocks > 148 * 8) blocks = 148 * 8;
     if (blocks < 1) blocks = 1;
     const dim3 grid(static_cast<unsigned>(blocks));

@@ -206,10 +206,10 @@ void build_work_list(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, i
     W.total_chunks = A.total_chunks;
 }
 
-int32_t deferred_avg_slots(const int32_t* merge_nslots, const int32_t* merge_deferred, int32_t n_deferred) {
-    int64_t sum = 0;
-    for (int32_t k = 0; k < n_deferred; ++k) sum += merge_nslots[merge_deferred[k]];
-    return n_deferred > 0 ? static_cast<int32_t>((sum + n_deferred - 1) / n_deferred) : 0;
+int32_t deferred_max_slots(const int32_t* merge_nslots, const int32_t* merge_deferred, int32_t n_deferred) {
+    int32_t mx = 0;
+    for (int32_t k = 0; k < n_deferred; ++k) mx = std::max(mx, merge_nslots[merge_deferred[k]]);
+    return mx;
 }
 
 int64_t decode_grid_ctas(int64_t total_chunks, int warps, int64_t max_ctas) {
@@ -220,8 +220,8 @@ int64_t decode_grid_ctas(int64_t total_chunks, int warps, int64_t max_ctas) {
     return ctas < 1 ? 1 : ctas;
 }
 
-static int32_t deferred_avg_slots(const WorkList& W) {
-    return deferred_avg_slots(W.merge_nslots.data(), W.merge_deferred.data(),
+static int32_t deferred_max_slots(const WorkList& W) {
+    return deferred_max_slots(W.merge_nslots.data(), W.merge_deferred.data(),
                               static_cast<int32_t>(W.merge_deferred.size()));
 }
 
@@ -478,7 +478,7 @@ int step_upload(Pool* p, const int32_t* tables, int32_t batch, int32_t max_block
     w.n_merge = static_cast<int32_t>(n_merge);
     w.merge_deferred = reinterpret_cast<const int32_t*>(d + L.mdef);
     w.n_deferred = static_cast<int32_t>(W.merge_deferred.size());
-    w.deferred_avg_slots = deferred_avg_slots(W);
+    w.deferred_max_slots = deferred_max_slots(W);
     w.merge_count = ws.d_merge_count;
     w.table_row = nullptr;
     ws.d_slots = reinterpret_cast<const int64_t*>(d + L.slots);
@@ -800,7 +800,7 @@ int step_prefill(Pool* p, int32_t layer, const void* d_q, int32_t q_dtype, float
     w.n_merge = static_cast<int32_t>(n_merge);
     w.merge_deferred = at(L.mdef);
     w.n_deferred = static_cast<int32_t>(W.merge_deferred.size());
-    w.deferred_avg_slots = deferred_avg_slots(W);
+    w.deferred_max_slots = deferred_max_slots(W);
     w.merge_count = ws.d_merge_count;
     w.table_row = at(rows_off);
     const float* qf = static_cast<const float*>(d_q);
