@@ -58,3 +58,10 @@ def test_version_and_error_string():
 
     assert "sm_100a" in glacier_kv.version()
     assert isinstance(glacier_kv.last_error(), str)
+
+
+def test_integration_guide_binds_every_declared_symbol():
+    """INTEGRATION.md's C# P/Invoke layer has a [LibraryImport] line for every entry point."""
+    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    bound = set(re.findall(r'EntryPoint = "(gkv_\w+)"', doc))
+    assert bound == _declared(), sorted(bound ^ _declared())
