@@ -213,19 +213,36 @@ __device__ __forceinline__ void finish_row(const DecodeArgs& a, int b, int qh, f
 }
 
 // Merge of the segments split into more than kFusedMergeMaxSlots pieces, run as a second
-// launch, when no deferred segment has more than kWarpMergeMaxSlots slots: one warp per
-// (deferred segment, head of a head group), eight per CTA.
+// launch.  The deferred list starts with the w.n_deferred_long segments of more than
+// kWarpMergeMaxSlots slots: each (long segment, head of a head group) gets a CTA of eight warps,
+// warp k merging an eighth of the slots, the eight results combined through shared memory by warp
+// 0.  The remaining (short segment, head) items get one warp each, eight per CTA, after the long
+// ones.  Every CTA has one role, so the barrier is CTA-uniform.
 template <int GP, int DV>
-__global__ void __launch_bounds__(256) deferred_merge_warp_kernel(ArenaGeom g, DecodeWork w,
-                                                             DecodeArgs a, int group,
-                                                             int head_groups) {
+__global__ void __launch_bounds__(256) deferred_merge_kernel(ArenaGeom g, DecodeWork w, DecodeArgs a, int group,
+                                                         int head_groups) {
     static_assert(DV % 32 == 0, "DV must be a multiple of 32");
+    constexpr int EPLV = DV / 32;
+    constexpr int NW = 8;
+    __shared__ float sm_m[NW], sm_l[NW];
+    __shared__ __align__(16) float sm_a[NW][DV];
+    const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int per_entry = head_groups * GP;
-    const int item = static_cast<int>(blockIdx.x) * 8 + static_cast<int>(threadIdx.x >> 5);
-    const bool live = item < w.n_deferred * per_entry;
-    const int di = live ? item / per_entry : 0;
-    const int y = item - di * per_entry;
+    const int long_ctas = w.n_deferred_long * per_entry;
+    const bool cta_role = static_cast<int>(blockIdx.x) < long_ctas;
+    int di, y;
+    bool live = true;
+    if (cta_role) {
+        di = static_cast<int>(blockIdx.x) / per_entry;
+        y = static_cast<int>(blockIdx.x) - di * per_entry;
+    } else {
+        const int item = (static_cast<int>(blockIdx.x) - long_ctas) * NW + warp;
+        live = item < (w.n_deferred - w.n_deferred_long) * per_entry;
+        const int k = live ? item / per_entry : 0;
+        y = item - k * per_entry;
+        di = w.n_deferred_long + k;
+    }
     const int hg = y / GP;
     const int gg = y - hg * GP;
     // the merge list comes from the step's host copy; the partials are the previous
@@ -240,44 +257,16 @@ __global__ void __launch_bounds__(256) deferred_merge_warp_kernel(ArenaGeom g, D
     const int gcount = min(GP, group - hg * GP);
     pdl_launch_dependents();
     pdl_wait();
-    if (!live || gg >= gcount) return;
+    if (!live || gg >= gcount) return;  // CTA-uniform in the CTA role
     const int64_t base = (static_cast<int64_t>(hg) * w.n_slots + s0) * GP + gg;  // + s * GP
-    float M, L, A[DV / 32];
-    merge_slots<GP, DV>(a, base, 0, ns, lane, M, L, A);
-    finish_row<DV>(a, b, q_head0 + gg, M, L, A, lane);
-}
-
-// The same merge when some segment has more than kWarpMergeMaxSlots slots: one CTA of eight
-// warps per (deferred segment, head group x head).  Warp w merges an eighth of the slots as
-// above; the eight partial results are combined through shared memory by warp 0.
-template <int GP, int DV>
-__global__ void __launch_bounds__(256) deferred_merge_cta_kernel(ArenaGeom g, DecodeWork w,
-                                                             DecodeArgs a, int group) {
-    constexpr int EPLV = DV / 32;
-    constexpr int NW = 8;
-    __shared__ float sm_m[NW], sm_l[NW];
-    __shared__ __align__(16) float sm_a[NW][DV];
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const int hg = blockIdx.y / GP;
-    const int gg = blockIdx.y - hg * GP;
-    const int mi = __ldg(w.merge_deferred + blockIdx.x);
-    const int seg = __ldg(w.merge_seg + mi);
-    const int s0 = __ldg(w.merge_slot0 + mi);
-    const int ns = __ldg(w.merge_nslots + mi);
-    const int b = seg / g.heads_kv;
-    const int h = seg - b * g.heads_kv;
-    const int q_head0 = h * group + hg * GP;
-    const int gcount = min(GP, group - hg * GP);
-    // the merge list above comes from the step's host copy; the partials are the previous
-    // (decode) kernel's output
-    pdl_launch_dependents();
-    pdl_wait();
-    if (gg >= gcount) return;
-    const int64_t base = (static_cast<int64_t>(hg) * w.n_slots + s0) * GP + gg;  // + s * GP
+    float M, L, A[EPLV];
+    if (!cta_role) {
+        merge_slots<GP, DV>(a, base, 0, ns, lane, M, L, A);
+        finish_row<DV>(a, b, q_head0 + gg, M, L, A, lane);
+        return;
+    }
     const int per = (ns + NW - 1) / NW;
     const int lo = min(ns, warp * per), hi = min(ns, lo + per);
-    float M, L, A[EPLV];
     merge_slots<GP, DV>(a, base, lo, hi, lane, M, L, A);
     if (lane == 0) {
         sm_m[warp] = M;

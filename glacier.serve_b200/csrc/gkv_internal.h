@@ -82,6 +82,7 @@ struct PlanArrays {
     // results
     int32_t n_pieces, n_slots, n_merge, n_deferred;
     int64_t total_chunks;
+    int32_t n_deferred_long;  // leading deferred entries with more than kWarpMergeMaxSlots slots
 };
 void plan_work_into(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, int32_t block_size,
                     int32_t n_workers, PlanArrays* out);
@@ -89,14 +90,13 @@ void plan_work_into(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, in
 // kMinChunksPerWorker chunks each, at most max_ctas CTAs of `warps` workers, >= 1 CTA when
 // there is work.
 int64_t decode_grid_ctas(int64_t total_chunks, int warps, int64_t max_ctas);
-// Largest partial-slot count of the deferred merge entries (selects the merge form).
-int32_t deferred_max_slots(const int32_t* merge_nslots, const int32_t* merge_deferred, int32_t n_deferred);
 
 struct WorkList {
     std::vector<int32_t> piece_seg, piece_c0, piece_c1, piece_slot, piece_merge, merge_deferred;
     std::vector<int32_t> worker_begin;  // n_workers + 1
     std::vector<int32_t> merge_seg, merge_slot0, merge_nslots;
     int32_t n_slots = 0;
+    int32_t n_deferred_long = 0;
     int64_t total_chunks = 0;
 };
 

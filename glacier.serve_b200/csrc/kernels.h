@@ -74,10 +74,10 @@ constexpr int kFusedMergeMaxSlots = 0;
 // fp32 decode from 0.782 to 0.807 of HBM and bf16 from 0.727 to 0.774; 8 was worse than 4;
 // the uniform 64 x 2049 batch was unchanged.
 constexpr int64_t kSegmentCost = 4;
-// Deferred merges run one warp per (segment, head) when no deferred segment has more than this
-// many slots, else one CTA of eight warps per (segment, head).  The longest segment bounds the
-// merge: on a lognormal 32-sequence batch one 21k-token sequence split into 240 slots took a
-// lone warp 18 us while the other 1000 merges took 3 us.
+// A deferred merge of a segment with more than this many slots gets a CTA of eight warps per
+// (segment, head), the others one warp each (eight per CTA), in the same launch.  On a lognormal
+// 32-sequence batch one 21k-token sequence split into 240 slots took a lone warp 18 us while the
+// other 1000 merges took 3 us; a CTA for every merge took 9 us (3.5 waves of mostly idle warps).
 constexpr int kWarpMergeMaxSlots = 32;
 
 // Work list of one step, built on the host (all pointers are device pointers).
@@ -106,7 +106,7 @@ struct DecodeWork {
     int32_t n_merge;
     const int32_t* merge_deferred;     // [n_deferred] merge entries left to the merge kernel
     int32_t n_deferred;
-    int32_t deferred_max_slots;        // most slots of a deferred entry (selects the merge form)
+    int32_t n_deferred_long;           // the first entries of merge_deferred with > kWarpMergeMaxSlots slots
     // Arrival counters of the fused merge, [head_groups][n_merge] ints.  They must be zero
     // when a launch starts; the worker that completes a segment resets its counter, so they
     // are zero again after every launch that ran to completion.

@@ -629,22 +629,18 @@ cudaError_t launch_lse_merge(const float* parts, int n_parts, int rows, int dv, 
 cudaError_t launch_deferred_merge(const ArenaGeom& g, const DecodeWork& w, const DecodeArgs& a,
                                   int group, int gp, int head_groups, cudaStream_t st) {
     if (w.n_deferred <= 0) return cudaSuccess;
-    const bool warp_form = w.deferred_max_slots <= kWarpMergeMaxSlots;
-    // warp form: one warp per (deferred segment, head), eight per CTA; CTA form: one CTA each
-    const int64_t items = static_cast<int64_t>(w.n_deferred) * head_groups * gp;
-    const dim3 wgrid(static_cast<unsigned>((items + 7) / 8));
-    const dim3 cgrid(static_cast<unsigned>(w.n_deferred), static_cast<unsigned>(head_groups * gp));
-    auto go = [&](auto wkern, auto ckern) {
-        return warp_form ? launch_pdl(wkern, wgrid, dim3(256), 0, st, g, w, a, group, head_groups)
-                         : launch_pdl(ckern, cgrid, dim3(256), 0, st, g, w, a, group);
-    };
-#define GKV_MERGE_DV(GPV)                                                                  \
-    switch (g.v_head_dim) {                                                               \
-        case 32: return go(deferred_merge_warp_kernel<GPV, 32>, deferred_merge_cta_kernel<GPV, 32>);    \
-        case 64: return go(deferred_merge_warp_kernel<GPV, 64>, deferred_merge_cta_kernel<GPV, 64>);    \
-        case 128: return go(deferred_merge_warp_kernel<GPV, 128>, deferred_merge_cta_kernel<GPV, 128>); \
-        case 256: return go(deferred_merge_warp_kernel<GPV, 256>, deferred_merge_cta_kernel<GPV, 256>); \
-        default: return cudaErrorInvalidValue;                                            \
+    // a CTA per (long segment, head), then a warp per (short segment, head), eight per CTA
+    const int64_t per_entry = static_cast<int64_t>(head_groups) * gp;
+    const int64_t short_items = static_cast<int64_t>(w.n_deferred - w.n_deferred_long) * per_entry;
+    const dim3 grid(static_cast<unsigned>(w.n_deferred_long * per_entry + (short_items + 7) / 8));
+    auto go = [&](auto kern) { return launch_pdl(kern, grid, dim3(256), 0, st, g, w, a, group, head_groups); };
+#define GKV_MERGE_DV(GPV)                                                      \
+    switch (g.v_head_dim) {                                                   \
+        case 32: return go(deferred_merge_kernel<GPV, 32>);                   \
+        case 64: return go(deferred_merge_kernel<GPV, 64>);                   \
+        case 128: return go(deferred_merge_kernel<GPV, 128>);                 \
+        case 256: return go(deferred_merge_kernel<GPV, 256>);                 \
+        default: return cudaErrorInvalidValue;                                \
     }
     switch (gp) {
         case 1: GKV_MERGE_DV(1)

@@ -181,7 +181,7 @@ extern "C" int gkv_paged_decode_noalloc(const gkv_arena_desc* arena, int32_t lay
     memcpy(h + L.ctx, h_ctx_lens, static_cast<size_t>(batch) * 4);
     auto at = [&](size_t off) { return reinterpret_cast<int32_t*>(h + off); };
     PlanArrays P{at(L.pseg), at(L.pc0), at(L.pc1), at(L.pslot), at(L.pmerge), at(L.wbeg),
-                 at(L.mseg), at(L.ms0), at(L.mns), at(L.mdef), 0, 0, 0, 0, 0};
+                 at(L.mseg), at(L.ms0), at(L.mns), at(L.mdef), 0, 0, 0, 0, 0, 0};
     plan_work_into(h_ctx_lens, batch, A.heads_kv, bs, n_workers, &P);
     const int32_t nslots = P.n_slots, nmerge = P.n_merge, ndef = P.n_deferred;
     // the fused merge's arrival counters must start at zero on every call
@@ -222,7 +222,7 @@ extern "C" int gkv_paged_decode_noalloc(const gkv_arena_desc* arena, int32_t lay
     w.merge_count = reinterpret_cast<int32_t*>(dbase + L.counters);
     w.merge_deferred = dp(L.mdef);
     w.n_deferred = ndef;
-    w.deferred_max_slots = deferred_max_slots(at(L.mns), at(L.mdef), ndef);
+    w.n_deferred_long = P.n_deferred_long;
 
     DecodeArgs a{};
     a.layer = layer;

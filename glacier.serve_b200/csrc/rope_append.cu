@@ -209,7 +209,7 @@ __device__ __forceinline__ void store_row(float* p, const float (&x)[E]) {
 template <typename KV, int E>
 __global__ void __launch_bounds__(256) rope_append_kernel(ArenaGeom g, RopeArgs a) {
     constexpr int D = 32 * E;
-    constexpr int U = 4;
+    constexpr int U = 8;
     const int lane = threadIdx.x & 31;
     const int n_warps = static_cast<int>((static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5);
     for (int t = static_cast<int>((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5); t < a.n_tok;

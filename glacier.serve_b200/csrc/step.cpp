@@ -180,9 +180,16 @@ void plan_work_into(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, in
         }
         i = j;
     }
+    // the merge kernel gives a segment of more than kWarpMergeMaxSlots slots a CTA of its own and
+    // the others a warp each: the long ones go first in the deferred list
+    std::stable_partition(A.merge_deferred, A.merge_deferred + deferred,
+                          [&](int32_t m) { return A.merge_nslots[m] > kWarpMergeMaxSlots; });
+    int32_t n_long = 0;
+    while (n_long < deferred && A.merge_nslots[A.merge_deferred[n_long]] > kWarpMergeMaxSlots) ++n_long;
     A.n_slots = slots;
     A.n_merge = merges;
     A.n_deferred = deferred;
+    A.n_deferred_long = n_long;
 }
 
 void build_work_list(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, int32_t block_size,
@@ -196,21 +203,17 @@ void build_work_list(const int32_t* ctx_lens, int32_t batch, int32_t heads_kv, i
     W.worker_begin.resize(static_cast<size_t>(n_workers > 0 ? n_workers : 0) + 1);
     PlanArrays A{W.piece_seg.data(), W.piece_c0.data(), W.piece_c1.data(), W.piece_slot.data(),
                  W.piece_merge.data(), W.worker_begin.data(), W.merge_seg.data(), W.merge_slot0.data(),
-                 W.merge_nslots.data(), W.merge_deferred.data(), 0, 0, 0, 0, 0};
+                 W.merge_nslots.data(), W.merge_deferred.data(), 0, 0, 0, 0, 0, 0};
     plan_work_into(ctx_lens, batch, heads_kv, block_size, n_workers, &A);
     for (auto* v : {&W.piece_seg, &W.piece_c0, &W.piece_c1, &W.piece_slot, &W.piece_merge})
         v->resize(static_cast<size_t>(A.n_pieces));
     for (auto* v : {&W.merge_seg, &W.merge_slot0, &W.merge_nslots}) v->resize(static_cast<size_t>(A.n_merge));
     W.merge_deferred.resize(static_cast<size_t>(A.n_deferred));
     W.n_slots = A.n_slots;
+    W.n_deferred_long = A.n_deferred_long;
     W.total_chunks = A.total_chunks;
 }
 
-int32_t deferred_max_slots(const int32_t* merge_nslots, const int32_t* merge_deferred, int32_t n_deferred) {
-    int32_t mx = 0;
-    for (int32_t k = 0; k < n_deferred; ++k) mx = std::max(mx, merge_nslots[merge_deferred[k]]);
-    return mx;
-}
 
 int64_t decode_grid_ctas(int64_t total_chunks, int warps, int64_t max_ctas) {
     if (total_chunks <= 0) return 0;
@@ -220,10 +223,6 @@ int64_t decode_grid_ctas(int64_t total_chunks, int warps, int64_t max_ctas) {
     return ctas < 1 ? 1 : ctas;
 }
 
-static int32_t deferred_max_slots(const WorkList& W) {
-    return deferred_max_slots(W.merge_nslots.data(), W.merge_deferred.data(),
-                              static_cast<int32_t>(W.merge_deferred.size()));
-}
 
 // Sizes the pinned + device metadata buffers for `bytes`.  Only called while no step of
 // this pool is in use by a kernel that has not been ordered before the next upload
@@ -478,7 +477,7 @@ int step_upload(Pool* p, const int32_t* tables, int32_t batch, int32_t max_block
     w.n_merge = static_cast<int32_t>(n_merge);
     w.merge_deferred = reinterpret_cast<const int32_t*>(d + L.mdef);
     w.n_deferred = static_cast<int32_t>(W.merge_deferred.size());
-    w.deferred_max_slots = deferred_max_slots(W);
+    w.n_deferred_long = W.n_deferred_long;
     w.merge_count = ws.d_merge_count;
     w.table_row = nullptr;
     ws.d_slots = reinterpret_cast<const int64_t*>(d + L.slots);
@@ -800,7 +799,7 @@ int step_prefill(Pool* p, int32_t layer, const void* d_q, int32_t q_dtype, float
     w.n_merge = static_cast<int32_t>(n_merge);
     w.merge_deferred = at(L.mdef);
     w.n_deferred = static_cast<int32_t>(W.merge_deferred.size());
-    w.deferred_max_slots = deferred_max_slots(W);
+    w.n_deferred_long = W.n_deferred_long;
     w.merge_count = ws.d_merge_count;
     w.table_row = at(rows_off);
     const float* qf = static_cast<const float*>(d_q);

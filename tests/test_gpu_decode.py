@@ -77,6 +77,9 @@ CASES = [
     (16, 2, 128, 128, 8, "bf16", [37, 8, 1, 100]),  # tensor-core kernel, block size 8
     (8, 1, 128, 128, 24, "bf16", [50, 24, 25, 3]),  # tensor-core kernel, block size 24
     (56, 8, 128, 128, 16, "bf16", [9000, 17]),      # group 7, long sequence: fused merge
+    # long and short splits in one batch: the merge gives the long ones a CTA, the others a warp
+    (28, 4, 128, 128, 16, "f32", [12000, 700, 300, 90, 5]),
+    (28, 4, 128, 128, 16, "bf16", [20000, 900, 64, 33]),
     # fp16 storage (the reference GPU pools' precision): tensor-core and CUDA-core kernels
     (28, 4, 128, 128, 16, "f16", [1500, 16, 2, 333, 4097]),
     (64, 8, 128, 128, 16, "f16", [5000, 3, 640]),
