@@ -204,12 +204,12 @@ __device__ __forceinline__ void store_row(float* p, const float (&x)[E]) {
 }
 
 // One warp per token: the lane's angles are computed once and serve every q and k head of the
-// token; q heads go U at a time (their loads issued together), then the k heads into the arena,
-// then the v heads.
+// token; q heads go U at a time (their loads issued together, the next U rows loading while the
+// current ones are processed), then the k heads into the arena, then the v heads.
 template <typename KV, int E>
 __global__ void __launch_bounds__(256) rope_append_kernel(ArenaGeom g, RopeArgs a) {
     constexpr int D = 32 * E;
-    constexpr int U = 8;
+    constexpr int U = 4;
     const int lane = threadIdx.x & 31;
     const int n_warps = static_cast<int>((static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5);
     for (int t = static_cast<int>((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5); t < a.n_tok;
@@ -218,11 +218,15 @@ __global__ void __launch_bounds__(256) rope_append_kernel(ArenaGeom g, RopeArgs 
         float sn[E], cs[E];
         lane_angles<E>(a, pos, lane, sn, cs);
         float* qt = a.q + static_cast<int64_t>(t) * a.n_heads * D + lane * E;
+        // the next U rows are loaded while the current U are processed
+        float x[U][E], nx[U][E];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (u < a.n_heads) load_row<E>(qt + u * D, x[u]);
         for (int h0 = 0; h0 < a.n_heads; h0 += U) {
-            float x[U][E];
 #pragma unroll
             for (int u = 0; u < U; ++u)
-                if (h0 + u < a.n_heads) load_row<E>(qt + (h0 + u) * D, x[u]);
+                if (h0 + U + u < a.n_heads) load_row<E>(qt + (h0 + U + u) * D, nx[u]);
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 if (h0 + u < a.n_heads) {  // warp-uniform
@@ -230,6 +234,10 @@ __global__ void __launch_bounds__(256) rope_append_kernel(ArenaGeom g, RopeArgs 
                     store_row<E>(qt + (h0 + u) * D, x[u]);
                 }
             }
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+                for (int e = 0; e < E; ++e) x[u][e] = nx[u][e];
         }
         const int64_t slot = __ldg(a.slots + t);
         if (slot < 0) continue;  // padding token: nothing to store
