@@ -326,29 +326,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
     return y;
 }
 
-// 2^e of two floats on the FMA and integer pipes, without the SFU (for work split between the
-// two when the SFU is the bottleneck).  e = n + f with n = rint(e), found by the addition of
-// 1.5 * 2^23 (which leaves n in the low mantissa bits), and f = e - n in [-1/2, 1/2]; 2^f by a
-// degree-4 polynomial fitted to 2^f on [-1/2, 1/2] in relative error (weighted least squares
-// with Lawson reweighting toward the minimax fit; max relative error 2.9e-6 in fp32); 2^n goes
-// into the exponent field.  e <= -127 gives 0, as the SFU's flush-to-zero result does; e must
-// stay below 128.
-__device__ __forceinline__ float2 exp2_fma2(float2 e) {
-    constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-    e = make_float2(fmaxf(e.x, -127.f), fmaxf(e.y, -127.f));
-    const float2 t = __fadd2_rn(e, make_float2(kRound, kRound));
-    const float2 n = __fadd2_rn(t, make_float2(-kRound, -kRound));
-    const float2 f = __fadd2_rn(e, make_float2(-n.x, -n.y));
-    float2 p = make_float2(0.009574665687978268f, 0.009574665687978268f);
-    p = __ffma2_rn(p, f, make_float2(0.05593142658472061f, 0.05593142658472061f));
-    p = __ffma2_rn(p, f, make_float2(0.2402474284172058f, 0.2402474284172058f));
-    p = __ffma2_rn(p, f, make_float2(0.6931197643280029f, 0.6931197643280029f));
-    p = __ffma2_rn(p, f, make_float2(0.9999992251396179f, 0.9999992251396179f));
-    // bits(t) = 0x4B400000 + n; the scale 2^n has exponent field n + 127 (0 for n = -127)
-    const float sx = __int_as_float((__float_as_int(t.x) - 0x4B400000 + 127) << 23);
-    const float sy = __int_as_float((__float_as_int(t.y) - 0x4B400000 + 127) << 23);
-    return __fmul2_rn(p, make_float2(sx, sy));
-}
 
 // Shared-memory matrix descriptor (sm_100): start address, leading / stride byte offsets,
 // version 1, 128-byte swizzle (layout type 2).

@@ -221,28 +221,36 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
     };
     p_load();
     pdl_wait();
+    // Lane 0 issues the K span and lane 1 the V span: a bulk copy occupies its issuing thread
+    // for on the order of a hundred cycles, so the two go in parallel.
     auto issue = [&](int st) {
         int page, tok0, ntok;
         chunk_geom(p_c0 + p_j, p_ctx, page, tok0, ntok);
+        int64_t blk = 0;
+        if (lane == 0) blk = __ldg(w.tables + table_row(w, p_b) * w.max_blocks + page);
+        blk = __shfl_sync(0xffffffffu, blk, 0);
+        uint64_t* bar = &my_bars[st];
+        const bool ok = blk >= 0 && blk < g.total_blocks && ntok > 0;
+        const uint32_t kb = static_cast<uint32_t>(ntok * D * Tr::EB);
+        const uint32_t vb = static_cast<uint32_t>(ntok * DV * Tr::EB);
         if (lane == 0) {
-            const int64_t blk = __ldg(w.tables + table_row(w, p_b) * w.max_blocks + page);
-            uint64_t* bar = &my_bars[st];
-            if (blk >= 0 && blk < g.total_blocks && ntok > 0) {
-                const uint32_t kb = static_cast<uint32_t>(ntok * D * Tr::EB);
-                const uint32_t vb = static_cast<uint32_t>(ntok * DV * Tr::EB);
-                const char* ks = Kb + (blk * g.k_block_stride + k_l + p_h * g.k_head_stride +
-                                       static_cast<int64_t>(tok0) * D) * Tr::EB;
-                const char* vs = Vb + (blk * g.v_block_stride + v_l + p_h * g.v_head_stride +
-                                       static_cast<int64_t>(tok0) * DV) * Tr::EB;
-                unsigned char* dst = my_stages + static_cast<size_t>(st) * Tr::STAGE;
-                fence_proxy_async_smem();
+            if (ok) {
                 mbar_arrive_expect_tx(bar, kb + vb);
-                bulk_g2s(dst, ks, kb, bar);
-                bulk_g2s(dst + Tr::KSTAGE, vs, vb, bar);
             } else {
                 if (a.err) atomicOr(a.err, kErrBadBlock);
                 mbar_arrive(bar);  // completes the phase without data; the consumer skips it
             }
+        }
+        __syncwarp();  // the expected byte count precedes both copies' completion
+        if (ok && lane < 2) {
+            unsigned char* dst = my_stages + static_cast<size_t>(st) * Tr::STAGE;
+            fence_proxy_async_smem();
+            if (lane == 0)
+                bulk_g2s(dst, Kb + (blk * g.k_block_stride + k_l + p_h * g.k_head_stride +
+                                    static_cast<int64_t>(tok0) * D) * Tr::EB, kb, bar);
+            else
+                bulk_g2s(dst + Tr::KSTAGE, Vb + (blk * g.v_block_stride + v_l + p_h * g.v_head_stride +
+                                                 static_cast<int64_t>(tok0) * DV) * Tr::EB, vb, bar);
         }
         if (++p_j >= p_cnt) {
             p_j = 0;

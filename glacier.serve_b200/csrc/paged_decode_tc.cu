@@ -111,25 +111,32 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_tc_kernel(
     };
     p_load();
     pdl_wait();
+    // Lanes 0-3 issue the chunk's four boxes, one each: a TMA instruction occupies its issuing
+    // thread for on the order of a hundred cycles, so four from one lane would hold the warp
+    // about as long as the chunk's math.
     auto issue = [&](int st) {
         int page, tok0, ntok;
         chunk_geom(p_c0 + p_j, p_ctx, page, tok0, ntok);
+        int64_t blk = 0;
+        if (lane == 0) blk = __ldg(w.tables + table_row(w, p_b) * w.max_blocks + page);
+        blk = __shfl_sync(0xffffffffu, blk, 0);
+        uint64_t* bar = &my_bars[st];
+        const bool ok = blk >= 0 && blk < g.total_blocks && ntok > 0;
         if (lane == 0) {
-            const int64_t blk = __ldg(w.tables + table_row(w, p_b) * w.max_blocks + page);
-            uint64_t* bar = &my_bars[st];
-            if (blk >= 0 && blk < g.total_blocks && ntok > 0) {
-                const int z = static_cast<int>((blk * g.layers + a.layer) * g.heads_kv + p_h);
-                unsigned char* dst = my_stages + static_cast<size_t>(st) * kStage;
-                fence_proxy_async_smem();
+            if (ok) {
                 mbar_arrive_expect_tx(bar, kStage);
-                tma_load_3d(dst, &tmk, 0, tok0, z, bar);
-                tma_load_3d(dst + kBox, &tmk, 64, tok0, z, bar);
-                tma_load_3d(dst + 2 * kBox, &tmv, 0, tok0, z, bar);
-                tma_load_3d(dst + 3 * kBox, &tmv, 64, tok0, z, bar);
             } else {
                 if (a.err) atomicOr(a.err, kErrBadBlock);
                 mbar_arrive(bar);
             }
+        }
+        __syncwarp();  // the expected byte count precedes every box's completion
+        if (ok && lane < 4) {
+            const int z = static_cast<int>((blk * g.layers + a.layer) * g.heads_kv + p_h);
+            unsigned char* dst = my_stages + static_cast<size_t>(st) * kStage + lane * kBox;
+            fence_proxy_async_smem();
+            tma_load_3d(dst, lane < 2 ? static_cast<const void*>(&tmk) : static_cast<const void*>(&tmv),
+                        (lane & 1) * 64, tok0, z, bar);
         }
         if (++p_j >= p_cnt) {
             p_j = 0;

@@ -60,7 +60,6 @@ constexpr size_t kSmemData = kQBytes + 4 * kTile;  // Q + 2 K stages + 2 V stage
 constexpr size_t kSmem = kSmemData + 256 + 1024;   // + barriers + 1024-byte alignment slack
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.f;
-constexpr int kPolyEvery = 4;  // 1 in kPolyEvery key pairs of the softmax takes 2^ on the FMA pipe
 
 // Instruction descriptor of tcgen05.mma kind::f16 with fp32 D, A K-major, and A and B both
 // bf16 (format 1) or both fp16 (format 0).
@@ -320,17 +319,14 @@ __global__ void __launch_bounds__(kThreads, 2)
                 m_run = mt;
                 l_run *= alpha;
             }
-            // p = 2^(s * sl - m): one packed FMA per key pair, then the SFU, except for every
-            // kPolyEvery-th pair, whose 2^ runs on the FMA pipe (the SFU would otherwise bound the
-            // tile as much as the tensor pipe: 8192 ex2 per 64-key tile at 16 per SM-cycle)
+            // p = 2^(s * sl - m): one packed FMA per key pair, then the SFU
             uint32_t pk[16];
             float2 sum2 = make_float2(0.f, 0.f);
             const float2 sl2 = make_float2(sl, sl), nm2 = make_float2(-m_run, -m_run);
 #pragma unroll
             for (int c = 0; c < 16; ++c) {
                 const float2 e = __ffma2_rn(make_float2(x[2 * c], x[2 * c + 1]), sl2, nm2);
-                const float2 p = (c % kPolyEvery == kPolyEvery - 1) ? exp2_fma2(e)
-                                                                     : make_float2(fast_exp2(e.x), fast_exp2(e.y));
+                const float2 p = make_float2(fast_exp2(e.x), fast_exp2(e.y));
                 sum2 = __fadd2_rn(sum2, p);
                 pk[c] = pack_16x2<F16>(p.x, p.y);
             }

@@ -104,11 +104,12 @@ __device__ __forceinline__ void lane_angles(const RopeArgs& a, int pos, int lane
 // One q or k head row of D = 32 * E elements, lane l holding elements [l*E, (l+1)*E): bias,
 // RMSNorm, rotation with the lane's precomputed angles.  RMSNorm: lane l sums the squares of its
 // elements in order (x*x, then fused multiply-adds), a butterfly over lanes 16, 8, 4, 2, 1 adds
-// the partial sums (every lane ends with the same value), r = sqrt(sum / D + eps),
-// y = (x / r) * w.  Rotation of pair (a, b): y_a = fma(x_a, c, -(x_b * s)),
-// y_b = fma(x_b, c, x_a * s), each times mscale.
+// the partial sums (every lane ends with the same value), r = sqrt(sum * (1/D) + eps) (1/D is
+// exact: D is a power of two), inv = 1 / r, y = (x * inv) * w.  Rotation of pair (a, b):
+// y_a = fma(x_a, c, -(x_b * s)), y_b = fma(x_b, c, x_a * s), each times mscale.  `nw` holds the
+// lane's elements of the norm weight (read once per token).
 template <int E>
-__device__ __forceinline__ void prologue_row(float (&x)[E], const float* bias, const float* norm,
+__device__ __forceinline__ void prologue_row(float (&x)[E], const float* bias, bool norm, const float (&nw)[E],
                                              const RopeArgs& a, const float (&sn)[E], const float (&cs)[E],
                                              int lane) {
     constexpr int D = 32 * E;
@@ -122,9 +123,10 @@ __device__ __forceinline__ void prologue_row(float (&x)[E], const float* bias, c
         for (int e = 1; e < E; ++e) p = __fmaf_rn(x[e], x[e], p);
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1) p = __fadd_rn(p, __shfl_xor_sync(0xffffffffu, p, off));
-        const float r = __fsqrt_rn(__fadd_rn(__fdiv_rn(p, static_cast<float>(D)), a.eps));
+        const float r = __fsqrt_rn(__fadd_rn(__fmul_rn(p, 1.f / static_cast<float>(D)), a.eps));
+        const float inv = __fdiv_rn(1.f, r);
 #pragma unroll
-        for (int e = 0; e < E; ++e) x[e] = __fmul_rn(__fdiv_rn(x[e], r), __ldg(norm + lane * E + e));
+        for (int e = 0; e < E; ++e) x[e] = __fmul_rn(__fmul_rn(x[e], inv), nw[e]);
     }
     const int R = a.rope_dim;
     if (R <= 0) return;
@@ -204,8 +206,8 @@ __device__ __forceinline__ void store_row(float* p, const float (&x)[E]) {
 }
 
 // One warp per token: the lane's angles are computed once and serve every q and k head of the
-// token; q heads go U at a time (their loads issued together, the next U rows loading while the
-// current ones are processed), then the k heads into the arena, then the v heads.
+// token; q heads go U at a time (their loads issued together), then the k heads into the arena,
+// then the v heads.
 template <typename KV, int E>
 __global__ void __launch_bounds__(256) rope_append_kernel(ArenaGeom g, RopeArgs a) {
     constexpr int D = 32 * E;
@@ -215,29 +217,27 @@ __global__ void __launch_bounds__(256) rope_append_kernel(ArenaGeom g, RopeArgs 
     for (int t = static_cast<int>((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5); t < a.n_tok;
          t += n_warps) {
         const int pos = __ldg(a.positions + t);
-        float sn[E], cs[E];
+        float sn[E], cs[E], qw[E], kw[E];
         lane_angles<E>(a, pos, lane, sn, cs);
-        float* qt = a.q + static_cast<int64_t>(t) * a.n_heads * D + lane * E;
-        // the next U rows are loaded while the current U are processed
-        float x[U][E], nx[U][E];
 #pragma unroll
-        for (int u = 0; u < U; ++u)
-            if (u < a.n_heads) load_row<E>(qt + u * D, x[u]);
+        for (int e = 0; e < E; ++e) {
+            qw[e] = a.q_norm ? __ldg(a.q_norm + lane * E + e) : 1.f;
+            kw[e] = a.k_norm ? __ldg(a.k_norm + lane * E + e) : 1.f;
+        }
+        float* qt = a.q + static_cast<int64_t>(t) * a.n_heads * D + lane * E;
         for (int h0 = 0; h0 < a.n_heads; h0 += U) {
+            float x[U][E];
 #pragma unroll
             for (int u = 0; u < U; ++u)
-                if (h0 + U + u < a.n_heads) load_row<E>(qt + (h0 + U + u) * D, nx[u]);
+                if (h0 + u < a.n_heads) load_row<E>(qt + (h0 + u) * D, x[u]);
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 if (h0 + u < a.n_heads) {  // warp-uniform
-                    prologue_row<E>(x[u], a.q_bias ? a.q_bias + (h0 + u) * D : nullptr, a.q_norm, a, sn, cs, lane);
+                    prologue_row<E>(x[u], a.q_bias ? a.q_bias + (h0 + u) * D : nullptr, a.q_norm != nullptr, qw, a, sn, cs,
+                                    lane);
                     store_row<E>(qt + (h0 + u) * D, x[u]);
                 }
             }
-#pragma unroll
-            for (int u = 0; u < U; ++u)
-#pragma unroll
-                for (int e = 0; e < E; ++e) x[u][e] = nx[u][e];
         }
         const int64_t slot = __ldg(a.slots + t);
         if (slot < 0) continue;  // padding token: nothing to store
@@ -256,7 +256,8 @@ __global__ void __launch_bounds__(256) rope_append_kernel(ArenaGeom g, RopeArgs 
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 if (h0 + u < g.heads_kv) {
-                    prologue_row<E>(x[u], a.k_bias ? a.k_bias + (h0 + u) * D : nullptr, a.k_norm, a, sn, cs, lane);
+                    prologue_row<E>(x[u], a.k_bias ? a.k_bias + (h0 + u) * D : nullptr, a.k_norm != nullptr, kw, a, sn, cs,
+                                    lane);
                     KV* dst = static_cast<KV*>(g.k) + blk * g.k_block_stride + a.layer * g.k_layer_stride +
                               (h0 + u) * g.k_head_stride + static_cast<int64_t>(off) * D + lane * E;
 #pragma unroll

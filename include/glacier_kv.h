@@ -254,7 +254,7 @@ typedef struct gkv_qkv_prologue {
  * d_q [n_tok][n_heads][head_dim] fp32 is rewritten in place (ready for gkv_paged_decode /
  * gkv_paged_prefill); d_k [n_tok][heads_kv][head_dim] and d_v [n_tok][heads_kv][v_head_dim]
  * fp32 are read only.  Formulas (QuantKernels' own are not in the reference tree):
- * RMSNorm y = (x / sqrt(sum(x^2) / head_dim + eps)) * w; rotation by angle pos * inv_freq[i]
+ * RMSNorm y = (x * (1 / sqrt(sum(x^2) / head_dim + eps))) * w; rotation by angle pos * inv_freq[i]
  * (one fp32 multiply): (a, b) -> (a cos - b sin, b cos + a sin), times mscale.  head_dim must
  * be 32, 64, 128 or 256 (GKV_EUNSUPPORTED otherwise). */
 GKV_API int gkv_rope_append(gkv_pool* pool, int32_t layer, float* d_q, const float* d_k,

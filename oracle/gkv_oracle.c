@@ -416,7 +416,8 @@ void oracle_sincos(float theta, float* s_out, float* c_out) {
 /* RMSNorm of one head row of length n = 32*E (E elements per lane of a 32-lane group): lane l
  * sums the squares of its elements [l*E, (l+1)*E) in order (first x*x, then fused multiply-adds),
  * the 32 partial sums are combined by a butterfly (lane l adds lane l^16's sum, then l^8, l^4,
- * l^2, l^1); then r = sqrt(sum / n + eps) and y_i = (x_i / r) * w_i, each step rounded. */
+ * l^2, l^1); then r = sqrt(sum * (1/n) + eps) (n a power of two: 1/n is exact), inv = 1 / r and
+ * y_i = (x_i * inv) * w_i, each step rounded. */
 static void rmsnorm_row(float* x, const float* w, int32_t n, float eps) {
     const int32_t E = n / 32;
     float part[32];
@@ -430,8 +431,9 @@ static void rmsnorm_row(float* x, const float* w, int32_t n, float eps) {
         for (int l = 0; l < 32; ++l) nxt[l] = part[l] + part[l ^ off];
         memcpy(part, nxt, sizeof(part));
     }
-    const float r = sqrtf(part[0] / (float)n + eps);
-    for (int32_t i = 0; i < n; ++i) x[i] = (x[i] / r) * w[i];
+    const float r = sqrtf(part[0] * (1.0f / (float)n) + eps);
+    const float inv = 1.0f / r;
+    for (int32_t i = 0; i < n; ++i) x[i] = (x[i] * inv) * w[i];
 }
 
 /* Rotation of one head row by position pos: pairs (i, i + R/2) (style 0, NEOX) or (2i, 2i+1)
