@@ -191,14 +191,6 @@ bool encode_arena_map(void* map, void* base, const ArenaGeom& g, int dim, int ro
 void decode_tc_config(DecodeConfig& c);
 cudaError_t launch_paged_decode_tc(const ArenaGeom& g, const DecodeWork& w, const DecodeArgs& a,
                                    int group, int head_groups, int* launches, cudaStream_t st);
-// Three-pass TF32 tensor-core variant (paged_decode_tf32.cu): fp32 KV, d = dv = 128, block size
-// a multiple of 8, query group 5..8 per head group.  Same work list and partial layout.
-bool decode_tf32_eligible(const ArenaGeom& g, int n_heads);
-void decode_tf32_config(DecodeConfig& c);
-// The fp32 arena view of encode_arena_map, boxes of 8 slots x 32 dims.
-bool encode_f32_arena_map(void* map, void* base, const ArenaGeom& g, int dim);
-cudaError_t launch_paged_decode_tf32(const ArenaGeom& g, const DecodeWork& w, const DecodeArgs& a,
-                                     int group, int head_groups, int* launches, cudaStream_t st);
 
 // ---- chunked causal prefill (paged_prefill_tc.cu) ----
 // One work item = up to 128 consecutive queries of one sequence; the kernel runs one CTA per

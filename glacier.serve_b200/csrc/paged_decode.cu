@@ -605,10 +605,6 @@ DecodeConfig decode_config(const ArenaGeom& g, int n_heads) {
         decode_tc_config(c);
         return c;
     }
-    if (decode_tf32_eligible(g, n_heads)) {
-        decode_tf32_config(c);
-        return c;
-    }
     dispatch(g, c.gp, [&](auto inst) { decltype(inst)::config(c); });
     return c;
 }
@@ -675,8 +671,6 @@ cudaError_t launch_paged_decode(const ArenaGeom& g, const DecodeWork& w, const D
                            reinterpret_cast<uintptr_t>(a.part_acc)) & 15) == 0;
     if (aligned && decode_tc_eligible(g, a.n_heads))
         return launch_paged_decode_tc(g, w, a, group, head_groups, launches, stream);
-    if (aligned && decode_tf32_eligible(g, a.n_heads))
-        return launch_paged_decode_tf32(g, w, a, group, head_groups, launches, stream);
     cudaError_t err = cudaErrorInvalidValue;
     dispatch(g, gp, [&](auto inst) {
         err = decltype(inst)::launch(g, w, a, group, head_groups, launches, stream);

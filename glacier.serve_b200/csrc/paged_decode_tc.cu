@@ -411,35 +411,19 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 bool tmap_encoder_available() { return encode_fn() != nullptr; }
 
-static bool encode_map3(void* map, CUtensorMapDataType type, const void* base, const uint64_t dims[3],
-                        const uint64_t strides[2], const uint32_t box[3]) {
+// The element type only sets the element size here (2 bytes): TMA copies bf16 and fp16 tiles
+// alike, so one encoder serves both arenas.
+bool encode_bf16_map3(void* map, const void* base, const uint64_t dims[3], const uint64_t strides[2],
+                      const uint32_t box[3]) {
     auto fn = encode_fn();
     if (!fn) return false;
     const cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
     const cuuint64_t s[2] = {strides[0], strides[1]};
     const cuuint32_t b[3] = {box[0], box[1], box[2]};
     const cuuint32_t estr[3] = {1, 1, 1};
-    return fn(static_cast<CUtensorMap*>(map), type, 3, const_cast<void*>(base), d, s, b, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-// The element type only sets the element size here (2 bytes): TMA copies bf16 and fp16 tiles
-// alike, so one encoder serves both arenas.
-bool encode_bf16_map3(void* map, const void* base, const uint64_t dims[3], const uint64_t strides[2],
-                      const uint32_t box[3]) {
-    return encode_map3(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, dims, strides, box);
-}
-
-// 3-D view [block * layer * head][slot][dim] of one fp32 arena, boxes of 8 slots x 32 dims (128
-// bytes, the swizzle span).
-bool encode_f32_arena_map(void* map, void* base, const ArenaGeom& g, int dim) {
-    if (g.block_size % kChunk != 0) return false;
-    const uint64_t dims[3] = {static_cast<uint64_t>(dim), static_cast<uint64_t>(g.block_size),
-                              static_cast<uint64_t>(g.total_blocks) * g.layers * g.heads_kv};
-    const uint64_t strides[2] = {static_cast<uint64_t>(dim) * 4, static_cast<uint64_t>(g.block_size) * dim * 4};
-    const uint32_t box[3] = {32, static_cast<uint32_t>(kChunk), 1};
-    return encode_map3(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, dims, strides, box);
+    return fn(static_cast<CUtensorMap*>(map), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), d, s,
+              b, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // 3-D view [block * layer * head][slot][dim] of one 16-bit arena, boxes of `rows` slots x 64 dims.

@@ -338,14 +338,8 @@ int gkv_pool_create(const gkv_pool_desc* desc, gkv_pool** out_pool) {
         g.k = k;
         g.v = v;
         P.has_arena = true;
-        // TMA maps for the tensor-core kernels (d = dv = 128, 8-token-aligned blocks).  fp32:
-        // 8 x 32-dim boxes for the TF32 decode.  16-bit storage: the copies move 2-byte
-        // elements, whichever 16-bit format they hold.
-        if (d.dtype == GKV_DTYPE_F32 && d.head_dim == 128 && d.v_head_dim == 128 && d.block_size % 8 == 0 &&
-            gkv::encode_f32_arena_map(P.tmap_k, g.k, g, 128) && gkv::encode_f32_arena_map(P.tmap_v, g.v, g, 128)) {
-            g.tmap_k = P.tmap_k;
-            g.tmap_v = P.tmap_v;
-        }
+        // TMA maps for the tensor-core kernels (16-bit storage, d = dv = 128, 8-token-aligned
+        // blocks); the copies move 2-byte elements, whichever 16-bit format they hold
         if (d.dtype != GKV_DTYPE_F32 && d.head_dim == 128 && d.v_head_dim == 128 && d.block_size % 8 == 0 &&
             gkv::encode_decode_tmaps(g, P.tmap_k, P.tmap_v)) {
             g.tmap_k = P.tmap_k;
