@@ -77,6 +77,10 @@ CASES = [
     (16, 2, 128, 128, 8, "bf16", [37, 8, 1, 100]),  # tensor-core kernel, block size 8
     (8, 1, 128, 128, 24, "bf16", [50, 24, 25, 3]),  # tensor-core kernel, block size 24
     (56, 8, 128, 128, 16, "bf16", [9000, 17]),      # group 7, long sequence: fused merge
+    # fp32 KV, wide groups, other block sizes
+    (16, 2, 128, 128, 8, "f32", [37, 8, 1, 100]),   # block size 8
+    (8, 1, 128, 128, 24, "f32", [50, 24, 25, 3]),   # block size 24: chunks of 8
+    (40, 8, 128, 128, 16, "f32", [3000, 7, 129]),   # group 5: three idle heads of the pass
     # long and short splits in one batch: the merge gives the long ones a CTA, the others a warp
     (28, 4, 128, 128, 16, "f32", [12000, 700, 300, 90, 5]),
     (28, 4, 128, 128, 16, "bf16", [20000, 900, 64, 33]),
@@ -170,7 +174,9 @@ def test_empty_sequences_leave_output_untouched(cuda):
     np.testing.assert_allclose(out[1], ref[1], atol=TOL["f32"], rtol=0)
 
 
-def test_sinks_per_head_and_scalar(cuda):
+@pytest.mark.parametrize("n_heads", [8, 28])
+def test_sinks_per_head_and_scalar(cuda, n_heads):
+    """Group 4 and group 14 (two head groups of eight heads)."""
     import torch
 
     rng = np.random.default_rng(13)
@@ -178,19 +184,21 @@ def test_sinks_per_head_and_scalar(cuda):
     K, V = random_arena(pool, rng)
     ctx = [200, 700]
     tables = random_tables(rng, ctx, 16, 64)
-    q = rng.standard_normal((2, 8, 128)).astype(np.float32)
+    q = rng.standard_normal((2, n_heads, 128)).astype(np.float32)
     sink = 0.75
-    out = gpu_decode(pool, 0, tables, ctx, q, 8, 0.09, sinks=np.full(8, sink, np.float32))
-    ref = O.decode_batch(K, V, geom_of(pool), 0, tables, np.array(ctx, np.int32), q, 8, 0.09, sink_logit=sink)
+    out = gpu_decode(pool, 0, tables, ctx, q, n_heads, 0.09, sinks=np.full(n_heads, sink, np.float32))
+    ref = O.decode_batch(K, V, geom_of(pool), 0, tables, np.array(ctx, np.int32), q, n_heads, 0.09,
+                         sink_logit=sink)
     np.testing.assert_allclose(out, ref, atol=TOL["f32"], rtol=0)
     # the scalar form through compute_attention (float? sinkLogit)
     t = G.BlockTable(pool)
     t.attach_prefix_blocks(tables[1][: (700 + 15) // 16].tolist(), 700)
     qd = torch.from_numpy(q[1].ravel()).to(cuda)
-    od = torch.zeros(8 * 128, device=cuda)
-    G.PagedAttentionKernel.compute_attention(0, 0, 699, qd, od, t, pool, 8, 2, 128, 128, 0.09, 4096, sink_logit=sink)
+    od = torch.zeros(n_heads * 128, device=cuda)
+    G.PagedAttentionKernel.compute_attention(0, 0, 699, qd, od, t, pool, n_heads, 2, 128, 128, 0.09, 4096,
+                                             sink_logit=sink)
     pool.sync()
-    np.testing.assert_allclose(od.view(8, 128).cpu().numpy(), ref[1], atol=TOL["f32"], rtol=0)
+    np.testing.assert_allclose(od.view(n_heads, 128).cpu().numpy(), ref[1], atol=TOL["f32"], rtol=0)
 
 
 def test_compute_attention_argument_errors(cuda):
