@@ -857,6 +857,25 @@ def main():
         step_ms = span_ms
     ms = max_over_ranks(step_ms)
     dec_ms = sum(a.elapsed_time(b) for a, b in dec_events) / args.steps
+    breakdown = None
+    if split_kv:
+        # the same decode of this rank's block ranges without the exchange: what the exchange and
+        # the cross-rank merge add to a split-KV decode
+        lse = torch.empty((w.batch, w.n_heads), dtype=torch.float32, device=dev)
+        tmp = torch.empty_like(out)
+        loc = [(ev(), ev()) for _ in range(args.steps)]
+        for i in range(args.steps):
+            pool.upload_step(w.tables, w.ctx_lens, w.slot_mapping, stream=stream)
+            loc[i][0].record(stream)
+            pool.paged_decode_lse(0, q, tmp, lse, w.n_heads, w.scale, stream=stream)
+            loc[i][1].record(stream)
+        torch.cuda.synchronize(dev)
+        local_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in loc) / args.steps)
+        dist_ms = max_over_ranks(dec_ms)
+        breakdown = {"local_decode_ms": local_ms, "split_kv_call_ms": dist_ms,
+                     "exchange_and_merge_ms": dist_ms - local_ms,
+                     "what": "max over ranks of: this rank's decode with lse alone, and the whole "
+                             "gkv_paged_decode_splitkv_dist call (decode + peer push + bounded wait + LSE merge)"}
     # strong-scaled configs split one global batch over the ranks; the others add a batch per rank
     seqs_per_step = global_batch if args.config in STRONG else world * w.batch
     value = seqs_per_step / (ms / 1e3)
@@ -946,6 +965,8 @@ def main():
             "gpu_launches": launches,
             "clocks": clk.summary(),
         }
+        if breakdown is not None:
+            line["split_kv_breakdown"] = breakdown
         if not args.no_cpu_baseline and world == 1:
             from oracle import pyoracle as O
 
