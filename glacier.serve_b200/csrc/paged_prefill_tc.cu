@@ -5,35 +5,31 @@
 // (PagedTransformerRunner.ForwardPrefillSubBatch, PagedTransformerRunner.cs:424-471): the
 // chunk's K/V are stored first, then query t runs ComputeAttention with pos = start + t,
 // whose causal length is min(TokenCount, pos + 1) (PagedAttentionKernel.cs:41).  Here one
-// CTA takes 128 consecutive queries of one sequence for a PAIR of query heads of the same kv
-// head (GQA), and streams the sequence's pages in tiles of 64 keys that both heads use:
+// CTA takes 128 consecutive queries of one (sequence, query head) and streams the
+// sequence's pages in tiles of 64 keys:
 //
-//  * warps 16 and 17 (TMA producers, K and V): the two Q tiles once (two boxes of 128 rows x
-//    64 dims each), then per key tile one box per page (16 slots; 8 when the block size is not
-//    a multiple of 16) and dim half, gathered from the arena through the block table with tiled
-//    cp.async.bulk.tensor (128-byte swizzle, no multicast) into 3-stage K and V rings.  Each
+//  * warps 8 and 9 (TMA producers, K and V): the Q tile once (two boxes of 128 rows x 64
+//    dims), then per key tile one box per page (16 slots; 8 when the block size is not a
+//    multiple of 16) and dim half, gathered from the arena through the block table with tiled
+//    cp.async.bulk.tensor (128-byte swizzle, no multicast) into 2-stage K and V rings.  Each
 //    lane issues one box: a TMA instruction occupies its issuing thread for on the order of
 //    a hundred cycles, so one thread alone starves the tensor cores.  K and V have their own
-//    warps so that V (which waits for P V three tiles back) never holds back K.
-//  * warps 18 and 19, one MMA issuer per head (one thread issues): S = Q K^T (M=128, N=64,
-//    K=128: 8 tcgen05.mma kind::f16, both operands K-major in shared memory) into one of two
-//    TMEM S buffers of that head, then O += P V (M=128, N=128, K=64: 4 MMAs, P read from TMEM,
-//    V MN-major in shared memory).  S of tile j+1 is issued before P V of tile j, so the tensor
-//    pipe works while the softmax runs; an issuer never waits for its own MMAs (they execute in
-//    issue order), and with one issuer per head neither head's chain waits on the other's.
-//    A K or V stage is free once both heads' MMAs on it have completed.
-//  * warps 0-7 (head 0) and 8-15 (head 1), two threads per query row through the 16x32bx2
-//    TMEM shape: load S, causal mask, base-2 online softmax with lazy rescaling (O in TMEM is
-//    rescaled only when the running max grows by more than 8, so P stays <= 2^8), P in the
-//    arena's 16-bit type (bf16 or fp16; A and B of one MMA share it) written back over its own
-//    S columns.  Epilogue: O / l staged through the head's own (then idle) Q tile and written
-//    as coalesced fp32 rows.
+//    warps so that V (which waits for P V two tiles back) never holds back K.
+//  * warp 10 (one thread issues): S = Q K^T (M=128, N=64, K=128: 8 tcgen05.mma kind::f16,
+//    both operands K-major in shared memory) into one of two TMEM S buffers, then
+//    O += P V (M=128, N=128, K=64: 4 MMAs, P read from TMEM, V MN-major in shared memory).
+//    S of tile j+1 is issued before P V of tile j, so the tensor pipe works while the
+//    softmax runs; the issuer never waits for its own MMAs (they execute in issue order).
+//  * warps 0-7 (two threads per query row through the 16x32bx2 TMEM shape): load S, causal
+//    mask, base-2 online softmax with lazy rescaling (O in TMEM is rescaled only when the
+//    running max grows by more than 8, so P stays <= 2^8), P in the arena's 16-bit type
+//    (bf16 or fp16; A and B of one MMA share it) written back over its own S columns.  Epilogue: O / l through shared memory as coalesced fp32 rows.
 //
-// Why pairs: with one head per CTA every K/V tile was gathered once per query head, and the
-// 2-stage rings that fit two such CTAs per SM let the TMA latency pace the pipe at ~2000
-// cycles per tile.  A pair halves the gathers per head, and one CTA per SM (160 KB of rings and
-// Q tiles, all 512 TMEM columns) affords 3-stage rings.  Every mbarrier wait is bounded: on
-// expiry the CTA raises kErrWaitTimeout, lets its copies and MMAs finish and frees its TMEM.
+// Two CTAs share an SM (96 KB shared memory and 256 TMEM columns each), so one CTA's softmax
+// overlaps the other's MMAs; one CTA with two Q tiles sharing K/V measured slower (its
+// single issuer waits on whichever tile's softmax is late), and so did a third K stage.
+// Every mbarrier wait is bounded: on expiry the CTA raises kErrWaitTimeout, lets its copies
+// and MMAs finish and frees its TMEM.
 #include <cuda.h>
 
 #include <atomic>
@@ -48,24 +44,19 @@ namespace gkv {
 
 namespace {
 
-constexpr int kBM = 128;                           // query rows per head
+constexpr int kBM = 128;                           // query rows per CTA
 constexpr int kBN = 64;                            // keys per tile
 constexpr int kD = 128;                            // head_dim = v_head_dim
-constexpr int kHP = 2;                             // query heads (of one kv head) per CTA
-constexpr int kSoftmaxWarps = 8;                   // per head: two threads per query row
-constexpr int kKWarp = kHP * kSoftmaxWarps;        // K producer
-constexpr int kVWarp = kKWarp + 1;                 // V producer
-constexpr int kMmaWarp = kVWarp + 1;               // MMA issuer of head 0; kMmaWarp + 1 for head 1
-constexpr int kThreads = (kMmaWarp + kHP) * 32;    // 640
-constexpr int kStages = 3;                         // K and V ring depth
-constexpr uint32_t kQBytes = kBM * kD * 2;         // 32 KB per head
+constexpr int kSoftmaxWarps = 8;                   // two threads per query row
+constexpr int kKWarp = 8, kVWarp = 9, kMmaWarp = 10;  // K producer, V producer, MMA issuer
+constexpr int kThreads = 352;
+constexpr uint32_t kQBytes = kBM * kD * 2;         // 32 KB
 constexpr uint32_t kQHalf = kQBytes / 2;           // 128 rows x 128 B (64 dims)
 constexpr uint32_t kTile = kBN * kD * 2;           // 16 KB: one K or V tile
 constexpr uint32_t kHalf = kTile / 2;              // 64 rows x 128 B
-constexpr uint32_t kHeadCols = 256;                // per head: S0 [0,64) S1 [64,128) O [128,256)
-constexpr uint32_t kTmemCols = kHP * kHeadCols;    // 512: the whole tensor memory
+constexpr uint32_t kTmemCols = 256;                // S0 [0,64) S1 [64,128) O [128,256)
 constexpr uint32_t kColO = 128;
-constexpr size_t kSmemData = kHP * kQBytes + 2 * kStages * kTile;  // 64 KB Q + 96 KB K/V rings
+constexpr size_t kSmemData = kQBytes + 4 * kTile;  // Q + 2 K stages + 2 V stages = 96 KB
 constexpr size_t kSmem = kSmemData + 256 + 1024;   // + barriers + 1024-byte alignment slack
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.f;
@@ -107,69 +98,49 @@ struct BoxLane {
     }
 };
 
-// Barriers of one head's S -> softmax -> P V chain.
-struct HeadBars {
-    uint64_t* s_full;   // [2] per S buffer
-    uint64_t* p_full;   // [2]
-    uint64_t* pv_done;  // [2]
-    uint64_t* drained;
-};
-
 template <int R, bool F16>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                             const __grid_constant__ CUtensorMap tmv, const ArenaGeom g, const PrefillArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t{1023});
-    uint8_t* sQ = smem;                       // [kHP][kQBytes]
-    uint8_t* sK = smem + kHP * kQBytes;       // [kStages][kTile]
-    uint8_t* sV = sK + kStages * kTile;       // [kStages][kTile]
-    uint64_t* bar = reinterpret_cast<uint64_t*>(sV + kStages * kTile);
+    uint8_t* sQ = smem;
+    uint8_t* sK = smem + kQBytes;
+    uint8_t* sV = sK + 2 * kTile;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sV + 2 * kTile);
     uint64_t* q_full = bar;
-    uint64_t* k_full = bar + 1;               // [kStages]
-    uint64_t* k_empty = k_full + kStages;     // [kStages]
-    uint64_t* v_full = k_empty + kStages;     // [kStages]
-    uint64_t* v_empty = v_full + kStages;     // [kStages]
-    uint64_t* hb0 = v_empty + kStages;        // 7 per head
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(hb0 + 7 * kHP);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(hb0 + 7 * kHP + 1);
-    auto head_bars = [&](int hs) {
-        uint64_t* p = hb0 + 7 * hs;
-        return HeadBars{p, p + 2, p + 4, p + 6};
-    };
+    uint64_t* k_full = bar + 1;   // [2] per stage
+    uint64_t* k_empty = bar + 3;  // [2]
+    uint64_t* v_full = bar + 5;   // [2]
+    uint64_t* v_empty = bar + 7;  // [2]
+    uint64_t* s_full = bar + 9;   // [2] per S buffer
+    uint64_t* p_full = bar + 11;  // [2]
+    uint64_t* pv_done = bar + 13; // [2]
+    uint64_t* drained = bar + 15;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 16);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 17);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int group = a.n_heads / g.heads_kv;
-    const int n_pairs = (group + kHP - 1) / kHP;
-    const int per_item = g.heads_kv * n_pairs;
-    const int item = blockIdx.x / per_item;
-    const int rem = blockIdx.x - item * per_item;
-    const int hkv = rem / n_pairs;
-    const int pair = rem - hkv * n_pairs;
-    const int h0 = hkv * group + pair * kHP;           // first query head of this CTA
-    const int n_valid = min(kHP, group - pair * kHP);  // heads of this CTA (the last pair may hold 1)
+    const int item = blockIdx.x / a.n_heads;
+    const int h = blockIdx.x - item * a.n_heads;
     const int32_t* it = a.items + static_cast<int64_t>(item) * kPrefillItemInts;
     const int seq = __ldg(it + 0), qpos0 = __ldg(it + 1), qrow0 = __ldg(it + 2);
     const int n_q = __ldg(it + 3), n_keys = __ldg(it + 4), tok = __ldg(it + 5);
     const int n_tiles = (n_keys + kBN - 1) / kBN;
+    const int hkv = h / (a.n_heads / g.heads_kv);
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < 2; ++s) {
             mbar_init(k_full + s, 1);
-            mbar_init(k_empty + s, n_valid);  // every head's S MMAs release a K stage
+            mbar_init(k_empty + s, 1);
             mbar_init(v_full + s, 1);
-            mbar_init(v_empty + s, n_valid);  // every head's P V MMAs release a V stage
+            mbar_init(v_empty + s, 1);
+            mbar_init(s_full + s, 1);
+            mbar_init(p_full + s, kSoftmaxWarps * 32);
+            mbar_init(pv_done + s, 1);
         }
-        for (int hs = 0; hs < kHP; ++hs) {
-            const HeadBars hb = head_bars(hs);
-            for (int s = 0; s < 2; ++s) {
-                mbar_init(hb.s_full + s, 1);
-                mbar_init(hb.p_full + s, kSoftmaxWarps * 32);
-                mbar_init(hb.pv_done + s, 1);
-            }
-            mbar_init(hb.drained, 1);
-        }
+        mbar_init(drained, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -181,7 +152,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == kKWarp || warp == kVWarp) {
         // ------------- TMA producers: one warp for K, one for V, one box per lane -------------
-        // Separate warps: V of tile j waits for P V of tile j-3, which must not hold back K.
+        // Separate warps: V of tile j waits for P V of tile j-2, which must not hold back K.
         using BL = BoxLane<R>;
         const BL bl(lane);
         const bool is_k = warp == kKWarp;
@@ -190,29 +161,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* ring = is_k ? sK : sV;
         const CUtensorMap* tm = is_k ? &tmk : &tmv;
         const int32_t* trow = a.tables + static_cast<int64_t>(seq) * a.max_blocks;
-        uint32_t armed[kStages] = {};  // lane 0's expect_tx count per stage
+        uint32_t armed0 = 0, armed1 = 0;  // lane 0's expect_tx count per stage
         if (is_k && lane == 0) {
-            mbar_arrive_expect_tx(q_full, n_valid * kQBytes);
-            for (int hs = 0; hs < n_valid; ++hs) {
-                tma_load_3d(sQ + hs * kQBytes, &tmq, 0, h0 + hs, qrow0, q_full);
-                tma_load_3d(sQ + hs * kQBytes + kQHalf, &tmq, 64, h0 + hs, qrow0, q_full);
-            }
+            mbar_arrive_expect_tx(q_full, kQBytes);
+            tma_load_3d(sQ, &tmq, 0, h, qrow0, q_full);
+            tma_load_3d(sQ + kQHalf, &tmq, 64, h, qrow0, q_full);
         }
         int blk = bl.block_of(0, n_keys, trow, g.block_size);
         bool ok = true;
         for (int j = 0; j < n_tiles; ++j) {
-            const int s = j % kStages;
-            const uint32_t round = static_cast<uint32_t>(j / kStages);
+            const int s = j & 1;
             // the next tile's table read is in flight while this tile waits for its stage
             const int blk_next = j + 1 < n_tiles ? bl.block_of(j + 1, n_keys, trow, g.block_size) : -1;
-            if (j >= kStages && !__all_sync(~0u, mbar_wait(empty + s, (round & 1u) ^ 1u))) {
+            if (j >= 2 && !__all_sync(~0u, mbar_wait(empty + s, ((j >> 1) & 1) ^ 1))) {
                 ok = false;
                 break;
             }
             if (__any_sync(~0u, *abort_flag != 0)) break;
             if (lane == 0) {
                 mbar_arrive_expect_tx(full + s, BL::tile_bytes(j * kBN, n_keys));
-                ++armed[s];
+                if (s) ++armed1; else ++armed0;
             }
             __syncwarp();  // expect_tx precedes every complete_tx of this stage
             if (blk >= 0 || (bl.active && j * kBN + bl.chunk * R < n_keys)) {
@@ -236,80 +204,74 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (*abort_flag) {
                 // every armed copy must land before the CTA's shared memory goes away
                 if (is_k) mbar_wait(q_full, 0);
-                for (int s = 0; s < kStages; ++s)
-                    if (armed[s]) mbar_wait(full + s, (armed[s] - 1) & 1);
+                if (armed0) mbar_wait(full, (armed0 - 1) & 1);
+                if (armed1) mbar_wait(full + 1, (armed1 - 1) & 1);
             }
         }
         __syncwarp();
-    } else if (warp >= kMmaWarp) {
-        // ---------------- MMA issuers, one per head ----------------
-        const int hs = warp - kMmaWarp;
-        const HeadBars hb = head_bars(hs);
-        if (lane == 0 && hs < n_valid) {
+    } else if (warp == kMmaWarp) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
             constexpr uint32_t kIdS = idesc_16(kBM, kBN, false, F16);
             constexpr uint32_t kIdO = idesc_16(kBM, kD, true, F16);
-            const uint32_t q_addr = smem_u32(sQ + hs * kQBytes), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
-            const uint32_t th = tbase + hs * kHeadCols;
+            const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
             bool ok = mbar_wait(q_full, 0);
             tc_fence_after();
             for (int j = 0; ok && j <= n_tiles; ++j) {
                 if (*abort_flag) break;
                 if (j < n_tiles) {
-                    const int b = j & 1, s = j % kStages;
+                    const int b = j & 1;
                     // S buffer b last held P of tile j-2, read by the P V issued before this
                     // point: tcgen05.mma from one thread execute in issue order, so the write of
                     // S_j cannot overtake that read and the issuer never waits for its own MMAs.
-                    if (!(ok = mbar_wait(k_full + s, (j / kStages) & 1))) break;
+                    if (!(ok = mbar_wait(k_full + b, (j >> 1) & 1))) break;
                     tc_fence_after();
-                    const uint32_t kb = k_addr + s * kTile;
+                    const uint32_t kb = k_addr + b * kTile;
 #pragma unroll
                     for (int kk = 0; kk < kD / 16; ++kk) {
                         const uint64_t da = umma_desc_sw128(q_addr + (kk >> 2) * kQHalf + (kk & 3) * 32, 16, 1024);
                         const uint64_t db = umma_desc_sw128(kb + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
-                        umma_f16(th + b * kBN, da, db, kIdS, kk > 0 ? 1u : 0u);
+                        umma_f16(tbase + b * kBN, da, db, kIdS, kk > 0 ? 1u : 0u);
                     }
-                    umma_commit(hb.s_full + b);
-                    umma_commit(k_empty + s);
+                    umma_commit(s_full + b);
+                    umma_commit(k_empty + b);
                 }
                 if (j >= 1) {
-                    const int jj = j - 1, b = jj & 1, s = jj % kStages;
-                    if (!(ok = mbar_wait(hb.p_full + b, (jj >> 1) & 1))) break;
-                    if (!(ok = mbar_wait(v_full + s, (jj / kStages) & 1))) break;
+                    const int jj = j - 1, b = jj & 1;
+                    if (!(ok = mbar_wait(p_full + b, (jj >> 1) & 1))) break;
+                    if (!(ok = mbar_wait(v_full + b, (jj >> 1) & 1))) break;
                     tc_fence_after();
-                    const uint32_t vb = v_addr + s * kTile;
+                    const uint32_t vb = v_addr + b * kTile;
 #pragma unroll
                     for (int kk = 0; kk < kBN / 16; ++kk) {
                         // V tile [key][dv]: MN-major, 8-key groups 1 KB apart (SBO), dv 64-127
                         // in the second half (LBO)
                         const uint64_t dv = umma_desc_sw128(vb + kk * 2048, kHalf, 1024);
-                        umma_f16_ts(th + kColO, th + b * kBN + kk * 8, dv, kIdO, (jj > 0 || kk > 0) ? 1u : 0u);
+                        umma_f16_ts(tbase + kColO, tbase + b * kBN + kk * 8, dv, kIdO,
+                                    (jj > 0 || kk > 0) ? 1u : 0u);
                     }
-                    umma_commit(hb.pv_done + b);
-                    umma_commit(v_empty + s);
+                    umma_commit(pv_done + b);
+                    umma_commit(v_empty + b);
                 }
             }
             if (!ok) {
                 atomicOr(a.err, kErrWaitTimeout);
                 *abort_flag = 1;
             }
-            umma_commit(hb.drained);  // all MMAs of this head complete before TMEM is freed
-            if (!mbar_wait(hb.drained, 0)) atomicOr(a.err, kErrWaitTimeout);
+            umma_commit(drained);  // all MMAs of this CTA complete before TMEM is freed
+            if (!mbar_wait(drained, 0)) atomicOr(a.err, kErrWaitTimeout);
         }
         __syncwarp();
-    } else if ((warp >> 3) < n_valid) {
+    } else {
         // ---------------- softmax + epilogue: two threads per query row ----------------
-        // Warps 8*hs .. 8*hs+7 serve head hs.  Local warp lw owns TMEM lanes [row0, row0 + 16),
-        // row0 = 32*(lw%4) + 16*(lw/4) (its own lane quarter); lane l takes row row0 + l%16 and key
-        // columns [32*(l/16), +32) of each tile (the 16x32bx2 TMEM shape), so the two halves of a
-        // row meet in one warp (shfl 16).
-        const int hs = warp >> 3, lw = warp & 7;
-        const HeadBars hb = head_bars(hs);
-        const int h = h0 + hs;
+        // Warp w owns TMEM lanes [row0, row0 + 16), row0 = 32*(w%4) + 16*(w/4) (its own lane
+        // quarter); lane l takes row row0 + l%16 and key columns [32*(l/16), +32) of each tile
+        // (the 16x32bx2 TMEM shape), so the two halves of a row meet in one warp (shfl 16).
         const int hc = lane >> 4;
         const int r16 = lane & 15;
-        const int row0 = 32 * (lw & 3) + 16 * (lw >> 2);
+        const int row0 = 32 * (warp & 3) + 16 * (warp >> 2);
         const int r = row0 + r16;
-        const uint32_t t_w = tbase + hs * kHeadCols + (static_cast<uint32_t>(row0) << 16);
+        const uint32_t t_w = tbase + (static_cast<uint32_t>(row0) << 16);
         const int qpos = qpos0 + r;
         const int limit = min(tok, qpos + 1);  // keys [0, limit) are visible to this row
         const float sl = a.scale * kLog2e;
@@ -322,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             const int b = j & 1;
-            if (!__all_sync(~0u, mbar_wait(hb.s_full + b, (j >> 1) & 1))) {
+            if (!__all_sync(~0u, mbar_wait(s_full + b, (j >> 1) & 1))) {
                 ok = false;
                 break;
             }
@@ -371,18 +333,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             l_run += sum2.x + sum2.y;
             if (j == n_tiles - 1 && tail < kBN) {
                 // keys past n_keys were never loaded (or are unwritten slots): zero their V
-                // rows so that P = 0 never meets a non-finite value in the MMA.  Both heads'
-                // softmax warps write the same zeros into the shared V stage: the stores are
-                // identical, so their order does not matter.
-                const int s = j % kStages;
-                if (!__all_sync(~0u, mbar_wait(v_full + s, (j / kStages) & 1))) {
+                // rows so that P = 0 never meets a non-finite value in the MMA
+                if (!__all_sync(~0u, mbar_wait(v_full + b, (j >> 1) & 1))) {
                     ok = false;
                     break;
                 }
-                const int t = lw * 32 + lane;  // 0..255: (dim half, key) = (t / 64, t % 64) for t < 128
+                const int t = threadIdx.x;  // 0..255: (dim half, key) = (t / 64, t % 64) for t < 128
                 const int row = t & (kBN - 1);
                 if (t < 2 * kBN && row >= tail) {
-                    uint4* dst = reinterpret_cast<uint4*>(sV + s * kTile + (t >> 6) * kHalf + (row >> 3) * 1024 +
+                    uint4* dst = reinterpret_cast<uint4*>(sV + b * kTile + (t >> 6) * kHalf + (row >> 3) * 1024 +
                                                           (row & 7) * 128);
 #pragma unroll
                     for (int i = 0; i < 8; ++i) dst[i] = make_uint4(0, 0, 0, 0);
@@ -393,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st16x2_16<16>(t_w + b * kBN, pk);
             if (j > 0 && __any_sync(~0u, need)) {
                 // O holds P V up to tile j-1: wait for it, then rescale the rows that need it
-                if (!__all_sync(~0u, mbar_wait(hb.pv_done + ((j - 1) & 1), ((j - 1) >> 1) & 1))) {
+                if (!__all_sync(~0u, mbar_wait(pv_done + ((j - 1) & 1), ((j - 1) >> 1) & 1))) {
                     tmem_wait_st();
                     ok = false;
                     break;
@@ -411,47 +370,43 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(hb.p_full + b);
+            mbar_arrive(p_full + b);
         }
         if (!ok) {
             atomicOr(a.err, kErrWaitTimeout);
             *abort_flag = 1;
-        } else if (!__all_sync(~0u, mbar_wait(hb.pv_done + ((n_tiles - 1) & 1), ((n_tiles - 1) >> 1) & 1))) {
+        } else if (!__all_sync(~0u, mbar_wait(pv_done + ((n_tiles - 1) & 1), ((n_tiles - 1) >> 1) & 1))) {
             atomicOr(a.err, kErrWaitTimeout);
             *abort_flag = 1;
         } else {
             tc_fence_after();
-            // every MMA of this head is complete, so its Q tile (32 KB) is free: each warp stages
-            // 16 rows x 64 columns (4 KB, 16-byte chunks XOR-swizzled by row) per round, two rounds
+            // all MMAs and copies are complete: the K/V rings (64 KB) become the staging area,
+            // 8 KB = 16 rows x 512 B per warp, 16-byte chunks XOR-swizzled by row
             const float inv = 1.f / (l_run + __shfl_xor_sync(~0u, l_run, 16));
-            uint8_t* stage = sQ + hs * kQBytes + lw * 4096;
+            uint8_t* stage = sK + warp * (16 * 512);
 #pragma unroll 1
             for (int c2 = 0; c2 < 2; ++c2) {
                 uint32_t o[32];
-                tmem_ld16x2_32<64>(t_w + kColO + c2 * 32, o);  // cols hc*64 + c2*32 + [0, 32)
+                tmem_ld16x2_32<64>(t_w + kColO + c2 * 32, o);
                 tmem_wait_ld();
+                const int ch0 = (hc * 64 + c2 * 32) / 4;
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
                     const float4 v = make_float4(__uint_as_float(o[4 * q]) * inv, __uint_as_float(o[4 * q + 1]) * inv,
                                                  __uint_as_float(o[4 * q + 2]) * inv,
                                                  __uint_as_float(o[4 * q + 3]) * inv);
-                    *reinterpret_cast<float4*>(stage + r16 * 256 + (((hc * 8 + q) ^ r16) << 4)) = v;
+                    *reinterpret_cast<float4*>(stage + r16 * 512 + (((ch0 + q) ^ (r16 & 7)) << 4)) = v;
                 }
-                __syncwarp();
-                // two rows per pass: lane l writes row 2*k + l/16, chunk l%16 (half l%16/8)
-#pragma unroll 2
-                for (int k = 0; k < 8; ++k) {
-                    const int rr = 2 * k + (lane >> 4);
-                    const int t = row0 + rr;
-                    const int c = lane & 15;
-                    if (t < n_q) {
-                        const float4 v = *reinterpret_cast<const float4*>(stage + rr * 256 + ((c ^ rr) << 4));
-                        float* dst = a.out + (static_cast<int64_t>(qrow0 + t) * a.n_heads + h) * kD +
-                                     (c >> 3) * 64 + c2 * 32 + (c & 7) * 4;
-                        __stcs(reinterpret_cast<float4*>(dst), v);
-                    }
+            }
+            __syncwarp();
+#pragma unroll 4
+            for (int rr = 0; rr < 16; ++rr) {
+                const int t = row0 + rr;
+                if (t < n_q) {
+                    const float4 v = *reinterpret_cast<const float4*>(stage + rr * 512 + ((lane ^ (rr & 7)) << 4));
+                    float* dst = a.out + (static_cast<int64_t>(qrow0 + t) * a.n_heads + h) * kD + lane * 4;
+                    __stcs(reinterpret_cast<float4*>(dst), v);
                 }
-                __syncwarp();
             }
         }
     }
@@ -566,9 +521,7 @@ cudaError_t launch_paged_prefill_tc(const ArenaGeom& g, const PrefillArgs& a, co
     }
     cudaError_t e = prefill_prepare();
     if (e != cudaSuccess) return e;
-    // one CTA per (item, kv head, pair of its query heads)
-    const int group = a.n_heads / g.heads_kv;
-    const int64_t grid = static_cast<int64_t>(a.n_items) * g.heads_kv * ((group + kHP - 1) / kHP);
+    const int64_t grid = static_cast<int64_t>(a.n_items) * a.n_heads;
     if (grid > 0x7fffffff) return cudaErrorInvalidValue;
     const bool f16 = g.dtype == GKV_DTYPE_F16;
     auto kern = rows == 16 ? (f16 ? paged_prefill_tc_kernel<16, true> : paged_prefill_tc_kernel<16, false>)
