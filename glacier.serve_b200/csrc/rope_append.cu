@@ -173,13 +173,6 @@ __device__ __forceinline__ void prologue_row(float (&x)[E], const float* bias, b
     }
 }
 
-// Asks L2 for the 128-byte lines of [p, p + bytes), spread over the warp's lanes.
-__device__ __forceinline__ void prefetch_l2(const void* p, int64_t bytes, int lane) {
-    const char* c = static_cast<const char*>(p);
-    for (int64_t off = static_cast<int64_t>(lane) * 128; off < bytes; off += 32 * 128)
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(c + off));
-}
-
 template <int E>
 __device__ __forceinline__ void load_row(const float* p, float (&x)[E]) {
     if constexpr (E % 4 == 0) {
@@ -216,22 +209,13 @@ __device__ __forceinline__ void store_row(float* p, const float (&x)[E]) {
 // token; q heads go U at a time (their loads issued together), then the k heads into the arena,
 // then the v heads.
 template <typename KV, int E>
-__global__ void __launch_bounds__(256, E >= 8 ? 1 : 3) rope_append_kernel(ArenaGeom g, RopeArgs a) {
+__global__ void __launch_bounds__(256) rope_append_kernel(ArenaGeom g, RopeArgs a) {
     constexpr int D = 32 * E;
     constexpr int U = 4;
     const int lane = threadIdx.x & 31;
     const int n_warps = static_cast<int>((static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5);
     for (int t = static_cast<int>((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5); t < a.n_tok;
          t += n_warps) {
-        // the rows of this warp's next token stream into L2 while this token is processed (a
-        // prefetch holds no registers, so more bytes are in flight than the loads below allow)
-        if (t + n_warps < a.n_tok) {
-            const int tn = t + n_warps;
-            prefetch_l2(a.q + static_cast<int64_t>(tn) * a.n_heads * D, static_cast<int64_t>(a.n_heads) * D * 4, lane);
-            prefetch_l2(a.k + static_cast<int64_t>(tn) * g.heads_kv * D, static_cast<int64_t>(g.heads_kv) * D * 4, lane);
-            prefetch_l2(a.v + static_cast<int64_t>(tn) * g.heads_kv * g.v_head_dim,
-                        static_cast<int64_t>(g.heads_kv) * g.v_head_dim * 4, lane);
-        }
         const int pos = __ldg(a.positions + t);
         float sn[E], cs[E], qw[E], kw[E];
         lane_angles<E>(a, pos, lane, sn, cs);
