@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <stdint.h>
 
 #include <utility>
@@ -170,6 +171,12 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
     __half2 v = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Two e4m3 values (the low byte first) as two fp32 values; e4m3 -> fp16 -> fp32 is exact.
+__device__ __forceinline__ float2 fp8x2_to_float2(uint32_t pair) {
+    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(pair), __NV_E4M3);
+    return __half22float2(__half2(h));
 }
 
 template <bool F16>

@@ -192,6 +192,8 @@ struct Pool {
 
     StepWorkspace ws;
     int last_launches = 0;
+    // FP8 pools: [4][layers][heads_kv] device floats (K scale, V scale, their reciprocals)
+    float* d_scales = nullptr;
     // TMA maps of the arena for the tensor-core decode, encoded once at creation
     alignas(64) unsigned char tmap_k[128];
     alignas(64) unsigned char tmap_v[128];

@@ -7,9 +7,11 @@
 
 namespace gkv {
 
-// Bytes per stored KV element of a GKV_DTYPE_* (fp32: 4; bf16 and fp16: 2).
-inline int elem_bytes_of(int dtype) { return dtype == 0 ? 4 : 2; }
-inline bool valid_kv_dtype(int dtype) { return dtype >= 0 && dtype <= 2; }
+// Bytes per stored KV element of a GKV_DTYPE_* (fp32: 4; bf16 and fp16: 2; fp8 e4m3: 1).
+inline int elem_bytes_of(int dtype) { return dtype == 0 ? 4 : (dtype == 3 ? 1 : 2); }
+inline bool valid_kv_dtype(int dtype) { return dtype >= 0 && dtype <= 3; }
+// Query / conversion types: fp32, bf16 and fp16 (fp8 is a storage format only).
+inline bool valid_q_dtype(int dtype) { return dtype >= 0 && dtype <= 2; }
 
 // Geometry of one pool's arenas, in ELEMENTS of the storage type.
 struct ArenaGeom {
@@ -26,6 +28,12 @@ struct ArenaGeom {
     // The same with boxes of 16 slots (block sizes that are multiples of 16), for the prefill.
     const void* tmap_pk = nullptr;
     const void* tmap_pv = nullptr;
+    // FP8 arenas: device [layers][heads_kv] K and V scales and their reciprocals (an element
+    // stores e4m3(x * inv) and reads back as e4m3 * scale); nullptr for every other type.
+    const float* k_scale = nullptr;
+    const float* v_scale = nullptr;
+    const float* k_inv = nullptr;
+    const float* v_inv = nullptr;
 };
 
 // ---- kv append ----

@@ -6,7 +6,8 @@
 // token i's row for kv head h is copied from the contiguous source [n_tok][heads_kv][dim]
 // into arena element (block, layer, h, offset) with block = slot / block_size,
 // offset = slot % block_size.  fp32 storage is a bit copy; bf16 and fp16 storage round to
-// nearest even.  HBM-bound: each (token, head) row is one warp moving 16-byte vectors, two rows per
+// nearest even; fp8 e4m3 stores x * (1 / scale) of the row's (layer, head), rounded to nearest
+// even and saturated.  HBM-bound: each (token, head) row is one warp moving 16-byte vectors, two rows per
 // warp iteration.
 #include "gkv_device.cuh"
 #include "kernels.h"
@@ -16,16 +17,24 @@ namespace gkv {
 
 namespace {
 
+// `inv` is the reciprocal of an FP8 arena's (layer, head) scale; the other types ignore it.
 template <typename KV>
-__device__ __forceinline__ void store4(KV* dst, float4 v);
+__device__ __forceinline__ void store4(KV* dst, float4 v, float inv);
 
 template <>
-__device__ __forceinline__ void store4<float>(float* dst, float4 v) {
+__device__ __forceinline__ void store4<float>(float* dst, float4 v, float) {
     *reinterpret_cast<float4*>(dst) = v;
 }
 
 template <>
-__device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* dst, float4 v) {
+__device__ __forceinline__ void store4<__nv_fp8_e4m3>(__nv_fp8_e4m3* dst, float4 v, float inv) {
+    const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(v.x * inv, v.y * inv), __NV_SATFINITE, __NV_E4M3);
+    const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(v.z * inv, v.w * inv), __NV_SATFINITE, __NV_E4M3);
+    *reinterpret_cast<uint32_t*>(dst) = lo | (hi << 16);
+}
+
+template <>
+__device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* dst, float4 v, float) {
     __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y);
     __nv_bfloat162 b = __floats2bfloat162_rn(v.z, v.w);
     uint2 w;
@@ -35,7 +44,7 @@ __device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* dst, float4
 }
 
 template <>
-__device__ __forceinline__ void store4<__half>(__half* dst, float4 v) {
+__device__ __forceinline__ void store4<__half>(__half* dst, float4 v, float) {
     __half2 a = __floats2half2_rn(v.x, v.y);
     __half2 b = __floats2half2_rn(v.z, v.w);
     uint2 w;
@@ -45,16 +54,20 @@ __device__ __forceinline__ void store4<__half>(__half* dst, float4 v) {
 }
 
 template <typename KV>
-__device__ __forceinline__ void store1(KV* dst, float v);
+__device__ __forceinline__ void store1(KV* dst, float v, float inv);
 template <>
-__device__ __forceinline__ void store1<float>(float* dst, float v) { *dst = v; }
+__device__ __forceinline__ void store1<float>(float* dst, float v, float) { *dst = v; }
 template <>
-__device__ __forceinline__ void store1<__nv_bfloat16>(__nv_bfloat16* dst, float v) {
+__device__ __forceinline__ void store1<__nv_bfloat16>(__nv_bfloat16* dst, float v, float) {
     *dst = __float2bfloat16_rn(v);
 }
 template <>
-__device__ __forceinline__ void store1<__half>(__half* dst, float v) {
+__device__ __forceinline__ void store1<__half>(__half* dst, float v, float) {
     *dst = __float2half_rn(v);
+}
+template <>
+__device__ __forceinline__ void store1<__nv_fp8_e4m3>(__nv_fp8_e4m3* dst, float v, float inv) {
+    dst->__x = __nv_cvt_float_to_fp8(v * inv, __NV_SATFINITE, __NV_E4M3);
 }
 
 // x / d and x % d for the non-negative row and slot indices; `shift` >= 0 when d is a power of
@@ -74,6 +87,7 @@ struct AppendRow {
     KV* dv;
     const float* sk;
     const float* sv;
+    float kinv, vinv;  // FP8: reciprocal scales of the row's (layer, head)
     bool ok;
 };
 
@@ -112,7 +126,7 @@ __device__ __forceinline__ void fetch_slots(int64_t (&s)[kRows], const AppendArg
 template <typename KV>
 __device__ __forceinline__ AppendRow<KV> resolve_row(const ArenaGeom& g, const AppendArgs& a,
                                                      int row, int64_t slot, int lane) {
-    AppendRow<KV> r{nullptr, nullptr, nullptr, nullptr, false};
+    AppendRow<KV> r{nullptr, nullptr, nullptr, nullptr, 1.f, 1.f, false};
     if (slot < 0) return r;  // past the end, or a padding token
     const int64_t blk = div_slot(slot, g.block_size, a.bs_shift);
     const int off = static_cast<int>(slot - blk * g.block_size);
@@ -128,6 +142,10 @@ __device__ __forceinline__ AppendRow<KV> resolve_row(const ArenaGeom& g, const A
            h * g.v_head_stride + static_cast<int64_t>(off) * g.v_head_dim;
     r.sk = a.k + i * a.k_tok_stride + static_cast<int64_t>(h) * g.head_dim;
     r.sv = a.v + i * a.v_tok_stride + static_cast<int64_t>(h) * g.v_head_dim;
+    if (g.k_inv) {
+        r.kinv = __ldg(g.k_inv + a.layer * g.heads_kv + h);
+        r.vinv = __ldg(g.v_inv + a.layer * g.heads_kv + h);
+    }
     r.ok = true;
     return r;
 }
@@ -161,16 +179,16 @@ __global__ void __launch_bounds__(256, 4) kv_append_kernel(ArenaGeom g, AppendAr
                 }
 #pragma unroll
                 for (int u = 0; u < kRows; ++u) {
-                    if (r[u].ok && e < hd) store4<KV>(r[u].dk + e, x[u]);
-                    if (r[u].ok && e < vhd) store4<KV>(r[u].dv + e, y[u]);
+                    if (r[u].ok && e < hd) store4<KV>(r[u].dk + e, x[u], r[u].kinv);
+                    if (r[u].ok && e < vhd) store4<KV>(r[u].dv + e, y[u], r[u].vinv);
                 }
             }
         } else {
 #pragma unroll
             for (int u = 0; u < kRows; ++u) {
                 if (!r[u].ok) continue;
-                for (int e = lane; e < hd; e += 32) store1<KV>(r[u].dk + e, __ldg(r[u].sk + e));
-                for (int e = lane; e < vhd; e += 32) store1<KV>(r[u].dv + e, __ldg(r[u].sv + e));
+                for (int e = lane; e < hd; e += 32) store1<KV>(r[u].dk + e, __ldg(r[u].sk + e), r[u].kinv);
+                for (int e = lane; e < vhd; e += 32) store1<KV>(r[u].dv + e, __ldg(r[u].sv + e), r[u].vinv);
             }
         }
     }
@@ -223,6 +241,7 @@ cudaError_t launch_kv_append(const ArenaGeom& g, int layer, const float* k, cons
     AppendArgs a{layer, k, v, k_tok_stride, v_tok_stride, slots, single_slot, n_tok, -1, -1, err};
     if (g.dtype == GKV_DTYPE_BF16) return launch_typed<__nv_bfloat16>(g, a, stream);
     if (g.dtype == GKV_DTYPE_F16) return launch_typed<__half>(g, a, stream);
+    if (g.dtype == GKV_DTYPE_FP8_E4M3) return launch_typed<__nv_fp8_e4m3>(g, a, stream);
     return launch_typed<float>(g, a, stream);
 }
 

@@ -99,6 +99,27 @@ __device__ __forceinline__ void load_pairs(const KV* p, float2 (&o)[(EPL + 1) / 
                 o[i / 2 + 3] = __half22float2(*reinterpret_cast<const __half2*>(&w.w));
             }
         }
+    } else if constexpr (std::is_same<KV, __nv_fp8_e4m3>::value) {
+        // e4m3 -> fp16 -> fp32 is exact; the (layer, head) scale is applied by the caller
+        const unsigned char* u = reinterpret_cast<const unsigned char*>(p);
+        if constexpr (EPL == 1) {
+            o[0] = make_float2(fp8x2_to_float2(u[0]).x, 0.f);
+        } else if constexpr (EPL == 2) {
+            o[0] = fp8x2_to_float2(*reinterpret_cast<const uint16_t*>(u));
+        } else if constexpr (EPL == 4) {
+            const uint32_t w = *reinterpret_cast<const uint32_t*>(u);
+            o[0] = fp8x2_to_float2(w & 0xffffu);
+            o[1] = fp8x2_to_float2(w >> 16);
+        } else {
+#pragma unroll
+            for (int i = 0; i < EPL; i += 8) {
+                const uint2 w = *reinterpret_cast<const uint2*>(u + i);
+                o[i / 2 + 0] = fp8x2_to_float2(w.x & 0xffffu);
+                o[i / 2 + 1] = fp8x2_to_float2(w.x >> 16);
+                o[i / 2 + 2] = fp8x2_to_float2(w.y & 0xffffu);
+                o[i / 2 + 3] = fp8x2_to_float2(w.y >> 16);
+            }
+        }
     } else {
         const uint16_t* u = reinterpret_cast<const uint16_t*>(p);
         if constexpr (EPL == 1) {
@@ -160,6 +181,7 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
                                                                DecodeArgs a, int group, int cpp) {
     using Tr = DecodeKernelTraits<KV, D, DV, GP, NW, S>;
     constexpr int EPL = Tr::EPL, EPLV = Tr::EPLV, EP2 = Tr::EP2, EV2 = Tr::EV2;
+    constexpr bool kFp8 = std::is_same<KV, __nv_fp8_e4m3>::value;
     constexpr int NV = Tr::NV, NB = Tr::NB, R = Tr::R, DUP = Tr::DUP, LG = Tr::LG;
     extern __shared__ __align__(128) unsigned char smem[];
 
@@ -281,6 +303,12 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
         const int ctx = __ldg(w.ctx_lens + b);
         const int q_head0 = h * group + hg * GP;
         const int gcount = min(GP, group - hg * GP);
+        // FP8: the K scale folds into the score scale, the V scale into the piece's output
+        float sl2 = scale_log2, vsc = 1.f;
+        if constexpr (kFp8) {
+            sl2 = scale_log2 * __ldg(g.k_scale + a.layer * g.heads_kv + h);
+            vsc = __ldg(g.v_scale + a.layer * g.heads_kv + h);
+        }
 
         // q in permuted slots: slot gs holds head gs ^ Xg
         float2 q[GP][EP2];
@@ -337,7 +365,7 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
                 float cmax = -INFINITY;
 #pragma unroll
                 for (int r = 0; r < R; ++r) {
-                    s2[r] = (t_own + r < ntok) ? sc[r] * scale_log2 : -INFINITY;
+                    s2[r] = (t_own + r < ntok) ? sc[r] * sl2 : -INFINITY;
                     cmax = fmaxf(cmax, s2[r]);
                 }
 #pragma unroll
@@ -434,7 +462,8 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
                     Ls = Ls * f + exp2f(sk - M2);
                     Mref = M2;
                 }
-                const float inv = Ls > 0.f ? f / Ls : 0.f;
+                float inv = Ls > 0.f ? f / Ls : 0.f;
+                if constexpr (kFp8) inv *= vsc;
                 if (a.lse && lane == 0) a.lse[static_cast<int64_t>(b) * a.n_heads + qh] = lse_ln(Mref, Ls);
                 float* op = a.out + (static_cast<int64_t>(b) * a.n_heads + qh) * DV + lane * EPLV;
 #pragma unroll
@@ -450,6 +479,7 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
                 float* ap = a.part_acc + (base + gg) * DV + lane * EPLV;
 #pragma unroll
                 for (int e = 0; e < EV2; ++e) {
+                    if constexpr (kFp8) acc[gg][e] = __fmul2_rn(acc[gg][e], make_float2(vsc, vsc));
                     ap[2 * e] = acc[gg][e].x;
                     if (2 * e + 1 < EPLV) ap[2 * e + 1] = acc[gg][e].y;
                 }
@@ -582,6 +612,13 @@ bool dispatch(const ArenaGeom& g, int gp, F&& f) {
     };
     if (g.dtype == GKV_DTYPE_BF16) return by_dims(__nv_bfloat16{});
     if (g.dtype == GKV_DTYPE_F16) return by_dims(__half{});
+    if (g.dtype == GKV_DTYPE_FP8_E4M3) {  // the common head dims only
+        if (g.head_dim == 128 && g.v_head_dim == 128)
+            return by_gp(__nv_fp8_e4m3{}, std::integral_constant<int, 128>{}, std::integral_constant<int, 128>{});
+        if (g.head_dim == 64 && g.v_head_dim == 64)
+            return by_gp(__nv_fp8_e4m3{}, std::integral_constant<int, 64>{}, std::integral_constant<int, 64>{});
+        return false;
+    }
     return by_dims(float{});
 }
 

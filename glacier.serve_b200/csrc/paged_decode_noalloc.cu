@@ -106,6 +106,8 @@ extern "C" int gkv_paged_decode_noalloc(const gkv_arena_desc* arena, int32_t lay
     if (A.total_blocks < 1 || A.layers < 1 || A.heads_kv < 1 || A.head_dim < 1 ||
         !valid_kv_dtype(A.dtype))
         return set_error(GKV_EINVAL, "invalid arena description");
+    if (A.dtype == GKV_DTYPE_FP8_E4M3)  // the description carries no per-head scales
+        return set_error(GKV_EINVAL, "an FP8 arena needs its pool's scales: use gkv_paged_decode");
     if (layer < 0 || layer >= A.layers) return set_error(GKV_EINVAL, "layer %d outside [0, %d)", layer, A.layers);
     if (n_heads <= 0 || n_heads % A.heads_kv != 0)
         return set_error(GKV_EINVAL, "n_heads %d is not a positive multiple of heads_kv %d", n_heads, A.heads_kv);

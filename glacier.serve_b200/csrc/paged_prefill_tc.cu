@@ -476,7 +476,7 @@ bool prefill_tc_eligible(const ArenaGeom& g, int n_heads) {
 cudaError_t launch_convert(const void* src, int32_t src_dtype, void* dst, int32_t dst_dtype, int64_t n,
                            cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
-    if (!valid_kv_dtype(src_dtype) || !valid_kv_dtype(dst_dtype) || src_dtype == dst_dtype)
+    if (!valid_q_dtype(src_dtype) || !valid_q_dtype(dst_dtype) || src_dtype == dst_dtype)
         return cudaErrorInvalidValue;
     int64_t blocks = (n + 255) / 256;
     if (blocks > 148 * 16) blocks = 148 * 16;

@@ -6,10 +6,12 @@
 // LIFO free list popped 0..N-1 first, atomic reference counts starting at 1, idempotent
 // release, prefix map with hash re-validation, copy-on-write forks.  What changes is that
 // the K/V arena lives in HBM and CoW copies become batched device block copies.
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
 #include <new>
+#include <vector>
 
 #include "gkv_internal.h"
 
@@ -272,7 +274,12 @@ int gkv_pool_create(const gkv_pool_desc* desc, gkv_pool** out_pool) {
     if (d.head_dim < 1) return set_error(GKV_EINVAL, "headDim must be >= 1 (got %d)", d.head_dim);
     if (d.block_size < 1) return set_error(GKV_EINVAL, "blockSize must be >= 1 (got %d)", d.block_size);
     if (!gkv::valid_kv_dtype(d.dtype))
-        return set_error(GKV_EINVAL, "dtype %d is not GKV_DTYPE_F32, GKV_DTYPE_BF16 or GKV_DTYPE_F16", d.dtype);
+        return set_error(GKV_EINVAL, "dtype %d is not GKV_DTYPE_F32, _BF16, _F16 or _FP8_E4M3", d.dtype);
+    // FP8 rows are whole 16-byte vectors (appends store 4 elements a lane, block copies move
+    // 2 bytes a lane at least, decode copies 8-token spans in 16-byte units)
+    if (d.dtype == GKV_DTYPE_FP8_E4M3 && (d.head_dim % 16 != 0 || d.v_head_dim % 16 != 0))
+        return set_error(GKV_EINVAL, "FP8 storage needs head dims that are multiples of 16 (got %d / %d)",
+                         d.head_dim, d.v_head_dim);
     if (d.allocate_device_arena && d.device < 0) return set_error(GKV_EINVAL, "device %d < 0", d.device);
 
     gkv_pool* p = new (std::nothrow) gkv_pool();
@@ -338,6 +345,26 @@ int gkv_pool_create(const gkv_pool_desc* desc, gkv_pool** out_pool) {
         g.k = k;
         g.v = v;
         P.has_arena = true;
+        if (d.dtype == GKV_DTYPE_FP8_E4M3) {
+            // scales and reciprocals start at 1
+            const size_t n = static_cast<size_t>(d.layers) * d.heads_kv;
+            std::vector<float> ones(4 * n, 1.f);
+            e = cudaMalloc(&P.d_scales, 4 * n * sizeof(float));
+            if (e == cudaSuccess) e = cudaMemcpy(P.d_scales, ones.data(), 4 * n * sizeof(float), cudaMemcpyHostToDevice);
+            if (e != cudaSuccess) {
+                const int rc = gkv::cuda_fail(e, "fp8 scale allocation");
+                if (P.d_scales) cudaFree(P.d_scales);
+                cudaFree(k);
+                cudaFree(v);
+                cudaFree(P.ws.d_err);
+                delete p;
+                return rc;
+            }
+            g.k_scale = P.d_scales;
+            g.v_scale = P.d_scales + n;
+            g.k_inv = P.d_scales + 2 * n;
+            g.v_inv = P.d_scales + 3 * n;
+        }
         // TMA maps for the tensor-core kernels (16-bit storage, d = dv = 128, 8-token-aligned
         // blocks); the copies move 2-byte elements, whichever 16-bit format they hold
         if (d.dtype != GKV_DTYPE_F32 && d.head_dim == 128 && d.v_head_dim == 128 && d.block_size % 8 == 0 &&
@@ -367,10 +394,35 @@ int gkv_pool_destroy(gkv_pool* pool) {
         if (P.h_copy_ops) cudaFreeHost(P.h_copy_ops);
         if (P.copy_ops_copied) cudaEventDestroy(P.copy_ops_copied);
         if (P.ws.d_err) cudaFree(P.ws.d_err);
+        if (P.d_scales) cudaFree(P.d_scales);
         cudaFree(P.geom.k);
         cudaFree(P.geom.v);
     }
     delete pool;
+    return GKV_OK;
+}
+
+int gkv_pool_set_kv_scales(gkv_pool* pool, const float* h_k_scales, const float* h_v_scales) {
+    GKV_CHECK_POOL(pool);
+    Pool& P = pool->impl;
+    if (P.desc.dtype != GKV_DTYPE_FP8_E4M3) return set_error(GKV_ESTATE, "KV scales belong to FP8 pools");
+    if (!h_k_scales || !h_v_scales) return set_error(GKV_EINVAL, "scales are NULL");
+    const size_t n = static_cast<size_t>(P.desc.layers) * P.desc.heads_kv;
+    std::vector<float> all(4 * n);
+    for (size_t i = 0; i < n; ++i) {
+        const float ks = h_k_scales[i], vs = h_v_scales[i];
+        if (!(ks > 0.f) || !(vs > 0.f) || !std::isfinite(ks) || !std::isfinite(vs))
+            return set_error(GKV_EINVAL, "scale %zu (%g, %g) is not positive and finite", i, static_cast<double>(ks),
+                             static_cast<double>(vs));
+        all[i] = ks;
+        all[n + i] = vs;
+        all[2 * n + i] = 1.f / ks;
+        all[3 * n + i] = 1.f / vs;
+    }
+    if (!P.has_arena) return GKV_OK;
+    gkv::DeviceGuard guard(P.desc.device);
+    cudaError_t e = cudaMemcpy(P.d_scales, all.data(), 4 * n * sizeof(float), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return gkv::cuda_fail(e, "cudaMemcpy(fp8 scales)");
     return GKV_OK;
 }
 

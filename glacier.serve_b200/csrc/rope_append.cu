@@ -73,14 +73,21 @@ struct RopeArgs {
     int* err;
 };
 
+// `inv` is the reciprocal of an FP8 arena's (layer, head) scale; the other types ignore it.
 template <typename KV>
-__device__ __forceinline__ void store_elem(KV* p, float x);
+__device__ __forceinline__ void store_elem(KV* p, float x, float inv);
 template <>
-__device__ __forceinline__ void store_elem<float>(float* p, float x) { *p = x; }
+__device__ __forceinline__ void store_elem<float>(float* p, float x, float) { *p = x; }
 template <>
-__device__ __forceinline__ void store_elem<__nv_bfloat16>(__nv_bfloat16* p, float x) { *p = __float2bfloat16_rn(x); }
+__device__ __forceinline__ void store_elem<__nv_bfloat16>(__nv_bfloat16* p, float x, float) {
+    *p = __float2bfloat16_rn(x);
+}
 template <>
-__device__ __forceinline__ void store_elem<__half>(__half* p, float x) { *p = __float2half_rn(x); }
+__device__ __forceinline__ void store_elem<__half>(__half* p, float x, float) { *p = __float2half_rn(x); }
+template <>
+__device__ __forceinline__ void store_elem<__nv_fp8_e4m3>(__nv_fp8_e4m3* p, float x, float inv) {
+    p->__x = __nv_cvt_float_to_fp8(x * inv, __NV_SATFINITE, __NV_E4M3);
+}
 
 // Angles of the pairs this lane's E elements belong to, for position pos: (sin, cos) per element
 // (elements from rope_dim on get none).  NEOX pairs (i, i + R/2): element j < R/2 is pair j, and
@@ -260,8 +267,9 @@ __global__ void __launch_bounds__(256) rope_append_kernel(ArenaGeom g, RopeArgs 
                                     lane);
                     KV* dst = static_cast<KV*>(g.k) + blk * g.k_block_stride + a.layer * g.k_layer_stride +
                               (h0 + u) * g.k_head_stride + static_cast<int64_t>(off) * D + lane * E;
+                    const float inv = g.k_inv ? __ldg(g.k_inv + a.layer * g.heads_kv + h0 + u) : 1.f;
 #pragma unroll
-                    for (int e = 0; e < E; ++e) store_elem<KV>(dst + e, x[u][e]);
+                    for (int e = 0; e < E; ++e) store_elem<KV>(dst + e, x[u][e], inv);
                 }
             }
         }
@@ -270,10 +278,11 @@ __global__ void __launch_bounds__(256) rope_append_kernel(ArenaGeom g, RopeArgs 
             const float* vp = a.v + (static_cast<int64_t>(t) * g.heads_kv + h) * dv;
             KV* dst = static_cast<KV*>(g.v) + blk * g.v_block_stride + a.layer * g.v_layer_stride +
                       h * g.v_head_stride + static_cast<int64_t>(off) * dv;
+            const float inv = g.v_inv ? __ldg(g.v_inv + a.layer * g.heads_kv + h) : 1.f;
             for (int e = lane; e < dv; e += 32) {
                 float x = __ldg(vp + e);
                 if (a.v_bias) x = __fadd_rn(x, __ldg(a.v_bias + h * dv + e));
-                store_elem<KV>(dst + e, x);
+                store_elem<KV>(dst + e, x, inv);
             }
         }
     }
@@ -310,6 +319,7 @@ cudaError_t launch_rope_append(const ArenaGeom& g, const RopeAppendParams& p, cu
                p.mscale, p.q_bias, p.k_bias, p.v_bias, p.q_norm, p.k_norm, p.eps, p.slots, p.err};
     if (g.dtype == GKV_DTYPE_BF16) return launch_typed<__nv_bfloat16>(g, a, st);
     if (g.dtype == GKV_DTYPE_F16) return launch_typed<__half>(g, a, st);
+    if (g.dtype == GKV_DTYPE_FP8_E4M3) return launch_typed<__nv_fp8_e4m3>(g, a, st);
     return launch_typed<float>(g, a, st);
 }
 

@@ -649,7 +649,7 @@ int step_prefill(Pool* p, int32_t layer, const void* d_q, int32_t q_dtype, float
     if (n_heads <= 0 || n_heads % p->desc.heads_kv != 0)
         return set_error(GKV_EINVAL, "n_heads %d is not a positive multiple of heads_kv %d", n_heads,
                          p->desc.heads_kv);
-    if (!valid_kv_dtype(q_dtype))
+    if (!valid_q_dtype(q_dtype))
         return set_error(GKV_EINVAL, "q_dtype %d is not GKV_DTYPE_F32, GKV_DTYPE_BF16 or GKV_DTYPE_F16", q_dtype);
     const int32_t batch = ws.batch;
     if (batch > 0 && (!q_start || !q_len)) return set_error(GKV_EINVAL, "q_start/q_len is NULL");

@@ -18,7 +18,7 @@ from typing import Iterable, Optional, Sequence, Tuple
 import numpy as np
 
 from . import _lib
-from ._lib import (DTYPES, GKV_DTYPE_BF16, GKV_DTYPE_F16, GKV_DTYPE_F32, GKV_EDEVICE, GKV_EINVAL, GKV_ESTATE,
+from ._lib import (DTYPES, GKV_DTYPE_BF16, GKV_DTYPE_F16, GKV_DTYPE_F32, GKV_DTYPE_FP8_E4M3, GKV_EDEVICE, GKV_EINVAL, GKV_ESTATE,
                    GKV_ETIMEDOUT, GKV_EUNSUPPORTED, GKV_OK, LIB_PATH, last_error, lib)
 
 GKV_ROPE_NEOX, GKV_ROPE_INTERLEAVED = 0, 1
@@ -215,8 +215,27 @@ class PagedBlockPool:
         _check(lib.gkv_pool_element_offset(self._h, which, block, layer, head_kv, slot, C.byref(out)))
         return out.value
 
+    def set_kv_scales(self, k_scales, v_scales) -> None:
+        """FP8 pools: the [layers][heads_kv] K and V scales (an element reads back as
+        e4m3 * scale and is stored as e4m3(x / scale)).  Set them before the first append."""
+        n = self._layers * self._heads_kv
+        ks = np.ascontiguousarray(np.asarray(k_scales, np.float32).reshape(-1))
+        vs = np.ascontiguousarray(np.asarray(v_scales, np.float32).reshape(-1))
+        if ks.size != n or vs.size != n:
+            raise ArgumentOutOfRangeError(GKV_EINVAL, f"scales need {n} values each")
+        pf = C.POINTER(C.c_float)
+        _check(lib.gkv_pool_set_kv_scales(self._h, ks.ctypes.data_as(pf), vs.ctypes.data_as(pf)))
+        self._kv_scales = (ks.reshape(self._layers, self._heads_kv).copy(), vs.reshape(self._layers, self._heads_kv).copy())
+
+    @property
+    def kv_scales(self):
+        """The FP8 pool's ([layers][heads_kv] K, V) scales as last set (ones by default)."""
+        ones = np.ones((self._layers, self._heads_kv), np.float32)
+        return getattr(self, "_kv_scales", (ones, ones))
+
     def key_view(self):
-        """torch view [blocks][layers][heads_kv][block_size][head_dim] of the K arena."""
+        """torch view [blocks][layers][heads_kv][block_size][head_dim] of the K arena (uint8
+        bytes for an FP8 pool, e4m3 bit patterns)."""
         return self._view(self._kv_ptrs()[0], self._head_dim)
 
     def value_view(self):
@@ -228,6 +247,8 @@ class PagedBlockPool:
         if not ptr:
             raise InvalidOperationError(GKV_ESTATE, "Host KV buffers were omitted.")
         shape = (self.total_blocks, self._layers, self._heads_kv, self.block_size, dim)
+        if self.dtype == "fp8":
+            return torch.as_tensor(_CudaArray(ptr, shape, "|u1"), device=f"cuda:{self.device}")
         if self.dtype in ("bf16", "f16"):
             t = torch.as_tensor(_CudaArray(ptr, shape, "<i2"), device=f"cuda:{self.device}")
             return t.view(torch.bfloat16 if self.dtype == "bf16" else torch.float16)

@@ -26,7 +26,8 @@ GKV_EUNSUPPORTED = -8
 GKV_DTYPE_F32 = 0
 GKV_DTYPE_BF16 = 1
 GKV_DTYPE_F16 = 2
-DTYPES = {"f32": GKV_DTYPE_F32, "bf16": GKV_DTYPE_BF16, "f16": GKV_DTYPE_F16}
+GKV_DTYPE_FP8_E4M3 = 3
+DTYPES = {"f32": GKV_DTYPE_F32, "bf16": GKV_DTYPE_BF16, "f16": GKV_DTYPE_F16, "fp8": GKV_DTYPE_FP8_E4M3}
 
 
 class gkv_pool_desc(C.Structure):
@@ -111,12 +112,14 @@ U64 = C.c_uint64
 F32 = C.c_float
 PI32 = C.POINTER(C.c_int32)
 PI64 = C.POINTER(C.c_int64)
+PF32 = C.POINTER(C.c_float)
 
 # name -> (restype, argtypes); every symbol of include/glacier_kv.h
 SIGNATURES = {
     "gkv_pool_create": (C.c_int, [C.POINTER(gkv_pool_desc), C.POINTER(P)]),
     "gkv_pool_destroy": (C.c_int, [P]),
     "gkv_pool_stats_get": (C.c_int, [P, C.POINTER(gkv_pool_stats)]),
+    "gkv_pool_set_kv_scales": (C.c_int, [P, PF32, PF32]),
     "gkv_pool_kv_ptrs": (C.c_int, [P, C.POINTER(P), C.POINTER(P)]),
     "gkv_pool_element_offset": (C.c_int, [P, I32, I32, I32, I32, I32, PI64]),
     "gkv_pool_try_allocate_block": (C.c_int, [P, PI32]),

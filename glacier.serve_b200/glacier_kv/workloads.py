@@ -50,7 +50,7 @@ class DecodeWorkload:
 
     @property
     def elem_bytes(self) -> int:
-        return 4 if self.dtype == "f32" else 2
+        return {"f32": 4, "bf16": 2, "f16": 2, "fp8": 1}[self.dtype]
 
     def kv_bytes(self) -> int:
         """Algorithmic KV bytes one decode step reads (each K/V row once)."""

@@ -55,8 +55,12 @@ enum {
 /* KV storage types of the device arena.  Sources handed to append/store are always fp32
  * (the reference stores fp32, PagedBlockPool.cs:151-161); bf16 and fp16 storage round to
  * nearest even on append.  GKV_DTYPE_F16 is the precision of the reference's GPU pools
- * (CudaPagedTransformerRunner.cs:118-119, KvCachePrecision.Fp16 at :139). */
-enum { GKV_DTYPE_F32 = 0, GKV_DTYPE_BF16 = 1, GKV_DTYPE_F16 = 2 };
+ * (CudaPagedTransformerRunner.cs:118-119, KvCachePrecision.Fp16 at :139).  GKV_DTYPE_FP8_E4M3 (no
+ * reference counterpart) keeps e4m3(x * (1 / scale)), rounded to nearest even and saturated at
+ * +-448, with one K scale and one V scale per (layer, kv head) (gkv_pool_set_kv_scales, default
+ * 1); it reads back as e4m3 * scale.  FP8 pools run the CUDA-core decode (head dims 64 and 128)
+ * and the decode-kernel prefill. */
+enum { GKV_DTYPE_F32 = 0, GKV_DTYPE_BF16 = 1, GKV_DTYPE_F16 = 2, GKV_DTYPE_FP8_E4M3 = 3 };
 
 typedef struct gkv_pool gkv_pool;
 typedef struct gkv_table gkv_table;
@@ -72,7 +76,7 @@ typedef struct gkv_pool_desc {
     int32_t head_dim;
     int32_t v_head_dim;            /* <= 0 means head_dim (PagedBlockPool.cs:73)          */
     int32_t block_size;            /* tokens per block; 0 means 16 (PagedBlockPool.cs:18) */
-    int32_t dtype;                 /* GKV_DTYPE_F32, GKV_DTYPE_BF16 or GKV_DTYPE_F16      */
+    int32_t dtype;                 /* GKV_DTYPE_F32, _BF16, _F16 or _FP8_E4M3             */
     int32_t allocate_device_arena; /* 0 = metadata-only pool: allocator, tables and CoW
                                       bookkeeping without any CUDA call (the reference's
                                       allocateHostBuffers:false, PagedBlockPool.cs:61,106) */
@@ -98,6 +102,11 @@ GKV_API int gkv_pool_create(const gkv_pool_desc* desc, gkv_pool** out_pool);
 GKV_API int gkv_pool_destroy(gkv_pool* pool);
 /* Counters of PagedBlockPool.cs:46-57. */
 GKV_API int gkv_pool_stats_get(const gkv_pool* pool, gkv_pool_stats* out_stats);
+/* The K and V scales of an FP8 pool, h_k_scales / h_v_scales [layers][heads_kv], positive and
+ * finite (GKV_EINVAL otherwise; GKV_ESTATE for a pool of another type).  Set them before the
+ * first append: elements already stored keep the scale they were stored with.  A synchronous
+ * host-to-device copy.  No reference counterpart (the reference stores fp32). */
+GKV_API int gkv_pool_set_kv_scales(gkv_pool* pool, const float* h_k_scales, const float* h_v_scales);
 /* KeyBufferAddress / ValueBufferAddress, PagedBlockPool.cs:58-59 (device pointers; NULL
  * for a metadata-only pool). */
 GKV_API int gkv_pool_kv_ptrs(const gkv_pool* pool, void** d_k, void** d_v);

@@ -87,7 +87,59 @@ void oracle_f32_to_f16_many(const float* src, uint16_t* dst, int64_t n) {
     for (int64_t i = 0; i < n; ++i) dst[i] = oracle_f32_to_f16(src[i]);
 }
 
-static size_t elem_size(const oracle_geom* g) { return g->dtype == ORACLE_F32 ? 4 : 2; }
+/* E4M3 from its definition, like the binary16 conversion above: rounding to nearest even on the
+ * integer significand, a carry moving into the exponent; results past 448 (the largest finite
+ * value, S.1111.110) saturate to it, and NaN stays NaN. */
+uint8_t oracle_f32_to_e4m3(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    const uint8_t sign = (uint8_t)((u >> 24) & 0x80u);
+    const int32_t e32 = (int32_t)((u >> 23) & 0xffu);
+    const uint32_t frac = u & 0x7fffffu;
+    if (e32 == 0xff && frac) return (uint8_t)(sign | 0x7fu); /* NaN */
+    if (e32 == 0xff) return (uint8_t)(sign | 0x7eu);         /* infinity saturates */
+    if (e32 == 0) return sign;                               /* far below the smallest subnormal */
+    const int32_t e8 = e32 - 127 + 7;                        /* biased e4m3 exponent */
+    if (e8 >= 16) return (uint8_t)(sign | 0x7eu);
+    const uint32_t sig = frac | 0x800000u;
+    uint32_t shift, base, kept, rem;
+    if (e8 >= 1) {                                           /* normal: keep 3 fraction bits */
+        shift = 20;
+        base = (uint32_t)e8 << 3;
+        kept = frac >> shift;
+        rem = frac & ((1u << shift) - 1u);
+    } else {                                                 /* subnormal: units of 2^-9 */
+        shift = (uint32_t)(21 - e8);
+        if (shift > 24) return sign;                         /* below a quarter unit */
+        base = 0;
+        kept = sig >> shift;
+        rem = sig & ((1u << shift) - 1u);
+    }
+    const uint32_t half = 1u << (shift - 1);
+    uint32_t r = base + kept;
+    if (rem > half || (rem == half && (kept & 1u))) ++r;     /* may carry into the exponent */
+    if (r > 0x7eu) r = 0x7eu;                                /* satfinite */
+    return (uint8_t)(sign | r);
+}
+
+float oracle_e4m3_to_f32(uint8_t b) {
+    const float sign = (b & 0x80u) ? -1.0f : 1.0f;
+    const uint32_t e = (b >> 3) & 0xfu, m = b & 7u;
+    if (e == 0xf && m == 7) return NAN;
+    if (e == 0) return sign * (float)m * 0.001953125f;       /* m * 2^-9 */
+    return sign * ldexpf(1.0f + (float)m * 0.125f, (int)e - 7);
+}
+
+void oracle_f32_to_e4m3_many(const float* src, uint8_t* dst, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) dst[i] = oracle_f32_to_e4m3(src[i]);
+}
+
+static size_t elem_size(const oracle_geom* g) { return g->dtype == ORACLE_F32 ? 4 : (g->dtype == ORACLE_FP8 ? 1 : 2); }
+
+/* Scale of (layer, head) of an FP8 arena (1 for every other type). */
+static float kv_scale(const float* scales, const oracle_geom* g, int32_t layer, int32_t h) {
+    return (g->dtype == ORACLE_FP8 && scales) ? scales[(int64_t)layer * g->heads_kv + h] : 1.0f;
+}
 
 /* Element offsets of GetKeyPtr / GetValuePtr, PagedBlockPool.cs:124-145. */
 static int64_t k_off(const oracle_geom* g, int64_t blk, int64_t layer, int64_t h, int64_t slot) {
@@ -104,17 +156,23 @@ static int64_t v_off(const oracle_geom* g, int64_t blk, int64_t layer, int64_t h
     return blk * bs + layer * ls + h * hs + slot * g->v_head_dim;
 }
 
-static inline float load_elem(const void* base, int dtype, int64_t i) {
+/* An element as fp32: FP8 elements are multiplied by their (layer, head) scale `sc`, every other
+ * type is read exactly (sc is 1). */
+static inline float load_elem(const void* base, int dtype, int64_t i, float sc) {
     if (dtype == ORACLE_BF16) return oracle_bf16_to_f32(((const uint16_t*)base)[i]);
     if (dtype == ORACLE_F16) return oracle_f16_to_f32(((const uint16_t*)base)[i]);
+    if (dtype == ORACLE_FP8) return oracle_e4m3_to_f32(((const uint8_t*)base)[i]) * sc;
     return ((const float*)base)[i];
 }
 
-static inline void store_elem(void* base, int dtype, int64_t i, float v) {
+/* Stores v in the arena's type; FP8 stores e4m3(v * inv_sc) with inv_sc = 1 / scale. */
+static inline void store_elem(void* base, int dtype, int64_t i, float v, float inv_sc) {
     if (dtype == ORACLE_BF16)
         ((uint16_t*)base)[i] = oracle_f32_to_bf16(v);
     else if (dtype == ORACLE_F16)
         ((uint16_t*)base)[i] = oracle_f32_to_f16(v);
+    else if (dtype == ORACLE_FP8)
+        ((uint8_t*)base)[i] = oracle_f32_to_e4m3(v * inv_sc);
     else
         ((float*)base)[i] = v;
 }
@@ -129,10 +187,12 @@ int oracle_store(void* kpool, void* vpool, const oracle_geom* g, int32_t block, 
     for (int32_t h = 0; h < g->heads_kv; ++h) {
         const int64_t ko = k_off(g, block, layer, h, slot);
         const int64_t vo = v_off(g, block, layer, h, slot);
+        const float kinv = 1.0f / kv_scale(g->k_scale, g, layer, h);
+        const float vinv = 1.0f / kv_scale(g->v_scale, g, layer, h);
         for (int32_t d = 0; d < g->head_dim; ++d)
-            store_elem(kpool, g->dtype, ko + d, k[(int64_t)h * g->head_dim + d]);
+            store_elem(kpool, g->dtype, ko + d, k[(int64_t)h * g->head_dim + d], kinv);
         for (int32_t d = 0; d < g->v_head_dim; ++d)
-            store_elem(vpool, g->dtype, vo + d, v[(int64_t)h * g->v_head_dim + d]);
+            store_elem(vpool, g->dtype, vo + d, v[(int64_t)h * g->v_head_dim + d], vinv);
     }
     return ORACLE_OK;
 }
@@ -186,9 +246,9 @@ int oracle_copy_many(void* kpool, void* vpool, const oracle_geom* g, const int32
 /* QuantKernels.VecDotF32 (NuGet Glacier.Inference 1.7.0, called at
  * PagedAttentionKernel.cs:64): source absent.  Restated as an in-order fp32 fused
  * multiply-add chain; the reference's lane order is unpinned. */
-static float vec_dot(const float* q, const void* kbase, int dtype, int64_t ko, int32_t n) {
+static float vec_dot(const float* q, const void* kbase, int dtype, int64_t ko, int32_t n, float ksc) {
     float s = 0.f;
-    for (int32_t i = 0; i < n; ++i) s = fmaf(q[i], load_elem(kbase, dtype, ko + i), s);
+    for (int32_t i = 0; i < n; ++i) s = fmaf(q[i], load_elem(kbase, dtype, ko + i, ksc), s);
     return s;
 }
 
@@ -245,7 +305,8 @@ int oracle_compute_attention(const void* kpool, const void* vpool, const oracle_
             const int32_t base = b * bsz;
             const int32_t tib = bsz < total - base ? bsz : total - base;
             for (int32_t t = 0; t < tib; ++t) {
-                const float dot = vec_dot(qh, kpool, g->dtype, k_off(g, pid, stage_layer, hkv, t), head_dim);
+                const float dot = vec_dot(qh, kpool, g->dtype, k_off(g, pid, stage_layer, hkv, t), head_dim,
+                                          kv_scale(g->k_scale, g, stage_layer, hkv));
                 scores[base + t] = dot * attn_scale;
             }
         }
@@ -263,7 +324,7 @@ int oracle_compute_attention(const void* kpool, const void* vpool, const oracle_
                 const float w = scores[base + t];
                 const int64_t vo = v_off(g, pid, stage_layer, hkv, t);
                 for (int32_t d = 0; d < v_head_dim; ++d)
-                    oh[d] = fmaf(w, load_elem(vpool, g->dtype, vo + d), oh[d]);
+                    oh[d] = fmaf(w, load_elem(vpool, g->dtype, vo + d, kv_scale(g->v_scale, g, stage_layer, hkv)), oh[d]);
             }
         }
     }
@@ -325,7 +386,8 @@ int oracle_decode_batch_parallel(const void* kpool, const void* vpool, const ora
                 const int32_t base = bb * bsz;
                 const int32_t tib = bsz < total - base ? bsz : total - base;
                 for (int32_t t = 0; t < tib; ++t)
-                    scores[base + t] = vec_dot(qh, kpool, g->dtype, k_off(g, ids[bb], layer, hkv, t), g->head_dim) * scale;
+                    scores[base + t] = vec_dot(qh, kpool, g->dtype, k_off(g, ids[bb], layer, hkv, t), g->head_dim,
+                                               kv_scale(g->k_scale, g, layer, hkv)) * scale;
             }
             softmax(scores, total, 0, 0.f);
             float* oh = out + ((int64_t)b * n_heads + h) * g->v_head_dim;
@@ -337,7 +399,7 @@ int oracle_decode_batch_parallel(const void* kpool, const void* vpool, const ora
                     const float w = scores[base + t];
                     const int64_t vo = v_off(g, ids[bb], layer, hkv, t);
                     for (int32_t d = 0; d < g->v_head_dim; ++d)
-                        oh[d] = fmaf(w, load_elem(vpool, g->dtype, vo + d), oh[d]);
+                        oh[d] = fmaf(w, load_elem(vpool, g->dtype, vo + d, kv_scale(g->v_scale, g, layer, hkv)), oh[d]);
                 }
             }
         }

@@ -25,13 +25,17 @@
 extern "C" {
 #endif
 
-enum { ORACLE_F32 = 0, ORACLE_BF16 = 1, ORACLE_F16 = 2 };
+enum { ORACLE_F32 = 0, ORACLE_BF16 = 1, ORACLE_F16 = 2, ORACLE_FP8 = 3 };
 enum { ORACLE_OK = 0, ORACLE_EINVAL = -1 };
 
 /* Geometry of a host copy of the arena, layout [block][layer][head_kv][slot][dim]
  * (PagedBlockPool.cs:77-83,124-145). */
 typedef struct oracle_geom {
     int32_t total_blocks, layers, heads_kv, head_dim, v_head_dim, block_size, dtype;
+    /* FP8 arenas: the K and V scales per (layer, kv head), [layers][heads_kv]; NULL means 1.
+     * An element stores e4m3(x * (1 / scale)) and reads back as e4m3 * scale. */
+    const float* k_scale;
+    const float* v_scale;
 } oracle_geom;
 
 /* fp32 -> bf16 round to nearest even (storage rounding of the bf16 arena). */
@@ -43,6 +47,11 @@ float oracle_bf16_to_f32(uint16_t h);
 uint16_t oracle_f32_to_f16(float f);
 float oracle_f16_to_f32(uint16_t h);
 void oracle_f32_to_f16_many(const float* src, uint16_t* dst, int64_t n);
+/* fp32 -> OCP FP8 E4M3 (1 sign, 4 exponent bits with bias 7, 3 fraction bits, no infinities,
+ * S.1111.111 = NaN), round to nearest even, saturating at +-448 (satfinite); and back (exact). */
+uint8_t oracle_f32_to_e4m3(float f);
+float oracle_e4m3_to_f32(uint8_t b);
+void oracle_f32_to_e4m3_many(const float* src, uint8_t* dst, int64_t n);
 
 /* PagedBlockPool.Store, PagedBlockPool.cs:151-161. */
 int oracle_store(void* kpool, void* vpool, const oracle_geom* g, int32_t block, int32_t layer,

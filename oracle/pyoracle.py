@@ -34,6 +34,12 @@ def _load() -> C.CDLL:
     lib.oracle_f16_to_f32.argtypes = [C.c_uint16]
     lib.oracle_f32_to_f16_many.restype = None
     lib.oracle_f32_to_f16_many.argtypes = [P, P, C.c_int64]
+    lib.oracle_f32_to_e4m3.restype = C.c_uint8
+    lib.oracle_f32_to_e4m3.argtypes = [F]
+    lib.oracle_e4m3_to_f32.restype = F
+    lib.oracle_e4m3_to_f32.argtypes = [C.c_uint8]
+    lib.oracle_f32_to_e4m3_many.restype = None
+    lib.oracle_f32_to_e4m3_many.argtypes = [P, P, C.c_int64]
     lib.oracle_store.argtypes = [P, P, P, I, I, I, P, P]
     lib.oracle_copy_block_data.argtypes = [P, P, P, I, I, I]
     lib.oracle_store_many.argtypes = [P, P, P, I, P, I, P, P]
@@ -56,12 +62,21 @@ def _load() -> C.CDLL:
 
 lib = _load()
 
-F32, BF16, F16 = 0, 1, 2
+F32, BF16, F16, FP8 = 0, 1, 2, 3
 
 
 class Geom(C.Structure):
     _fields_ = [(n, C.c_int32) for n in
-                ("total_blocks", "layers", "heads_kv", "head_dim", "v_head_dim", "block_size", "dtype")]
+                ("total_blocks", "layers", "heads_kv", "head_dim", "v_head_dim", "block_size", "dtype")] + [
+        ("k_scale", C.c_void_p), ("v_scale", C.c_void_p)]
+
+    def set_scales(self, k_scale, v_scale):
+        """FP8 arenas: [layers][heads_kv] K and V scales (kept alive with the geometry)."""
+        self._ks = np.ascontiguousarray(k_scale, np.float32)
+        self._vs = np.ascontiguousarray(v_scale, np.float32)
+        self.k_scale = self._ks.ctypes.data
+        self.v_scale = self._vs.ctypes.data
+        return self
 
 
 def geom(total_blocks, layers, heads_kv, head_dim, v_head_dim=None, block_size=16, dtype=F32) -> Geom:
@@ -76,7 +91,7 @@ def _p(a: np.ndarray) -> int:
 def new_arena(g: Geom):
     kshape = (g.total_blocks, g.layers, g.heads_kv, g.block_size, g.head_dim)
     vshape = (g.total_blocks, g.layers, g.heads_kv, g.block_size, g.v_head_dim)
-    dt = np.float32 if g.dtype == F32 else np.uint16
+    dt = {F32: np.float32, BF16: np.uint16, F16: np.uint16, FP8: np.uint8}[g.dtype]
     return np.zeros(kshape, dt), np.zeros(vshape, dt)
 
 
@@ -102,12 +117,32 @@ def f16_bits_to_f32(h: np.ndarray) -> np.ndarray:
     return np.asarray(h, dtype=np.uint16).view(np.float16).astype(np.float32)
 
 
+def f32_to_e4m3_bits(x: np.ndarray) -> np.ndarray:
+    """fp32 -> FP8 E4M3 bytes through the oracle's round-to-nearest-even, saturating conversion."""
+    src = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(src.shape, np.uint8)
+    lib.oracle_f32_to_e4m3_many(_p(src), _p(out), src.size)
+    return out
+
+
+_E4M3 = None
+
+
+def e4m3_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    global _E4M3
+    if _E4M3 is None:
+        _E4M3 = np.array([lib.oracle_e4m3_to_f32(i) for i in range(256)], np.float32)
+    return _E4M3[np.asarray(b, dtype=np.uint8)]
+
+
 def to_storage_bits(x: np.ndarray, dtype: int) -> np.ndarray:
-    """fp32 values in an arena's storage representation (F32: unchanged)."""
+    """fp32 values in an arena's storage representation (F32: unchanged; FP8 with scale 1)."""
     if dtype == BF16:
         return f32_to_bf16_bits(x)
     if dtype == F16:
         return f32_to_f16_bits(x)
+    if dtype == FP8:
+        return f32_to_e4m3_bits(x)
     return np.ascontiguousarray(x, dtype=np.float32)
 
 

@@ -5,8 +5,10 @@ import numpy as np
 
 from oracle import pyoracle as O
 
-TOL = {"f32": 1e-4, "bf16": 2e-2, "f16": 2e-2}  # max-abs parity bars: fp32 KV, 16-bit KV storage
-ODT = {"f32": O.F32, "bf16": O.BF16, "f16": O.F16}
+# max-abs parity bars: fp32 KV; 16-bit KV storage (the tensor-core decode rounds q and p);
+# fp8 KV (the CUDA-core decode computes in fp32 on the same stored values)
+TOL = {"f32": 1e-4, "bf16": 2e-2, "f16": 2e-2, "fp8": 1e-4}
+ODT = {"f32": O.F32, "bf16": O.BF16, "f16": O.F16, "fp8": O.FP8}
 
 
 def torch():
@@ -15,15 +17,20 @@ def torch():
     return _t
 
 
-def geom_of(pool):
-    return O.geom(pool.total_blocks, pool.layers, pool.heads_kv, pool.head_dim, pool.value_head_dim,
-                  pool.block_size, ODT[pool.dtype])
+def geom_of(pool, total_blocks=None):
+    g = O.geom(pool.total_blocks if total_blocks is None else total_blocks, pool.layers, pool.heads_kv,
+               pool.head_dim, pool.value_head_dim, pool.block_size, ODT[pool.dtype])
+    if pool.dtype == "fp8":
+        g.set_scales(*pool.kv_scales)
+    return g
 
 
 def arena_to_host(pool):
     """Host copies of the K and V arenas in the oracle's representation."""
     t = torch()
     k, v = pool.key_view(), pool.value_view()
+    if pool.dtype == "fp8":
+        return k.cpu().numpy(), v.cpu().numpy()
     if pool.dtype != "f32":
         return (k.view(t.int16).cpu().numpy().view(np.uint16), v.view(t.int16).cpu().numpy().view(np.uint16))
     return k.cpu().numpy(), v.cpu().numpy()
@@ -32,7 +39,9 @@ def arena_to_host(pool):
 def host_to_arena(pool, K, V):
     t = torch()
     for view, arr in ((pool.key_view(), K), (pool.value_view(), V)):
-        if pool.dtype != "f32":
+        if pool.dtype == "fp8":
+            view.copy_(t.from_numpy(np.ascontiguousarray(arr, np.uint8)))
+        elif pool.dtype != "f32":
             view.view(t.int16).copy_(t.from_numpy(np.ascontiguousarray(arr).view(np.int16)))
         else:
             view.copy_(t.from_numpy(np.ascontiguousarray(arr)))
@@ -85,7 +94,9 @@ def compact(pool, tables, ctx, rows):
     idx = t.tensor(ids, dtype=t.long, device=f"cuda:{pool.device}")
     k = pool.key_view().index_select(0, idx)
     v = pool.value_view().index_select(0, idx)
-    if pool.dtype != "f32":
+    if pool.dtype == "fp8":
+        K, V = k.cpu().numpy(), v.cpu().numpy()
+    elif pool.dtype != "f32":
         K = k.view(t.int16).cpu().numpy().view(np.uint16)
         V = v.view(t.int16).cpu().numpy().view(np.uint16)
     else:
@@ -94,8 +105,7 @@ def compact(pool, tables, ctx, rows):
     for i, (r, c) in enumerate(zip(sub, np.asarray(ctx)[rows])):
         n = (int(c) + pool.block_size - 1) // pool.block_size
         new[i, :n] = [remap[int(b)] for b in r[:n]]
-    g = O.geom(len(ids), pool.layers, pool.heads_kv, pool.head_dim, pool.value_head_dim, pool.block_size,
-               ODT[pool.dtype])
+    g = geom_of(pool, len(ids))
     return g, np.ascontiguousarray(K), np.ascontiguousarray(V), new
 
 

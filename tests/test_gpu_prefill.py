@@ -48,7 +48,7 @@ def _run(pool, rng, prefixes, q_lens, n_heads, layer=0, q_dtype="bf16", starts=N
     qt = torch.from_numpy(q).to(dev)
     if q_dtype != "f32":
         qt = qt.to(torch.bfloat16 if q_dtype == "bf16" else torch.float16)  # exact: q is rounded already
-    if pool.dtype != "f32" and d == 128:
+    if pool.dtype in ("bf16", "f16") and d == 128:
         q = _round(q, pool.dtype)  # the tensor-core path computes with q in the arena's type
     out = torch.full((total_q, n_heads, pool.value_head_dim), out_init, dtype=torch.float32, device=dev)
     pool.upload_step(tables, np.asarray(toks, np.int32))

@@ -256,3 +256,62 @@ def test_f16_store_rounds_and_decodes_from_the_rounded_values():
     O.store(K2, V2, g, 2, 0, 0, k, v)
     out = O.decode_batch(K2, V2, g, 0, tables, np.array([1], np.int32), q, 2, 0.25)
     assert np.array_equal(out.reshape(-1), O.f16_bits_to_f32(O.f32_to_f16_bits(v)))
+
+
+def test_e4m3_storage_rounding_matches_torch_float8_e4m3fn():
+    """The oracle's fp32 -> FP8 E4M3 conversion (the storage rounding of FP8 arenas) is OCP
+    E4M3 round-to-nearest-even saturated at +-448: over random values spanning the whole e4m3
+    range, ties and the edges it agrees with torch's float8_e4m3fn cast of the value clamped to
+    [-448, 448] (torch's cast itself does not saturate), and all 256 bytes decode as torch
+    decodes them."""
+    import numpy as np
+    import torch
+
+    from oracle import pyoracle as O
+
+    rng = np.random.default_rng(8)
+    mag = np.exp2(rng.uniform(-12.0, 9.5, 1_000_000)).astype(np.float32)
+    x = mag * rng.choice(np.array([-1.0, 1.0], np.float32), mag.size)
+    # exact ties between neighbouring e4m3 values, normals and subnormals
+    grid = torch.arange(256, dtype=torch.uint8).view(torch.float8_e4m3fn).float().numpy()
+    grid = np.unique(grid[np.isfinite(grid)])
+    ties = ((grid[:-1].astype(np.float64) + grid[1:]) / 2).astype(np.float32)
+    edge = np.array([0.0, -0.0, 448.0, 464.0, 480.0, 1e9, np.inf, -np.inf, 2.0**-9, 2.0**-10, 2.0**-11,
+                     2.0**-6, 0.0009765625, 1e-30], np.float32)
+    x = np.concatenate([x, ties, edge])
+    got = O.f32_to_e4m3_bits(x)
+    want = torch.from_numpy(np.clip(x, -448.0, 448.0)).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert np.array_equal(got, want)
+    nan = O.f32_to_e4m3_bits(np.array([np.nan], np.float32))[0]
+    assert (nan & 0x7F) == 0x7F
+    b = np.arange(256, dtype=np.uint8)
+    back = O.e4m3_bits_to_f32(b)
+    ref = torch.from_numpy(b).view(torch.float8_e4m3fn).float().numpy()
+    assert ((back == ref) | (np.isnan(back) & np.isnan(ref))).all()
+
+
+def test_fp8_store_applies_the_per_head_scales_and_decode_reads_them_back():
+    """An FP8 arena stores e4m3(x * (1 / scale)) with the (layer, head) scale of the row and
+    reads e4m3 * scale: one attended token returns its value row as stored and scaled back."""
+    import numpy as np
+
+    from oracle import pyoracle as O
+
+    rng = np.random.default_rng(18)
+    g = O.geom(4, 2, 2, 16, 16, 4, O.FP8)
+    ks = np.array([[0.5, 2.0], [0.25, 4.0]], np.float32)
+    vs = np.array([[3.0, 0.125], [1.5, 0.75]], np.float32)
+    g.set_scales(ks, vs)
+    K, V = O.new_arena(g)
+    k = (rng.standard_normal(32) * 8).astype(np.float32)
+    v = (rng.standard_normal(32) * 8).astype(np.float32)
+    assert O.store(K, V, g, 2, 1, 0, k, v) == 0
+    for h in range(2):
+        inv_k = np.float32(1.0) / ks[1, h]
+        inv_v = np.float32(1.0) / vs[1, h]
+        assert np.array_equal(K[2, 1, h, 0], O.f32_to_e4m3_bits(k[h * 16:(h + 1) * 16] * inv_k))
+        assert np.array_equal(V[2, 1, h, 0], O.f32_to_e4m3_bits(v[h * 16:(h + 1) * 16] * inv_v))
+    q = rng.standard_normal((1, 2, 16)).astype(np.float32)
+    out = O.decode_batch(K, V, g, 1, np.array([[2]], np.int32), np.array([1], np.int32), q, 2, 0.25)
+    want = np.concatenate([O.e4m3_bits_to_f32(V[2, 1, h, 0]) * vs[1, h] for h in range(2)])
+    assert np.array_equal(out.reshape(-1), want)

@@ -431,3 +431,24 @@ def test_table_edges():
         assert t.append_token()[0]
     assert t.append_token() == (False, -1, -1)  # pool exhausted at a block boundary
     assert t.token_count == 8
+
+
+# ---- FP8 E4M3 storage (no reference counterpart) ---------------------------------------
+
+def test_fp8_pool_checks_head_dims_and_scales():
+    """An FP8 pool needs head dims that are multiples of 16 and positive, finite scales, one
+    K and one V scale per (layer, kv head); scales belong to FP8 pools only."""
+    with pytest.raises(ArgumentOutOfRangeError):
+        PagedBlockPool(8, 1, 2, 24, 16, allocate_device_arena=False, dtype="fp8")
+    p = PagedBlockPool(8, 2, 2, 64, 16, allocate_device_arena=False, dtype="fp8")
+    p.set_kv_scales(np.full((2, 2), 0.5), np.full((2, 2), 2.0))
+    for bad in (0.0, -1.0, np.inf, np.nan):
+        ks = np.ones((2, 2), np.float32)
+        ks[1, 0] = bad
+        with pytest.raises(ArgumentOutOfRangeError):
+            p.set_kv_scales(ks, np.ones((2, 2)))
+    with pytest.raises(ArgumentOutOfRangeError):
+        p.set_kv_scales(np.ones(3), np.ones(4))
+    f = PagedBlockPool(8, 2, 2, 64, 16, allocate_device_arena=False, dtype="bf16")
+    with pytest.raises(InvalidOperationError):
+        f.set_kv_scales(np.ones((2, 2)), np.ones((2, 2)))
