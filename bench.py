@@ -53,8 +53,8 @@ def peaks():
 # Configs whose sequences are one fixed global batch split over the GPUs (strong scaling):
 # cfg3 by longest-first partitioning, cfg5 by block range.  cfg1 / cfg2 give every GPU its own
 # batch (weak scaling).
-STRONG = ("cfg3", "cfg3-bf16", "cfg3-f16", "cfg5")
-CFG3 = {"cfg3": "f32", "cfg3-bf16": "bf16", "cfg3-f16": "f16"}
+STRONG = ("cfg3", "cfg3-bf16", "cfg3-f16", "cfg3-fp8", "cfg5")
+CFG3 = {"cfg3": "f32", "cfg3-bf16": "bf16", "cfg3-f16": "f16", "cfg3-fp8": "fp8"}
 
 
 def workload(name: str, rank: int, world: int = 1, batch: int = 0):
@@ -180,7 +180,7 @@ def cpu_baseline_run(w, steps: int, budget_s: float, threads: int, seed: int):
     for i, n in enumerate(nblk):
         tables[i, :n] = np.arange(at, at + n, dtype=np.int32)
         at += n
-    g = O.geom(at, 1, w.heads_kv, w.head_dim, w.v_head_dim, bs, {"f32": O.F32, "bf16": O.BF16, "f16": O.F16}[w.dtype])
+    g = O.geom(at, 1, w.heads_kv, w.head_dim, w.v_head_dim, bs, {"f32": O.F32, "bf16": O.BF16, "f16": O.F16, "fp8": O.FP8}[w.dtype])
     K, V = O.new_arena(g)
     for arr in (K, V):
         arr[...] = O.to_storage_bits(rng.standard_normal(arr.shape, dtype=np.float32), g.dtype)

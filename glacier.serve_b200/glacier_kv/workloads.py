@@ -298,7 +298,10 @@ def fill_arena_randn(pool, seed: int, blocks: Optional[np.ndarray] = None) -> No
         step = max(1, (1 << 26) // flat.shape[1])
         for i in range(0, flat.shape[0], step):
             chunk = torch.randn(flat[i: i + step].shape, generator=g, device=view.device, dtype=torch.float32)
-            flat[i: i + step].copy_(chunk.to(view.dtype))
+            if view.dtype == torch.uint8:  # FP8 arena: e4m3 bytes (|x| << 448, scale 1)
+                flat[i: i + step].copy_(chunk.to(torch.float8_e4m3fn).view(torch.uint8))
+            else:
+                flat[i: i + step].copy_(chunk.to(view.dtype))
 
 
 def randn(shape, seed: int, device: str = "cpu"):
