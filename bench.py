@@ -719,8 +719,9 @@ def main():
     ap.add_argument("--batch", type=int, default=0,
                     help="sequences of cfg2/cfg3 (default: the config's own); for small profiler captures")
     ap.add_argument("--share", type=int, default=0,
-                    help="cfg3 on one GPU: decode only rank 0's longest-first share of an N-GPU split "
-                         "(the per-rank step of the N-GPU run, for profiling it on one GPU)")
+                    help="cfg3 / cfg5 on one GPU: decode only rank 0's share of an N-GPU split (cfg3: its "
+                         "longest-first sequences; cfg5: its block range, without the exchange) -- the per-rank "
+                         "step of the N-GPU run, for profiling it on one GPU")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -768,6 +769,11 @@ def main():
 
         w = W.lpt_share(w, 0, args.share)
         global_batch = w.batch  # this GPU decodes its share only
+    elif args.share > 1 and world == 1 and args.config == "cfg5":
+        from glacier_kv import workloads as W
+
+        w = W.cfg5_local(0, args.share, W.SEED)  # rank 0's block range, decoded without the exchange
+        global_batch = w.batch
     pool = W.make_pool(w, device=local)
     W.fill_arena_randn(pool, seed=w.seed)
     stream = torch.cuda.current_stream(dev)
@@ -832,6 +838,7 @@ def main():
     clk.mark(0)
     t0 = ev()
     t0.record(stream)
+    h0 = time.perf_counter()
     for i in range(args.steps):
         if flush is not None:
             flush.zero_()
@@ -842,6 +849,7 @@ def main():
             launches += step()
     t1 = ev()
     t1.record(stream)
+    host_ms = (time.perf_counter() - h0) * 1e3 / args.steps  # enqueue cost per step on the host
     torch.cuda.synchronize(dev)
     clk.mark(1)
     clk.__exit__()
@@ -938,6 +946,9 @@ def main():
                        "parallelism": (f"split-KV: each sequence's blocks split over {world} GPU(s), (out, lse) "
                                        "exchanged through peer-memory mailboxes (NCCL all-gather fallback) + LSE "
                                        "merge") if split_kv else
+                                      (f"rank 0's block range of each sequence split over {args.share} GPUs, decoded "
+                                       "alone on one GPU without the exchange")
+                                      if args.share > 1 and args.config == "cfg5" else
                                       (f"rank 0's share ({w.batch} sequences) of the 256 split over {args.share} GPUs "
                                        "by longest-first partitioning, run alone on one GPU")
                                       if args.share > 1 else
@@ -963,6 +974,7 @@ def main():
                     "l2": ("the L2 flush between steps is outside the timed span (its device time is "
                            "subtracted)") if flush is not None else "no flush (inputs larger than L2)"},
             "gpu_launches": launches,
+            "host_enqueue_ms_per_step": host_ms,
             "clocks": clk.summary(),
         }
         if breakdown is not None:

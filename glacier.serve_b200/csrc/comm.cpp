@@ -8,14 +8,16 @@
 // out = sum_r exp(lse_r - LSE) * out_r, LSE = ln(sum_r exp(lse_r) [+ exp(sink)]).
 //
 // The exchange itself goes through peer memory when the ranks can map each other's HBM (CUDA
-// IPC over NVLink, set up once with two small NCCL all-gathers): each rank stores its block
-// straight into every rank's mailbox and the merge waits on epoch flags (exchange.cu).  That
+// IPC over NVLink, set up once with two small NCCL all-gathers): each rank's decode writes its
+// block into its own mailbox, and one kernel publishes an epoch flag to every rank, waits for
+// every rank's flag and merges all blocks with plain loads over NVLink (exchange.cu).  That
 // replaces a ring all-gather whose N-1 latency-bound steps cost more than the decode itself
 // at 8 ranks.  Without peer mappings the ranks agree to use ncclAllGather instead.
 //
 // Every NCCL wait is bounded: the communicator is created non-blocking and polled against a
 // host timeout, and a timeout aborts it (ncclCommAbort) and returns GKV_ETIMEDOUT.  The merge
 // kernel's wait on peer flags is bounded too (kErrWaitTimeout in the pool's error word).
+#include <algorithm>
 #include <dlfcn.h>
 #include <nccl.h>
 
@@ -312,7 +314,7 @@ int gkv_paged_decode_splitkv_dist(gkv_pool* pool, gkv_comm* c, int32_t layer, co
     const int32_t dv = P.desc.v_head_dim;
     const int64_t rows = static_cast<int64_t>(P.ws.batch) * n_heads;
     const size_t per = static_cast<size_t>(rows) * (dv + 1);
-    const size_t per4 = (per + 3) / 4 * 4;  // the push moves whole float4s
+    const size_t per4 = (per + 3) / 4 * 4;  // mailbox slots hold whole float4s
     if (per4 > c->cap_floats) {
         cudaDeviceSynchronize();
         if (c->d_send) cudaFree(c->d_send);
@@ -324,31 +326,39 @@ int gkv_paged_decode_splitkv_dist(gkv_pool* pool, gkv_comm* c, int32_t layer, co
         if (e != cudaSuccess) return gkv::cuda_fail(e, "cudaMalloc(split-KV exchange)");
         c->cap_floats = per4;
     }
-    float* send_out = c->d_send;
-    float* send_lse = c->d_send + rows * dv;
-    P.last_launches = 0;
-    // rows this rank holds no tokens of keep lse = -inf (weight 0 in the merge)
-    cudaError_t e = gkv::launch_fill(send_lse, rows, -INFINITY, st);
-    if (e != cudaSuccess) return gkv::cuda_fail(e, "fill launch");
-    int rc = gkv::step_decode_lse(&P, layer, d_q, send_out, send_lse, n_heads, scale, nullptr, st);
-    if (rc != GKV_OK) return rc;
-    const int launches = P.last_launches + 1;
-    if (c->kind == 0) {
-        rc = setup_exchange(c, static_cast<int64_t>(per), st);
+    if (c->kind == 0) {  // first call: map the mailboxes (or agree on the NCCL fallback)
+        int rc = setup_exchange(c, static_cast<int64_t>(per), st);
         if (rc != GKV_OK) return rc;
     }
     // the slot size is fixed at set-up; every rank sees the same rows, so all take the same path
-    if (c->kind == 2 && static_cast<int64_t>(per4) <= c->peers.slot) {
-        const unsigned ep = ++c->epoch;
-        const int parity = static_cast<int>(ep & 1u);
-        e = gkv::launch_exchange_push(c->d_send, static_cast<int64_t>(per), c->peers, c->rank, ep, parity, st);
-        if (e != cudaSuccess) return gkv::cuda_fail(e, "exchange push launch");
-        const float* mb = c->peers.mbox[c->rank] + static_cast<int64_t>(parity) * c->n_ranks * c->peers.slot;
-        const unsigned* fl = c->peers.flags[c->rank] + parity * c->n_ranks;
-        e = gkv::launch_exchange_merge(mb, fl, c->n_ranks, c->peers.slot, static_cast<int>(rows), dv, d_sinks, n_heads,
-                                       d_out, ep, P.ws.d_err, st);
+    const bool p2p = c->kind == 2 && static_cast<int64_t>(per4) <= c->peers.slot && dv % 4 == 0;
+    unsigned ep = 0;
+    int parity = 0;
+    float* send_out = c->d_send;
+    if (p2p) {  // the decode writes straight into this rank's own mailbox slot
+        ep = ++c->epoch;
+        parity = static_cast<int>(ep & 1u);
+        send_out = gkv::exchange_slot(c->peers, c->rank, parity);
+    }
+    float* send_lse = send_out + rows * dv;
+    P.last_launches = 0;
+    // rows this rank holds no tokens of keep lse = -inf (weight 0 in the merge); when every
+    // sequence has tokens here the decode writes every row and the fill launch is skipped
+    cudaError_t e = cudaSuccess;
+    int fills = 0;
+    if (std::find(P.ws.h_ctx.begin(), P.ws.h_ctx.end(), 0) != P.ws.h_ctx.end()) {
+        e = gkv::launch_fill(send_lse, rows, -INFINITY, st);
+        if (e != cudaSuccess) return gkv::cuda_fail(e, "fill launch");
+        fills = 1;
+    }
+    int rc = gkv::step_decode_lse(&P, layer, d_q, send_out, send_lse, n_heads, scale, nullptr, st);
+    if (rc != GKV_OK) return rc;
+    const int launches = P.last_launches + fills;
+    if (p2p) {
+        e = gkv::launch_exchange_pull_merge(c->peers, c->rank, parity, ep, static_cast<int>(rows), dv, d_sinks, n_heads,
+                                            d_out, P.ws.d_err, st);
         if (e != cudaSuccess) return gkv::cuda_fail(e, "exchange merge launch");
-        P.last_launches = launches + 2;
+        P.last_launches = launches + 1;
         return GKV_OK;
     }
     ncclResult_t r = nccl().AllGather(c->d_send, c->d_recv, per, ncclFloat, c->comm, st);

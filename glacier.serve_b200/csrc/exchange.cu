@@ -1,16 +1,19 @@
-// Peer-memory exchange of split-KV partials over NVLink, and the merge that waits for it.
+// Peer-memory exchange of split-KV partials over NVLink, fused with the merge that needs it.
 //
 // Each rank owns a mailbox in its own HBM, [2 parities][n_ranks][slot] floats followed by
 // [2][n_ranks] epoch flags, mapped into every other rank's address space once (CUDA IPC).
-// Per split-KV decode (epoch e, parity e & 1):
-//  * push_kernel: CTA r stores this rank's (out, lse) block into rank r's mailbox slot
-//    [parity][me] with plain 16-byte stores to peer memory (no TMA, no multicast), fences at
-//    system scope and publishes e in rank r's flag [parity][me] (st.release.sys).
-//  * wait_merge_kernel: every CTA waits until all n_ranks flags of its own mailbox read e
-//    (ld.acquire.sys, bounded: on expiry it raises kErrWaitTimeout and writes nothing), then
-//    merges the blocks by log-sum-exp exactly as lse_merge_kernel.
-// Two parities suffice: a rank pushes epoch e+2 only after its merge of e+1, which waited for
-// every peer's push of e+1, which each peer issued after its own merge of e.
+// Per split-KV decode (epoch e, parity e & 1) a rank's decode kernels write its (out, lse)
+// block straight into its OWN mailbox, slot [parity][me] -- no send buffer, no push kernel.
+// Then ONE kernel (pull_merge_kernel, launched as a programmatic dependent of the decode):
+//  * after griddepcontrol.wait (the decode and its merge have completed), threads 0..n-1 of
+//    CTA 0 publish e in flag [parity][me] of every rank (fence.sc.sys, then st.release.sys);
+//  * every CTA waits until all n_ranks flags of its own mailbox read e (ld.acquire.sys,
+//    bounded: on expiry it raises kErrWaitTimeout and writes nothing);
+//  * one warp per output row merges the n_ranks blocks by log-sum-exp, reading rank r's block
+//    from rank r's mailbox with plain loads over NVLink (no TMA, no multicast).
+// Two parities suffice: rank r rewrites its slot of parity p at epoch e+2 only after its own
+// merge of e+1, which waited for every peer's flag of e+1, which each peer published only
+// after its merge of e -- the last read of r's slot of epoch e -- had completed.
 #include <cmath>
 
 #include "gkv_device.cuh"
@@ -32,26 +35,38 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     return v;
 }
 
-__global__ void __launch_bounds__(1024) push_kernel(const float4* __restrict__ src, int64_t n4, ExchangePeers p,
-                                                    int me, unsigned epoch, int parity) {
-    const int r = blockIdx.x;
-    float4* dst = reinterpret_cast<float4*>(p.mbox[r] + (static_cast<int64_t>(parity) * p.n_ranks + me) * p.slot);
-    for (int64_t i = threadIdx.x; i < n4; i += blockDim.x) dst[i] = src[i];
-    __threadfence_system();  // this thread's stores reach rank r before the flag below
-    __syncthreads();
-    if (threadIdx.x == 0) st_release_sys(p.flags[r] + parity * p.n_ranks + me, epoch);
+// Loads from another GPU's memory that a later epoch rewrites: never served from L1.
+__device__ __forceinline__ float ld_peer(const float* p) {
+    float v;
+    asm volatile("ld.relaxed.sys.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ float4 ld_peer4(const float4* p) {
+    float4 v;
+    asm volatile("ld.relaxed.sys.global.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
 }
 
-__global__ void __launch_bounds__(256) wait_merge_kernel(const float* __restrict__ mbox, const unsigned* flags,
-                                                         int n_parts, int64_t slot, int rows, int dv,
-                                                         const float* __restrict__ sinks, int n_heads,
-                                                         float* __restrict__ out, unsigned epoch, int* err) {
+// A slot holds out [rows][dv] fp32 (dv a multiple of 4), then lse [rows].
+__global__ void __launch_bounds__(256) pull_merge_kernel(ExchangePeers p, int me, int parity, unsigned epoch,
+                                                         int rows, int dv, const float* __restrict__ sinks,
+                                                         int n_heads, float* __restrict__ out, int* err) {
     __shared__ int ready;
+    pdl_wait();  // this rank's block is complete in its own mailbox
+    const int n = p.n_ranks;
+    if (blockIdx.x == 0 && threadIdx.x < n) {
+        __threadfence_system();
+        st_release_sys(p.flags[threadIdx.x] + parity * n + me, epoch);
+    }
     if (threadIdx.x == 0) {
+        const unsigned* fl = p.flags[me] + parity * n;
         int good = 1;
-        for (int r = 0; r < n_parts && good; ++r) {
+        for (int r = 0; r < n && good; ++r) {
             uint32_t it = 0;
-            while (ld_acquire_sys(flags + r) != epoch) {
+            while (ld_acquire_sys(fl + r) != epoch) {
                 if (++it > kFlagWaitLimit) {
                     good = 0;
                     atomicOr(err, kErrWaitTimeout);
@@ -65,52 +80,56 @@ __global__ void __launch_bounds__(256) wait_merge_kernel(const float* __restrict
     __syncthreads();
     if (!ready) return;
     const int lane = threadIdx.x & 31;
-    const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int row = static_cast<int>((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
     if (row >= rows) return;
-    // the blocks were written by other GPUs: read through L2 (never a stale L1 line)
-    const float* lses = mbox + static_cast<int64_t>(rows) * dv;  // lse block of part 0
-    float M = -INFINITY;
-    for (int p = 0; p < n_parts; ++p) M = fmaxf(M, __ldcg(lses + p * slot + row));
+    const int64_t slot_off = static_cast<int64_t>(parity) * n * p.slot;
+    // lane r < n holds rank r's lse of this row
+    float l = -INFINITY;
+    if (lane < n) l = ld_peer(p.mbox[lane] + slot_off + lane * p.slot + static_cast<int64_t>(rows) * dv + row);
+    float M = l;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
     float sk = -INFINITY;
     if (sinks) {
         sk = __ldg(sinks + row % n_heads);
         M = fmaxf(M, sk);
     }
-    float den = (M == -INFINITY) ? 0.f : ((sk == -INFINITY) ? 0.f : expf(sk - M));
-    for (int p = 0; p < n_parts; ++p) {
-        const float l = __ldcg(lses + p * slot + row);
-        if (l != -INFINITY) den += expf(l - M);
-    }
-    for (int d = lane; d < dv; d += 32) {
-        float acc = 0.f;
-        for (int p = 0; p < n_parts; ++p) {
-            const float l = __ldcg(lses + p * slot + row);
-            if (l == -INFINITY) continue;
-            acc = fmaf(expf(l - M), __ldcg(mbox + p * slot + row * dv + d), acc);
+    const float w = (l == -INFINITY) ? 0.f : expf(l - M);
+    float den = w;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+    if (sk != -INFINITY) den += expf(sk - M);
+    const float inv = den > 0.f ? 1.f / den : 0.f;
+    for (int d = lane * 4; d < dv; d += 128) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int r = 0; r < n; ++r) {
+            const float wr = __shfl_sync(0xffffffffu, w, r);
+            if (wr == 0.f) continue;  // no tokens there (its block may hold anything)
+            const float4 v = ld_peer4(reinterpret_cast<const float4*>(p.mbox[r] + slot_off + r * p.slot +
+                                                                        static_cast<int64_t>(row) * dv + d));
+            acc.x = fmaf(wr, v.x, acc.x);
+            acc.y = fmaf(wr, v.y, acc.y);
+            acc.z = fmaf(wr, v.z, acc.z);
+            acc.w = fmaf(wr, v.w, acc.w);
         }
-        out[row * dv + d] = den > 0.f ? acc / den : 0.f;
+        *reinterpret_cast<float4*>(out + static_cast<int64_t>(row) * dv + d) =
+            make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
     }
 }
 
 }  // namespace
 
-cudaError_t launch_exchange_push(const float* src, int64_t n_floats, const ExchangePeers& p, int me, unsigned epoch,
-                                 int parity, cudaStream_t st) {
-    if (n_floats <= 0) return cudaSuccess;
-    const int64_t n4 = (n_floats + 3) / 4;  // src and the slots hold whole float4s
-    push_kernel<<<static_cast<unsigned>(p.n_ranks), 1024, 0, st>>>(reinterpret_cast<const float4*>(src), n4, p, me,
-                                                                   epoch, parity);
-    return cudaGetLastError();
+float* exchange_slot(const ExchangePeers& p, int me, int parity) {
+    return p.mbox[me] + (static_cast<int64_t>(parity) * p.n_ranks + me) * p.slot;
 }
 
-cudaError_t launch_exchange_merge(const float* mbox_parity, const unsigned* flags_parity, int n_parts, int64_t slot,
-                                  int rows, int dv, const float* sinks, int n_heads, float* out, unsigned epoch,
-                                  int* err, cudaStream_t st) {
+cudaError_t launch_exchange_pull_merge(const ExchangePeers& p, int me, int parity, unsigned epoch, int rows, int dv,
+                                       const float* sinks, int n_heads, float* out, int* err, cudaStream_t st) {
     if (rows <= 0) return cudaSuccess;
+    if (dv % 4 != 0) return cudaErrorInvalidValue;
     const int64_t threads = static_cast<int64_t>(rows) * 32;
-    wait_merge_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, st>>>(
-        mbox_parity, flags_parity, n_parts, slot, rows, dv, sinks, n_heads, out, epoch, err);
-    return cudaGetLastError();
+    return launch_pdl(pull_merge_kernel, dim3(static_cast<unsigned>((threads + 255) / 256)), dim3(256), 0, st, p,
+                      me, parity, epoch, rows, dv, sinks, n_heads, out, err);
 }
 
 }  // namespace gkv

@@ -158,15 +158,15 @@ struct ExchangePeers {
     int n_ranks;
     int64_t slot;  // floats per slot, a multiple of 4
 };
-// Stores this rank's n_floats (rounded up to whole float4s; src must hold them) into slot
-// [parity][me] of every rank's mailbox, then publishes `epoch` in its flag [parity][me].
-cudaError_t launch_exchange_push(const float* src, int64_t n_floats, const ExchangePeers& p, int me, unsigned epoch,
-                                 int parity, cudaStream_t st);
-// Waits (bounded) until all n_parts flags of this rank's mailbox parity read `epoch`, then
-// merges the n_parts (out, lse) blocks as launch_lse_merge.
-cudaError_t launch_exchange_merge(const float* mbox_parity, const unsigned* flags_parity, int n_parts, int64_t slot,
-                                  int rows, int dv, const float* sinks, int n_heads, float* out, unsigned epoch,
-                                  int* err, cudaStream_t st);
+// Slot [parity][me] of this rank's own mailbox: where its decode writes (out [rows][dv], then
+// lse [rows]) for an epoch of that parity.
+float* exchange_slot(const ExchangePeers& p, int me, int parity);
+// After the decode that filled this rank's slot (a programmatic dependent launch): publishes
+// `epoch` in flag [parity][me] of every rank, waits (bounded) until all of this rank's flags
+// of the parity read `epoch`, then merges every rank's block of the parity by log-sum-exp into
+// out [rows][dv] (dv a multiple of 4), as launch_lse_merge.
+cudaError_t launch_exchange_pull_merge(const ExchangePeers& p, int me, int parity, unsigned epoch, int rows, int dv,
+                                       const float* sinks, int n_heads, float* out, int* err, cudaStream_t st);
 
 // Launch configuration the decode kernel uses for this geometry and query-head count.
 struct DecodeConfig {

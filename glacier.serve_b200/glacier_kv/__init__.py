@@ -421,7 +421,8 @@ class PagedBlockPool:
 
     def paged_decode_splitkv_dist(self, comm: "Comm", layer: int, q, out, n_heads: int, scale: float,
                                   sinks=None, stream=None) -> None:
-        """This rank's block ranges -> NCCL all-gather of (out, lse) -> LSE merge into out."""
+        """This rank's block ranges -> exchange of (out, lse) over the ranks (peer mailboxes over
+        NVLink, or an NCCL all-gather) -> LSE merge into out on every rank."""
         _check(lib.gkv_paged_decode_splitkv_dist(self._h, comm.handle, layer, _f32_dev(q, "q"),
                                                  _f32_dev(out, "out"), n_heads, float(scale),
                                                  None if sinks is None else _f32_dev(sinks, "sinks"),

@@ -431,8 +431,9 @@ GKV_API int gkv_comm_init(const uint8_t* unique_id_128, int32_t n_ranks, int32_t
 GKV_API int gkv_comm_abort(gkv_comm* comm);
 GKV_API int gkv_comm_destroy(gkv_comm* comm);
 /* How the communicator's split-KV decodes exchange their partials: 0 = not decided yet (the
- * first gkv_paged_decode_splitkv_dist decides, collectively), 1 = NCCL all-gather, 2 = direct
- * stores into every rank's mailbox over NVLink (CUDA IPC peer mappings). */
+ * first gkv_paged_decode_splitkv_dist decides, collectively), 1 = NCCL all-gather, 2 = peer
+ * mailboxes over NVLink (CUDA IPC peer mappings): each rank's decode writes its block into its
+ * own mailbox and every rank's merge reads all blocks with plain peer loads. */
 GKV_API int gkv_comm_exchange_kind(const gkv_comm* comm);
 /* This rank's share of a split-KV decode: decode of the uploaded step (this rank's block
  * ranges) with lse, NCCL all-gather of (out, lse) over the ranks, log-sum-exp merge (plus the

@@ -185,3 +185,37 @@ def test_two_gpu_nccl_split_kv(cuda):
     assert ret[0] < TOL["bf16"] and ret[1] < TOL["bf16"], dict(ret)
     # NVLink peers map each other's mailboxes: the exchange must not fall back to NCCL
     assert ret["kind0"] == 2 and ret["kind1"] == 2, dict(ret)
+
+
+def test_one_rank_comm_runs_the_mailbox_exchange(cuda):
+    """A one-rank communicator takes the peer-mailbox path on one GPU (the decode writes into
+    its own mailbox slot, the merge kernel publishes, waits and merges): over calls of both
+    parities, with and without sinks, it equals the oracle's decode; a sequence with no tokens
+    (the lse fill path) merges to zeros."""
+    import torch
+
+    rng = np.random.default_rng(47)
+    bs, d, nH, nKv = 16, 128, 64, 8
+    ctx = [3000, 17, 0, 640]
+    need = sum((c + bs - 1) // bs for c in ctx)
+    pool = G.PagedBlockPool(need + 2, 1, nKv, d, bs, dtype="bf16")
+    K, V = random_arena(pool, rng)
+    tables = random_tables(rng, ctx, bs, need + 2)
+    comm = G.Comm(G.Comm.unique_id(), 1, 0, cuda.index or 0, timeout_ms=60_000)
+    pool.upload_step(tables, np.array(ctx, np.int32))
+    live = [b for b, c in enumerate(ctx) if c > 0]
+    for step in range(4):
+        q = rng.standard_normal((len(ctx), nH, d)).astype(np.float32)
+        sk = 0.3 if step == 3 else None
+        sinks = None if sk is None else torch.full((nH,), sk, device=cuda)
+        out = torch.full((len(ctx), nH, d), 7.0, device=cuda)
+        pool.paged_decode_splitkv_dist(comm, 0, torch.from_numpy(q).to(cuda), out, nH, 1 / math.sqrt(d), sinks=sinks)
+        pool.sync()
+        got = out.cpu().numpy()
+        ref = O.decode_batch(K, V, geom_of(pool), 0, tables, np.array(ctx, np.int32), q, nH, 1 / math.sqrt(d),
+                             sink_logit=sk)
+        np.testing.assert_allclose(got[live], ref[live], atol=TOL["bf16"], rtol=0)
+        assert np.array_equal(got[2], np.zeros((nH, d), np.float32))
+    assert comm.exchange_kind == 2
+    comm.close()
+    pool.close()
