@@ -14,6 +14,33 @@
 
 namespace gkv {
 
+// The work list a launch runs: `w` itself, or (static step layout, w.dyn set) the pointers
+// and counts of the header the step's upload wrote at w.dyn.  The buffer comes from a host
+// copy ordered before the launch, so it may be read before pdl_wait.
+__device__ __forceinline__ DecodeWork resolve_work(DecodeWork w) {
+    if (!w.dyn) return w;
+    const int32_t* h = reinterpret_cast<const int32_t*>(w.dyn);
+    auto at = [&](int k) { return reinterpret_cast<const int32_t*>(w.dyn + __ldg(h + k)); };
+    w.max_blocks = __ldg(h + kHdrMaxBlocks);
+    w.n_slots = __ldg(h + kHdrSlots);
+    w.n_merge = __ldg(h + kHdrMerge);
+    w.n_deferred = __ldg(h + kHdrDeferred);
+    w.n_deferred_long = __ldg(h + kHdrDeferredLong);
+    w.tables = at(kHdrTables);
+    w.ctx_lens = at(kHdrCtx);
+    w.piece_seg = at(kHdrPseg);
+    w.piece_c0 = at(kHdrPc0);
+    w.piece_c1 = at(kHdrPc1);
+    w.piece_slot = at(kHdrPslot);
+    w.piece_merge = at(kHdrPmerge);
+    w.worker_piece_begin = at(kHdrWbeg);
+    w.merge_seg = at(kHdrMseg);
+    w.merge_slot0 = at(kHdrMs0);
+    w.merge_nslots = at(kHdrMns);
+    w.merge_deferred = at(kHdrMdef);
+    return w;
+}
+
 // Block-table row of sequence b of a work list.
 __device__ __forceinline__ int64_t table_row(const DecodeWork& w, int b) {
     return w.table_row ? static_cast<int64_t>(__ldg(w.table_row + b)) : static_cast<int64_t>(b);
@@ -217,8 +244,10 @@ __device__ __forceinline__ void finish_row(const DecodeArgs& a, int b, int qh, f
 // kWarpMergeMaxSlots slots: each (long segment, head of a head group) gets a CTA of eight warps,
 // warp k merging an eighth of the slots, the eight results combined through shared memory by warp
 // 0.  The remaining (short segment, head) items get one warp each, eight per CTA, after the long
-// ones.  Every CTA has one role, so the barrier is CTA-uniform.
-template <int GP, int DV>
+// ones.  These "CTA items" are numbered 0 .. n_items-1; CTA x takes item x (LOOP = false: one CTA
+// per item) or items x, x + gridDim.x, ... (LOOP: the fixed grid of the static step layout).
+// Every item has one role for the whole CTA, so the barriers are CTA-uniform.
+template <int GP, int DV, bool LOOP>
 __global__ void __launch_bounds__(256) deferred_merge_kernel(ArenaGeom g, DecodeWork w, DecodeArgs a, int group,
                                                          int head_groups) {
     static_assert(DV % 32 == 0, "DV must be a multiple of 32");
@@ -228,68 +257,77 @@ __global__ void __launch_bounds__(256) deferred_merge_kernel(ArenaGeom g, Decode
     __shared__ __align__(16) float sm_a[NW][DV];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int per_entry = head_groups * GP;
-    const int long_ctas = w.n_deferred_long * per_entry;
-    const bool cta_role = static_cast<int>(blockIdx.x) < long_ctas;
-    int di, y;
-    bool live = true;
-    if (cta_role) {
-        di = static_cast<int>(blockIdx.x) / per_entry;
-        y = static_cast<int>(blockIdx.x) - di * per_entry;
-    } else {
-        const int item = (static_cast<int>(blockIdx.x) - long_ctas) * NW + warp;
-        live = item < (w.n_deferred - w.n_deferred_long) * per_entry;
-        const int k = live ? item / per_entry : 0;
-        y = item - k * per_entry;
-        di = w.n_deferred_long + k;
-    }
-    const int hg = y / GP;
-    const int gg = y - hg * GP;
     // the merge list comes from the step's host copy; the partials are the previous
     // (decode) kernel's output
-    const int mi = live ? __ldg(w.merge_deferred + di) : 0;
-    const int seg = live ? __ldg(w.merge_seg + mi) : 0;
-    const int s0 = live ? __ldg(w.merge_slot0 + mi) : 0;
-    const int ns = live ? __ldg(w.merge_nslots + mi) : 0;
-    const int b = seg / g.heads_kv;
-    const int h = seg - b * g.heads_kv;
-    const int q_head0 = h * group + hg * GP;
-    const int gcount = min(GP, group - hg * GP);
+    w = resolve_work(w);
+    const int per_entry = head_groups * GP;
+    const int long_ctas = w.n_deferred_long * per_entry;
+    const int n_items = long_ctas + ((w.n_deferred - w.n_deferred_long) * per_entry + NW - 1) / NW;
     pdl_launch_dependents();
     pdl_wait();
-    if (!live || gg >= gcount) return;  // CTA-uniform in the CTA role
-    const int64_t base = (static_cast<int64_t>(hg) * w.n_slots + s0) * GP + gg;  // + s * GP
-    float M, L, A[EPLV];
-    if (!cta_role) {
-        merge_slots<GP, DV>(a, base, 0, ns, lane, M, L, A);
-        finish_row<DV>(a, b, q_head0 + gg, M, L, A, lane);
-        return;
+    // LOOP (the static layout's fixed grid): items x, x + gridDim.x, ...; otherwise item x alone
+#pragma unroll 1
+    for (int item = static_cast<int>(blockIdx.x); item < n_items;
+         item = LOOP ? item + static_cast<int>(gridDim.x) : n_items) {
+        const bool cta_role = item < long_ctas;
+        int di, y;
+        bool live = true;
+        if (cta_role) {
+            di = item / per_entry;
+            y = item - di * per_entry;
+        } else {
+            const int it = (item - long_ctas) * NW + warp;
+            live = it < (w.n_deferred - w.n_deferred_long) * per_entry;
+            const int k = live ? it / per_entry : 0;
+            y = it - k * per_entry;
+            di = w.n_deferred_long + k;
+        }
+        const int hg = y / GP;
+        const int gg = y - hg * GP;
+        const int mi = live ? __ldg(w.merge_deferred + di) : 0;
+        const int seg = live ? __ldg(w.merge_seg + mi) : 0;
+        const int s0 = live ? __ldg(w.merge_slot0 + mi) : 0;
+        const int ns = live ? __ldg(w.merge_nslots + mi) : 0;
+        const int b = seg / g.heads_kv;
+        const int h = seg - b * g.heads_kv;
+        const int q_head0 = h * group + hg * GP;
+        const int gcount = min(GP, group - hg * GP);
+        if (!live || gg >= gcount) continue;  // CTA-uniform in the CTA role
+        const int64_t base = (static_cast<int64_t>(hg) * w.n_slots + s0) * GP + gg;  // + s * GP
+        float M, L, A[EPLV];
+        if (!cta_role) {
+            merge_slots<GP, DV>(a, base, 0, ns, lane, M, L, A);
+            finish_row<DV>(a, b, q_head0 + gg, M, L, A, lane);
+            continue;
+        }
+        const int per = (ns + NW - 1) / NW;
+        const int lo = min(ns, warp * per), hi = min(ns, lo + per);
+        merge_slots<GP, DV>(a, base, lo, hi, lane, M, L, A);
+        if (lane == 0) {
+            sm_m[warp] = M;
+            sm_l[warp] = L;
+        }
+#pragma unroll
+        for (int e = 0; e < EPLV; ++e) sm_a[warp][lane * EPLV + e] = A[e];
+        __syncthreads();
+        if (warp == 0) {
+            float Mt = sm_m[0];
+#pragma unroll
+            for (int k = 1; k < NW; ++k) Mt = fmaxf(Mt, sm_m[k]);
+            float Lt = 0.f, At[EPLV];
+#pragma unroll
+            for (int e = 0; e < EPLV; ++e) At[e] = 0.f;
+#pragma unroll
+            for (int k = 0; k < NW; ++k) {
+                const float f = (sm_m[k] == -INFINITY || Mt == -INFINITY) ? 0.f : exp2f(sm_m[k] - Mt);
+                Lt = fmaf(sm_l[k], f, Lt);
+#pragma unroll
+                for (int e = 0; e < EPLV; ++e) At[e] = fmaf(f, sm_a[k][lane * EPLV + e], At[e]);
+            }
+            finish_row<DV>(a, b, q_head0 + gg, Mt, Lt, At, lane);
+        }
+        __syncthreads();  // warp 0 has read the shared arrays before the next item writes them
     }
-    const int per = (ns + NW - 1) / NW;
-    const int lo = min(ns, warp * per), hi = min(ns, lo + per);
-    merge_slots<GP, DV>(a, base, lo, hi, lane, M, L, A);
-    if (lane == 0) {
-        sm_m[warp] = M;
-        sm_l[warp] = L;
-    }
-#pragma unroll
-    for (int e = 0; e < EPLV; ++e) sm_a[warp][lane * EPLV + e] = A[e];
-    __syncthreads();
-    if (warp != 0) return;
-    float Mt = sm_m[0];
-#pragma unroll
-    for (int k = 1; k < NW; ++k) Mt = fmaxf(Mt, sm_m[k]);
-    float Lt = 0.f, At[EPLV];
-#pragma unroll
-    for (int e = 0; e < EPLV; ++e) At[e] = 0.f;
-#pragma unroll
-    for (int k = 0; k < NW; ++k) {
-        const float f = (sm_m[k] == -INFINITY || Mt == -INFINITY) ? 0.f : exp2f(sm_m[k] - Mt);
-        Lt = fmaf(sm_l[k], f, Lt);
-#pragma unroll
-        for (int e = 0; e < EPLV; ++e) At[e] = fmaf(f, sm_a[k][lane * EPLV + e], At[e]);
-    }
-    finish_row<DV>(a, b, q_head0 + gg, Mt, Lt, At, lane);
 }
 
 // Cross-part merge of normalised outputs with their log-sum-exps (multi-GPU split-KV: the

@@ -38,15 +38,14 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
 // Loads from another GPU's memory that a later epoch rewrites: never served from L1.
 __device__ __forceinline__ float ld_peer(const float* p) {
     float v;
-    asm volatile("ld.relaxed.sys.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.sys.global.f32 %0, [%1];" : "=f"(v) : "l"(p));
     return v;
 }
 __device__ __forceinline__ float4 ld_peer4(const float4* p) {
     float4 v;
     asm volatile("ld.relaxed.sys.global.v4.f32 {%0, %1, %2, %3}, [%4];"
                  : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "l"(p)
-                 : "memory");
+                 : "l"(p));
     return v;
 }
 
@@ -100,17 +99,33 @@ __global__ void __launch_bounds__(256) pull_merge_kernel(ExchangePeers p, int me
     for (int o = 16; o >= 1; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
     if (sk != -INFINITY) den += expf(sk - M);
     const float inv = den > 0.f ? 1.f / den : 0.f;
+    // Peer loads take on the order of a microsecond: each group of kGroup ranks' float4s is
+    // issued back to back before any of them is used, so a row waits about one round trip
+    // per group instead of one per rank.
+    constexpr int kGroup = 8;
     for (int d = lane * 4; d < dv; d += 128) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int r = 0; r < n; ++r) {
-            const float wr = __shfl_sync(0xffffffffu, w, r);
-            if (wr == 0.f) continue;  // no tokens there (its block may hold anything)
-            const float4 v = ld_peer4(reinterpret_cast<const float4*>(p.mbox[r] + slot_off + r * p.slot +
-                                                                        static_cast<int64_t>(row) * dv + d));
-            acc.x = fmaf(wr, v.x, acc.x);
-            acc.y = fmaf(wr, v.y, acc.y);
-            acc.z = fmaf(wr, v.z, acc.z);
-            acc.w = fmaf(wr, v.w, acc.w);
+        for (int r0 = 0; r0 < n; r0 += kGroup) {
+            float4 v[kGroup];
+            float wr[kGroup];
+#pragma unroll
+            for (int i = 0; i < kGroup; ++i) {
+                const int r = r0 + i;
+                wr[i] = __shfl_sync(0xffffffffu, w, r & 31);
+                // no tokens there (its block may hold anything): weight 0, nothing loaded
+                v[i] = (r < n && wr[i] != 0.f)
+                           ? ld_peer4(reinterpret_cast<const float4*>(p.mbox[r] + slot_off + r * p.slot +
+                                                                      static_cast<int64_t>(row) * dv + d))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int i = 0; i < kGroup; ++i) {
+                if (r0 + i >= n || wr[i] == 0.f) continue;
+                acc.x = fmaf(wr[i], v[i].x, acc.x);
+                acc.y = fmaf(wr[i], v[i].y, acc.y);
+                acc.z = fmaf(wr[i], v[i].z, acc.z);
+                acc.w = fmaf(wr[i], v[i].w, acc.w);
+            }
         }
         *reinterpret_cast<float4*>(out + static_cast<int64_t>(row) * dv + d) =
             make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);

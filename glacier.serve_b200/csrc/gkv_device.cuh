@@ -161,6 +161,14 @@ __device__ __forceinline__ void mma_1688(float (&d)[4], uint32_t a0, uint32_t a1
             : "r"(a0), "r"(a1), "r"(b0));
 }
 
+// max(a, b, c) in one instruction (the three-input form of max.f32, sm_100); NaN inputs are
+// ignored as by fmaxf.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 // Two fp32 values as one bf16x2 word (lo in bits 0-15), round to nearest even.
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);

@@ -129,6 +129,11 @@ struct StepWorkspace {
     bool meta_marked[2] = {false, false};
     cudaStream_t meta_stream = nullptr;
     int meta_flip = 0;
+    // Static step layout (gkv_step_set_static): every upload goes to d_meta[0] on the caller's
+    // stream and the launches read the header there, so that they can be captured once in a
+    // CUDA graph and replayed every step; grids are the reserved maxima.
+    bool static_mode = false;
+    int32_t static_merge_grid = 0;
     // partial results of split segments
     float* d_part_acc = nullptr;
     float* d_part_ml = nullptr;
@@ -211,6 +216,10 @@ struct Pool {
     int refs(int32_t b) const;
     bool try_find_prefix(uint64_t h, int32_t* out);
     bool try_fork(int32_t src, int32_t valid, int32_t* out);
+    size_t stats_pending_copies() {
+        std::lock_guard<std::mutex> lk(pending_mu);
+        return pending.size() / 3;
+    }
     // device helpers (caller holds a DeviceGuard)
     int flush_copies(cudaStream_t st);
     // Moves movable live blocks into the lowest free ids (compact.cpp); returns the number of
@@ -235,6 +244,7 @@ int step_append(Pool* p, int32_t layer, const float* d_k, const float* d_v, int3
                 cudaStream_t st);
 int step_decode_lse(Pool* p, int32_t layer, const float* d_q, float* d_out, float* d_lse,
                     int32_t n_heads, float scale, const float* d_sinks, cudaStream_t st);
+int step_set_static(Pool* p, bool enable);
 int step_reserve(Pool* p, int32_t max_batch, int32_t max_blocks, int32_t max_tokens,
                  int32_t n_heads);
 int step_prefill(Pool* p, int32_t layer, const void* d_q, int32_t q_dtype, float* d_out,

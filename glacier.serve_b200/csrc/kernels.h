@@ -36,12 +36,29 @@ struct ArenaGeom {
     const float* v_inv = nullptr;
 };
 
+// ---- packed step metadata ----
+// The step's metadata is one buffer: a header of counts and byte offsets, then the slot
+// mapping (at a fixed offset), then the tables, context lengths and work list.  A launch
+// normally receives the pointers and counts by value; in the static step layout (the launches
+// of a step captured once in a CUDA graph and replayed every step) it receives the buffer's
+// base (DecodeWork::dyn) and reads them from the header, which every upload rewrites.
+enum : int {
+    kHdrTok, kHdrBatch, kHdrMaxBlocks, kHdrSlots, kHdrMerge, kHdrDeferred, kHdrDeferredLong, kHdrWorkers,
+    kHdrTables, kHdrCtx, kHdrPseg, kHdrPc0, kHdrPc1, kHdrPslot, kHdrPmerge, kHdrWbeg, kHdrMseg, kHdrMs0,
+    kHdrMns, kHdrMdef, kHdrInts
+};
+constexpr size_t kHdrBytes = 128;  // the slot mapping starts here
+static_assert(kHdrInts * 4 <= static_cast<int>(kHdrBytes), "step header");
+
 // ---- kv append ----
 // Writes token i's K/V rows into slot slots[i] (or `single_slot` when slots == nullptr and
-// n_tok == 1).  Source row stride in elements per token: k_tok_stride / v_tok_stride.
+// n_tok == 1).  Source row stride in elements per token: k_tok_stride / v_tok_stride.  With
+// dyn_tok set (the static step layout), the token count is read from *dyn_tok on the device
+// (at most n_tok, which then sizes the grid).
 cudaError_t launch_kv_append(const ArenaGeom& g, int layer, const float* k, const float* v,
                              int64_t k_tok_stride, int64_t v_tok_stride, const int64_t* slots,
-                             int64_t single_slot, int n_tok, int* err, cudaStream_t stream);
+                             int64_t single_slot, int n_tok, int* err, cudaStream_t stream,
+                             const int32_t* dyn_tok = nullptr);
 
 // ---- fused q/k/v prologue + KV append (rope_append.cu) ----
 struct RopeAppendParams {
@@ -122,6 +139,13 @@ struct DecodeWork {
     // [batch] table row of each sequence, or nullptr for row = sequence.  The prefill over
     // the decode kernel makes every query of a sequence a sequence of its own on one row.
     const int32_t* table_row;
+    // Static step layout: the packed step buffer, whose header supplies every pointer and
+    // count above except merge_count and table_row (nullptr: use the fields as given).
+    const unsigned char* dyn;
+    // Static step layout: the deferred-merge kernel is launched on every call with this fixed
+    // grid and loops over the entries the header counts (0: launched only when n_deferred > 0,
+    // with one CTA per item group).
+    int32_t merge_grid;
 };
 
 struct DecodeArgs {
@@ -180,7 +204,8 @@ struct DecodeConfig {
 };
 DecodeConfig decode_config(const ArenaGeom& g, int n_heads);
 
-// Second launch of a decode whose work list defers merges (w.n_deferred > 0).
+// Second launch of a decode whose work list defers merges (w.n_deferred > 0, or w.merge_grid
+// > 0 in the static step layout).
 cudaError_t launch_deferred_merge(const ArenaGeom& g, const DecodeWork& w, const DecodeArgs& a,
                                   int group, int gp, int head_groups, cudaStream_t st);
 

@@ -110,6 +110,7 @@ struct AppendArgs {
     int n_tok;
     int bs_shift, heads_shift;  // log2 of block_size / heads_kv, or -1
     int* err;
+    const int32_t* dyn_tok;     // static step layout: the token count, read on the device
 };
 
 __device__ __forceinline__ void fetch_slots(int64_t (&s)[kRows], const AppendArgs& a,
@@ -155,7 +156,8 @@ __global__ void __launch_bounds__(256, 4) kv_append_kernel(ArenaGeom g, AppendAr
     const int lane = threadIdx.x & 31;
     const int warp = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
     const int n_warps = static_cast<int>((gridDim.x * blockDim.x) >> 5);
-    const int total = a.n_tok * g.heads_kv;  // <= kMaxRowsPerLaunch
+    const int n_tok = a.dyn_tok ? min(__ldg(a.dyn_tok), a.n_tok) : a.n_tok;
+    const int total = n_tok * g.heads_kv;  // <= kMaxRowsPerLaunch
     const int step = kRows * n_warps;
     const int hd = g.head_dim, vhd = g.v_head_dim;
     int64_t next[kRows];
@@ -236,9 +238,12 @@ cudaError_t launch_typed(const ArenaGeom& g, AppendArgs a, cudaStream_t stream) 
 
 cudaError_t launch_kv_append(const ArenaGeom& g, int layer, const float* k, const float* v,
                              int64_t k_tok_stride, int64_t v_tok_stride, const int64_t* slots,
-                             int64_t single_slot, int n_tok, int* err, cudaStream_t stream) {
+                             int64_t single_slot, int n_tok, int* err, cudaStream_t stream,
+                             const int32_t* dyn_tok) {
     if (n_tok <= 0) return cudaSuccess;
-    AppendArgs a{layer, k, v, k_tok_stride, v_tok_stride, slots, single_slot, n_tok, -1, -1, err};
+    // a device-side count must fit one launch (the host splits only counts it knows)
+    if (dyn_tok && static_cast<int64_t>(n_tok) * g.heads_kv > kMaxRowsPerLaunch) return cudaErrorInvalidValue;
+    AppendArgs a{layer, k, v, k_tok_stride, v_tok_stride, slots, single_slot, n_tok, -1, -1, err, dyn_tok};
     if (g.dtype == GKV_DTYPE_BF16) return launch_typed<__nv_bfloat16>(g, a, stream);
     if (g.dtype == GKV_DTYPE_F16) return launch_typed<__half>(g, a, stream);
     if (g.dtype == GKV_DTYPE_FP8_E4M3) return launch_typed<__nv_fp8_e4m3>(g, a, stream);

@@ -189,6 +189,7 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
     const int lane = threadIdx.x & 31;
     const int hg = blockIdx.y;
     const int worker = blockIdx.x * NW + warp;
+    w = resolve_work(w);
 
     uint64_t* my_bars = reinterpret_cast<uint64_t*>(smem + Tr::OFF_BAR) + warp * S;
     float* pbuf = reinterpret_cast<float*>(smem + Tr::OFF_PBUF) + warp * Tr::PBUF;
@@ -574,7 +575,7 @@ struct Inst {
                        a, group, cpp);
         if (e != cudaSuccess) return e;
         *launches = 1;
-        if (w.n_deferred > 0) {
+        if (w.n_deferred > 0 || w.merge_grid > 0) {
             e = launch_deferred_merge(g, w, a, group, GP, head_groups, st);
             if (e == cudaSuccess) *launches = 2;
         }
@@ -673,19 +674,24 @@ cudaError_t launch_lse_merge(const float* parts, int n_parts, int rows, int dv, 
 
 cudaError_t launch_deferred_merge(const ArenaGeom& g, const DecodeWork& w, const DecodeArgs& a,
                                   int group, int gp, int head_groups, cudaStream_t st) {
-    if (w.n_deferred <= 0) return cudaSuccess;
-    // a CTA per (long segment, head), then a warp per (short segment, head), eight per CTA
+    if (w.n_deferred <= 0 && w.merge_grid <= 0) return cudaSuccess;
+    // a CTA per (long segment, head), then a warp per (short segment, head), eight per CTA;
+    // in the static step layout a fixed grid loops over them
     const int64_t per_entry = static_cast<int64_t>(head_groups) * gp;
     const int64_t short_items = static_cast<int64_t>(w.n_deferred - w.n_deferred_long) * per_entry;
-    const dim3 grid(static_cast<unsigned>(w.n_deferred_long * per_entry + (short_items + 7) / 8));
-    auto go = [&](auto kern) { return launch_pdl(kern, grid, dim3(256), 0, st, g, w, a, group, head_groups); };
-#define GKV_MERGE_DV(GPV)                                                      \
-    switch (g.v_head_dim) {                                                   \
-        case 32: return go(deferred_merge_kernel<GPV, 32>);                   \
-        case 64: return go(deferred_merge_kernel<GPV, 64>);                   \
-        case 128: return go(deferred_merge_kernel<GPV, 128>);                 \
-        case 256: return go(deferred_merge_kernel<GPV, 256>);                 \
-        default: return cudaErrorInvalidValue;                                \
+    const dim3 grid(w.merge_grid > 0 ? static_cast<unsigned>(w.merge_grid)
+                                     : static_cast<unsigned>(w.n_deferred_long * per_entry + (short_items + 7) / 8));
+    auto go = [&](auto k_once, auto k_loop) {
+        return w.merge_grid > 0 ? launch_pdl(k_loop, grid, dim3(256), 0, st, g, w, a, group, head_groups)
+                                : launch_pdl(k_once, grid, dim3(256), 0, st, g, w, a, group, head_groups);
+    };
+#define GKV_MERGE_DV(GPV)                                                                             \
+    switch (g.v_head_dim) {                                                                          \
+        case 32: return go(deferred_merge_kernel<GPV, 32, false>, deferred_merge_kernel<GPV, 32, true>);    \
+        case 64: return go(deferred_merge_kernel<GPV, 64, false>, deferred_merge_kernel<GPV, 64, true>);    \
+        case 128: return go(deferred_merge_kernel<GPV, 128, false>, deferred_merge_kernel<GPV, 128, true>); \
+        case 256: return go(deferred_merge_kernel<GPV, 256, false>, deferred_merge_kernel<GPV, 256, true>); \
+        default: return cudaErrorInvalidValue;                                                       \
     }
     switch (gp) {
         case 1: GKV_MERGE_DV(1)

@@ -63,6 +63,7 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_tc_kernel(
     const int lane = threadIdx.x & 31;
     const int hg = blockIdx.y;
     const int worker = blockIdx.x * NW + warp;
+    w = resolve_work(w);
     const int gq = lane >> 2;   // query head of this lane's S rows / softmax
     const int tig = lane & 3;   // token pair 2*tig, 2*tig+1; accumulator heads 2*tig, 2*tig+1
 
@@ -491,7 +492,7 @@ cudaError_t launch_paged_decode_tc(const ArenaGeom& g, const DecodeWork& w, cons
                          a, group, cpp);
     if (e != cudaSuccess) return e;
     *launches = 1;
-    if (w.n_deferred > 0) {
+    if (w.n_deferred > 0 || w.merge_grid > 0) {
         e = launch_deferred_merge(g, w, a, group, kGP, head_groups, st);
         if (e == cudaSuccess) *launches = 2;
     }

@@ -40,7 +40,7 @@ int sm_count(int device) {
 
 // Byte layout of the packed step metadata (identical on host and device).
 struct MetaLayout {
-    size_t slots, tables, ctx, pseg, pc0, pc1, pslot, pmerge, wbeg, mseg, ms0, mns, mdef, total;
+    size_t hdr, slots, tables, ctx, pseg, pc0, pc1, pslot, pmerge, wbeg, mseg, ms0, mns, mdef, total;
 };
 
 MetaLayout meta_layout(int64_t n_tok, int64_t batch, int64_t max_blocks, int64_t n_pieces,
@@ -52,6 +52,7 @@ MetaLayout meta_layout(int64_t n_tok, int64_t batch, int64_t max_blocks, int64_t
         o = align_up(o + bytes, 16);
         return at;
     };
+    L.hdr = take(kHdrBytes);  // counts + offsets (kHdr*), then the slots at kHdrBytes
     L.slots = take(static_cast<size_t>(n_tok) * 8);
     L.tables = take(static_cast<size_t>(batch * max_blocks) * 4);
     L.ctx = take(static_cast<size_t>(batch) * 4);
@@ -328,6 +329,32 @@ int step_reserve(Pool* p, int32_t max_batch, int32_t max_blocks, int32_t max_tok
     return decode_buffers(p, n_heads, workers + n_seg, n_seg);
 }
 
+int step_set_static(Pool* p, bool enable) {
+    StepWorkspace& ws = p->ws;
+    if (!p->has_arena) return set_error(GKV_ESTATE, "pool has no device arena (metadata-only pool)");
+    if (enable) {
+        if (ws.meta_cap == 0 || ws.max_batch <= 0 || ws.n_heads <= 0)
+            return set_error(GKV_ESTATE, "reserve the step first (gkv_step_reserve with the batch, blocks, tokens "
+                                         "and query heads of the largest step)");
+        if (!ws.cfg.supported)
+            return set_error(GKV_EUNSUPPORTED, "decode not built for head_dim %d / v_head_dim %d", p->desc.head_dim,
+                             p->desc.v_head_dim);
+        if (static_cast<int64_t>(ws.max_tokens) * p->desc.heads_kv > (int64_t{1} << 30))
+            return set_error(GKV_EINVAL, "max_tokens %d too large for one append launch", ws.max_tokens);
+        // pinned staging buffers may still feed copies into d_meta[1]: settle them
+        for (int i = 0; i < 2; ++i)
+            if (ws.meta_pending[i]) {
+                cudaError_t e = cudaEventSynchronize(ws.meta_copied[i]);
+                if (e != cudaSuccess) return cuda_fail(e, "cudaEventSynchronize(step metadata)");
+                ws.meta_pending[i] = false;
+            }
+        ws.static_merge_grid = sm_count(p->desc.device);  // the looping merge kernel: one CTA per SM
+    }
+    ws.static_mode = enable;
+    ws.uploaded = false;  // the next upload writes the layout the launches will read
+    return GKV_OK;
+}
+
 void step_free(Pool* p) {
     StepWorkspace& ws = p->ws;
     if (ws.meta_stream) cudaStreamSynchronize(ws.meta_stream);
@@ -398,25 +425,33 @@ int step_upload(Pool* p, const int32_t* tables, int32_t batch, int32_t max_block
             return set_error(GKV_EINVAL, "slot_mapping[%d] = %lld outside [-1, %lld)", i,
                              static_cast<long long>(slots[i]), static_cast<long long>(n_slots_total));
 
-    if (batch > ws.max_batch || max_blocks > ws.max_blocks || n_tok > ws.max_tokens ||
-        ws.meta_cap == 0) {
+    if (ws.static_mode) {  // the captured launches were sized for the reservation
+        if (batch > ws.max_batch || max_blocks > ws.max_blocks || n_tok > ws.max_tokens)
+            return set_error(GKV_EINVAL, "batch %d / max_blocks %d / n_tok %d exceed the static step reservation "
+                             "(%d / %d / %d)", batch, max_blocks, n_tok, ws.max_batch, ws.max_blocks, ws.max_tokens);
+    } else if (batch > ws.max_batch || max_blocks > ws.max_blocks || n_tok > ws.max_tokens || ws.meta_cap == 0) {
         const int rc = step_reserve(p, batch, max_blocks, n_tok, ws.n_heads);
         if (rc != GKV_OK) return rc;
     }
-    // Work list over a persistent grid: enough workers for the chunks, at most one wave.
+    // Work list over a persistent grid: enough workers for the chunks, at most one wave (the
+    // whole wave in the static layout, whose grid is fixed).
     int64_t total = 0;
     for (int32_t b = 0; b < batch; ++b) total += chunks_of(ctx_lens[b], bs);
     total *= p->desc.heads_kv;
     const int warps = ws.cfg.supported ? ws.cfg.warps : 4;
-    const int64_t ctas = decode_grid_ctas(total, warps, ws.n_ctas_max);
+    const int64_t ctas = ws.static_mode ? ws.n_ctas_max : decode_grid_ctas(total, warps, ws.n_ctas_max);
     WorkList& W = ws.wl;
     build_work_list(ctx_lens, batch, p->desc.heads_kv, bs, static_cast<int32_t>(ctas * warps), &W);
     const int64_t n_pieces = static_cast<int64_t>(W.piece_seg.size());
     const int64_t n_workers = static_cast<int64_t>(ctas) * warps;
     const int64_t n_merge = static_cast<int64_t>(W.merge_seg.size());
     const MetaLayout L = meta_layout(n_tok, batch, max_blocks, n_pieces, n_workers, n_merge);
-    int mrc = ensure_meta(p, L.total);
-    if (mrc != GKV_OK) return mrc;
+    if (ws.static_mode) {
+        if (L.total > ws.meta_cap) return set_error(GKV_ESTATE, "static step buffer too small");
+    } else {
+        int mrc = ensure_meta(p, L.total);
+        if (mrc != GKV_OK) return mrc;
+    }
 
     // This staging buffer fed the copy two uploads ago, normally long finished.
     const int mi = ws.meta_flip;
@@ -442,23 +477,50 @@ int step_upload(Pool* p, const int32_t* tables, int32_t batch, int32_t max_block
     put(L.ms0, W.merge_slot0);
     put(L.mns, W.merge_nslots);
     put(L.mdef, W.merge_deferred);
+    {
+        int32_t hd[kHdrInts];
+        hd[kHdrTok] = n_tok;
+        hd[kHdrBatch] = batch;
+        hd[kHdrMaxBlocks] = max_blocks;
+        hd[kHdrSlots] = W.n_slots;
+        hd[kHdrMerge] = static_cast<int32_t>(n_merge);
+        hd[kHdrDeferred] = static_cast<int32_t>(W.merge_deferred.size());
+        hd[kHdrDeferredLong] = W.n_deferred_long;
+        hd[kHdrWorkers] = static_cast<int32_t>(n_workers);
+        const size_t offs[] = {L.tables, L.ctx, L.pseg, L.pc0, L.pc1, L.pslot, L.pmerge,
+                               L.wbeg, L.mseg, L.ms0, L.mns, L.mdef};
+        for (int k = 0; k < kHdrInts - kHdrTables; ++k) hd[kHdrTables + k] = static_cast<int32_t>(offs[k]);
+        memcpy(h + L.hdr, hd, sizeof(hd));
+    }
+    cudaError_t e = cudaSuccess;
+    if (ws.static_mode) {
+        // one device buffer at a fixed address, rewritten in stream order: the previous step's
+        // launches (queued before on `st`) have read it by the time the copy runs
+        e = cudaMemcpyAsync(ws.d_meta[0], h, L.total, cudaMemcpyHostToDevice, st);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(step metadata)");
+        e = cudaEventRecord(ws.meta_copied[mi], st);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord(step metadata)");
+        ws.meta_pending[mi] = true;
+        ws.meta_flip ^= 1;
+    }
     // Device buffer mi last served the step uploaded two calls ago, whose kernels were queued
     // before the previous upload: the copy waits for the mark that upload recorded, then the
     // caller's stream waits for the copy.
-    cudaError_t e = cudaSuccess;
-    if (ws.meta_marked[mi ^ 1]) e = cudaStreamWaitEvent(ws.meta_stream, ws.meta_mark[mi ^ 1], 0);
-    if (e == cudaSuccess) e = cudaEventRecord(ws.meta_mark[mi], st);
-    if (e != cudaSuccess) return cuda_fail(e, "step metadata ordering");
-    ws.meta_marked[mi] = true;
-    e = cudaMemcpyAsync(ws.d_meta[mi], h, L.total, cudaMemcpyHostToDevice, ws.meta_stream);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(step metadata)");
-    e = cudaEventRecord(ws.meta_copied[mi], ws.meta_stream);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(st, ws.meta_copied[mi], 0);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord(step metadata)");
-    ws.meta_pending[mi] = true;
-    ws.meta_flip ^= 1;
+    else {
+        if (ws.meta_marked[mi ^ 1]) e = cudaStreamWaitEvent(ws.meta_stream, ws.meta_mark[mi ^ 1], 0);
+        if (e == cudaSuccess) e = cudaEventRecord(ws.meta_mark[mi], st);
+        if (e != cudaSuccess) return cuda_fail(e, "step metadata ordering");
+        ws.meta_marked[mi] = true;
+        e = cudaMemcpyAsync(ws.d_meta[mi], h, L.total, cudaMemcpyHostToDevice, ws.meta_stream);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(step metadata)");
+        e = cudaEventRecord(ws.meta_copied[mi], ws.meta_stream);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(st, ws.meta_copied[mi], 0);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord(step metadata)");
+        ws.meta_pending[mi] = true;
+        ws.meta_flip ^= 1;
+    }
 
-    char* d = ws.d_meta[mi];
+    char* d = ws.static_mode ? ws.d_meta[0] : ws.d_meta[mi];
     DecodeWork& w = ws.work;
     w.tables = reinterpret_cast<const int32_t*>(d + L.tables);
     w.ctx_lens = reinterpret_cast<const int32_t*>(d + L.ctx);
@@ -468,7 +530,7 @@ int step_upload(Pool* p, const int32_t* tables, int32_t batch, int32_t max_block
     w.piece_c1 = reinterpret_cast<const int32_t*>(d + L.pc1);
     w.piece_slot = reinterpret_cast<const int32_t*>(d + L.pslot);
     w.worker_piece_begin = reinterpret_cast<const int32_t*>(d + L.wbeg);
-    w.n_ctas = total > 0 ? static_cast<int32_t>(ctas) : 0;
+    w.n_ctas = (total > 0 || ws.static_mode) ? static_cast<int32_t>(ctas) : 0;
     w.n_slots = W.n_slots;
     w.merge_seg = reinterpret_cast<const int32_t*>(d + L.mseg);
     w.merge_slot0 = reinterpret_cast<const int32_t*>(d + L.ms0);
@@ -480,6 +542,8 @@ int step_upload(Pool* p, const int32_t* tables, int32_t batch, int32_t max_block
     w.n_deferred_long = W.n_deferred_long;
     w.merge_count = ws.d_merge_count;
     w.table_row = nullptr;
+    w.dyn = ws.static_mode ? reinterpret_cast<const unsigned char*>(d) : nullptr;
+    w.merge_grid = ws.static_mode ? ws.static_merge_grid : 0;
     ws.d_slots = reinterpret_cast<const int64_t*>(d + L.slots);
     ws.h_ctx.assign(ctx_lens, ctx_lens + batch);
     ws.batch = batch;
@@ -489,22 +553,42 @@ int step_upload(Pool* p, const int32_t* tables, int32_t batch, int32_t max_block
     return GKV_OK;
 }
 
+// In the static step layout a launch must not depend on host state that changes between steps:
+// copy-on-write copies queued since the last flush would be captured into the graph.
+static int static_guard(Pool* p) {
+    if (p->ws.static_mode && p->stats_pending_copies() > 0)
+        return set_error(GKV_ESTATE, "static step layout: flush the queued block copies (gkv_pool_flush_copies) "
+                                     "before the captured launches");
+    return GKV_OK;
+}
+
 int step_append(Pool* p, int32_t layer, const float* d_k, const float* d_v, int32_t n_tok,
                 cudaStream_t st) {
     StepWorkspace& ws = p->ws;
     if (!ws.uploaded) return set_error(GKV_ESTATE, "no step uploaded (call gkv_upload_step first)");
     if (layer < 0 || layer >= p->desc.layers)
         return set_error(GKV_EINVAL, "layer %d outside [0, %d)", layer, p->desc.layers);
-    if (n_tok < 0 || n_tok > ws.n_tok)
+    if (!ws.static_mode && (n_tok < 0 || n_tok > ws.n_tok))  // static: the uploaded count is used
         return set_error(GKV_EINVAL, "n_tok %d exceeds the uploaded slot mapping (%d)", n_tok, ws.n_tok);
     if (n_tok > 0 && (!d_k || !d_v)) return set_error(GKV_EINVAL, "k/v source is NULL");
-    int rc = p->flush_copies(st);
+    int rc = static_guard(p);
     if (rc != GKV_OK) return rc;
-    if (n_tok == 0) return GKV_OK;
+    rc = p->flush_copies(st);
+    if (rc != GKV_OK) return rc;
+    // static layout: the kernel appends the uploaded step's token count, read on the device,
+    // with a grid for the reserved maximum (d_k / d_v must hold that many rows)
+    if (ws.static_mode) {
+        if (ws.max_tokens == 0) return GKV_OK;
+        if (!d_k || !d_v) return set_error(GKV_EINVAL, "k/v source is NULL");
+    } else if (n_tok == 0) {
+        return GKV_OK;
+    }
+    const int32_t* dyn_tok =
+        ws.static_mode ? reinterpret_cast<const int32_t*>(ws.d_meta[0]) + kHdrTok : nullptr;
     cudaError_t e = launch_kv_append(p->geom, layer, d_k, d_v,
                                      static_cast<int64_t>(p->desc.heads_kv) * p->desc.head_dim,
                                      static_cast<int64_t>(p->desc.heads_kv) * p->desc.v_head_dim,
-                                     ws.d_slots, 0, n_tok, ws.d_err, st);
+                                     ws.d_slots, 0, ws.static_mode ? ws.max_tokens : n_tok, ws.d_err, st, dyn_tok);
     if (e != cudaSuccess) return cuda_fail(e, "kv_append launch");
     p->last_launches += 1;
     return GKV_OK;
@@ -521,7 +605,14 @@ static int decode_common(Pool* p, int32_t layer, const float* d_q, float* d_out,
         return set_error(GKV_EINVAL, "n_heads %d is not a positive multiple of heads_kv %d", n_heads,
                          p->desc.heads_kv);
     if (ws.batch > 0 && (!d_q || !d_out)) return set_error(GKV_EINVAL, "q/out is NULL");
-    {
+    if (ws.static_mode) {  // the reservation fixed the configuration and every buffer
+        if (n_heads != ws.n_heads)
+            return set_error(GKV_EINVAL, "static step layout reserved for %d query heads, not %d", ws.n_heads,
+                             n_heads);
+        if (d_lse && ws.max_batch > 0 && !d_out) return set_error(GKV_EINVAL, "out is NULL");
+        const int rc = static_guard(p);
+        if (rc != GKV_OK) return rc;
+    } else {
         // decode config + partial/counter capacity for the uploaded work list; the uploaded
         // metadata itself is left alone (the work list works with any kernel variant: every
         // variant runs the same number of warps per CTA)
@@ -643,6 +734,8 @@ int step_prefill(Pool* p, int32_t layer, const void* d_q, int32_t q_dtype, float
                  const int32_t* q_start, const int32_t* q_len, int32_t n_heads, float scale,
                  cudaStream_t st) {
     StepWorkspace& ws = p->ws;
+    if (ws.static_mode)
+        return set_error(GKV_ESTATE, "the chunked prefill is not available in the static step layout");
     if (!ws.uploaded) return set_error(GKV_ESTATE, "no step uploaded (call gkv_upload_step first)");
     if (layer < 0 || layer >= p->desc.layers)
         return set_error(GKV_EINVAL, "layer %d outside [0, %d)", layer, p->desc.layers);
@@ -926,7 +1019,16 @@ int gkv_step_reserve(gkv_pool* pool, int32_t max_batch, int32_t max_blocks_per_s
                      int32_t max_tokens, int32_t n_heads) {
     GKV_DEVICE_POOL(pool);
     gkv::DeviceGuard guard(pool->impl.desc.device);
+    if (pool->impl.ws.static_mode)
+        return set_error(GKV_ESTATE, "the static step layout is fixed: disable it before reserving again");
     return gkv::step_reserve(&pool->impl, max_batch, max_blocks_per_seq, max_tokens, n_heads);
+}
+
+int gkv_step_set_static(gkv_pool* pool, int32_t enable) {
+    if (!pool) return set_error(GKV_EINVAL, "pool handle is NULL");
+    if (!pool->impl.has_arena) return set_error(GKV_ESTATE, "pool has no device arena (metadata-only pool)");
+    gkv::DeviceGuard guard(pool->impl.desc.device);
+    return gkv::step_set_static(&pool->impl, enable != 0);
 }
 
 int gkv_upload_step(gkv_pool* pool, const int32_t* h_block_tables, int32_t batch,

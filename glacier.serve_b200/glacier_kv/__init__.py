@@ -328,6 +328,12 @@ class PagedBlockPool:
     def reserve_step(self, max_batch: int, max_blocks_per_seq: int, max_tokens: int, n_heads: int) -> None:
         _check(lib.gkv_step_reserve(self._h, max_batch, max_blocks_per_seq, max_tokens, n_heads))
 
+    def set_static_step(self, enable: bool = True) -> None:
+        """gkv_step_set_static: fixed-address step metadata read on the device, so that the
+        per-layer kv_append + paged_decode launches can be captured once in a CUDA graph and
+        replayed after every upload_step on the same stream (reserve_step first)."""
+        _check(lib.gkv_step_set_static(self._h, 1 if enable else 0))
+
     def upload_step(self, block_tables: np.ndarray, ctx_lens: np.ndarray,
                     slot_mapping: Optional[np.ndarray] = None, stream=None) -> None:
         bt = np.ascontiguousarray(block_tables, dtype=np.int32)

@@ -146,6 +146,7 @@ SIGNATURES = {
     "gkv_table_block_ids": (C.c_int, [P, P, I32]),
     "gkv_table_release_all": (C.c_int, [P]),
     "gkv_step_reserve": (C.c_int, [P, I32, I32, I32, I32]),
+    "gkv_step_set_static": (C.c_int, [P, I32]),
     "gkv_upload_step": (C.c_int, [P, P, I32, I32, P, P, I32, P]),
     "gkv_upload_step_tables": (C.c_int, [P, P, I32, P, P, I32, P]),
     "gkv_kv_append": (C.c_int, [P, I32, P, P, I32, P]),

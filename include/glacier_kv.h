@@ -206,6 +206,24 @@ GKV_API int gkv_pool_compact(gkv_pool* pool, gkv_table* const* tables, int32_t n
  * the device block-table buffer of CudaPagedTransformerRunner.cs:115-120,143. */
 GKV_API int gkv_step_reserve(gkv_pool* pool, int32_t max_batch, int32_t max_blocks_per_seq,
                              int32_t max_tokens, int32_t n_heads);
+/* Static step layout (enable != 0), for a decode iteration captured ONCE in a CUDA graph
+ * (stream capture of the caller's per-layer gkv_kv_append + gkv_paged_decode calls, across
+ * all layers) and replayed every step after gkv_upload_step on the same stream -- the
+ * reference's per-sequence launches and uploads of CudaPagedTransformerRunner.ForwardBatch
+ * (CudaPagedTransformerRunner.cs:307-364) become one graph launch per step.  While enabled:
+ *  - every upload writes one device buffer at a fixed address with a copy on the caller's
+ *    stream, and the launches read the step's counts and work list from its header, so the
+ *    captured launch parameters stay valid; grids are the reservation's maxima;
+ *  - uploads must fit the reservation (GKV_EINVAL otherwise) and decodes use its n_heads;
+ *  - gkv_kv_append appends the UPLOADED step's token count (its n_tok argument is ignored;
+ *    the sources must hold max_tokens rows);
+ *  - queued copy-on-write copies must be flushed (gkv_pool_flush_copies) before the captured
+ *    launches run: a capturable call refuses to run with copies pending (GKV_ESTATE);
+ *  - gkv_paged_prefill is refused (GKV_ESTATE); gkv_rope_append works but copies its host
+ *    positions per call, so it is not capturable.
+ * Requires a prior gkv_step_reserve (GKV_ESTATE otherwise).  Enabling or disabling drops the
+ * uploaded step.  No reference counterpart (the reference has no CUDA graphs). */
+GKV_API int gkv_step_set_static(gkv_pool* pool, int32_t enable);
 /* Uploads one step's packed metadata with ONE host-to-device copy, ordered before the rest
  * of `stream`:
  *   h_block_tables [batch][max_blocks] int32 (unused entries may hold -1),
