@@ -258,41 +258,55 @@ __global__ void __launch_bounds__(256) deferred_merge_kernel(ArenaGeom g, Decode
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     // the merge list comes from the step's host copy; the partials are the previous
-    // (decode) kernel's output
-    w = resolve_work(w);
+    // (decode) kernel's output.  LOOP is only launched in the static step layout.
+    if constexpr (LOOP) w = resolve_work(w);
     const int per_entry = head_groups * GP;
     const int long_ctas = w.n_deferred_long * per_entry;
     const int n_items = long_ctas + ((w.n_deferred - w.n_deferred_long) * per_entry + NW - 1) / NW;
-    pdl_launch_dependents();
-    pdl_wait();
-    // LOOP (the static layout's fixed grid): items x, x + gridDim.x, ...; otherwise item x alone
-#pragma unroll 1
-    for (int item = static_cast<int>(blockIdx.x); item < n_items;
-         item = LOOP ? item + static_cast<int>(gridDim.x) : n_items) {
-        const bool cta_role = item < long_ctas;
+    // One item's merge entry.  The first item's is read before pdl_wait: it comes from the
+    // step's host copy, so its load latency overlaps the decode's tail.
+    struct Item {
+        bool cta_role, live;
+        int hg, gg, seg, s0, ns;
+    };
+    auto prep = [&](int item) {
+        Item r;
+        r.cta_role = item < long_ctas;
+        r.live = item < n_items;
         int di, y;
-        bool live = true;
-        if (cta_role) {
+        if (r.cta_role) {
             di = item / per_entry;
             y = item - di * per_entry;
         } else {
             const int it = (item - long_ctas) * NW + warp;
-            live = it < (w.n_deferred - w.n_deferred_long) * per_entry;
-            const int k = live ? it / per_entry : 0;
+            r.live = r.live && it < (w.n_deferred - w.n_deferred_long) * per_entry;
+            const int k = r.live ? it / per_entry : 0;
             y = it - k * per_entry;
             di = w.n_deferred_long + k;
         }
-        const int hg = y / GP;
-        const int gg = y - hg * GP;
-        const int mi = live ? __ldg(w.merge_deferred + di) : 0;
-        const int seg = live ? __ldg(w.merge_seg + mi) : 0;
-        const int s0 = live ? __ldg(w.merge_slot0 + mi) : 0;
-        const int ns = live ? __ldg(w.merge_nslots + mi) : 0;
-        const int b = seg / g.heads_kv;
-        const int h = seg - b * g.heads_kv;
+        r.hg = y / GP;
+        r.gg = y - r.hg * GP;
+        const int mi = r.live ? __ldg(w.merge_deferred + di) : 0;
+        r.seg = r.live ? __ldg(w.merge_seg + mi) : 0;
+        r.s0 = r.live ? __ldg(w.merge_slot0 + mi) : 0;
+        r.ns = r.live ? __ldg(w.merge_nslots + mi) : 0;
+        return r;
+    };
+    Item cur = prep(static_cast<int>(blockIdx.x));
+    pdl_launch_dependents();
+    pdl_wait();
+    // LOOP (the static layout's fixed grid): items x, x + gridDim.x, ...; otherwise item x alone
+    const int step = LOOP ? static_cast<int>(gridDim.x) : n_items;
+#pragma unroll 1
+    for (int item = static_cast<int>(blockIdx.x); item < n_items; item += step) {
+        if (item != static_cast<int>(blockIdx.x)) cur = prep(item);
+        const bool cta_role = cur.cta_role;
+        const int hg = cur.hg, gg = cur.gg, s0 = cur.s0, ns = cur.ns;
+        const int b = cur.seg / g.heads_kv;
+        const int h = cur.seg - b * g.heads_kv;
         const int q_head0 = h * group + hg * GP;
         const int gcount = min(GP, group - hg * GP);
-        if (!live || gg >= gcount) continue;  // CTA-uniform in the CTA role
+        if (!cur.live || gg >= gcount) continue;  // CTA-uniform in the CTA role
         const int64_t base = (static_cast<int64_t>(hg) * w.n_slots + s0) * GP + gg;  // + s * GP
         float M, L, A[EPLV];
         if (!cta_role) {

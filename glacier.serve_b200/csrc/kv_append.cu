@@ -153,6 +153,9 @@ __device__ __forceinline__ AppendRow<KV> resolve_row(const ArenaGeom& g, const A
 
 template <typename KV, bool VEC>
 __global__ void __launch_bounds__(256, 4) kv_append_kernel(ArenaGeom g, AppendArgs a) {
+    // the decode that follows (a programmatic dependent launch) may be scheduled now; it waits
+    // for this grid's completion before it reads the arena
+    pdl_launch_dependents();
     const int lane = threadIdx.x & 31;
     const int warp = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
     const int n_warps = static_cast<int>((gridDim.x * blockDim.x) >> 5);

@@ -50,7 +50,9 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk16) {
     return static_cast<uint32_t>(row * 128 + ((chunk16 ^ row) << 4));
 }
 
-template <int NW, int S, bool F16>
+// DYN: the static step layout (the work list comes from the header at w.dyn); a separate
+// instantiation, so the by-value work list of the normal launch stays in the parameter bank.
+template <int NW, int S, bool F16, bool DYN>
 __global__ void __launch_bounds__(NW * 32) paged_decode_tc_kernel(
     const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
     ArenaGeom g, DecodeWork w, DecodeArgs a, int group, int cpp) {
@@ -63,7 +65,7 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_tc_kernel(
     const int lane = threadIdx.x & 31;
     const int hg = blockIdx.y;
     const int worker = blockIdx.x * NW + warp;
-    w = resolve_work(w);
+    if constexpr (DYN) w = resolve_work(w);
     const int gq = lane >> 2;   // query head of this lane's S rows / softmax
     const int tig = lane & 3;   // token pair 2*tig, 2*tig+1; accumulator heads 2*tig, 2*tig+1
 
@@ -384,11 +386,10 @@ cudaError_t tc_prepare() {
     if (e != cudaSuccess) return e;
     const uint64_t bit = 1ull << (dev & 63);
     if (done_mask.load(std::memory_order_acquire) & bit) return cudaSuccess;
-    e = cudaFuncSetAttribute(paged_decode_tc_kernel<kNW, kS, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kTcSmem));
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(paged_decode_tc_kernel<kNW, kS, true>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kTcSmem));
+    for (auto k : {paged_decode_tc_kernel<kNW, kS, false, false>, paged_decode_tc_kernel<kNW, kS, true, false>,
+                   paged_decode_tc_kernel<kNW, kS, false, true>, paged_decode_tc_kernel<kNW, kS, true, true>})
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kTcSmem));
     if (e == cudaSuccess) done_mask.fetch_or(bit, std::memory_order_acq_rel);
     return e;
 }
@@ -459,7 +460,7 @@ void decode_tc_config(DecodeConfig& c) {
     c.smem = kTcSmem;
     int per_sm = 1;
     if (tc_prepare() != cudaSuccess ||
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, paged_decode_tc_kernel<kNW, kS, false>, c.threads,
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, paged_decode_tc_kernel<kNW, kS, false, false>, c.threads,
                                                       kTcSmem) != cudaSuccess ||
         per_sm < 1) {
         cudaGetLastError();
@@ -485,11 +486,14 @@ cudaError_t launch_paged_decode_tc(const ArenaGeom& g, const DecodeWork& w, cons
     if (e != cudaSuccess) return e;
     const int cpp = (g.block_size + kChunk - 1) / kChunk;
     dim3 grid(static_cast<unsigned>(w.n_ctas), static_cast<unsigned>(head_groups));
-    e = g.dtype == GKV_DTYPE_F16
-            ? launch_pdl(paged_decode_tc_kernel<kNW, kS, true>, grid, dim3(kNW * 32), kTcSmem, st, *tk, *tv, g, w,
-                         a, group, cpp)
-            : launch_pdl(paged_decode_tc_kernel<kNW, kS, false>, grid, dim3(kNW * 32), kTcSmem, st, *tk, *tv, g, w,
-                         a, group, cpp);
+    auto go = [&](auto kern) {
+        return launch_pdl(kern, grid, dim3(kNW * 32), kTcSmem, st, *tk, *tv, g, w, a, group, cpp);
+    };
+    const bool f16 = g.dtype == GKV_DTYPE_F16;
+    if (w.dyn)
+        e = f16 ? go(paged_decode_tc_kernel<kNW, kS, true, true>) : go(paged_decode_tc_kernel<kNW, kS, false, true>);
+    else
+        e = f16 ? go(paged_decode_tc_kernel<kNW, kS, true, false>) : go(paged_decode_tc_kernel<kNW, kS, false, false>);
     if (e != cudaSuccess) return e;
     *launches = 1;
     if (w.n_deferred > 0 || w.merge_grid > 0) {

@@ -217,6 +217,7 @@ __device__ __forceinline__ void store_row(float* p, const float (&x)[E]) {
 // then the v heads.
 template <typename KV, int E>
 __global__ void __launch_bounds__(256) rope_append_kernel(ArenaGeom g, RopeArgs a) {
+    pdl_launch_dependents();  // the decode that follows waits for this grid before reading the arena
     constexpr int D = 32 * E;
     constexpr int U = 4;
     const int lane = threadIdx.x & 31;
