@@ -23,8 +23,11 @@ struct ArenaGeom {
     int32_t dtype;           // GKV_DTYPE_*
     // Host-side cache of the TMA tensor maps of K and V (CUtensorMap, 64-byte aligned) for
     // the tensor-core decode; nullptr means "encode at launch".  Never read on the device.
+    // 16-bit arenas: rank 4 = one box per 8-token chunk (both 64-dim halves), rank 3 = one box
+    // per half (the fallback when the 4-D view is refused).  FP8 arenas: rank 3, one box.
     const void* tmap_k = nullptr;
     const void* tmap_v = nullptr;
+    int32_t tmap_rank = 0;
     // The same with boxes of 16 slots (block sizes that are multiples of 16), for the prefill.
     const void* tmap_pk = nullptr;
     const void* tmap_pv = nullptr;
@@ -213,7 +216,11 @@ cudaError_t launch_deferred_merge(const ArenaGeom& g, const DecodeWork& w, const
 // 8, query group 5..8 per head group.  Same work list and partial layout; 4 warps per CTA.
 bool decode_tc_eligible(const ArenaGeom& g, int n_heads);
 // Encodes the K and V TMA maps of the arena into two 128-byte, 64-byte aligned buffers.
-bool encode_decode_tmaps(const ArenaGeom& g, void* tmap_k, void* tmap_v);
+// Encodes the decode maps of a bf16 / fp16 arena (d = dv = 128, 8-token boxes, 128-byte
+// swizzle): returns their rank (4: [dim % 64][slot][dim / 64][block*layer*head], one box of
+// 8 slots x 128 dims; 3: [dim][slot][block*layer*head], boxes of 8 slots x 64 dims), 0 on
+// failure.  FP8 arenas: rank 3 with boxes of 8 slots x 128 one-byte dims.
+int encode_decode_tmaps(const ArenaGeom& g, void* tmap_k, void* tmap_v);
 // Tiled TMA maps (bf16, 128-byte swizzle, no interleave; `map` is a 64-byte aligned
 // 128-byte CUtensorMap).  encode_arena_map: the 3-D view [block*layer*head][slot][dim] of
 // one arena with boxes of `rows` slots x 64 dims.
@@ -222,6 +229,12 @@ bool encode_bf16_map3(void* map, const void* base, const uint64_t dims[3], const
                       const uint32_t box[3]);
 bool encode_arena_map(void* map, void* base, const ArenaGeom& g, int dim, int rows = kDecodeChunk);
 void decode_tc_config(DecodeConfig& c);
+// Tensor-core variant for FP8 E4M3 KV (paged_decode_fp8.cu): d = dv = 128, block size a
+// multiple of 8, query group 5..8 per head group, scales present.  Same work list and partials.
+bool decode_fp8_tc_eligible(const ArenaGeom& g, int n_heads);
+void decode_fp8_tc_config(DecodeConfig& c);
+cudaError_t launch_paged_decode_fp8_tc(const ArenaGeom& g, const DecodeWork& w, const DecodeArgs& a, int group,
+                                       int head_groups, int* launches, cudaStream_t st);
 cudaError_t launch_paged_decode_tc(const ArenaGeom& g, const DecodeWork& w, const DecodeArgs& a,
                                    int group, int head_groups, int* launches, cudaStream_t st);
 

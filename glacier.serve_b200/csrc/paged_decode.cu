@@ -176,7 +176,9 @@ struct DecodeKernelTraits {
     static_assert(GP == 1 || GP == 2 || GP == 4 || GP == 8, "GP");
 };
 
-template <typename KV, int D, int DV, int GP, int NW, int S>
+// DYN: the static step layout (the work list comes from the header at w.dyn); a separate
+// instantiation, so the by-value work list of the normal launch stays in the parameter bank.
+template <typename KV, int D, int DV, int GP, int NW, int S, bool DYN>
 __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, DecodeWork w,
                                                                DecodeArgs a, int group, int cpp) {
     using Tr = DecodeKernelTraits<KV, D, DV, GP, NW, S>;
@@ -189,7 +191,7 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
     const int lane = threadIdx.x & 31;
     const int hg = blockIdx.y;
     const int worker = blockIdx.x * NW + warp;
-    w = resolve_work(w);
+    if constexpr (DYN) w = resolve_work(w);
 
     uint64_t* my_bars = reinterpret_cast<uint64_t*>(smem + Tr::OFF_BAR) + warp * S;
     float* pbuf = reinterpret_cast<float*>(smem + Tr::OFF_PBUF) + warp * Tr::PBUF;
@@ -541,9 +543,11 @@ struct Inst {
         if (e != cudaSuccess) return e;
         const uint64_t bit = 1ull << (dev & 63);
         if (done_mask.load(std::memory_order_acquire) & bit) return cudaSuccess;
-        e = cudaFuncSetAttribute(paged_decode_kernel<KV, D, DV, GP, NW, S>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(Tr::SMEM));
+        e = cudaFuncSetAttribute(paged_decode_kernel<KV, D, DV, GP, NW, S, false>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(Tr::SMEM));
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(paged_decode_kernel<KV, D, DV, GP, NW, S, true>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(Tr::SMEM));
         if (e == cudaSuccess) done_mask.fetch_or(bit, std::memory_order_acq_rel);
         return e;
     }
@@ -552,15 +556,18 @@ struct Inst {
         c.warps = NW;
         c.threads = NW * 32;
         c.smem = Tr::SMEM;
-        int per_sm = 1;
+        // the persistent grid must be resident in either instantiation
+        int per_sm = 1, per_sm_dyn = 1;
         if (prepare() != cudaSuccess ||
             cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                &per_sm, paged_decode_kernel<KV, D, DV, GP, NW, S>, c.threads, Tr::SMEM) !=
-                cudaSuccess ||
-            per_sm < 1) {
+                &per_sm, paged_decode_kernel<KV, D, DV, GP, NW, S, false>, c.threads, Tr::SMEM) != cudaSuccess ||
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                &per_sm_dyn, paged_decode_kernel<KV, D, DV, GP, NW, S, true>, c.threads, Tr::SMEM) != cudaSuccess ||
+            per_sm < 1 || per_sm_dyn < 1) {
             cudaGetLastError();
-            per_sm = 1;
+            per_sm = per_sm_dyn = 1;
         }
+        if (per_sm_dyn < per_sm) per_sm = per_sm_dyn;
         c.ctas_per_sm = per_sm;
         c.supported = true;
     }
@@ -571,8 +578,10 @@ struct Inst {
         cudaError_t e = prepare();
         if (e != cudaSuccess) return e;
         dim3 grid(static_cast<unsigned>(w.n_ctas), static_cast<unsigned>(head_groups));
-        e = launch_pdl(paged_decode_kernel<KV, D, DV, GP, NW, S>, grid, dim3(NW * 32), Tr::SMEM, st, g, w,
-                       a, group, cpp);
+        e = w.dyn ? launch_pdl(paged_decode_kernel<KV, D, DV, GP, NW, S, true>, grid, dim3(NW * 32), Tr::SMEM, st,
+                               g, w, a, group, cpp)
+                  : launch_pdl(paged_decode_kernel<KV, D, DV, GP, NW, S, false>, grid, dim3(NW * 32), Tr::SMEM, st,
+                               g, w, a, group, cpp);
         if (e != cudaSuccess) return e;
         *launches = 1;
         if (w.n_deferred > 0 || w.merge_grid > 0) {
@@ -641,6 +650,10 @@ DecodeConfig decode_config(const ArenaGeom& g, int n_heads) {
     c.head_groups = (group + c.gp - 1) / c.gp;
     if (decode_tc_eligible(g, n_heads)) {
         decode_tc_config(c);
+        return c;
+    }
+    if (decode_fp8_tc_eligible(g, n_heads)) {
+        decode_fp8_tc_config(c);
         return c;
     }
     dispatch(g, c.gp, [&](auto inst) { decltype(inst)::config(c); });
@@ -714,6 +727,8 @@ cudaError_t launch_paged_decode(const ArenaGeom& g, const DecodeWork& w, const D
                            reinterpret_cast<uintptr_t>(a.part_acc)) & 15) == 0;
     if (aligned && decode_tc_eligible(g, a.n_heads))
         return launch_paged_decode_tc(g, w, a, group, head_groups, launches, stream);
+    if (aligned && decode_fp8_tc_eligible(g, a.n_heads))
+        return launch_paged_decode_fp8_tc(g, w, a, group, head_groups, launches, stream);
     cudaError_t err = cudaErrorInvalidValue;
     dispatch(g, gp, [&](auto inst) {
         err = decltype(inst)::launch(g, w, a, group, head_groups, launches, stream);

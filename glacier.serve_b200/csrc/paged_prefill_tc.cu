@@ -509,11 +509,14 @@ cudaError_t launch_paged_prefill_tc(const ArenaGeom& g, const PrefillArgs& a, co
     const uint64_t strides[2] = {static_cast<uint64_t>(kD) * 2, static_cast<uint64_t>(a.n_heads) * kD * 2};
     const uint32_t box[3] = {64, 1, static_cast<uint32_t>(kBM)};
     if (!encode_bf16_map3(&mq, q16, dims, strides, box)) return cudaErrorInvalidValue;
-    // whole 16-slot pages per box when the block size allows, else 8-slot boxes; the pool
-    // caches both map pairs
+    // whole 16-slot pages per box when the block size allows, else 8-slot boxes.  The pool
+    // caches the 16-slot pair; the decode's 8-slot pair is reused only when it is the 3-D view
+    // this kernel's loads address (a 4-D decode map must never reach a 3-D load)
     const int rows = g.block_size % 16 == 0 ? 16 : 8;
-    const CUtensorMap* tk = static_cast<const CUtensorMap*>(rows == 16 ? g.tmap_pk : g.tmap_k);
-    const CUtensorMap* tv = static_cast<const CUtensorMap*>(rows == 16 ? g.tmap_pv : g.tmap_v);
+    const void* ck = rows == 16 ? g.tmap_pk : (g.tmap_rank == 3 ? g.tmap_k : nullptr);
+    const void* cv = rows == 16 ? g.tmap_pv : (g.tmap_rank == 3 ? g.tmap_v : nullptr);
+    const CUtensorMap* tk = static_cast<const CUtensorMap*>(ck);
+    const CUtensorMap* tv = static_cast<const CUtensorMap*>(cv);
     if (!tk || !tv) {
         if (!encode_arena_map(&ek, g.k, g, kD, rows) || !encode_arena_map(&ev, g.v, g, kD, rows))
             return cudaErrorInvalidValue;

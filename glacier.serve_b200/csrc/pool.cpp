@@ -365,12 +365,17 @@ int gkv_pool_create(const gkv_pool_desc* desc, gkv_pool** out_pool) {
             g.k_inv = P.d_scales + 2 * n;
             g.v_inv = P.d_scales + 3 * n;
         }
-        // TMA maps for the tensor-core kernels (16-bit storage, d = dv = 128, 8-token-aligned
-        // blocks); the copies move 2-byte elements, whichever 16-bit format they hold
-        if (d.dtype != GKV_DTYPE_F32 && d.head_dim == 128 && d.v_head_dim == 128 && d.block_size % 8 == 0 &&
-            gkv::encode_decode_tmaps(g, P.tmap_k, P.tmap_v)) {
+        // TMA maps for the tensor-core kernels (16-bit or FP8 storage, d = dv = 128,
+        // 8-token-aligned blocks); 16-bit copies move 2-byte elements, whichever format
+        int rank = 0;
+        if (d.dtype != GKV_DTYPE_F32 && d.head_dim == 128 && d.v_head_dim == 128 && d.block_size % 8 == 0)
+            rank = gkv::encode_decode_tmaps(g, P.tmap_k, P.tmap_v);
+        if (rank > 0) {
             g.tmap_k = P.tmap_k;
             g.tmap_v = P.tmap_v;
+            g.tmap_rank = rank;
+        }
+        if (rank > 0 && d.dtype != GKV_DTYPE_FP8_E4M3) {
             // whole-page boxes (16 slots) for the prefill kernel when the block size allows
             if (d.block_size % 16 == 0 && gkv::encode_arena_map(P.tmap_pk, g.k, g, 128, 16) &&
                 gkv::encode_arena_map(P.tmap_pv, g.v, g, 128, 16)) {
