@@ -111,16 +111,6 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int x, 
         : "memory");
 }
 
-// Tiled 4-D TMA load (no multicast), as tma_load_3d.
-__device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, int x, int y, int z, int w,
-                                            uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-        "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
-        : "memory");
-}
-
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
                                         uint32_t& r3) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"

@@ -22,9 +22,8 @@ struct ArenaGeom {
     int32_t total_blocks, layers, heads_kv, head_dim, v_head_dim, block_size;
     int32_t dtype;           // GKV_DTYPE_*
     // Host-side cache of the TMA tensor maps of K and V (CUtensorMap, 64-byte aligned) for
-    // the tensor-core decode; nullptr means "encode at launch".  Never read on the device.
-    // 16-bit arenas: rank 4 = one box per 8-token chunk (both 64-dim halves), rank 3 = one box
-    // per half (the fallback when the 4-D view is refused).  FP8 arenas: rank 3, one box.
+    // the tensor-core decodes; nullptr means "encode at launch".  Never read on the device.
+    // tmap_rank is the maps' rank (3) once encoded, 0 when there are none.
     const void* tmap_k = nullptr;
     const void* tmap_v = nullptr;
     int32_t tmap_rank = 0;
@@ -216,10 +215,9 @@ cudaError_t launch_deferred_merge(const ArenaGeom& g, const DecodeWork& w, const
 // 8, query group 5..8 per head group.  Same work list and partial layout; 4 warps per CTA.
 bool decode_tc_eligible(const ArenaGeom& g, int n_heads);
 // Encodes the K and V TMA maps of the arena into two 128-byte, 64-byte aligned buffers.
-// Encodes the decode maps of a bf16 / fp16 arena (d = dv = 128, 8-token boxes, 128-byte
-// swizzle): returns their rank (4: [dim % 64][slot][dim / 64][block*layer*head], one box of
-// 8 slots x 128 dims; 3: [dim][slot][block*layer*head], boxes of 8 slots x 64 dims), 0 on
-// failure.  FP8 arenas: rank 3 with boxes of 8 slots x 128 one-byte dims.
+// Encodes the decode maps of an arena with d = dv = 128 (8-token boxes, 128-byte swizzle) and
+// returns their rank (3), 0 on failure: bf16 / fp16 views [dim][slot][block*layer*head] with
+// boxes of 8 slots x 64 dims; FP8 views with boxes of 8 slots x 128 one-byte dims.
 int encode_decode_tmaps(const ArenaGeom& g, void* tmap_k, void* tmap_v);
 // Tiled TMA maps (bf16, 128-byte swizzle, no interleave; `map` is a 64-byte aligned
 // 128-byte CUtensorMap).  encode_arena_map: the 3-D view [block*layer*head][slot][dim] of

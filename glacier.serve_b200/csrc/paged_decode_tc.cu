@@ -7,11 +7,11 @@
 // configurations where the CUDA-core kernel is limited by the FP32 pipe, not by HBM
 // (arithmetic intensity 2 * group / 2 bytes = 7-8 FLOP per KV byte).  Per chunk:
 //
-//  * One tiled TMA load (cp.async.bulk.tensor, 128-byte swizzle, no multicast) brings the
-//    chunk's K rows and one its V rows: a box of 8 tokens x both 64-dim halves (2 KB) from a
-//    4-D view [dim % 64][slot][dim / 64][block*layer*head] of this GPU's own arena, which lands
-//    as [half][token][64 dims].  (Without the 4-D view: two 3-D boxes of 8 tokens x 64 dims
-//    per operand, the same bytes.)  The swizzle makes the ldmatrix reads bank-conflict free.
+//  * Two tiled TMA loads (cp.async.bulk.tensor, 128-byte swizzle, no multicast) bring the
+//    chunk's K rows and two bring its V rows: boxes of 8 tokens x 64 dims (1 KB each) from
+//    a 3-D view [block*layer*head][slot][dim] of this GPU's own arena.  The swizzle makes the
+//    ldmatrix reads below bank-conflict free.  (One 4-D box per operand -- both halves in one
+//    2 KB copy -- measured the same on the full batch and 2 % slower on an 8th of it.)
 //  * S^T[8 heads x 8 tokens] = Q . K^T with mma.m16n8k16 (16-bit in, fp32 accumulate; rows
 //    8..15 of the A operand are zero).  Q is split into hi + lo parts of the arena's type (two
 //    MMAs), so the scores carry ~16 (bf16) or ~22 (fp16) mantissa bits of q; K is exact.  For
@@ -115,12 +115,9 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_tc_kernel(
     };
     p_load();
     pdl_wait();
-    // Lanes 0-1 issue the chunk's K and V boxes (4-D maps: 2 KB each), or lanes 0-3 its four
-    // half boxes (3-D maps): a TMA instruction occupies its issuing thread for on the order of a
-    // hundred cycles, and the SM's TMA unit accepts about one every 60 cycles, so fewer, larger
-    // boxes per chunk raise the ceiling on the bytes it can fetch (1 KB boxes capped the kernel
-    // near 0.8 of HBM).
-    const bool rank4 = g.tmap_rank == 4;
+    // Lanes 0-3 issue the chunk's four boxes, one each: a TMA instruction occupies its issuing
+    // thread for on the order of a hundred cycles, so four from one lane would hold the warp
+    // about as long as the chunk's math.
     auto issue = [&](int st) {
         int page, tok0, ntok;
         chunk_geom(p_c0 + p_j, p_ctx, page, tok0, ntok);
@@ -138,19 +135,12 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_tc_kernel(
             }
         }
         __syncwarp();  // the expected byte count precedes every box's completion
-        const int n_boxes = rank4 ? 2 : 4;  // one box per operand (both halves) or per half
-        if (ok && lane < n_boxes) {
+        if (ok && lane < 4) {
             const int z = static_cast<int>((blk * g.layers + a.layer) * g.heads_kv + p_h);
+            unsigned char* dst = my_stages + static_cast<size_t>(st) * kStage + lane * kBox;
             fence_proxy_async_smem();
-            if (rank4) {
-                unsigned char* dst = my_stages + static_cast<size_t>(st) * kStage + lane * 2 * kBox;
-                tma_load_4d(dst, lane == 0 ? static_cast<const void*>(&tmk) : static_cast<const void*>(&tmv), 0,
-                            tok0, 0, z, bar);
-            } else {
-                unsigned char* dst = my_stages + static_cast<size_t>(st) * kStage + lane * kBox;
-                tma_load_3d(dst, lane < 2 ? static_cast<const void*>(&tmk) : static_cast<const void*>(&tmv),
-                            (lane & 1) * 64, tok0, z, bar);
-            }
+            tma_load_3d(dst, lane < 2 ? static_cast<const void*>(&tmk) : static_cast<const void*>(&tmv),
+                        (lane & 1) * 64, tok0, z, bar);
         }
         if (++p_j >= p_cnt) {
             p_j = 0;
@@ -449,19 +439,6 @@ bool encode_bf16_map3(void* map, const void* base, const uint64_t dims[3], const
     return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box);
 }
 
-// 4-D view [dim % 64][slot][dim / 64][block * layer * head] of one 16-bit arena (d = 128): the
-// slot stride (256 B) is larger than the half stride (128 B), so that a box of 8 slots x both
-// halves lands in shared memory as [half][slot][64 dims] -- the same bytes, and the same
-// 128-byte swizzle (line index = slot), as two boxes of 8 slots x 64 dims.
-static bool encode_arena_map4(void* map, void* base, const ArenaGeom& g, int dim) {
-    if (dim != 128 || g.block_size % kChunk != 0) return false;
-    const uint64_t dims[4] = {64, static_cast<uint64_t>(g.block_size), 2,
-                              static_cast<uint64_t>(g.total_blocks) * g.layers * g.heads_kv};
-    const uint64_t strides[3] = {static_cast<uint64_t>(dim) * 2, 128, static_cast<uint64_t>(g.block_size) * dim * 2};
-    const uint32_t box[4] = {64, static_cast<uint32_t>(kChunk), 2, 1};
-    return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, base, dims, strides, box);
-}
-
 // 3-D view [dim byte][slot][block * layer * head] of one FP8 arena (d = 128), 8-slot boxes.
 static bool encode_fp8_map(void* map, void* base, const ArenaGeom& g, int dim) {
     if (dim != 128 || g.block_size % kChunk != 0) return false;
@@ -485,7 +462,6 @@ bool encode_arena_map(void* map, void* base, const ArenaGeom& g, int dim, int ro
 int encode_decode_tmaps(const ArenaGeom& g, void* tmap_k, void* tmap_v) {
     if (g.dtype == GKV_DTYPE_FP8_E4M3)
         return encode_fp8_map(tmap_k, g.k, g, g.head_dim) && encode_fp8_map(tmap_v, g.v, g, g.v_head_dim) ? 3 : 0;
-    if (encode_arena_map4(tmap_k, g.k, g, kD) && encode_arena_map4(tmap_v, g.v, g, kDV)) return 4;
     return encode_arena_map(static_cast<CUtensorMap*>(tmap_k), g.k, g, kD) &&
                    encode_arena_map(static_cast<CUtensorMap*>(tmap_v), g.v, g, kDV)
                ? 3
