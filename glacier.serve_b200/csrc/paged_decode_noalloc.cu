@@ -20,8 +20,9 @@
 //    whose kernels overlap on the GPU (different streams, no ordering between them) race on
 //    it; order them on one stream or with events.
 //  * The first call on each device resolves the array's device address with
-//    cudaGetSymbolAddress (with that device current) and caches it; make that first call
-//    before any stream capture.
+//    cudaGetSymbolAddress (with that device current) and caches it.  No call may be captured
+//    in a CUDA graph (its table upload would not be replayed): a capturing stream gets
+//    GKV_ESTATE.
 //  * A kernel that meets a bad block id or gives up a bounded wait ORs a bit into an error word
 //    at the end of the array.  Calls never clear it; gkv_paged_decode_noalloc_status waits for
 //    the caller's stream, reads the word and clears it, so bits of every call since the last
@@ -165,6 +166,14 @@ extern "C" int gkv_paged_decode_noalloc(const gkv_arena_desc* arena, int32_t lay
     }
     char* dbase = static_cast<char*>(g_scratch_dev[dev]);
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    {
+        // the host-to-device copy of this call's tables is not something a graph can replay
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
+            return set_error(GKV_ESTATE, "gkv_paged_decode_noalloc must not be captured (its table upload would not be "
+                                         "replayed); capture pool decodes in the static step layout instead");
+        cudaGetLastError();
+    }
     if (batch == 0 || total == 0) return GKV_OK;
 
     int sms = 0;

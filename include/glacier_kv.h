@@ -363,10 +363,11 @@ typedef struct gkv_arena_desc {
  * gkv_paged_decode); the packed tables, the work list and the split-KV partials live in one
  * fixed 16 MiB device array per GPU inside the library, held until the process exits.
  * Calls that would need more (about 4 MiB of tables and work list, 12 MiB of partials)
- * return GKV_EINVAL.  Runs on the calling thread's current device and on `stream`.  The
- * first call on each device looks up that array's device address; make it before any stream
- * capture.  All calls on a device share the array and leave their contents in it; calls
- * whose kernels overlap on the GPU race on it, so order them on one stream. */
+ * return GKV_EINVAL.  Runs on the calling thread's current device and on `stream`.  Not
+ * capturable in a CUDA graph (its table upload would not be replayed): a capturing stream
+ * gets GKV_ESTATE -- gkv_step_set_static is the capturable decode.  All calls on a device
+ * share the array and leave their contents in it; calls whose kernels overlap on the GPU race
+ * on it, so order them on one stream. */
 GKV_API int gkv_paged_decode_noalloc(const gkv_arena_desc* arena, int32_t layer,
                                      const int32_t* h_block_tables, int32_t batch,
                                      int32_t max_blocks, const int32_t* h_ctx_lens,

@@ -118,3 +118,23 @@ def test_noalloc_sees_a_fork_queued_on_the_pool(cuda):
     ora = O.decode_batch(K, V, geom_of(pool), 0, tables, ctx, q_np, 4, 0.088)
     np.testing.assert_allclose(out.cpu().numpy(), ora, atol=TOL["f32"], rtol=0)
     pool.close()
+
+
+def test_noalloc_refuses_stream_capture(cuda):
+    """Its table upload cannot be replayed by a CUDA graph, so a capturing stream is refused
+    (GKV_ESTATE) before anything is enqueued; the static step layout is the capturable path."""
+    import torch
+
+    pool = G.PagedBlockPool(8, 1, 2, 128, 16, dtype="bf16")
+    q = torch.zeros((1, 8, 128), device=cuda)
+    out = torch.zeros((1, 8, 128), device=cuda)
+    tables, ctx = np.array([[0]], np.int32), np.array([5], np.int32)
+    G.paged_decode_noalloc(pool, 0, tables, ctx, q, out, 8, 0.125)  # resolves the scratch address
+    torch.cuda.synchronize(cuda)
+    s = torch.cuda.Stream(cuda)
+    graph = torch.cuda.CUDAGraph()
+    with pytest.raises(G.InvalidOperationError):
+        with torch.cuda.graph(graph, stream=s):
+            G.paged_decode_noalloc(pool, 0, tables, ctx, q, out, 8, 0.125, stream=s)
+    torch.cuda.synchronize(cuda)
+    pool.close()
