@@ -37,7 +37,7 @@ def _steps(rng, n_steps, max_batch, bs, total_blocks, max_ctx):
     return out
 
 
-@pytest.mark.parametrize("dtype,nH,nKv", [("f32", 28, 4), ("bf16", 28, 4), ("f16", 16, 8)])
+@pytest.mark.parametrize("dtype,nH,nKv", [("f32", 28, 4), ("bf16", 28, 4), ("f16", 16, 8), ("fp8", 28, 4)])
 def test_graph_replayed_decode_iteration_matches_oracle(cuda, dtype, nH, nKv):
     import torch
 
