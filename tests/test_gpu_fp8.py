@@ -217,3 +217,41 @@ def test_fp8_unsupported_shapes_and_noalloc_are_refused(cuda):
     with pytest.raises(G.ArgumentOutOfRangeError):
         G.paged_decode_noalloc(pool, 0, np.array([[0]], np.int32), np.array([5], np.int32), q, out, 4, 0.125)
     pool.close()
+
+
+def test_fp8_tensor_core_sinks_and_lse(cuda):
+    """The tensor-core FP8 decode (group 7, d 128) with per-head sinks matches the oracle, and its
+    lse output is ln of the softmax denominator over the scaled keys (long sequences split over
+    warps, so the merged partials carry the scales too)."""
+    import torch
+
+    rng = np.random.default_rng(81)
+    nH, nKv, d, bs = 28, 4, 128, 16
+    ctx = [3000, 13, 700]
+    need = sum((c + bs - 1) // bs for c in ctx)
+    pool = _pool(need + 2, 1, nKv, d, bs, seed=9, lo=0.25, hi=1.5)
+    K, V = random_arena(pool, rng)
+    tables = random_tables(rng, ctx, bs, need + 2)
+    q = rng.standard_normal((len(ctx), nH, d)).astype(np.float32)
+    g = geom_of(pool)
+    sink = 0.6
+    out = gpu_decode(pool, 0, tables, ctx, q, nH, scale_of(d), sinks=np.full(nH, sink, np.float32))
+    ref = O.decode_batch(K, V, g, 0, tables, np.array(ctx, np.int32), q, nH, scale_of(d), sink_logit=sink)
+    vmax = float(np.abs(O.e4m3_bits_to_f32(V)).max() * pool.kv_scales[1].max())
+    np.testing.assert_allclose(out, ref, atol=TOL["fp8"] * max(1.0, vmax), rtol=0)
+    # lse without sinks
+    qd = torch.from_numpy(q).to(cuda)
+    o2 = torch.zeros((len(ctx), nH, d), device=cuda)
+    lse = torch.zeros((len(ctx), nH), device=cuda)
+    pool.upload_step(tables, np.array(ctx, np.int32))
+    pool.paged_decode_lse(0, qd, o2, lse, nH, scale_of(d))
+    pool.sync()
+    ks, _ = pool.kv_scales
+    for b, c in enumerate(ctx):
+        for h in (0, 13, 27):
+            hk = h // (nH // nKv)
+            kk = np.stack([O.e4m3_bits_to_f32(K[tables[b, t // bs], 0, hk, t % bs]) for t in range(c)]).astype(np.float64)
+            s = kk @ q[b, h].astype(np.float64) * float(ks[0, hk]) * scale_of(d)
+            want = s.max() + math.log(np.exp(s - s.max()).sum())
+            assert abs(float(lse[b, h]) - want) < 1e-3 * max(1.0, abs(want))
+    pool.close()
