@@ -455,9 +455,12 @@ GKV_API int gkv_comm_destroy(gkv_comm* comm);
  * own mailbox and every rank's merge reads all blocks with plain peer loads. */
 GKV_API int gkv_comm_exchange_kind(const gkv_comm* comm);
 /* This rank's share of a split-KV decode: decode of the uploaded step (this rank's block
- * ranges) with lse, NCCL all-gather of (out, lse) over the ranks, log-sum-exp merge (plus the
- * optional sinks, applied once) into d_out [batch][n_heads][v_head_dim] on every rank.
- * All ranks must call it with the same batch and n_heads. */
+ * ranges) with lse, exchange of (out, lse) over the ranks -- through the peer mailboxes when
+ * the ranks map each other (gkv_comm_exchange_kind 2: the decode writes into this rank's own
+ * mailbox, one kernel publishes an epoch flag, waits for every rank's and merges), else an NCCL
+ * all-gather -- and the log-sum-exp merge (plus the optional sinks, applied once) into d_out
+ * [batch][n_heads][v_head_dim] on every rank.  All ranks must call it with the same batch and
+ * n_heads.  Merged rows of sequences with no tokens on any rank are 0. */
 GKV_API int gkv_paged_decode_splitkv_dist(gkv_pool* pool, gkv_comm* comm, int32_t layer,
                                           const float* d_q, float* d_out, int32_t n_heads,
                                           float scale, const float* d_sinks, void* stream);
