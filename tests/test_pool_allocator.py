@@ -452,3 +452,13 @@ def test_fp8_pool_checks_head_dims_and_scales():
     f = PagedBlockPool(8, 2, 2, 64, 16, allocate_device_arena=False, dtype="bf16")
     with pytest.raises(InvalidOperationError):
         f.set_kv_scales(np.ones((2, 2)), np.ones((2, 2)))
+
+
+def test_static_step_layout_needs_a_device_arena():
+    """gkv_step_set_static fixes device metadata for CUDA-graph capture: a metadata-only pool
+    (no device arena) refuses it, as it refuses every device call."""
+    p = PagedBlockPool(8, 1, 2, 64, 16, allocate_device_arena=False)
+    with pytest.raises(InvalidOperationError):
+        p.set_static_step(True)
+    with pytest.raises(InvalidOperationError):
+        p.set_static_step(False)
