@@ -82,9 +82,23 @@ __global__ void __launch_bounds__(256) pull_merge_kernel(ExchangePeers p, int me
     const int row = static_cast<int>((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
     if (row >= rows) return;
     const int64_t slot_off = static_cast<int64_t>(parity) * n * p.slot;
+    // Peer loads take on the order of a microsecond: each group of kGroup ranks' float4s is
+    // issued back to back before any of them is used, so a row waits about one round trip
+    // per group instead of one per rank.  The first group of the first dims is issued with the
+    // lse loads, before the weights are known (a rank with no tokens is loaded and ignored: its
+    // slot is mapped memory of any content), so the common dv <= 128, n <= 8 row takes one trip.
+    constexpr int kGroup = 8;
+    auto out_of = [&](int r, int d) {
+        return reinterpret_cast<const float4*>(p.mbox[r] + slot_off + r * p.slot + static_cast<int64_t>(row) * dv + d);
+    };
     // lane r < n holds rank r's lse of this row
     float l = -INFINITY;
     if (lane < n) l = ld_peer(p.mbox[lane] + slot_off + lane * p.slot + static_cast<int64_t>(rows) * dv + row);
+    float4 v0[kGroup];
+    const int d0 = lane * 4;
+#pragma unroll
+    for (int i = 0; i < kGroup; ++i)
+        v0[i] = (i < n && d0 < dv) ? ld_peer4(out_of(i, d0)) : make_float4(0.f, 0.f, 0.f, 0.f);
     float M = l;
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
@@ -99,11 +113,7 @@ __global__ void __launch_bounds__(256) pull_merge_kernel(ExchangePeers p, int me
     for (int o = 16; o >= 1; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
     if (sk != -INFINITY) den += expf(sk - M);
     const float inv = den > 0.f ? 1.f / den : 0.f;
-    // Peer loads take on the order of a microsecond: each group of kGroup ranks' float4s is
-    // issued back to back before any of them is used, so a row waits about one round trip
-    // per group instead of one per rank.
-    constexpr int kGroup = 8;
-    for (int d = lane * 4; d < dv; d += 128) {
+    for (int d = d0; d < dv; d += 128) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int r0 = 0; r0 < n; r0 += kGroup) {
             float4 v[kGroup];
@@ -112,11 +122,10 @@ __global__ void __launch_bounds__(256) pull_merge_kernel(ExchangePeers p, int me
             for (int i = 0; i < kGroup; ++i) {
                 const int r = r0 + i;
                 wr[i] = __shfl_sync(0xffffffffu, w, r & 31);
-                // no tokens there (its block may hold anything): weight 0, nothing loaded
-                v[i] = (r < n && wr[i] != 0.f)
-                           ? ld_peer4(reinterpret_cast<const float4*>(p.mbox[r] + slot_off + r * p.slot +
-                                                                      static_cast<int64_t>(row) * dv + d))
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
+                if (d == d0 && r0 == 0)
+                    v[i] = v0[i];
+                else  // no tokens there (its block may hold anything): weight 0, nothing loaded
+                    v[i] = (r < n && wr[i] != 0.f) ? ld_peer4(out_of(r, d)) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
             for (int i = 0; i < kGroup; ++i) {
