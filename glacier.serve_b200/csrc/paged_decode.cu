@@ -178,7 +178,11 @@ struct DecodeKernelTraits {
 
 // DYN: the static step layout (the work list comes from the header at w.dyn); a separate
 // instantiation, so the by-value work list of the normal launch stays in the parameter bank.
-template <typename KV, int D, int DV, int GP, int NW, int S, bool DYN>
+// LD: the group is GP - 1 heads (7 of 8, 3 of 4), so head slot GP - 1 is padding in every
+// piece; its P.V products and rescales are compiled out (its accumulator stays 0 and is never
+// output).  Its scores still go through the transpose-reduce, whose lane permutation spreads
+// every head over all slots.
+template <typename KV, int D, int DV, int GP, int NW, int S, bool DYN, bool LD>
 __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, DecodeWork w,
                                                                DecodeArgs a, int group, int cpp) {
     using Tr = DecodeKernelTraits<KV, D, DV, GP, NW, S>;
@@ -398,6 +402,7 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
                 if (__any_sync(0xffffffffu, changed)) {
 #pragma unroll
                     for (int gg = 0; gg < GP; ++gg) {
+                        if (LD && gg == GP - 1) continue;
                         const float mn = mbuf[gg];
                         const float alpha = exp2f(m[gg] - mn);
                         m[gg] = mn;
@@ -415,6 +420,7 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
                         load_pairs<KV, EPLV>(Vs + (t + 1) * DV + lane * EPLV, v1);
 #pragma unroll
                         for (int gg = 0; gg < GP; ++gg) {
+                            if (LD && gg == GP - 1) continue;
                             const float4 pp = *reinterpret_cast<const float4*>(pdup + gg * kChunk + t);
                             const float2 pa = make_float2(pp.x, pp.y), pb2 = make_float2(pp.z, pp.w);
 #pragma unroll
@@ -432,6 +438,7 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
                             load_pairs<KV, EPLV>(Vs + t * DV + lane * EPLV, v0);
 #pragma unroll
                             for (int gg = 0; gg < GP; ++gg) {
+                                if (LD && gg == GP - 1) continue;
                                 const float2 pa = pdup[gg * kChunk + t];
 #pragma unroll
                                 for (int e = 0; e < EV2; ++e) acc[gg][e] = __ffma2_rn(pa, v0[e], acc[gg][e]);
@@ -529,7 +536,7 @@ struct RingShape {
     static constexpr int S = S_FIT < 2 ? 2 : (S_FIT < S_MAX ? S_FIT : S_MAX);
 };
 
-template <typename KV, int D, int DV, int GP>
+template <typename KV, int D, int DV, int GP, bool LD = false>
 struct Inst {
     static constexpr int NW = RingShape<KV, D, DV>::NW;
     static constexpr int S = RingShape<KV, D, DV>::S;
@@ -543,10 +550,10 @@ struct Inst {
         if (e != cudaSuccess) return e;
         const uint64_t bit = 1ull << (dev & 63);
         if (done_mask.load(std::memory_order_acquire) & bit) return cudaSuccess;
-        e = cudaFuncSetAttribute(paged_decode_kernel<KV, D, DV, GP, NW, S, false>,
+        e = cudaFuncSetAttribute(paged_decode_kernel<KV, D, DV, GP, NW, S, false, LD>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(Tr::SMEM));
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(paged_decode_kernel<KV, D, DV, GP, NW, S, true>,
+            e = cudaFuncSetAttribute(paged_decode_kernel<KV, D, DV, GP, NW, S, true, LD>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(Tr::SMEM));
         if (e == cudaSuccess) done_mask.fetch_or(bit, std::memory_order_acq_rel);
         return e;
@@ -560,9 +567,9 @@ struct Inst {
         int per_sm = 1, per_sm_dyn = 1;
         if (prepare() != cudaSuccess ||
             cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                &per_sm, paged_decode_kernel<KV, D, DV, GP, NW, S, false>, c.threads, Tr::SMEM) != cudaSuccess ||
+                &per_sm, paged_decode_kernel<KV, D, DV, GP, NW, S, false, LD>, c.threads, Tr::SMEM) != cudaSuccess ||
             cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                &per_sm_dyn, paged_decode_kernel<KV, D, DV, GP, NW, S, true>, c.threads, Tr::SMEM) != cudaSuccess ||
+                &per_sm_dyn, paged_decode_kernel<KV, D, DV, GP, NW, S, true, LD>, c.threads, Tr::SMEM) != cudaSuccess ||
             per_sm < 1 || per_sm_dyn < 1) {
             cudaGetLastError();
             per_sm = per_sm_dyn = 1;
@@ -578,9 +585,9 @@ struct Inst {
         cudaError_t e = prepare();
         if (e != cudaSuccess) return e;
         dim3 grid(static_cast<unsigned>(w.n_ctas), static_cast<unsigned>(head_groups));
-        e = w.dyn ? launch_pdl(paged_decode_kernel<KV, D, DV, GP, NW, S, true>, grid, dim3(NW * 32), Tr::SMEM, st,
+        e = w.dyn ? launch_pdl(paged_decode_kernel<KV, D, DV, GP, NW, S, true, LD>, grid, dim3(NW * 32), Tr::SMEM, st,
                                g, w, a, group, cpp)
-                  : launch_pdl(paged_decode_kernel<KV, D, DV, GP, NW, S, false>, grid, dim3(NW * 32), Tr::SMEM, st,
+                  : launch_pdl(paged_decode_kernel<KV, D, DV, GP, NW, S, false, LD>, grid, dim3(NW * 32), Tr::SMEM, st,
                                g, w, a, group, cpp);
         if (e != cudaSuccess) return e;
         *launches = 1;
@@ -592,9 +599,10 @@ struct Inst {
     }
 };
 
-// Dispatch over (storage type, head dims, GP); `f` receives a value of the Inst type.
+// Dispatch over (storage type, head dims, GP); `f` receives a value of the Inst type.  fp32
+// pools with a group of 7 or 3 get the LD instantiation (padding slot compiled out).
 template <typename F>
-bool dispatch(const ArenaGeom& g, int gp, F&& f) {
+bool dispatch(const ArenaGeom& g, int gp, int group, F&& f) {
     auto by_gp = [&](auto kv_tag, auto d_tag, auto dv_tag) -> bool {
         using KV = decltype(kv_tag);
         constexpr int D = decltype(d_tag)::value;
@@ -602,8 +610,16 @@ bool dispatch(const ArenaGeom& g, int gp, F&& f) {
         switch (gp) {
             case 1: f(Inst<KV, D, DV, 1>{}); return true;
             case 2: f(Inst<KV, D, DV, 2>{}); return true;
-            case 4: f(Inst<KV, D, DV, 4>{}); return true;
-            case 8: f(Inst<KV, D, DV, 8>{}); return true;
+            case 4:
+                if constexpr (std::is_same<KV, float>::value)
+                    if (group == 3) return f(Inst<KV, D, DV, 4, true>{}), true;
+                f(Inst<KV, D, DV, 4>{});
+                return true;
+            case 8:
+                if constexpr (std::is_same<KV, float>::value)
+                    if (group == 7) return f(Inst<KV, D, DV, 8, true>{}), true;
+                f(Inst<KV, D, DV, 8>{});
+                return true;
         }
         return false;
     };
@@ -656,7 +672,7 @@ DecodeConfig decode_config(const ArenaGeom& g, int n_heads) {
         decode_fp8_tc_config(c);
         return c;
     }
-    dispatch(g, c.gp, [&](auto inst) { decltype(inst)::config(c); });
+    dispatch(g, c.gp, group, [&](auto inst) { decltype(inst)::config(c); });
     return c;
 }
 
@@ -730,7 +746,7 @@ cudaError_t launch_paged_decode(const ArenaGeom& g, const DecodeWork& w, const D
     if (aligned && decode_fp8_tc_eligible(g, a.n_heads))
         return launch_paged_decode_fp8_tc(g, w, a, group, head_groups, launches, stream);
     cudaError_t err = cudaErrorInvalidValue;
-    dispatch(g, gp, [&](auto inst) {
+    dispatch(g, gp, group, [&](auto inst) {
         err = decltype(inst)::launch(g, w, a, group, head_groups, launches, stream);
     });
     return err;

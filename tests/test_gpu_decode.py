@@ -81,6 +81,7 @@ CASES = [
     (16, 2, 128, 128, 8, "f32", [37, 8, 1, 100]),   # block size 8
     (8, 1, 128, 128, 24, "f32", [50, 24, 25, 3]),   # block size 24: chunks of 8
     (40, 8, 128, 128, 16, "f32", [3000, 7, 129]),   # group 5: three idle heads of the pass
+    (12, 4, 128, 128, 16, "f32", [2049, 300, 5, 17]),  # group 3: the padding slot compiled out
     # long and short splits in one batch: the merge gives the long ones a CTA, the others a warp
     (28, 4, 128, 128, 16, "f32", [12000, 700, 300, 90, 5]),
     (28, 4, 128, 128, 16, "bf16", [20000, 900, 64, 33]),
