@@ -19,7 +19,9 @@
 //    transpose-reduce in which each shuffle level halves the values a lane holds.  Each
 //    lane stores its partials at register positions XOR-permuted by its lane id, so at
 //    every level the half a lane keeps is the lower half of its registers and the half it
-//    sends is the upper half: one shuffle and one add per value, no selects.
+//    sends is the upper half: one shuffle and one add per value, no selects.  fp32 pools with
+//    d 128 and 8 head slots score with a half-warp split instead (HALF below): each half-warp
+//    takes 4 of the chunk's tokens at 8 dims per lane, so the reduce runs over 16 lanes.
 //  * Products use the packed two-wide fp32 FMA of sm_100 (fma.rn.f32x2).
 //  * Softmax is online (running max and sum per head, base-2 exponent).  A piece that is a
 //    whole segment writes the normalised output.  Otherwise it writes an unnormalised
@@ -293,12 +295,21 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
     int ck = 0;         // chunks consumed by this warp
     const float scale_log2 = a.scale * kLog2e;
     // this lane's register-position permutation and its first reduced value
-    const int X = (NB >= 5) ? (lane << (NB - 5)) : (lane >> (5 - NB));
-    const int Xg = X >> 3;
-    const int Xt = X & 7;
-    const int idx0 = (NV >= 32) ? lane * R : (lane / DUP);
-    const int g_own = idx0 / kChunk;
-    const int t_own = idx0 - g_own * kChunk;
+    // HALF (fp32, d 128, GP 8): the two half-warps score different tokens of a chunk (lanes
+    // [16 hf, 16 hf + 16) tokens 4 hf .. 4 hf + 3), each lane over 8 dims: [4 l, 4 l + 4) and
+    // [64 + 4 l, 64 + 4 l + 4), l = lane % 16 (two 16-byte pieces 256 bytes apart, so the 8
+    // lanes of a shared-memory phase hit 8 distinct bank groups).  The GP x 4 partials of a
+    // lane reduce over its half-warp: 30 shuffles and adds instead of 62, and half the
+    // pair-sums of the dot products.  Afterwards lane (hf, l) holds head l / 2, tokens
+    // 4 hf + 2 (l % 2) + {0, 1}; a head's four lanes differ in lane bits 0 and 4.
+    constexpr bool HALF = std::is_same<KV, float>::value && D == 128 && GP == 8;
+    const int l16 = lane & 15, hf = lane >> 4;
+    const int X = HALF ? (l16 << 1) : (NB >= 5) ? (lane << (NB - 5)) : (lane >> (5 - NB));
+    const int Xg = HALF ? (X >> 2) : (X >> 3);
+    const int Xt = HALF ? (X & 3) : (X & 7);
+    const int g_own = HALF ? (l16 >> 1) : ((NV >= 32) ? lane * R : (lane / DUP)) / kChunk;
+    const int t_own = HALF ? (4 * hf + 2 * (l16 & 1)) : ((NV >= 32) ? lane * R : (lane / DUP)) - g_own * kChunk;
+    const int idx0 = g_own * kChunk + t_own;
 
 #pragma unroll 1
     for (int i = pb; i < pe; ++i) {
@@ -318,17 +329,26 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
         }
 
         // q in permuted slots: slot gs holds head gs ^ Xg
-        float2 q[GP][EP2];
+        constexpr int QP2 = HALF ? 4 : EP2;
+        float2 q[GP][QP2];
 #pragma unroll
         for (int gs = 0; gs < GP; ++gs) {
             const int gh = gs ^ Xg;
-            const float* qp =
-                a.q + (static_cast<int64_t>(b) * a.n_heads + q_head0 + gh) * D + lane * EPL;
+            const bool live = gh < gcount;
+            const float* qh = a.q + (static_cast<int64_t>(b) * a.n_heads + q_head0 + gh) * D;
+            if constexpr (HALF) {
 #pragma unroll
-            for (int e = 0; e < EP2; ++e) {
-                const bool live = gh < gcount;
-                q[gs][e].x = live ? __ldg(qp + 2 * e) : 0.f;
-                q[gs][e].y = (live && 2 * e + 1 < EPL) ? __ldg(qp + 2 * e + 1) : 0.f;
+                for (int e = 0; e < 4; ++e) {
+                    const float* qp = qh + (e >> 1) * 64 + 4 * l16 + 2 * (e & 1);
+                    q[gs][e] = live ? make_float2(__ldg(qp), __ldg(qp + 1)) : make_float2(0.f, 0.f);
+                }
+            } else {
+                const float* qp = qh + lane * EPL;
+#pragma unroll
+                for (int e = 0; e < EP2; ++e) {
+                    q[gs][e].x = live ? __ldg(qp + 2 * e) : 0.f;
+                    q[gs][e].y = (live && 2 * e + 1 < EPL) ? __ldg(qp + 2 * e + 1) : 0.f;
+                }
             }
         }
         float m[GP];
@@ -358,15 +378,29 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
                 const KV* Ks = reinterpret_cast<const KV*>(stage);
                 const KV* Vs = reinterpret_cast<const KV*>(stage + Tr::KSTAGE);
                 // ---- scores at permuted positions, then the selectless transpose-reduce ----
-                float sc[NV];
+                float sc[HALF ? NV / 2 : NV];
+                if constexpr (HALF) {
 #pragma unroll
-                for (int ts = 0; ts < kChunk; ++ts) {
-                    float2 kv[EP2];
-                    load_pairs<KV, EPL>(Ks + (ts ^ Xt) * D + lane * EPL, kv);
+                    for (int ts = 0; ts < 4; ++ts) {
+                        const float* kr = reinterpret_cast<const float*>(Ks) + (4 * hf + (ts ^ Xt)) * D + 4 * l16;
+                        const float4 k0 = *reinterpret_cast<const float4*>(kr);
+                        const float4 k1 = *reinterpret_cast<const float4*>(kr + 64);
+                        const float2 kv[4] = {make_float2(k0.x, k0.y), make_float2(k0.z, k0.w),
+                                              make_float2(k1.x, k1.y), make_float2(k1.z, k1.w)};
 #pragma unroll
-                    for (int gs = 0; gs < GP; ++gs) sc[gs * kChunk + ts] = dot_pairs<EP2>(q[gs], kv);
+                        for (int gs = 0; gs < GP; ++gs) sc[gs * 4 + ts] = dot_pairs<4>(q[gs], kv);
+                    }
+                    transpose_reduce<NV / 2, 8>(sc);
+                } else {
+#pragma unroll
+                    for (int ts = 0; ts < kChunk; ++ts) {
+                        float2 kv[EP2];
+                        load_pairs<KV, EPL>(Ks + (ts ^ Xt) * D + lane * EPL, kv);
+#pragma unroll
+                        for (int gs = 0; gs < GP; ++gs) sc[gs * kChunk + ts] = dot_pairs<EP2>(q[gs], kv);
+                    }
+                    transpose_reduce<NV, 16>(sc);
                 }
-                transpose_reduce<NV, 16>(sc);
                 // ---- online softmax of this lane's head ----
                 float s2[R];
                 float cmax = -INFINITY;
@@ -375,9 +409,14 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
                     s2[r] = (t_own + r < ntok) ? sc[r] * sl2 : -INFINITY;
                     cmax = fmaxf(cmax, s2[r]);
                 }
+                if constexpr (HALF) {
+                    cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 1));
+                    cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 16));
+                } else {
 #pragma unroll
-                for (int mask = LG / 2; mask >= DUP; mask >>= 1)
-                    cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, mask));
+                    for (int mask = LG / 2; mask >= DUP; mask >>= 1)
+                        cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, mask));
+                }
                 const float m_new = fmaxf(m_own, cmax);
                 float p[R];
                 float psum = 0.f;
@@ -386,9 +425,14 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
                     p[r] = exp2f(s2[r] - m_new);
                     psum += p[r];
                 }
+                if constexpr (HALF) {
+                    psum += __shfl_xor_sync(0xffffffffu, psum, 1);
+                    psum += __shfl_xor_sync(0xffffffffu, psum, 16);
+                } else {
 #pragma unroll
-                for (int mask = LG / 2; mask >= DUP; mask >>= 1)
-                    psum += __shfl_xor_sync(0xffffffffu, psum, mask);
+                    for (int mask = LG / 2; mask >= DUP; mask >>= 1)
+                        psum += __shfl_xor_sync(0xffffffffu, psum, mask);
+                }
                 const bool changed = m_new > m_own;
                 l_own = l_own * exp2f(m_own - m_new) + psum;
                 m_own = m_new;
@@ -396,7 +440,7 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
 #pragma unroll
                     for (int r = 0; r < R; ++r) pdup[idx0 + r] = make_float2(p[r], p[r]);
                 }
-                if ((lane % LG) == 0) mbuf[g_own] = m_new;
+                if (HALF ? (lane & 17) == 0 : (lane % LG) == 0) mbuf[g_own] = m_new;
                 __syncwarp();
                 // ---- rescale the accumulators if any head's maximum moved ----
                 if (__any_sync(0xffffffffu, changed)) {
@@ -457,7 +501,7 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
         // ---- end of piece: final output, or partial + fused merge ----
         float lg[GP];
 #pragma unroll
-        for (int gg = 0; gg < GP; ++gg) lg[gg] = __shfl_sync(0xffffffffu, l_own, gg * LG);
+        for (int gg = 0; gg < GP; ++gg) lg[gg] = __shfl_sync(0xffffffffu, l_own, HALF ? 2 * gg : gg * LG);
         const int slot = __ldg(w.piece_slot + i);
         if (slot < 0) {
 #pragma unroll
