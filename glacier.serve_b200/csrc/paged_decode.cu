@@ -47,6 +47,13 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 constexpr int ilog2(int x) { return x <= 1 ? 0 : 1 + ilog2(x / 2); }
 
+// fp32, d 128, a group of 7 in 8 head slots (the half-warp score split with the padding slot
+// compiled out): three CTAs of 4 warps per SM, at most 168 registers and 2 ring stages each --
+// 12 warps per SM hide the per-chunk shuffle and exp latencies better than 8 warps with 3
+// stages.  (A full group of 8 spills more at 168 registers and keeps two CTAs.)
+template <typename KV, int D, int GP, bool LD>
+constexpr bool kThreeCtas = std::is_same<KV, float>::value && D == 128 && GP == 8 && LD;
+
 // Selectless warp transpose-reduce of CUR values per lane (see file comment).  Positions
 // must hold value j at position j ^ X(lane); afterwards lane L holds its R values at
 // positions 0..R-1.
@@ -185,7 +192,7 @@ struct DecodeKernelTraits {
 // output).  Its scores still go through the transpose-reduce, whose lane permutation spreads
 // every head over all slots.
 template <typename KV, int D, int DV, int GP, int NW, int S, bool DYN, bool LD>
-__global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, DecodeWork w,
+__global__ void __launch_bounds__(NW * 32, kThreeCtas<KV, D, GP, LD> ? 3 : 1) paged_decode_kernel(ArenaGeom g, DecodeWork w,
                                                                DecodeArgs a, int group, int cpp) {
     using Tr = DecodeKernelTraits<KV, D, DV, GP, NW, S>;
     constexpr int EPL = Tr::EPL, EPLV = Tr::EPLV, EP2 = Tr::EP2, EV2 = Tr::EV2;
@@ -570,20 +577,21 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_kernel(ArenaGeom g, Deco
 }
 
 // Warp workers per CTA and ring stages per warp.  Sized so that two CTAs fit on an SM
-// (<= ~110 KB of shared memory each) with 2-6 chunks of 8 tokens in flight per warp.
-template <typename KV, int D, int DV>
+// (<= ~110 KB of shared memory each), three for kThreeCtas (<= ~74 KB), with 2-6 chunks of
+// 8 tokens in flight per warp.
+template <typename KV, int D, int DV, int GP, bool LD>
 struct RingShape {
     static constexpr int NW = 4;
     static constexpr int STAGE = kChunk * (D + DV) * static_cast<int>(sizeof(KV));
     static constexpr int S_MAX = sizeof(KV) == 4 ? 3 : 6;
-    static constexpr int S_FIT = (108 * 1024) / (NW * STAGE);
+    static constexpr int S_FIT = ((kThreeCtas<KV, D, GP, LD> ? 72 : 108) * 1024) / (NW * STAGE);
     static constexpr int S = S_FIT < 2 ? 2 : (S_FIT < S_MAX ? S_FIT : S_MAX);
 };
 
 template <typename KV, int D, int DV, int GP, bool LD = false>
 struct Inst {
-    static constexpr int NW = RingShape<KV, D, DV>::NW;
-    static constexpr int S = RingShape<KV, D, DV>::S;
+    static constexpr int NW = RingShape<KV, D, DV, GP, LD>::NW;
+    static constexpr int S = RingShape<KV, D, DV, GP, LD>::S;
     using Tr = DecodeKernelTraits<KV, D, DV, GP, NW, S>;
 
     static cudaError_t prepare() {
