@@ -148,8 +148,11 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_fp8_kernel(const __grid_
             if (++p_piece < pe) p_load();
         }
     };
-#pragma unroll 1
-    for (int s = 0; s < S && p_piece < pe; ++s) issue(s);
+    // Only the first stage goes out at launch: with every warp of the grid requesting at once,
+    // each warp's first chunk lands sooner when it is alone in the queue; the other stages
+    // follow as soon as it has landed.
+    if (p_piece < pe) issue(0);
+    bool primed = S == 1;
 
     bool dead = false;
     int ck = 0;
@@ -223,6 +226,11 @@ __global__ void __launch_bounds__(NW * 32) paged_decode_fp8_kernel(const __grid_
             if (!dead && !__all_sync(0xffffffffu, mbar_wait(&my_bars[st], ph))) {
                 dead = true;
                 if (lane == 0 && a.err) atomicOr(a.err, kErrWaitTimeout);
+            }
+            if (!primed) {
+                primed = true;
+#pragma unroll 1
+                for (int s2 = 1; s2 < S && p_piece < pe && !dead; ++s2) issue(s2);
             }
             if (!dead && blk >= 0 && blk < g.total_blocks && ntok > 0) {
                 const unsigned char* stage = my_stages + static_cast<size_t>(st) * kStage;
