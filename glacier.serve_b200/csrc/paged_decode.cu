@@ -12,7 +12,8 @@
 //  * Every warp is an independent worker.  The host splits the flattened chunk stream of
 //    all segments into equal contiguous ranges, one per warp (warp-level stream-K); a
 //    range intersects a few segments ("pieces").  Each warp prefetches S chunks ahead with
-//    its own ring, across piece boundaries, and never waits for another warp.
+//    its own ring, across piece boundaries, and never waits for another warp (at launch only
+//    its first chunk is requested; the rest of the ring follows once that chunk has landed).
 //  * One pass serves all GP query heads that share the kv head, so each K/V byte is read
 //    from HBM once.  Lane l owns dims [l*D/32, (l+1)*D/32) of q and of the accumulators.
 //    The GP x 8 partial dot products of a chunk are reduced across the warp with a
