@@ -1,6 +1,6 @@
 """The static step layout (gkv_step_set_static): the per-layer kv_append + paged_decode launches
 of a decode iteration captured ONCE in a CUDA graph and replayed every step after upload_step
-(SURVEY's CUDA-graph decode iteration over CudaPagedTransformerRunner.ForwardBatch,
+(a CUDA-graph form of the decode iteration of CudaPagedTransformerRunner.ForwardBatch,
 CudaPagedTransformerRunner.cs:307-364).  Every step changes the batch, the tables, the
 context lengths and the appended slots; each replay must equal the oracle's Store + decode."""
 import math
